@@ -1,0 +1,458 @@
+#!/usr/bin/env python
+"""Benchmark: batched IVF-PQ search QPS at recall@10 on the B200 engine.
+
+One step = one batched search of the configuration's query batch.  `value`
+runs with queries and results resident in HBM; `e2e` goes through the same
+C-ABI call with pinned host buffers (host->device copy of the queries and
+device->host copy of the results inside every timed step).  L2 is flushed
+(a 512 MiB write) between timed steps because the index codes fit in L2.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl engine|reference]
+
+N > 1 runs under torchrun, one rank per GPU: the inverted lists are sharded
+by list across ranks, every rank searches the same batch and the per-rank
+top-k are merged with one NCCL all-gather (strong scaling: total work fixed).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "IVF-PQ queries/sec at recall@10 (1/2/4/8 B200); ADC scan HBM GB/s vs peak"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--config", type=int, default=1)
+    p.add_argument("--impl", choices=["engine", "reference"], default="engine")
+    p.add_argument("--train-sample", type=int, default=131_072)
+    p.add_argument("--train-iters", type=int, default=20)
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return json.loads(path.read_text()), "measured"
+        except Exception:
+            pass
+    return {"hbm_gbs": FALLBACK_HBM_GBS}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.rows: list[list[str]] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.device)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except FileNotFoundError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in self.rows:
+            if len(r) >= 9:
+                for name, val in zip(names, r[5:9]):
+                    if val.lower() == "active":
+                        reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------
+# engine arm
+# --------------------------------------------------------------------------
+
+def run_engine(args):
+    import torch
+    import torch.distributed as dist
+
+    from vicinity_b200 import IVFPQIndex, _lib, nccl_unique_id
+    from vicinity_b200.synthetic import CONFIGS, config_data
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("gloo", timeout=timedelta(seconds=900))
+
+    cfg = CONFIGS[args.config]
+    if cfg["centre"] == "flat":
+        raise SystemExit("config 2 is the flat path; the IVF-PQ bench runs configs 0, 1, 3")
+    n, d, nq, k = cfg["n"], cfg["d"], cfg["nq"], cfg["k"]
+    t0 = time.time()
+    x, q = config_data(args.config, seed=0)
+    ix = IVFPQIndex(d, num_clusters=cfg["nlist"], num_codebooks=cfg["M"], codebook_size=cfg["ks"],
+                    nprobe=cfg["nprobe"], seed=42, device=local)
+    ix.add_items(x)
+    ix.build(training_sample_size=min(args.train_sample, n), kmeans_max_iter=args.train_iters)
+    build_s = time.time() - t0
+    if world > 1:
+        obj = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        ix.shard(rank, world, obj[0], timeout_ms=120_000)
+
+    stream = torch.cuda.current_stream()
+    ix.set_stream(stream.cuda_stream)
+    qd = torch.from_numpy(q).cuda()
+    ids_d = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+    dist_d = torch.empty((nq, k), dtype=torch.float32, device="cuda")
+    cnt_d = torch.empty((nq,), dtype=torch.int32, device="cuda")
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
+
+    def step_device():
+        ix.search_raw(qd.data_ptr(), nq, k, 0, ids_d.data_ptr(), dist_d.data_ptr(), cnt_d.data_ptr())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(step, steps):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        barrier()
+        torch.cuda.synchronize()
+        for a, b in evs:
+            flush.zero_()  # L2 flush between timed steps (not timed)
+            a.record(stream)
+            step()
+            b.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return sum(a.elapsed_time(b) for a, b in evs)
+
+    for _ in range(args.warmup):
+        step_device()
+    torch.cuda.synchronize()
+
+    ix.set_profiling(True)
+    ix.reset_profile()
+    clocks = ClockSampler(local)
+    clocks.start()
+    dev_ms = timed(step_device, args.steps)
+    clock_info = clocks.stop()
+    prof = ix.profile()
+    ix.set_profiling(False)
+    dev_ms_max = max_over_ranks(dev_ms)
+    value = nq * args.steps / (dev_ms_max / 1e3)
+
+    # end to end through the same call with pinned host buffers
+    q_h = torch.from_numpy(q).pin_memory()
+    ids_h = torch.empty((nq, k), dtype=torch.int32).pin_memory()
+    dist_h = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+    cnt_h = torch.empty((nq,), dtype=torch.int32).pin_memory()
+
+    def step_e2e():
+        ix.search_raw(q_h.data_ptr(), nq, k, 0, ids_h.data_ptr(), dist_h.data_ptr(), cnt_h.data_ptr())
+
+    for _ in range(max(1, args.warmup // 2)):
+        step_e2e()
+    e2e_ms = max_over_ranks(timed(step_e2e, args.steps))
+    e2e_value = nq * args.steps / (e2e_ms / 1e3)
+
+    # recall@10 against the exact top-10 of the normalised data (flat engine search)
+    recall = None
+    if rank == 0:
+        import ctypes as C
+
+        vec_d = torch.empty((n, d), dtype=torch.float32, device="cuda")
+        _lib.check(ix._lib.vg_ivfpq_export(ix.handle, _lib.EXPORT_VECTORS, vec_d.data_ptr(), vec_d.numel() * 4))
+        qn = q / np.maximum(np.linalg.norm(q, axis=1, keepdims=True), 1e-30)
+        qn_d = torch.from_numpy(qn.astype(np.float32)).cuda()
+        gt = torch.empty((nq, k), dtype=torch.int32, device="cuda")
+        gd = torch.empty((nq, k), dtype=torch.float32, device="cuda")
+        _lib.check(ix._lib.vg_flat_search_ip(vec_d.data_ptr(), n, qn_d.data_ptr(), nq, d, k, local,
+                                             gt.data_ptr(), gd.data_ptr(), C.c_void_p(0)))
+        got = ids_h.numpy().astype(np.int64)
+        truth = gt.cpu().numpy().astype(np.int64)
+        recall = float(np.mean([len(set(a) & set(b)) / k for a, b in zip(got.tolist(), truth.tolist())]))
+        del vec_d
+
+    # roofline of the fused probe kernel (live CUDA events on the launching stream)
+    peaks, peak_kind = measured_peaks()
+    calls = max(1, int(prof["calls"]))
+    scan_ms = prof["scan_ms"] / calls
+    scan_bytes = prof["scanned_code_bytes"] / calls
+    achieved = scan_bytes / (scan_ms * 1e-3) / 1e9 if scan_ms > 0 else 0.0
+    peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
+    traffic = scan_traffic_from_profiles(args.config)
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_baseline = cpu_baseline_port(ix, x, q, cfg, args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 1),
+            "unit": "queries/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(dev_ms_max / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic: seeded Gaussian mixture with the configuration's generator (no dataset)",
+            "config": {
+                "workload": cfg["name"], "n": n, "d": d, "nlist": cfg["nlist"], "M": cfg["M"],
+                "codebook_size": cfg["ks"], "nprobe": cfg["nprobe"], "k": k, "batch": nq,
+                "recall_at_10": None if recall is None else round(recall, 4),
+                "train_sample": min(args.train_sample, n), "train_iters": args.train_iters,
+                "l2": "flushed between timed steps (512 MiB write; index codes fit in L2)",
+                "parallelism": f"list-sharded x{world}" if world > 1 else "single GPU",
+                "build_s": round(build_s, 1),
+            },
+            "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
+                    "h2d_bytes_per_step": nq * d * 4, "d2h_bytes_per_step": nq * k * 8 + nq * 4},
+            "roofline": {
+                "kernel": "ivfpq_scan (fused residual + ADC table + code scan + per-pair top-k)",
+                "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_kind,
+                "algorithmic_bytes_per_launch": int(scan_bytes), "launch_ms": round(scan_ms, 4),
+            },
+            "phases_ms_per_step": {key: round(prof[key] / calls, 4) for key in
+                                   ("normalize_ms", "coarse_ms", "select_ms", "pairs_ms", "scan_ms", "merge_ms",
+                                    "collective_ms", "total_ms")},
+            "gpu_launches": int(prof["kernel_launches"]),
+            "clocks": clock_info,
+            "cpu_baseline": cpu_baseline,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        ix.close()
+        dist.destroy_process_group()
+
+
+def scan_traffic_from_profiles(config: int):
+    """DRAM bytes per launch of the probe kernel from the committed ncu
+    summary of this workload (None until one exists)."""
+    path = ROOT / "profiles" / f"ivfpq_scan_c{config}.md"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(float(line.split(":", 1)[1].strip()))
+            except ValueError:
+                return None
+    return None
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline_port(ix, x, q, cfg, budget_s):
+    """The oracle port of the reference search (search.rs:1175-1391) on the
+    same index (same centroids, codebooks, codes) on all host threads."""
+    import oracle as orc
+
+    threads = host_threads()
+    info = ix.info()
+    ref = orc.OracleIndex(cfg["d"], int(info.num_centroids), cfg["M"], cfg["ks"], cfg["nprobe"])
+    ref.set_trained(ix.centroids(), ix.codebooks())
+    ref.add(ix.doc_ids(), x)
+    ref.adopt_codes(ix.assignments(), ix.codes())
+    probe = q[: max(threads * 2, 16)]
+    t = time.time()
+    ref.search_batch(probe, cfg["k"], threads=threads)
+    per_q = (time.time() - t) / probe.shape[0]
+    s = int(min(q.shape[0], max(probe.shape[0], budget_s / max(per_q, 1e-9))))
+    t = time.time()
+    ref.search_batch(q[:s], cfg["k"], threads=threads)
+    el = time.time() - t
+    return {"value": round(s / el, 1), "unit": "queries/s", "cores": threads, "kind": "port",
+            "sample": f"{s} of the {q.shape[0]} batch queries ({el:.1f} s), oracle port of the reference search on the same index"}
+
+
+# --------------------------------------------------------------------------
+# reference arm: the reference's CPU algorithm (oracle port) on host cores
+# --------------------------------------------------------------------------
+
+def numpy_train_and_encode(x, cfg, sample, iters, seed=42):
+    """CPU index construction for the reference arm (untimed): spherical
+    Lloyd for the coarse lists and Euclidean Lloyd per PQ subspace, with
+    BLAS matmuls; returns centroids, codebooks, assignments and codes."""
+    rng = np.random.default_rng(seed)
+    n, d = x.shape
+    L, M, ks = cfg["nlist"], cfg["M"], cfg["ks"]
+    dsub = d // M
+    xn = x / np.maximum(np.linalg.norm(x, axis=1, keepdims=True), 1e-10)
+    xn = xn.astype(np.float32)
+    tr = xn[np.sort(rng.choice(n, min(sample, n), replace=False))]
+    cent = tr[rng.choice(tr.shape[0], L, replace=False)].copy()
+
+    def assign(rows, c):
+        out = np.empty(rows.shape[0], np.int64)
+        blk = max(1, (1 << 27) // c.shape[0])
+        for s in range(0, rows.shape[0], blk):
+            out[s:s + blk] = np.argmax(rows[s:s + blk] @ c.T, axis=1)
+        return out
+
+    for _ in range(iters):
+        a = assign(tr, cent)
+        sums = np.zeros_like(cent)
+        np.add.at(sums, a, tr)
+        cnt = np.bincount(a, minlength=L)
+        nz = cnt > 0
+        sums[nz] /= cnt[nz, None]
+        norms = np.linalg.norm(sums[nz], axis=1, keepdims=True)
+        cent[nz] = sums[nz] / np.maximum(norms, 1e-10)
+    a_tr = assign(tr, cent)
+    res = tr - cent[a_tr]
+    cb = np.empty((M, ks, dsub), np.float32)
+    for m in range(M):
+        sub = res[:, m * dsub:(m + 1) * dsub]
+        cw = sub[rng.choice(sub.shape[0], ks, replace=False)].copy()
+        for _ in range(iters):
+            dd = (sub ** 2).sum(1, keepdims=True) - 2 * sub @ cw.T + (cw ** 2).sum(1)[None]
+            lab = np.argmin(dd, axis=1)
+            s2 = np.zeros_like(cw)
+            np.add.at(s2, lab, sub)
+            c2 = np.bincount(lab, minlength=ks)
+            nz = c2 > 0
+            cw[nz] = s2[nz] / c2[nz, None]
+        cb[m] = cw
+    assign_all = assign(xn, cent).astype(np.uint32)
+    codes = np.empty((n, M), np.uint8)
+    blk = 1 << 18
+    for s in range(0, n, blk):
+        r = xn[s:s + blk] - cent[assign_all[s:s + blk]]
+        for m in range(M):
+            sub = r[:, m * dsub:(m + 1) * dsub]
+            dd = (sub ** 2).sum(1, keepdims=True) - 2 * sub @ cb[m].T + (cb[m] ** 2).sum(1)[None]
+            codes[s:s + blk, m] = np.argmin(dd, axis=1)
+    return cent, cb, assign_all, codes
+
+
+def run_reference(args):
+    if int(os.environ.get("RANK", "0")) != 0:
+        return  # rank 0 alone runs the CPU reference arm
+    import oracle as orc
+    from vicinity_b200.synthetic import CONFIGS, config_data
+
+    cfg = CONFIGS[args.config]
+    threads = host_threads()
+    x, q = config_data(args.config, seed=0)
+    cent, cb, assign, codes = numpy_train_and_encode(x, cfg, min(args.train_sample, 65_536), 8)
+    ref = orc.OracleIndex(cfg["d"], cfg["nlist"], cfg["M"], cfg["ks"], cfg["nprobe"])
+    ref.set_trained(cent, cb)
+    ref.add(np.arange(x.shape[0], dtype=np.uint32), x)
+    ref.adopt_codes(assign, codes)
+    probe = q[: max(2 * threads, 16)]
+    t = time.time()
+    ref.search_batch(probe, cfg["k"], threads=threads)
+    per_q = (time.time() - t) / probe.shape[0]
+    # each step: a bounded sample sized so warm-up + steps take about two minutes
+    per_step_s = 120.0 / max(1, args.steps + args.warmup)
+    s = int(min(q.shape[0], max(threads, per_step_s / max(per_q, 1e-9))))
+    for i in range(args.warmup):
+        ref.search_batch(q[:s], cfg["k"], threads=threads)
+    total = 0.0
+    for i in range(args.steps):
+        sl = q[(i * s) % max(1, q.shape[0] - s):][:s]
+        t = time.time()
+        ref.search_batch(sl, cfg["k"], threads=threads)
+        total += time.time() - t
+    value = s * args.steps / total
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "queries/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total / args.steps * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: seeded Gaussian mixture with the configuration's generator (no dataset)",
+        "config": {"workload": cfg["name"], "n": cfg["n"], "d": cfg["d"], "nlist": cfg["nlist"],
+                   "M": cfg["M"], "codebook_size": cfg["ks"], "nprobe": cfg["nprobe"], "k": cfg["k"],
+                   "batch": cfg["nq"], "step_sample": s},
+        "cpu_baseline": {"value": round(value, 1), "unit": "queries/s", "cores": threads, "kind": "port",
+                         "sample": f"{s} queries per step of the {cfg['nq']}-query batch, oracle port of the reference search on all host threads"},
+        "e2e": {"value": round(value, 1), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_engine(args)
+
+
+if __name__ == "__main__":
+    main()

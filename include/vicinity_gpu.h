@@ -1,0 +1,211 @@
+/*
+ * vicinity_gpu.h -- C ABI of the B200 IVF-PQ engine.
+ *
+ * This is the boundary a host binding links against in place of the
+ * reference's in-process Rust implementation of `vicinity::ivf_pq`
+ * (vicinity 0.12.0).  Each entry point cites the reference interface it
+ * replaces (paths are relative to the vicinity crate root).
+ *
+ * Conventions
+ *   - Every function returns an int status: VG_OK (0) or a negative
+ *     vg_status mirroring the reference's RetrieveError variants
+ *     (src/error.rs:17-147).  vg_last_error() returns the message of the
+ *     last failure on the calling thread.  Nothing throws across the ABI.
+ *   - Array arguments may be host or device memory; device pointers
+ *     (checked with cudaPointerGetAttributes) are used in place, host
+ *     buffers are copied.  Output buffers are caller-owned.
+ *   - A vg_index is externally synchronised, as the reference's callers
+ *     serialise searches (src/python.rs:1081-1084).  Search calls block
+ *     until their outputs are written.
+ *   - Distances follow the reference: squared L2 between the L2-normalised
+ *     query and the reconstruction, no square root (src/ivf_pq/mod.rs:100-110).
+ */
+#ifndef VICINITY_GPU_H
+#define VICINITY_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum vg_status {
+  VG_OK = 0,
+  VG_ERR_EMPTY_INDEX = -1,        /* RetrieveError::EmptyIndex */
+  VG_ERR_INVALID_PARAMETER = -2,  /* RetrieveError::InvalidParameter */
+  VG_ERR_INVALID_CONFIG = -3,     /* RetrieveError::InvalidConfig */
+  VG_ERR_NOT_BUILT = -4,          /* RetrieveError::NotBuilt */
+  VG_ERR_ALREADY_BUILT = -5,      /* RetrieveError::AlreadyBuilt */
+  VG_ERR_UNSUPPORTED = -6,        /* RetrieveError::Unsupported */
+  VG_ERR_DIMENSION_MISMATCH = -7, /* RetrieveError::DimensionMismatch */
+  VG_ERR_IO = -8,                 /* RetrieveError::Io */
+  VG_ERR_FORMAT = -9,             /* RetrieveError::FormatError */
+  VG_ERR_CUDA = -10,              /* device failure (no reference variant) */
+  VG_ERR_NCCL = -11,              /* collective failure (no reference variant) */
+  VG_ERR_OUT_OF_MEMORY = -12,     /* device allocation failed */
+  VG_ERR_OTHER = -13              /* RetrieveError::Other */
+} vg_status;
+
+/* src/ivf_pq/search.rs:286-329 (IVFPQParams). */
+typedef struct vg_ivfpq_params {
+  uint64_t num_clusters;  /* default 1024 */
+  uint64_t nprobe;        /* default 100 */
+  uint64_t num_codebooks; /* default 8 */
+  uint64_t codebook_size; /* default 256, at most 256 */
+  int32_t use_opq;        /* must be 0: OPQ is not built by this engine */
+  int32_t reserved;
+  uint64_t seed;          /* default 42 */
+} vg_ivfpq_params;
+
+typedef struct vg_ivfpq_info {
+  uint64_t dimension, num_vectors, num_clusters, num_centroids, nprobe;
+  uint64_t num_codebooks, codebook_size, subvector_dim;
+  int32_t built, trained, compacted, use_opq;
+  int32_t device, shard_rank, shard_world, reserved;
+  uint64_t device_bytes; /* bytes of index state resident on the device */
+} vg_ivfpq_info;
+
+/* Per-phase device timings (CUDA events on the index stream) and counters,
+ * accumulated over search calls while profiling is on.  Mirrors
+ * IVFPQSearchProfile (src/ivf_pq/search.rs:86-139). */
+typedef struct vg_search_profile {
+  double h2d_ms, normalize_ms, coarse_ms, select_ms, pairs_ms, scan_ms,
+      merge_ms, collective_ms, d2h_ms, total_ms;
+  uint64_t calls, queries, probed_pairs, scanned_vectors, scanned_code_bytes;
+  uint64_t kernel_launches, scan_launches;
+} vg_search_profile;
+
+typedef struct vg_index vg_index;
+
+/* Message of the last failed call on this thread (always NUL-terminated). */
+int vg_last_error(char *buf, size_t len);
+
+/* Engine version, e.g. "vicinity-b200 0.1.0 (sm_100a)". */
+const char *vg_version(void);
+
+/* Number of CUDA devices visible (0 when none). */
+int vg_device_count(int *out);
+
+/* src/ivf_pq/search.rs:382-413 (IVFPQIndex::new): InvalidConfig for a zero
+ * dimension, codebook_size > 256, or num_codebooks not dividing dim. */
+int vg_ivfpq_create(size_t dim, const vg_ivfpq_params *params, int device,
+                    vg_index **out);
+
+/* Drop (frees every device buffer the index owns). */
+int vg_ivfpq_destroy(vg_index *ix);
+
+/* src/ivf_pq/search.rs:478-512 (add / add_slice) over n rows: every row is
+ * L2-normalised on insertion; AlreadyBuilt after build. */
+int vg_ivfpq_add(vg_index *ix, const uint32_t *doc_ids, const float *x,
+                 size_t n);
+
+/* Adopt trained coarse centroids [num_centroids][dim] and PQ codebooks
+ * [num_codebooks][codebook_size][dim/num_codebooks], so that build skips
+ * training (the state src/ivf_pq/search.rs:606-775 produces before
+ * encoding; also the parity hook for identical codebooks). */
+int vg_ivfpq_set_trained(vg_index *ix, const float *centroids,
+                         size_t num_centroids, const float *codebooks);
+
+/* src/ivf_pq/search.rs:515-787 (build, build_with_training_sample,
+ * build_with_training_options): training_sample_size 0 trains on every
+ * vector; kmeans_max_iter bounds both k-means stages.  Then assigns,
+ * encodes residuals and lays out the inverted lists on the device. */
+int vg_ivfpq_build(vg_index *ix, size_t training_sample_size,
+                   size_t kmeans_max_iter);
+
+/* src/ivf_pq/search.rs:347 (set_nprobe). */
+int vg_ivfpq_set_nprobe(vg_index *ix, size_t nprobe);
+
+/* Run the index's device work on `stream` (a cudaStream_t of the index's
+ * device; NULL restores the index's own stream).  No reference counterpart:
+ * the reference has no device streams. */
+int vg_ivfpq_set_stream(vg_index *ix, void *stream);
+
+/* src/ivf_pq/search.rs:352-379 getters, plus engine state. */
+int vg_ivfpq_get_info(const vg_index *ix, vg_ivfpq_info *out);
+
+/* src/ivf_pq/search.rs:1087-1093 (search) over nq query rows, batched as
+ * src/python.rs:745-795 (batch_search): out_ids/out_dist are [nq][k] in
+ * ascending distance; rows with fewer than k results are padded with id
+ * 0xFFFFFFFF and +inf, and out_count[nq] (nullable) holds the real count.
+ * nprobe 0 uses the index default. k at most 256. */
+int vg_ivfpq_search_batch(vg_index *ix, const float *queries, size_t nq,
+                          size_t k, size_t nprobe, uint32_t *out_ids,
+                          float *out_dist, uint32_t *out_count);
+
+/* src/ivf_pq/search.rs:1117-1158 (search_reranked) over nq rows: the
+ * candidate_pool best approximate candidates re-scored by exact cosine
+ * distance 1 - dot.  Unsupported after compact. */
+int vg_ivfpq_search_batch_reranked(vg_index *ix, const float *queries,
+                                   size_t nq, size_t k, size_t candidate_pool,
+                                   size_t nprobe, uint32_t *out_ids,
+                                   float *out_dist, uint32_t *out_count);
+
+/* src/ivf_pq/search.rs:857-884 (reconstruct) of insertion index idx. */
+int vg_ivfpq_reconstruct(const vg_index *ix, size_t idx, float *out);
+
+/* src/ivf_pq/search.rs:901-904 (compact): drop the raw vectors. */
+int vg_ivfpq_compact(vg_index *ix);
+
+/* Copies of index state for parity checks and persistence (host or device
+ * destination, `bytes` must match):
+ *   VG_EXPORT_CENTROIDS    f32 [num_centroids][dim]
+ *   VG_EXPORT_CODEBOOKS    f32 [M][ks][dsub]
+ *   VG_EXPORT_ASSIGNMENTS  u32 [n]       list of each insertion index
+ *   VG_EXPORT_CODES        u8  [n][M]    vector order (codes.bin)
+ *   VG_EXPORT_LIST_OFFSETS u64 [num_centroids+1] vector offsets
+ *   VG_EXPORT_LIST_IDS     u32 [n]       insertion indices, list order
+ *   VG_EXPORT_DOC_IDS      u32 [n]
+ *   VG_EXPORT_VECTORS      f32 [n][dim]  normalised rows (until compact) */
+enum {
+  VG_EXPORT_CENTROIDS = 0,
+  VG_EXPORT_CODEBOOKS = 1,
+  VG_EXPORT_ASSIGNMENTS = 2,
+  VG_EXPORT_CODES = 3,
+  VG_EXPORT_LIST_OFFSETS = 4,
+  VG_EXPORT_LIST_IDS = 5,
+  VG_EXPORT_DOC_IDS = 6,
+  VG_EXPORT_VECTORS = 7
+};
+int vg_ivfpq_export(const vg_index *ix, int what, void *dst, size_t bytes);
+
+/* Turn per-phase profiling on (1) or off (0); reset clears the totals. */
+int vg_ivfpq_set_profiling(vg_index *ix, int on);
+int vg_ivfpq_get_profile(const vg_index *ix, vg_search_profile *out);
+int vg_ivfpq_reset_profile(vg_index *ix);
+
+/* ---- multi-GPU: inverted lists sharded by list across ranks ----------- */
+
+/* A 128-byte NCCL unique id for a new communicator (call on one rank and
+ * distribute the bytes to the others). */
+int vg_nccl_unique_id(uint8_t out[128]);
+
+/* Make a built index one shard of a world_size-rank group: lists are
+ * assigned to ranks by greedy size-balanced packing (largest list first),
+ * the rank scans only its lists, and each search merges the per-rank
+ * top-k with one all-gather.  Every rank must hold the same built index
+ * and call every search with the same queries. */
+int vg_ivfpq_shard(vg_index *ix, int rank, int world_size,
+                   const uint8_t nccl_id[128], int timeout_ms);
+
+/* The list owner map used by vg_ivfpq_shard (host-only; no device work):
+ * owner[l] in [0, world_size) for list sizes sizes[0..num_lists). */
+int vg_shard_assign_lists(const uint64_t *sizes, size_t num_lists,
+                          int world_size, int32_t *owner);
+
+/* ---- exact flat search ------------------------------------------------ */
+
+/* Exhaustive inner-product search (src/distance.rs:125-130, distance -dot,
+ * ascending, ties to the lower row; the exhaustive ground truth of
+ * src/benchmark/evaluation.rs:250-268): out_ids/out_dist [nq][k] padded
+ * like vg_ivfpq_search_batch. Runs on `device`. k at most 256. */
+int vg_flat_search_ip(const float *db, size_t n, const float *queries,
+                      size_t nq, size_t dim, size_t k, int device,
+                      uint32_t *out_ids, float *out_dist, uint32_t *out_count);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VICINITY_GPU_H */

@@ -1,0 +1,28 @@
+"""B200-native IVF-PQ search engine with the interface of vicinity's IVF-PQ path.
+
+The compute path is the CUDA library ``libvicinity_gpu.so`` (sm_100a),
+reached through its C ABI (``include/vicinity_gpu.h``); this package is the
+Python host binding, shaped like the reference's ``pyvicinity.IVFPQIndex``.
+"""
+from ._lib import VicinityError, device_count
+from .ivf_pq import (
+    MISSING_DISTANCE,
+    MISSING_LABEL,
+    IVFPQIndex,
+    default_ivfpq_codebooks,
+    flat_search_ip,
+    nccl_unique_id,
+    shard_assign_lists,
+)
+
+__all__ = [
+    "IVFPQIndex",
+    "MISSING_DISTANCE",
+    "MISSING_LABEL",
+    "VicinityError",
+    "default_ivfpq_codebooks",
+    "device_count",
+    "flat_search_ip",
+    "nccl_unique_id",
+    "shard_assign_lists",
+]

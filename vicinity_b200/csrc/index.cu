@@ -1,0 +1,1127 @@
+// C ABI of the B200 IVF-PQ engine (include/vicinity_gpu.h): the index object,
+// its device-resident layout, build and search orchestration, sharding over
+// NCCL, and the exact flat search.
+//
+// Device layout of a built index (one GPU):
+//   vectors    f32 [n][d]          L2-normalised rows (dropped by compact)
+//   doc_ids    u32 [n]             caller ids by insertion index
+//   centroids  f32 [Lc][d]         coarse centroids (Lc <= num_clusters)
+//   codebooks  f32 [M][ks][dsub]   product quantizer (pq.rs:396-398 layout)
+//   assign     u32 [n]             list of each insertion index
+//   codes      u8  [n][M]          codes in insertion order (codes.bin)
+//   list_off   u64 [Lc+1]          CSR offsets of the inverted lists
+//   list_ids   u32 [n]             insertion indices, ascending within a list
+//   code_off   u64 [Lc]            16-byte aligned byte offset of each list's
+//   list_codes u8                  list-contiguous codes (list_codes.bin)
+//   pack_off   u64 [Lc]            (ks == 16) byte offset of each list's
+//   packed     u8                  32-vector FastScan blocks (pq_simd.rs:426)
+#include <nccl.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <numeric>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "vicinity_gpu.h"
+
+using namespace vg;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string &msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+  int code = e == cudaErrorMemoryAllocation ? VG_ERR_OUT_OF_MEMORY : VG_ERR_CUDA;
+  cudaGetLastError();  // clear a sticky launch error so later calls start clean
+  return fail(code, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define VG_CU(call)                                         \
+  do {                                                      \
+    cudaError_t vg_e_ = (call);                             \
+    if (vg_e_ != cudaSuccess) return cuda_fail(vg_e_, #call); \
+  } while (0)
+
+#define VG_TRY(call)            \
+  do {                          \
+    int vg_s_ = (call);         \
+    if (vg_s_ != VG_OK) return vg_s_; \
+  } while (0)
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+// Owning device buffer with grow-only capacity.  reserve() discards contents.
+struct DevBuf {
+  void *p = nullptr;
+  size_t cap = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf &) = delete;
+  DevBuf &operator=(const DevBuf &) = delete;
+  DevBuf(DevBuf &&o) noexcept : p(o.p), cap(o.cap) {
+    o.p = nullptr;
+    o.cap = 0;
+  }
+  DevBuf &operator=(DevBuf &&o) noexcept {
+    if (this != &o) {
+      release();
+      p = o.p;
+      cap = o.cap;
+      o.p = nullptr;
+      o.cap = 0;
+    }
+    return *this;
+  }
+  ~DevBuf() { release(); }
+  cudaError_t reserve(size_t bytes) {
+    if (bytes <= cap) return cudaSuccess;
+    release();
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e == cudaSuccess) cap = bytes;
+    else p = nullptr;
+    return e;
+  }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    cap = 0;
+  }
+  template <class T>
+  T *as() const {
+    return static_cast<T *>(p);
+  }
+};
+
+bool is_device_ptr(const void *ptr) {
+  if (!ptr) return false;
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+uint64_t splitmix64(uint64_t &s) {
+  uint64_t z = (s += 0x9E3779B97F4A7C15ull);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// Seeded Fisher-Yates prefix: the first `take` entries of a permutation of
+// [0, n).  (The reference shuffles with rand's StdRng, search.rs:808-810;
+// training is not bit-reproducible across implementations, so any seeded
+// permutation serves.)
+std::vector<uint32_t> seeded_prefix(size_t n, size_t take, uint64_t seed) {
+  std::vector<uint32_t> idx(n);
+  std::iota(idx.begin(), idx.end(), 0u);
+  uint64_t s = seed;
+  for (size_t i = 0; i < take && i + 1 < n; ++i) {
+    size_t j = i + static_cast<size_t>(splitmix64(s) % (n - i));
+    std::swap(idx[i], idx[j]);
+  }
+  idx.resize(take);
+  return idx;
+}
+
+constexpr size_t kDistBudgetBytes = size_t(1) << 30;  // coarse distance tile
+constexpr size_t kAssignChunk = size_t(4) << 20;      // rows per argmin launch
+constexpr int kPhaseEvents = 12;
+
+}  // namespace
+
+struct vg_index {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;      // stream in use
+  cudaStream_t own_stream = nullptr;  // stream the index created
+  size_t d = 0, dsub = 0;
+  vg_ivfpq_params params{};
+  size_t n = 0, cap = 0;
+  size_t num_centroids = 0;
+  bool trained = false, built = false, compacted = false;
+
+  DevBuf vectors, doc_ids, centroids, codebooks, assign, codes;
+  DevBuf list_off, list_ids, code_off, list_codes, pack_off, packed;
+  std::vector<uint64_t> h_list_off;
+  std::vector<uint32_t> h_doc_ids;
+
+  // sharding
+  int rank = 0, world = 1;
+  ncclComm_t comm = nullptr;
+  int comm_timeout_ms = 60000;
+  DevBuf owner;
+
+  // search workspace
+  DevBuf ws_q, ws_qn, ws_dist, ws_probes, ws_pdist, ws_counts, ws_cursor, ws_work, ws_scalars,
+      ws_pair_out, ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count;
+  DevBuf stats;  // u64 [pairs, vectors, code bytes] accumulated while profiling
+
+  // profiling
+  bool profiling = false;
+  cudaEvent_t ev[kPhaseEvents] = {};
+  vg_search_profile prof{};
+  uint64_t launches = 0;
+
+  size_t device_bytes() const {
+    return vectors.cap + doc_ids.cap + centroids.cap + codebooks.cap + assign.cap + codes.cap +
+           list_off.cap + list_ids.cap + code_off.cap + list_codes.cap + pack_off.cap + packed.cap +
+           owner.cap;
+  }
+};
+
+namespace {
+
+int validate_shape(size_t dim, const vg_ivfpq_params &p) {
+  if (dim == 0) return fail(VG_ERR_INVALID_CONFIG, "invalid config `dimension`: must be greater than 0");
+  if (p.codebook_size > 256)
+    return fail(VG_ERR_INVALID_CONFIG,
+                "invalid config `codebook_size`: must be at most 256 because PQ codes are stored as u8");
+  if (p.num_codebooks == 0 || p.codebook_size == 0 || p.num_clusters == 0)
+    return fail(VG_ERR_INVALID_CONFIG,
+                "invalid config `num_clusters, num_codebooks, codebook_size`: must all be greater than 0");
+  if (dim % p.num_codebooks != 0)
+    return fail(VG_ERR_INVALID_CONFIG, "invalid config `dimension`: must be divisible by num_codebooks");
+  if (p.use_opq)
+    return fail(VG_ERR_UNSUPPORTED, "unsupported: OPQ rotation is not built by the B200 engine");
+  if (p.codebook_size == 16 && p.num_codebooks > 65535 / 255)
+    return fail(VG_ERR_INVALID_PARAMETER,
+                "FastScan accumulates LUT terms in u16: at most 257 codebooks are supported");
+  if (p.num_clusters > 0x7fffffffull || p.num_codebooks > 4096)
+    return fail(VG_ERR_INVALID_CONFIG, "invalid config: num_clusters or num_codebooks out of range");
+  return VG_OK;
+}
+
+int sync_stream(vg_index *ix) {
+  if (!ix->comm) {
+    VG_CU(cudaStreamSynchronize(ix->stream));
+    return VG_OK;
+  }
+  // Bounded wait: a peer that never arrives must not hang the caller.
+  auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(ix->comm_timeout_ms);
+  for (;;) {
+    cudaError_t q = cudaStreamQuery(ix->stream);
+    if (q == cudaSuccess) return VG_OK;
+    if (q != cudaErrorNotReady) return cuda_fail(q, "cudaStreamQuery");
+    ncclResult_t ar = ncclSuccess;
+    ncclCommGetAsyncError(ix->comm, &ar);
+    if (ar != ncclSuccess && ar != ncclInProgress) {
+      ncclCommAbort(ix->comm);
+      ix->comm = nullptr;
+      return fail(VG_ERR_NCCL, std::string("NCCL async error: ") + ncclGetErrorString(ar));
+    }
+    if (std::chrono::steady_clock::now() > deadline) {
+      ncclCommAbort(ix->comm);
+      ix->comm = nullptr;
+      return fail(VG_ERR_NCCL, "collective did not complete within the shard timeout; communicator aborted");
+    }
+    std::this_thread::yield();
+  }
+}
+
+int nccl_wait_ready(ncclComm_t comm, int timeout_ms) {
+  auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms);
+  for (;;) {
+    ncclResult_t r = ncclSuccess;
+    ncclCommGetAsyncError(comm, &r);
+    if (r == ncclSuccess) return VG_OK;
+    if (r != ncclInProgress) return fail(VG_ERR_NCCL, std::string("NCCL: ") + ncclGetErrorString(r));
+    if (std::chrono::steady_clock::now() > deadline)
+      return fail(VG_ERR_NCCL, "NCCL operation did not complete within the timeout");
+    std::this_thread::yield();
+  }
+}
+
+void mark(vg_index *ix, int i) {
+  if (ix->profiling) cudaEventRecord(ix->ev[i], ix->stream);
+}
+
+// ---- training (device Lloyd iterations; not bit-pinned to the reference's
+// third-party k-means, see src/partitioning/kmeans.rs:64-90) --------------
+
+int train(vg_index *ix, size_t n_train, size_t max_iter) {
+  cudaStream_t s = ix->stream;
+  const size_t d = ix->d, M = ix->params.num_codebooks, ks = ix->params.codebook_size;
+  const size_t Lc = std::min<size_t>(ix->params.num_clusters, n_train);
+
+  // training rows (ascending, search.rs:789-814)
+  std::vector<uint32_t> rows;
+  if (n_train < ix->n) {
+    rows = seeded_prefix(ix->n, n_train, ix->params.seed);
+    std::sort(rows.begin(), rows.end());
+  }
+  DevBuf train_x, rows_d, best, assign_t, assign_prev, keys_sorted, ids_sorted, iota, seg, temp, scal, newc;
+  const float *X = ix->vectors.as<float>();
+  if (!rows.empty()) {
+    VG_CU(rows_d.reserve(n_train * 4));
+    VG_CU(cudaMemcpyAsync(rows_d.p, rows.data(), n_train * 4, cudaMemcpyHostToDevice, s));
+    VG_CU(train_x.reserve(n_train * d * 4));
+    VG_CU(launch_gather_rows(X, static_cast<int>(d), rows_d.as<uint32_t>(), n_train, train_x.as<float>(), s));
+    X = train_x.as<float>();
+  }
+
+  // coarse: spherical Lloyd from a seeded sample of training rows
+  VG_CU(ix->centroids.reserve(Lc * d * 4));
+  {
+    std::vector<uint32_t> init = seeded_prefix(n_train, Lc, ix->params.seed);
+    DevBuf init_d;
+    VG_CU(init_d.reserve(Lc * 4));
+    VG_CU(cudaMemcpyAsync(init_d.p, init.data(), Lc * 4, cudaMemcpyHostToDevice, s));
+    VG_CU(launch_gather_rows(X, static_cast<int>(d), init_d.as<uint32_t>(), Lc, ix->centroids.as<float>(), s));
+    VG_CU(cudaStreamSynchronize(s));
+  }
+  VG_CU(best.reserve(n_train * 8));
+  VG_CU(assign_t.reserve(n_train * 4));
+  VG_CU(assign_prev.reserve(n_train * 4));
+  VG_CU(keys_sorted.reserve(n_train * 4));
+  VG_CU(ids_sorted.reserve(n_train * M * 4 > n_train * 4 ? n_train * M * 4 : n_train * 4));
+  VG_CU(iota.reserve(n_train * M * 4));
+  VG_CU(seg.reserve((std::max(Lc, M * ks) + 1) * 4));
+  VG_CU(scal.reserve(16));
+  VG_CU(newc.reserve(std::max(Lc * d, M * ks * (d / M)) * 4));
+  size_t temp_bytes = 0, tb2 = 0;
+  VG_CU(sort_pairs_u32(nullptr, temp_bytes, nullptr, nullptr, nullptr, nullptr, n_train * M, 32, s));
+  VG_CU(sort_pairs_u32(nullptr, tb2, nullptr, nullptr, nullptr, nullptr, n_train, 32, s));
+  temp_bytes = std::max(temp_bytes, tb2);
+  VG_CU(temp.reserve(temp_bytes));
+  VG_CU(launch_iota(iota.as<uint32_t>(), n_train, s));
+
+  auto assign_rows = [&](const float *cent, size_t L) -> int {
+    for (size_t r0 = 0; r0 < n_train; r0 += kAssignChunk) {
+      size_t rows_n = std::min(kAssignChunk, n_train - r0);
+      VG_CU(cudaMemsetAsync(best.as<unsigned long long>() + r0, 0xff, rows_n * 8, s));
+      VG_CU(launch_coarse_argmin(X + r0 * d, rows_n, cent, L, static_cast<int>(d),
+                                 best.as<unsigned long long>() + r0, s));
+    }
+    return VG_OK;
+  };
+
+  unsigned int changed = 1;
+  for (size_t it = 0; it < max_iter && changed; ++it) {
+    VG_TRY(assign_rows(ix->centroids.as<float>(), Lc));
+    VG_CU(cudaMemsetAsync(scal.p, 0, 4, s));
+    VG_CU(launch_keys_to_assign(best.as<unsigned long long>(), n_train, assign_t.as<uint32_t>(),
+                                it ? assign_prev.as<uint32_t>() : nullptr, scal.as<unsigned int>(), s));
+    size_t tb = temp_bytes;
+    VG_CU(sort_pairs_u32(temp.p, tb, assign_t.as<uint32_t>(), keys_sorted.as<uint32_t>(), iota.as<uint32_t>(),
+                         ids_sorted.as<uint32_t>(), n_train, 32, s));
+    VG_CU(launch_segments(keys_sorted.as<uint32_t>(), n_train, Lc, seg.as<uint32_t>(), s));
+    VG_CU(launch_kmeans_update(X, static_cast<int>(d), ids_sorted.as<uint32_t>(), seg.as<uint32_t>(), Lc,
+                               ix->centroids.as<float>(), newc.as<float>(), 1, s));
+    VG_CU(cudaMemcpyAsync(ix->centroids.p, newc.p, Lc * d * 4, cudaMemcpyDeviceToDevice, s));
+    VG_CU(cudaMemcpyAsync(assign_prev.p, assign_t.p, n_train * 4, cudaMemcpyDeviceToDevice, s));
+    VG_CU(cudaMemcpyAsync(&changed, scal.p, 4, cudaMemcpyDeviceToHost, s));
+    VG_CU(cudaStreamSynchronize(s));
+    if (it == 0) changed = 1;
+  }
+
+  // PQ: Euclidean Lloyd per subspace on training residuals (pq.rs:452-501)
+  VG_TRY(assign_rows(ix->centroids.as<float>(), Lc));
+  VG_CU(launch_keys_to_assign(best.as<unsigned long long>(), n_train, assign_t.as<uint32_t>(), nullptr, nullptr, s));
+  DevBuf resid, codes_t, codes_prev, pkeys;
+  VG_CU(resid.reserve(n_train * d * 4));
+  VG_CU(launch_residuals(X, n_train, static_cast<int>(d), assign_t.as<uint32_t>(), ix->centroids.as<float>(),
+                         resid.as<float>(), s));
+  const size_t dsub = d / M;
+  VG_CU(ix->codebooks.reserve(M * ks * dsub * 4));
+  {
+    std::vector<float> cb_init(M * ks * dsub);
+    std::vector<float> host_res;  // gather the seeded rows per subspace on the host
+    for (size_t m = 0; m < M; ++m) {
+      std::vector<uint32_t> pick = seeded_prefix(n_train, ks, ix->params.seed + m);
+      DevBuf pick_d, rows_out;
+      VG_CU(pick_d.reserve(ks * 4));
+      VG_CU(rows_out.reserve(ks * d * 4));
+      VG_CU(cudaMemcpyAsync(pick_d.p, pick.data(), ks * 4, cudaMemcpyHostToDevice, s));
+      VG_CU(launch_gather_rows(resid.as<float>(), static_cast<int>(d), pick_d.as<uint32_t>(), ks,
+                               rows_out.as<float>(), s));
+      host_res.resize(ks * d);
+      VG_CU(cudaMemcpyAsync(host_res.data(), rows_out.p, ks * d * 4, cudaMemcpyDeviceToHost, s));
+      VG_CU(cudaStreamSynchronize(s));
+      for (size_t c = 0; c < ks; ++c)
+        std::memcpy(&cb_init[(m * ks + c) * dsub], &host_res[c * d + m * dsub], dsub * 4);
+    }
+    VG_CU(cudaMemcpyAsync(ix->codebooks.p, cb_init.data(), cb_init.size() * 4, cudaMemcpyHostToDevice, s));
+  }
+  VG_CU(codes_t.reserve(n_train * M));
+  VG_CU(codes_prev.reserve(n_train * M));
+  VG_CU(pkeys.reserve(n_train * M * 4));
+  DevBuf pvals, pkeys_sorted;
+  VG_CU(pvals.reserve(n_train * M * 4));
+  VG_CU(pkeys_sorted.reserve(n_train * M * 4));
+  int end_bit = 1;
+  while ((size_t(1) << end_bit) < M * ks) ++end_bit;
+  changed = 1;
+  for (size_t it = 0; it < max_iter && changed; ++it) {
+    VG_CU(launch_encode_residuals(resid.as<float>(), n_train, static_cast<int>(d), ix->codebooks.as<float>(),
+                                  static_cast<int>(M), static_cast<int>(ks), codes_t.as<uint8_t>(), s));
+    VG_CU(cudaMemsetAsync(scal.p, 0, 4, s));
+    if (it) VG_CU(launch_count_diff_u8(codes_t.as<uint8_t>(), codes_prev.as<uint8_t>(), n_train * M,
+                                       scal.as<unsigned int>(), s));
+    VG_CU(launch_pq_keys(codes_t.as<uint8_t>(), n_train, static_cast<int>(M), static_cast<int>(ks),
+                         pkeys.as<uint32_t>(), pvals.as<uint32_t>(), s));
+    size_t tb = temp_bytes;
+    VG_CU(sort_pairs_u32(temp.p, tb, pkeys.as<uint32_t>(), pkeys_sorted.as<uint32_t>(), pvals.as<uint32_t>(),
+                         ids_sorted.as<uint32_t>(), n_train * M, end_bit, s));
+    VG_CU(launch_segments(pkeys_sorted.as<uint32_t>(), n_train * M, M * ks, seg.as<uint32_t>(), s));
+    VG_CU(launch_pq_update(resid.as<float>(), n_train, static_cast<int>(d), static_cast<int>(M),
+                           static_cast<int>(ks), ids_sorted.as<uint32_t>(), seg.as<uint32_t>(),
+                           ix->codebooks.as<float>(), newc.as<float>(), s));
+    VG_CU(cudaMemcpyAsync(ix->codebooks.p, newc.p, M * ks * dsub * 4, cudaMemcpyDeviceToDevice, s));
+    VG_CU(cudaMemcpyAsync(codes_prev.p, codes_t.p, n_train * M, cudaMemcpyDeviceToDevice, s));
+    VG_CU(cudaMemcpyAsync(&changed, scal.p, 4, cudaMemcpyDeviceToHost, s));
+    VG_CU(cudaStreamSynchronize(s));
+    if (it == 0) changed = 1;
+  }
+  ix->num_centroids = Lc;
+  ix->trained = true;
+  return VG_OK;
+}
+
+// ---- encode and list layout (search.rs:620-848) ---------------------------
+
+int encode_and_layout(vg_index *ix) {
+  cudaStream_t s = ix->stream;
+  const size_t n = ix->n, d = ix->d, M = ix->params.num_codebooks, ks = ix->params.codebook_size;
+  const size_t Lc = ix->num_centroids;
+  DevBuf best;
+  VG_CU(best.reserve(std::min(n, kAssignChunk) * 8));
+  VG_CU(ix->assign.reserve(n * 4));
+  for (size_t r0 = 0; r0 < n; r0 += kAssignChunk) {
+    size_t rows = std::min(kAssignChunk, n - r0);
+    VG_CU(cudaMemsetAsync(best.p, 0xff, rows * 8, s));
+    VG_CU(launch_coarse_argmin(ix->vectors.as<float>() + r0 * d, rows, ix->centroids.as<float>(), Lc,
+                               static_cast<int>(d), best.as<unsigned long long>(), s));
+    VG_CU(launch_keys_to_assign(best.as<unsigned long long>(), rows, ix->assign.as<uint32_t>() + r0, nullptr,
+                                nullptr, s));
+  }
+  best.release();
+  VG_CU(ix->codes.reserve(n * M));
+  VG_CU(launch_encode(ix->vectors.as<float>(), n, static_cast<int>(d), ix->assign.as<uint32_t>(),
+                      ix->centroids.as<float>(), ix->codebooks.as<float>(), static_cast<int>(M),
+                      static_cast<int>(ks), ix->codes.as<uint8_t>(), s));
+
+  // stable sort by list keeps insertion order inside each list
+  DevBuf iota, sorted_lists, temp, seg;
+  VG_CU(iota.reserve(n * 4));
+  VG_CU(sorted_lists.reserve(n * 4));
+  VG_CU(ix->list_ids.reserve(n * 4));
+  VG_CU(seg.reserve((Lc + 1) * 4));
+  VG_CU(launch_iota(iota.as<uint32_t>(), n, s));
+  size_t temp_bytes = 0;
+  VG_CU(sort_pairs_u32(nullptr, temp_bytes, nullptr, nullptr, nullptr, nullptr, n, 32, s));
+  VG_CU(temp.reserve(temp_bytes));
+  VG_CU(sort_pairs_u32(temp.p, temp_bytes, ix->assign.as<uint32_t>(), sorted_lists.as<uint32_t>(),
+                       iota.as<uint32_t>(), ix->list_ids.as<uint32_t>(), n, 32, s));
+  VG_CU(launch_segments(sorted_lists.as<uint32_t>(), n, Lc, seg.as<uint32_t>(), s));
+  std::vector<uint32_t> hseg(Lc + 1);
+  VG_CU(cudaMemcpyAsync(hseg.data(), seg.p, (Lc + 1) * 4, cudaMemcpyDeviceToHost, s));
+  VG_CU(cudaStreamSynchronize(s));
+
+  ix->h_list_off.assign(hseg.begin(), hseg.end());
+  std::vector<uint64_t> h_code_off(Lc), h_pack_off(Lc);
+  uint64_t code_bytes = 0, pack_bytes = 0;
+  for (size_t l = 0; l < Lc; ++l) {
+    uint64_t len = ix->h_list_off[l + 1] - ix->h_list_off[l];
+    h_code_off[l] = code_bytes;
+    code_bytes += (len * M + 15) & ~uint64_t(15);
+    h_pack_off[l] = pack_bytes;
+    if (ks == 16 && len >= 16) pack_bytes += ((len + 31) / 32) * M * 16;
+  }
+  VG_CU(ix->list_off.reserve((Lc + 1) * 8));
+  VG_CU(ix->code_off.reserve(Lc * 8));
+  VG_CU(ix->pack_off.reserve(Lc * 8));
+  VG_CU(ix->list_codes.reserve(std::max<uint64_t>(code_bytes, 16)));
+  VG_CU(cudaMemcpyAsync(ix->list_off.p, ix->h_list_off.data(), (Lc + 1) * 8, cudaMemcpyHostToDevice, s));
+  VG_CU(cudaMemcpyAsync(ix->code_off.p, h_code_off.data(), Lc * 8, cudaMemcpyHostToDevice, s));
+  VG_CU(cudaMemcpyAsync(ix->pack_off.p, h_pack_off.data(), Lc * 8, cudaMemcpyHostToDevice, s));
+  VG_CU(launch_gather_list_codes(ix->codes.as<uint8_t>(), ix->list_ids.as<uint32_t>(), sorted_lists.as<uint32_t>(),
+                                 n, static_cast<int>(M), ix->list_off.as<uint64_t>(), ix->code_off.as<uint64_t>(),
+                                 ix->list_codes.as<uint8_t>(), s));
+  if (ks == 16) {
+    VG_CU(ix->packed.reserve(std::max<uint64_t>(pack_bytes, 16)));
+    VG_CU(launch_pack_lists_4bit(ix->list_codes.as<uint8_t>(), ix->list_off.as<uint64_t>(),
+                                 ix->code_off.as<uint64_t>(), ix->pack_off.as<uint64_t>(), Lc, static_cast<int>(M),
+                                 ix->packed.as<uint8_t>(), s));
+  }
+  VG_CU(cudaStreamSynchronize(s));
+  ix->built = true;
+  return VG_OK;
+}
+
+// ---- search -------------------------------------------------------------
+
+int write_padding(vg_index *ix, size_t nq, size_t k, uint32_t *out_ids, float *out_dist, uint32_t *out_count) {
+  std::vector<uint32_t> ids(nq * k, 0xffffffffu), cnt(nq, 0);
+  std::vector<float> dist(nq * k, __builtin_inff());
+  if (nq * k) {
+    VG_CU(cudaMemcpyAsync(out_ids, ids.data(), nq * k * 4, cudaMemcpyDefault, ix->stream));
+    VG_CU(cudaMemcpyAsync(out_dist, dist.data(), nq * k * 4, cudaMemcpyDefault, ix->stream));
+  }
+  if (out_count && nq) VG_CU(cudaMemcpyAsync(out_count, cnt.data(), nq * 4, cudaMemcpyDefault, ix->stream));
+  VG_CU(cudaStreamSynchronize(ix->stream));
+  return VG_OK;
+}
+
+int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t pool, size_t nprobe,
+                uint32_t *out_ids, float *out_dist, uint32_t *out_count) {
+  if (!ix->built) return fail(VG_ERR_NOT_BUILT, "IVF-PQ index is not built: cannot search");
+  if (k > 256) return fail(VG_ERR_INVALID_PARAMETER, "k must be at most 256");
+  const bool rerank = pool > 0;
+  if (rerank && ix->compacted)
+    return fail(VG_ERR_UNSUPPORTED,
+                "unsupported: search_reranked after compact(); use search() instead, or keep raw vectors");
+  const size_t kk = rerank ? std::max(pool, k) : k;
+  if (kk > 256) return fail(VG_ERR_INVALID_PARAMETER, "candidate_pool must be at most 256");
+  if (nq == 0 || k == 0) return write_padding(ix, nq, k, out_ids, out_dist, out_count);
+  if ((nq && !queries) || !out_ids || !out_dist)
+    return fail(VG_ERR_INVALID_PARAMETER, "null query or output buffer");
+  const size_t Lc = ix->num_centroids, d = ix->d, M = ix->params.num_codebooks;
+  const size_t P = std::min(nprobe ? nprobe : static_cast<size_t>(ix->params.nprobe), Lc);
+  if (P == 0) return write_padding(ix, nq, k, out_ids, out_dist, out_count);
+  if (nq * P > 0xffffffffull) return fail(VG_ERR_INVALID_PARAMETER, "nq * nprobe must fit in 32 bits");
+  cudaStream_t s = ix->stream;
+  const bool prof = ix->profiling;
+  uint64_t launches0 = ix->launches;
+
+  mark(ix, 0);
+  const float *dq = queries;
+  if (!is_device_ptr(queries)) {
+    VG_CU(ix->ws_q.reserve(nq * d * 4));
+    VG_CU(cudaMemcpyAsync(ix->ws_q.p, queries, nq * d * 4, cudaMemcpyHostToDevice, s));
+    dq = ix->ws_q.as<float>();
+  }
+  mark(ix, 1);
+  VG_CU(ix->ws_qn.reserve(nq * d * 4));
+  VG_CU(launch_normalize_rows(dq, nq, static_cast<int>(d), ix->ws_qn.as<float>(), s));
+  ix->launches += 1;
+  mark(ix, 2);
+
+  // coarse distances + top-nprobe, tiled over queries
+  const size_t tile = std::max<size_t>(1, std::min(nq, kDistBudgetBytes / (Lc * 4)));
+  VG_CU(ix->ws_dist.reserve(tile * Lc * 4));
+  VG_CU(ix->ws_probes.reserve(nq * P * 4));
+  VG_CU(ix->ws_pdist.reserve(nq * P * 4));
+  double coarse_ms = 0, select_ms = 0;
+  for (size_t r0 = 0; r0 < nq; r0 += tile) {
+    size_t rows = std::min(tile, nq - r0);
+    VG_CU(launch_coarse_dist(ix->ws_qn.as<float>() + r0 * d, rows, ix->centroids.as<float>(), Lc,
+                             static_cast<int>(d), ix->ws_dist.as<float>(), Lc, s));
+    mark(ix, 3);
+    VG_CU(launch_select_rows(ix->ws_dist.as<float>(), rows, Lc, Lc, static_cast<int>(P),
+                             ix->ws_probes.as<uint32_t>() + r0 * P, ix->ws_pdist.as<float>() + r0 * P, P, 0, s));
+    mark(ix, 4);
+    ix->launches += 2;
+    if (prof && r0 + tile < nq) {  // accumulate per tile when tiled
+      float a = 0, b = 0;
+      VG_CU(cudaEventSynchronize(ix->ev[4]));
+      cudaEventElapsedTime(&a, ix->ev[2], ix->ev[3]);
+      cudaEventElapsedTime(&b, ix->ev[3], ix->ev[4]);
+      coarse_ms += a;
+      select_ms += b;
+      mark(ix, 2);
+    }
+  }
+
+  // list-major pair grouping
+  VG_CU(ix->ws_counts.reserve(Lc * 4));
+  VG_CU(ix->ws_cursor.reserve(Lc * 4));
+  VG_CU(ix->ws_work.reserve(nq * P * 4));
+  VG_CU(ix->ws_scalars.reserve(64));
+  uint32_t *d_total = ix->ws_scalars.as<uint32_t>();
+  uint32_t *d_counter = d_total + 1;
+  VG_CU(launch_build_pairs(ix->ws_probes.as<uint32_t>(), nq, static_cast<int>(P),
+                           ix->world > 1 ? ix->owner.as<uint8_t>() : nullptr, Lc, ix->ws_counts.as<uint32_t>(),
+                           ix->ws_cursor.as<uint32_t>(), ix->ws_work.as<uint32_t>(), d_total,
+                           prof ? ix->list_off.as<uint64_t>() : nullptr, static_cast<int>(M),
+                           ix->params.codebook_size == 16, prof ? ix->stats.as<unsigned long long>() : nullptr, s));
+  ix->launches += 3;
+  VG_CU(ix->ws_pair_out.reserve(nq * P * kk * 8));
+  VG_CU(cudaMemsetAsync(ix->ws_pair_out.p, 0xff, nq * P * kk * 8, s));
+  VG_CU(cudaMemsetAsync(d_counter, 0, 4, s));
+  mark(ix, 5);
+
+  vg::ScanParams sp{};
+  sp.qn = ix->ws_qn.as<float>();
+  sp.centroids = ix->centroids.as<float>();
+  sp.codebooks = ix->codebooks.as<float>();
+  sp.probes = ix->ws_probes.as<uint32_t>();
+  sp.work = ix->ws_work.as<uint32_t>();
+  sp.total = d_total;
+  sp.counter = d_counter;
+  sp.list_off = ix->list_off.as<uint64_t>();
+  sp.code_off = ix->code_off.as<uint64_t>();
+  sp.list_codes = ix->list_codes.as<uint8_t>();
+  sp.pack_off = ix->pack_off.as<uint64_t>();
+  sp.packed = ix->packed.as<uint8_t>();
+  sp.list_ids = ix->list_ids.as<uint32_t>();
+  sp.d = static_cast<int>(d);
+  sp.M = static_cast<int>(M);
+  sp.ks = static_cast<int>(ix->params.codebook_size);
+  sp.dsub = static_cast<int>(ix->dsub);
+  sp.P = static_cast<int>(P);
+  sp.k = static_cast<int>(kk);
+  sp.pair_out = ix->ws_pair_out.as<unsigned long long>();
+  VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
+  ix->launches += 1;
+  mark(ix, 6);
+
+  // outputs: device pointers are written in place, host ones via staging
+  const bool dev_out = is_device_ptr(out_ids) && is_device_ptr(out_dist) && (!out_count || is_device_ptr(out_count));
+  uint32_t *o_ids = out_ids, *o_cnt = out_count;
+  float *o_dist = out_dist;
+  if (!dev_out) {
+    VG_CU(ix->ws_out_ids.reserve(nq * k * 4));
+    VG_CU(ix->ws_out_dist.reserve(nq * k * 4));
+    VG_CU(ix->ws_out_count.reserve(nq * 4));
+    o_ids = ix->ws_out_ids.as<uint32_t>();
+    o_dist = ix->ws_out_dist.as<float>();
+    o_cnt = ix->ws_out_count.as<uint32_t>();
+  }
+  const uint32_t *doc_map = ix->doc_ids.as<uint32_t>();
+  const size_t width = P * kk;
+  if (ix->world == 1) {
+    if (rerank) {
+      VG_CU(ix->ws_keys.reserve(nq * kk * 8));
+      VG_CU(launch_merge_keys(ix->ws_pair_out.as<unsigned long long>(), nq, width, width, static_cast<int>(kk),
+                              nullptr, nullptr, nullptr, nullptr, ix->ws_keys.as<unsigned long long>(), s));
+      mark(ix, 7);
+      VG_CU(launch_rerank(ix->ws_qn.as<float>(), ix->vectors.as<float>(), static_cast<int>(d),
+                          ix->ws_keys.as<unsigned long long>(), nq, static_cast<int>(kk), static_cast<int>(k),
+                          doc_map, o_ids, o_dist, o_cnt, s));
+      ix->launches += 2;
+    } else {
+      VG_CU(launch_merge_keys(ix->ws_pair_out.as<unsigned long long>(), nq, width, width, static_cast<int>(k),
+                              doc_map, o_ids, o_dist, o_cnt, nullptr, s));
+      mark(ix, 7);
+      ix->launches += 1;
+    }
+  } else {
+    VG_CU(ix->ws_keys.reserve(nq * kk * 8));
+    VG_CU(ix->ws_all_keys.reserve(static_cast<size_t>(ix->world) * nq * kk * 8));
+    VG_CU(launch_merge_keys(ix->ws_pair_out.as<unsigned long long>(), nq, width, width, static_cast<int>(kk),
+                            nullptr, nullptr, nullptr, nullptr, ix->ws_keys.as<unsigned long long>(), s));
+    ix->launches += 1;
+    mark(ix, 7);
+    ncclResult_t r = ncclAllGather(ix->ws_keys.p, ix->ws_all_keys.p, nq * kk, ncclUint64, ix->comm, s);
+    if (r == ncclInProgress) VG_TRY(nccl_wait_ready(ix->comm, ix->comm_timeout_ms));
+    else if (r != ncclSuccess) return fail(VG_ERR_NCCL, std::string("ncclAllGather: ") + ncclGetErrorString(r));
+    mark(ix, 8);
+    if (rerank) {
+      VG_CU(launch_merge_shards(ix->ws_all_keys.as<unsigned long long>(), ix->world, nq, static_cast<int>(kk),
+                                nullptr, nullptr, nullptr, nullptr, ix->ws_keys.as<unsigned long long>(), s));
+      VG_CU(launch_rerank(ix->ws_qn.as<float>(), ix->vectors.as<float>(), static_cast<int>(d),
+                          ix->ws_keys.as<unsigned long long>(), nq, static_cast<int>(kk), static_cast<int>(k),
+                          doc_map, o_ids, o_dist, o_cnt, s));
+      ix->launches += 2;
+    } else {
+      VG_CU(launch_merge_shards(ix->ws_all_keys.as<unsigned long long>(), ix->world, nq, static_cast<int>(k),
+                                doc_map, o_ids, o_dist, o_cnt, nullptr, s));
+      ix->launches += 1;
+    }
+  }
+  mark(ix, 9);
+  if (!dev_out) {
+    VG_CU(cudaMemcpyAsync(out_ids, o_ids, nq * k * 4, cudaMemcpyDeviceToHost, s));
+    VG_CU(cudaMemcpyAsync(out_dist, o_dist, nq * k * 4, cudaMemcpyDeviceToHost, s));
+    if (out_count) VG_CU(cudaMemcpyAsync(out_count, o_cnt, nq * 4, cudaMemcpyDeviceToHost, s));
+  }
+  mark(ix, 10);
+  VG_TRY(sync_stream(ix));
+
+  if (prof) {
+    auto el = [&](int a, int b) {
+      float ms = 0;
+      cudaEventElapsedTime(&ms, ix->ev[a], ix->ev[b]);
+      return static_cast<double>(ms);
+    };
+    vg_search_profile &p = ix->prof;
+    p.h2d_ms += el(0, 1);
+    p.normalize_ms += el(1, 2);
+    p.coarse_ms += coarse_ms + el(2, 3);
+    p.select_ms += select_ms + el(3, 4);
+    p.pairs_ms += el(4, 5);
+    p.scan_ms += el(5, 6);
+    if (ix->world > 1) {
+      p.merge_ms += el(6, 7) + el(8, 9);
+      p.collective_ms += el(7, 8);
+    } else {
+      p.merge_ms += el(6, 9);
+    }
+    p.d2h_ms += el(9, 10);
+    p.total_ms += el(0, 10);
+    p.calls += 1;
+    p.queries += nq;
+    p.kernel_launches += ix->launches - launches0;
+    p.scan_launches += 1;
+  }
+  return VG_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+int vg_last_error(char *buf, size_t len) {
+  if (!buf || len == 0) return VG_ERR_INVALID_PARAMETER;
+  size_t m = std::min(len - 1, g_last_error.size());
+  std::memcpy(buf, g_last_error.data(), m);
+  buf[m] = '\0';
+  return VG_OK;
+}
+
+const char *vg_version(void) { return "vicinity-b200 0.1.0 (sm_100a)"; }
+
+int vg_device_count(int *out) {
+  if (!out) return fail(VG_ERR_INVALID_PARAMETER, "null output");
+  int c = 0;
+  cudaError_t e = cudaGetDeviceCount(&c);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    c = 0;
+  }
+  *out = c;
+  return VG_OK;
+}
+
+int vg_ivfpq_create(size_t dim, const vg_ivfpq_params *params, int device, vg_index **out) {
+  if (!params || !out) return fail(VG_ERR_INVALID_PARAMETER, "null params or output");
+  *out = nullptr;
+  VG_TRY(validate_shape(dim, *params));
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count) {
+    cudaGetLastError();
+    return fail(VG_ERR_CUDA, "no CUDA device " + std::to_string(device) + " (the engine has no CPU path)");
+  }
+  DeviceGuard g(device);
+  auto *ix = new vg_index();
+  ix->device = device;
+  ix->d = dim;
+  ix->params = *params;
+  ix->dsub = dim / params->num_codebooks;
+  cudaDeviceGetAttribute(&ix->num_sms, cudaDevAttrMultiProcessorCount, device);
+  cudaError_t e = cudaStreamCreateWithFlags(&ix->own_stream, cudaStreamNonBlocking);
+  ix->stream = ix->own_stream;
+  for (int i = 0; e == cudaSuccess && i < kPhaseEvents; ++i) e = cudaEventCreate(&ix->ev[i]);
+  if (e != cudaSuccess) {
+    vg_ivfpq_destroy(ix);
+    return cuda_fail(e, "stream/event creation");
+  }
+  *out = ix;
+  return VG_OK;
+}
+
+int vg_ivfpq_destroy(vg_index *ix) {
+  if (!ix) return VG_OK;
+  {
+    DeviceGuard g(ix->device);
+    if (ix->stream) cudaStreamSynchronize(ix->stream);
+    if (ix->comm) ncclCommDestroy(ix->comm);
+    for (DevBuf *b : {&ix->vectors, &ix->doc_ids, &ix->centroids, &ix->codebooks, &ix->assign, &ix->codes,
+                      &ix->list_off, &ix->list_ids, &ix->code_off, &ix->list_codes, &ix->pack_off, &ix->packed,
+                      &ix->owner, &ix->ws_q, &ix->ws_qn, &ix->ws_dist, &ix->ws_probes, &ix->ws_pdist,
+                      &ix->ws_counts, &ix->ws_cursor, &ix->ws_work, &ix->ws_scalars, &ix->ws_pair_out,
+                      &ix->ws_keys, &ix->ws_all_keys, &ix->ws_out_ids, &ix->ws_out_dist, &ix->ws_out_count,
+                      &ix->stats})
+      b->release();
+    for (int i = 0; i < kPhaseEvents; ++i)
+      if (ix->ev[i]) cudaEventDestroy(ix->ev[i]);
+    if (ix->own_stream) cudaStreamDestroy(ix->own_stream);
+  }
+  delete ix;
+  return VG_OK;
+}
+
+int vg_ivfpq_add(vg_index *ix, const uint32_t *doc_ids, const float *x, size_t n) {
+  if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
+  if (ix->built)
+    return fail(VG_ERR_ALREADY_BUILT, "IVF-PQ index is already built: cannot add vectors");
+  if (n == 0) return VG_OK;
+  if (!doc_ids || !x) return fail(VG_ERR_INVALID_PARAMETER, "null doc_ids or vectors");
+  if (ix->n + n > 0xffffffffull) return fail(VG_ERR_INVALID_PARAMETER, "at most 2^32 - 1 vectors per index");
+  DeviceGuard g(ix->device);
+  cudaStream_t s = ix->stream;
+  const size_t d = ix->d;
+  if (ix->n + n > ix->cap) {
+    size_t cap = std::max(ix->n + n, ix->cap * 2);
+    DevBuf nv, nd;
+    VG_CU(nv.reserve(cap * d * 4));
+    VG_CU(nd.reserve(cap * 4));
+    if (ix->n) {
+      VG_CU(cudaMemcpyAsync(nv.p, ix->vectors.p, ix->n * d * 4, cudaMemcpyDeviceToDevice, s));
+      VG_CU(cudaMemcpyAsync(nd.p, ix->doc_ids.p, ix->n * 4, cudaMemcpyDeviceToDevice, s));
+      VG_CU(cudaStreamSynchronize(s));
+    }
+    ix->vectors = std::move(nv);
+    ix->doc_ids = std::move(nd);
+    ix->cap = cap;
+  }
+  const float *src = x;
+  DevBuf stage;
+  if (!is_device_ptr(x)) {
+    VG_CU(stage.reserve(n * d * 4));
+    VG_CU(cudaMemcpyAsync(stage.p, x, n * d * 4, cudaMemcpyHostToDevice, s));
+    src = stage.as<float>();
+  }
+  VG_CU(launch_normalize_rows(src, n, static_cast<int>(d), ix->vectors.as<float>() + ix->n * d, s));
+  VG_CU(cudaMemcpyAsync(ix->doc_ids.as<uint32_t>() + ix->n, doc_ids, n * 4, cudaMemcpyDefault, s));
+  size_t old = ix->h_doc_ids.size();
+  ix->h_doc_ids.resize(old + n);
+  VG_CU(cudaMemcpyAsync(ix->h_doc_ids.data() + old, doc_ids, n * 4, cudaMemcpyDefault, s));
+  VG_CU(cudaStreamSynchronize(s));
+  ix->n += n;
+  return VG_OK;
+}
+
+int vg_ivfpq_set_trained(vg_index *ix, const float *centroids, size_t num_centroids, const float *codebooks) {
+  if (!ix || !centroids || !codebooks) return fail(VG_ERR_INVALID_PARAMETER, "null argument");
+  if (ix->built) return fail(VG_ERR_ALREADY_BUILT, "IVF-PQ index is already built: cannot replace its training");
+  if (num_centroids == 0 || num_centroids > ix->params.num_clusters)
+    return fail(VG_ERR_INVALID_PARAMETER, "num_centroids must be in 1..=num_clusters");
+  DeviceGuard g(ix->device);
+  const size_t M = ix->params.num_codebooks, ks = ix->params.codebook_size;
+  VG_CU(ix->centroids.reserve(num_centroids * ix->d * 4));
+  VG_CU(ix->codebooks.reserve(M * ks * ix->dsub * 4));
+  VG_CU(cudaMemcpy(ix->centroids.p, centroids, num_centroids * ix->d * 4, cudaMemcpyDefault));
+  VG_CU(cudaMemcpy(ix->codebooks.p, codebooks, M * ks * ix->dsub * 4, cudaMemcpyDefault));
+  ix->num_centroids = num_centroids;
+  ix->trained = true;
+  return VG_OK;
+}
+
+int vg_ivfpq_build(vg_index *ix, size_t training_sample_size, size_t kmeans_max_iter) {
+  if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
+  if (ix->built) return VG_OK;  // search.rs:550-552
+  if (ix->n == 0) return fail(VG_ERR_EMPTY_INDEX, "index is empty");
+  const size_t ks = ix->params.codebook_size, L = ix->params.num_clusters;
+  if (ix->n < ks)
+    return fail(VG_ERR_INVALID_PARAMETER,
+                "invalid parameter: IVF-PQ requires at least codebook_size training vectors (got " +
+                    std::to_string(ix->n) + " vectors, codebook_size = " + std::to_string(ks) + ")");
+  if (kmeans_max_iter == 0)
+    return fail(VG_ERR_INVALID_CONFIG, "invalid config `kmeans_max_iter`: must be greater than 0");
+  const size_t n_train = (training_sample_size == 0 || training_sample_size >= ix->n) ? ix->n : training_sample_size;
+  const size_t min_train = std::max(std::min(L, ix->n), ks);
+  if (n_train < min_train)
+    return fail(VG_ERR_INVALID_PARAMETER, "invalid parameter: IVF-PQ training sample is too small (got " +
+                                              std::to_string(n_train) + ", need at least " +
+                                              std::to_string(min_train) + ")");
+  DeviceGuard g(ix->device);
+  if (!ix->trained) VG_TRY(train(ix, n_train, kmeans_max_iter));
+  return encode_and_layout(ix);
+}
+
+int vg_ivfpq_set_nprobe(vg_index *ix, size_t nprobe) {
+  if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
+  ix->params.nprobe = nprobe;
+  return VG_OK;
+}
+
+int vg_ivfpq_set_stream(vg_index *ix, void *stream) {
+  if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
+  DeviceGuard g(ix->device);
+  VG_CU(cudaStreamSynchronize(ix->stream));
+  ix->stream = stream ? static_cast<cudaStream_t>(stream) : ix->own_stream;
+  return VG_OK;
+}
+
+int vg_ivfpq_get_info(const vg_index *ix, vg_ivfpq_info *out) {
+  if (!ix || !out) return fail(VG_ERR_INVALID_PARAMETER, "null argument");
+  std::memset(out, 0, sizeof(*out));
+  out->dimension = ix->d;
+  out->num_vectors = ix->n;
+  out->num_clusters = ix->params.num_clusters;
+  out->num_centroids = ix->num_centroids;
+  out->nprobe = ix->params.nprobe;
+  out->num_codebooks = ix->params.num_codebooks;
+  out->codebook_size = ix->params.codebook_size;
+  out->subvector_dim = ix->dsub;
+  out->built = ix->built;
+  out->trained = ix->trained;
+  out->compacted = ix->compacted;
+  out->use_opq = ix->params.use_opq;
+  out->device = ix->device;
+  out->shard_rank = ix->rank;
+  out->shard_world = ix->world;
+  out->device_bytes = ix->device_bytes();
+  return VG_OK;
+}
+
+int vg_ivfpq_search_batch(vg_index *ix, const float *queries, size_t nq, size_t k, size_t nprobe,
+                          uint32_t *out_ids, float *out_dist, uint32_t *out_count) {
+  if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
+  DeviceGuard g(ix->device);
+  return search_impl(ix, queries, nq, k, 0, nprobe, out_ids, out_dist, out_count);
+}
+
+int vg_ivfpq_search_batch_reranked(vg_index *ix, const float *queries, size_t nq, size_t k, size_t candidate_pool,
+                                   size_t nprobe, uint32_t *out_ids, float *out_dist, uint32_t *out_count) {
+  if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
+  DeviceGuard g(ix->device);
+  return search_impl(ix, queries, nq, k, std::max<size_t>(candidate_pool, 1), nprobe, out_ids, out_dist, out_count);
+}
+
+int vg_ivfpq_reconstruct(const vg_index *ix, size_t idx, float *out) {
+  if (!ix || !out) return fail(VG_ERR_INVALID_PARAMETER, "null argument");
+  if (!ix->built) return fail(VG_ERR_INVALID_PARAMETER, "invalid parameter: index must be built before reconstruct");
+  if (idx >= ix->n)
+    return fail(VG_ERR_INVALID_PARAMETER, "invalid parameter: vector index " + std::to_string(idx) +
+                                              " out of range (num_vectors = " + std::to_string(ix->n) + ")");
+  DeviceGuard g(ix->device);
+  const size_t d = ix->d, M = ix->params.num_codebooks, ks = ix->params.codebook_size, dsub = ix->dsub;
+  uint32_t a = 0;
+  std::vector<uint8_t> code(M);
+  std::vector<float> cent(d), cb(M * ks * dsub);
+  VG_CU(cudaMemcpy(&a, ix->assign.as<uint32_t>() + idx, 4, cudaMemcpyDeviceToHost));
+  VG_CU(cudaMemcpy(code.data(), ix->codes.as<uint8_t>() + idx * M, M, cudaMemcpyDeviceToHost));
+  VG_CU(cudaMemcpy(cent.data(), ix->centroids.as<float>() + static_cast<size_t>(a) * d, d * 4, cudaMemcpyDeviceToHost));
+  VG_CU(cudaMemcpy(cb.data(), ix->codebooks.p, cb.size() * 4, cudaMemcpyDeviceToHost));
+  std::vector<float> res(d);
+  for (size_t m = 0; m < M; ++m)
+    for (size_t j = 0; j < dsub; ++j) res[m * dsub + j] = cb[(m * ks + code[m]) * dsub + j] + cent[m * dsub + j];
+  VG_CU(cudaMemcpy(out, res.data(), d * 4, cudaMemcpyDefault));
+  return VG_OK;
+}
+
+int vg_ivfpq_compact(vg_index *ix) {
+  if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
+  if (!ix->built) return fail(VG_ERR_NOT_BUILT, "IVF-PQ index is not built: cannot compact");
+  DeviceGuard g(ix->device);
+  ix->vectors.release();
+  ix->compacted = true;
+  return VG_OK;
+}
+
+int vg_ivfpq_export(const vg_index *ix, int what, void *dst, size_t bytes) {
+  if (!ix || (!dst && bytes)) return fail(VG_ERR_INVALID_PARAMETER, "null argument");
+  DeviceGuard g(ix->device);
+  const size_t n = ix->n, d = ix->d, M = ix->params.num_codebooks, ks = ix->params.codebook_size;
+  const void *src = nullptr;
+  size_t need = 0;
+  bool needs_build = true;
+  switch (what) {
+    case VG_EXPORT_CENTROIDS: src = ix->centroids.p; need = ix->num_centroids * d * 4; needs_build = false; break;
+    case VG_EXPORT_CODEBOOKS: src = ix->codebooks.p; need = ix->trained ? M * ks * ix->dsub * 4 : 0; needs_build = false; break;
+    case VG_EXPORT_ASSIGNMENTS: src = ix->assign.p; need = n * 4; break;
+    case VG_EXPORT_CODES: src = ix->codes.p; need = n * M; break;
+    case VG_EXPORT_LIST_OFFSETS: src = ix->list_off.p; need = (ix->num_centroids + 1) * 8; break;
+    case VG_EXPORT_LIST_IDS: src = ix->list_ids.p; need = n * 4; break;
+    case VG_EXPORT_DOC_IDS: src = ix->doc_ids.p; need = n * 4; needs_build = false; break;
+    case VG_EXPORT_VECTORS:
+      if (ix->compacted) return fail(VG_ERR_UNSUPPORTED, "raw vectors were dropped by compact()");
+      src = ix->vectors.p; need = n * d * 4; needs_build = false; break;
+    default: return fail(VG_ERR_INVALID_PARAMETER, "unknown export selector");
+  }
+  if (needs_build && !ix->built) return fail(VG_ERR_NOT_BUILT, "IVF-PQ index is not built: nothing to export");
+  if (bytes != need)
+    return fail(VG_ERR_INVALID_PARAMETER, "export size mismatch: expected " + std::to_string(need) + " bytes");
+  if (need) VG_CU(cudaMemcpy(dst, src, need, cudaMemcpyDefault));
+  return VG_OK;
+}
+
+int vg_ivfpq_set_profiling(vg_index *ix, int on) {
+  if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
+  DeviceGuard g(ix->device);
+  if (on && !ix->stats.p) {
+    VG_CU(ix->stats.reserve(3 * 8));
+    VG_CU(cudaMemset(ix->stats.p, 0, 3 * 8));
+  }
+  ix->profiling = on != 0;
+  return VG_OK;
+}
+
+int vg_ivfpq_get_profile(const vg_index *ix, vg_search_profile *out) {
+  if (!ix || !out) return fail(VG_ERR_INVALID_PARAMETER, "null argument");
+  *out = ix->prof;
+  if (ix->stats.p) {
+    DeviceGuard g(ix->device);
+    unsigned long long st[3] = {0, 0, 0};
+    VG_CU(cudaMemcpy(st, ix->stats.p, sizeof(st), cudaMemcpyDeviceToHost));
+    out->probed_pairs = st[0];
+    out->scanned_vectors = st[1];
+    out->scanned_code_bytes = st[2];
+  }
+  return VG_OK;
+}
+
+int vg_ivfpq_reset_profile(vg_index *ix) {
+  if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
+  ix->prof = vg_search_profile{};
+  if (ix->stats.p) {
+    DeviceGuard g(ix->device);
+    VG_CU(cudaMemset(ix->stats.p, 0, 3 * 8));
+  }
+  return VG_OK;
+}
+
+int vg_nccl_unique_id(uint8_t out[128]) {
+  if (!out) return fail(VG_ERR_INVALID_PARAMETER, "null output");
+  static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
+  ncclUniqueId id;
+  ncclResult_t r = ncclGetUniqueId(&id);
+  if (r != ncclSuccess) return fail(VG_ERR_NCCL, std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+  std::memcpy(out, &id, 128);
+  return VG_OK;
+}
+
+int vg_shard_assign_lists(const uint64_t *sizes, size_t num_lists, int world_size, int32_t *owner) {
+  if ((!sizes || !owner) && num_lists) return fail(VG_ERR_INVALID_PARAMETER, "null argument");
+  if (world_size < 1) return fail(VG_ERR_INVALID_PARAMETER, "world_size must be at least 1");
+  std::vector<size_t> order(num_lists);
+  std::iota(order.begin(), order.end(), size_t(0));
+  std::stable_sort(order.begin(), order.end(), [&](size_t a, size_t b) { return sizes[a] > sizes[b]; });
+  std::vector<uint64_t> load(world_size, 0);
+  for (size_t l : order) {
+    int best = 0;
+    for (int r = 1; r < world_size; ++r)
+      if (load[r] < load[best]) best = r;
+    owner[l] = best;
+    load[best] += sizes[l];
+  }
+  return VG_OK;
+}
+
+int vg_ivfpq_shard(vg_index *ix, int rank, int world_size, const uint8_t nccl_id[128], int timeout_ms) {
+  if (!ix || !nccl_id) return fail(VG_ERR_INVALID_PARAMETER, "null argument");
+  if (!ix->built) return fail(VG_ERR_NOT_BUILT, "IVF-PQ index is not built: cannot shard");
+  if (world_size < 1 || rank < 0 || rank >= world_size)
+    return fail(VG_ERR_INVALID_PARAMETER, "rank must be in [0, world_size)");
+  if (ix->comm) return fail(VG_ERR_ALREADY_BUILT, "index is already sharded");
+  DeviceGuard g(ix->device);
+  const size_t Lc = ix->num_centroids;
+  std::vector<uint64_t> sizes(Lc);
+  for (size_t l = 0; l < Lc; ++l) sizes[l] = ix->h_list_off[l + 1] - ix->h_list_off[l];
+  std::vector<int32_t> owner(Lc);
+  VG_TRY(vg_shard_assign_lists(sizes.data(), Lc, world_size, owner.data()));
+  std::vector<uint8_t> mine(Lc);
+  for (size_t l = 0; l < Lc; ++l) mine[l] = owner[l] == rank;
+  VG_CU(ix->owner.reserve(std::max<size_t>(Lc, 1)));
+  VG_CU(cudaMemcpy(ix->owner.p, mine.data(), Lc, cudaMemcpyHostToDevice));
+  ix->comm_timeout_ms = timeout_ms > 0 ? timeout_ms : 60000;
+  if (world_size > 1) {
+    ncclUniqueId id;
+    std::memcpy(&id, nccl_id, 128);
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclComm_t comm = nullptr;
+    ncclResult_t r = ncclCommInitRankConfig(&comm, world_size, id, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress)
+      return fail(VG_ERR_NCCL, std::string("ncclCommInitRankConfig: ") + ncclGetErrorString(r));
+    int st = nccl_wait_ready(comm, ix->comm_timeout_ms);
+    if (st != VG_OK) {
+      ncclCommAbort(comm);
+      return st;
+    }
+    ix->comm = comm;
+  }
+  ix->rank = rank;
+  ix->world = world_size;
+  return VG_OK;
+}
+
+// ---- flat exact search ----------------------------------------------------
+
+int vg_flat_search_ip(const float *db, size_t n, const float *queries, size_t nq, size_t dim, size_t k, int device,
+                      uint32_t *out_ids, float *out_dist, uint32_t *out_count) {
+  if (dim == 0) return fail(VG_ERR_INVALID_CONFIG, "invalid config `dimension`: must be greater than 0");
+  if (k > 256) return fail(VG_ERR_INVALID_PARAMETER, "k must be at most 256");
+  if (n > 0xfffffffeull) return fail(VG_ERR_INVALID_PARAMETER, "at most 2^32 - 2 database rows");
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count) {
+    cudaGetLastError();
+    return fail(VG_ERR_CUDA, "no CUDA device " + std::to_string(device) + " (the engine has no CPU path)");
+  }
+  if (nq == 0 || k == 0) return VG_OK;
+  if (!db || !queries || !out_ids || !out_dist) return fail(VG_ERR_INVALID_PARAMETER, "null argument");
+  DeviceGuard g(device);
+  // One cached stream and workspace per device, serialised by a mutex.
+  struct FlatCtx {
+    std::mutex mu;
+    cudaStream_t s = nullptr;
+    DevBuf db, q, dist, chunk, ids, dst, cnt;
+  };
+  static FlatCtx *ctx = new FlatCtx[64];  // intentionally never freed (process lifetime)
+  if (device >= 64) return fail(VG_ERR_INVALID_PARAMETER, "device index out of range");
+  FlatCtx &c = ctx[device];
+  std::lock_guard<std::mutex> lock(c.mu);
+  if (!c.s) VG_CU(cudaStreamCreateWithFlags(&c.s, cudaStreamNonBlocking));
+  cudaStream_t s = c.s;
+  const float *ddb = db, *dq = queries;
+  if (!is_device_ptr(db)) {
+    VG_CU(c.db.reserve(n * dim * 4));
+    VG_CU(cudaMemcpyAsync(c.db.p, db, n * dim * 4, cudaMemcpyHostToDevice, s));
+    ddb = c.db.as<float>();
+  }
+  if (!is_device_ptr(queries)) {
+    VG_CU(c.q.reserve(nq * dim * 4));
+    VG_CU(cudaMemcpyAsync(c.q.p, queries, nq * dim * 4, cudaMemcpyHostToDevice, s));
+    dq = c.q.as<float>();
+  }
+  size_t tile = kDistBudgetBytes * 2 / (nq * 4);
+  tile = std::max<size_t>(128, tile / 128 * 128);
+  tile = std::min(tile, std::max<size_t>(n, 1));
+  const size_t chunks = n ? (n + tile - 1) / tile : 0;
+  const bool dev_out = is_device_ptr(out_ids) && is_device_ptr(out_dist) && (!out_count || is_device_ptr(out_count));
+  uint32_t *o_ids = out_ids, *o_cnt = out_count;
+  float *o_dist = out_dist;
+  if (!dev_out) {
+    VG_CU(c.ids.reserve(nq * k * 4));
+    VG_CU(c.dst.reserve(nq * k * 4));
+    VG_CU(c.cnt.reserve(nq * 4));
+    o_ids = c.ids.as<uint32_t>();
+    o_dist = c.dst.as<float>();
+    o_cnt = c.cnt.as<uint32_t>();
+  }
+  if (chunks) {
+    VG_CU(c.dist.reserve(nq * tile * 4));
+    VG_CU(c.chunk.reserve(nq * chunks * k * 8));
+    for (size_t ci = 0; ci < chunks; ++ci) {
+      size_t c0 = ci * tile, cols = std::min(tile, n - c0);
+      VG_CU(launch_neg_dot(dq, nq, ddb + c0 * dim, cols, static_cast<int>(dim), c.dist.as<float>(), tile, s));
+      VG_CU(launch_select_rows_keys(c.dist.as<float>(), nq, cols, tile, static_cast<int>(k),
+                                    c.chunk.as<unsigned long long>() + ci * k, chunks * k,
+                                    static_cast<uint32_t>(c0), s));
+    }
+    VG_CU(launch_merge_keys(c.chunk.as<unsigned long long>(), nq, chunks * k, chunks * k, static_cast<int>(k),
+                            nullptr, o_ids, o_dist, o_cnt, nullptr, s));
+  } else {
+    VG_CU(cudaMemsetAsync(o_ids, 0xff, nq * k * 4, s));
+    std::vector<float> inf(nq * k, __builtin_inff());
+    VG_CU(cudaMemcpyAsync(o_dist, inf.data(), nq * k * 4, cudaMemcpyHostToDevice, s));
+    if (o_cnt) VG_CU(cudaMemsetAsync(o_cnt, 0, nq * 4, s));
+    VG_CU(cudaStreamSynchronize(s));
+  }
+  if (!dev_out) {
+    VG_CU(cudaMemcpyAsync(out_ids, o_ids, nq * k * 4, cudaMemcpyDeviceToHost, s));
+    VG_CU(cudaMemcpyAsync(out_dist, o_dist, nq * k * 4, cudaMemcpyDeviceToHost, s));
+    if (out_count) VG_CU(cudaMemcpyAsync(out_count, o_cnt, nq * 4, cudaMemcpyDeviceToHost, s));
+  }
+  VG_CU(cudaStreamSynchronize(s));
+  return VG_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,192 @@
+// Host-side launchers for the engine's CUDA kernels.  Every launcher enqueues
+// on the given stream and returns the launch status; none synchronises.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace vg {
+
+// ---- search_kernels.cu ----------------------------------------------------
+
+// out[i] = x[i] / ||x[i]|| when the norm exceeds 1e-10, else x[i]
+// (search.rs:55-62, 503-508).  Sequential sum, IEEE sqrt and divide.
+cudaError_t launch_normalize_rows(const float *x, size_t n, int d, float *out,
+                                  cudaStream_t s);
+
+// dist[b][c] = 1 - dot(q[b], cent[c]) with the dot summed in index order
+// (search.rs:1602-1617, distance.rs:104-109).  Writes rows [0, B) of a
+// row-major matrix with leading dimension ld.
+cudaError_t launch_coarse_dist(const float *q, size_t B, const float *cent,
+                               size_t L, int d, float *dist, size_t ld,
+                               cudaStream_t s);
+
+// best[b] = min over c of pack_key(1 - dot(q[b], cent[c]), c): the argmin
+// centroid with ties to the lowest index.  best must be pre-set to ~0.
+cudaError_t launch_coarse_argmin(const float *q, size_t B, const float *cent,
+                                 size_t L, int d, unsigned long long *best,
+                                 cudaStream_t s);
+
+// best[b] = min over c of pack_key(-dot(q[b], db[c]), c + col_base) for the
+// flat inner-product path; dist written when non-null like coarse_dist but
+// with -dot.
+cudaError_t launch_neg_dot(const float *q, size_t B, const float *db, size_t n,
+                           int d, float *dist, size_t ld, cudaStream_t s);
+
+// Per row: the k smallest (value, column) of a row-major [rows][cols]
+// matrix, ascending, ties to the lower column.  Rows with fewer than k
+// columns are padded with id 0xffffffff and +inf.  k <= 256.
+cudaError_t launch_select_rows(const float *dist, size_t rows, size_t cols,
+                               size_t ld, int k, uint32_t *out_ids,
+                               float *out_dist, size_t out_ld,
+                               uint32_t col_base, cudaStream_t s);
+
+// Same selection, but writing packed keys (for later merging).
+cudaError_t launch_select_rows_keys(const float *dist, size_t rows,
+                                    size_t cols, size_t ld, int k,
+                                    unsigned long long *out_keys,
+                                    size_t out_ld, uint32_t col_base,
+                                    cudaStream_t s);
+
+// Build the list-major pair order: probes is [B][P] list ids (0xffffffff =
+// none); owner (nullable) marks lists this device scans.  Produces
+// work[0..total) = pair ids (b*P + slot) grouped by list, and total in
+// *d_total.  counts/cursor are [L] scratch.  When stats is non-null,
+// stats[0..3) accumulates (pairs, scanned vectors, scanned code bytes) using
+// list_off and the code layout (M bytes per vector, or M/2 packed for
+// 4-bit lists of at least 16 vectors).
+cudaError_t launch_build_pairs(const uint32_t *probes, size_t B, int P,
+                               const uint8_t *owner, size_t L,
+                               uint32_t *counts, uint32_t *cursor,
+                               uint32_t *work, uint32_t *d_total,
+                               const uint64_t *list_off, int M, bool four_bit,
+                               unsigned long long *stats, cudaStream_t s);
+
+// Per row r: the k smallest of keys[r][0..width) (sentinel ~0 = none);
+// emits doc ids (ids_map[key id]) and distances, padded with 0xffffffff/+inf,
+// the real count, and optionally the raw keys [rows][k].
+cudaError_t launch_merge_keys(const unsigned long long *keys, size_t rows,
+                              size_t width, size_t row_stride, int k,
+                              const uint32_t *ids_map, uint32_t *out_ids,
+                              float *out_dist, uint32_t *out_count,
+                              unsigned long long *out_keys, cudaStream_t s);
+
+// Merge G shard results laid out [G][rows][k] into [rows][k].
+cudaError_t launch_merge_shards(const unsigned long long *keys, int G,
+                                size_t rows, int k, const uint32_t *ids_map,
+                                uint32_t *out_ids, float *out_dist,
+                                uint32_t *out_count, unsigned long long *out_keys,
+                                cudaStream_t s);
+
+// Exact rerank of [rows][width] candidate keys (internal ids) by
+// 1 - dot(qn[row], vectors[id]); emits the k best as doc ids (ids_map).
+cudaError_t launch_rerank(const float *qn, const float *vectors, int d,
+                          const unsigned long long *cand, size_t rows, int width,
+                          int k, const uint32_t *ids_map, uint32_t *out_ids,
+                          float *out_dist, uint32_t *out_count, cudaStream_t s);
+
+// Number of positions where a[i] != b[i] added to *changed.
+cudaError_t launch_count_diff_u8(const uint8_t *a, const uint8_t *b, size_t n,
+                                 unsigned int *changed, cudaStream_t s);
+
+// ---- scan_kernels.cu ------------------------------------------------------
+
+struct ScanParams {
+  const float *qn;          // [B][d] normalised queries
+  const float *centroids;   // [L][d]
+  const float *codebooks;   // [M][ks][dsub]
+  const uint32_t *probes;   // [B][P]
+  const uint32_t *work;     // pair ids, list-major
+  const uint32_t *total;    // device scalar: number of pairs in work
+  uint32_t *counter;        // device scalar, zeroed before launch
+  const uint64_t *list_off; // [L+1] vector offsets into list_ids
+  const uint64_t *code_off; // [L] byte offsets into list_codes (16-aligned)
+  const uint8_t *list_codes;
+  const uint64_t *pack_off; // [L] byte offsets into packed (4-bit only)
+  const uint8_t *packed;
+  const uint32_t *list_ids; // internal vector ids, list order
+  int d, M, ks, dsub, P, k;
+  unsigned long long *pair_out;  // [B*P][k] keys
+};
+
+// Fused per-(query, list) kernel: query residual, ADC table in shared memory,
+// code scan (8-bit table sum or 4-bit FastScan), per-pair top-k.
+cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms,
+                              cudaStream_t s);
+
+// Name of the kernel variant launch_ivfpq_scan would run for p.
+int ivfpq_scan_variant_name(const ScanParams &p, char *buf, size_t len);
+
+// ---- build_kernels.cu -----------------------------------------------------
+
+// codes[i][m] = first argmin_c ||(x[i] - cent[assign[i]])_m - cw[m][c]||^2
+// (search.rs:720-729 residuals, pq.rs:513-538 quantize).
+cudaError_t launch_encode(const float *xn, size_t n, int d,
+                          const uint32_t *assign, const float *cent,
+                          const float *codebooks, int M, int ks,
+                          uint8_t *codes, cudaStream_t s);
+
+// Same argmin on rows that are already residuals (training).
+cudaError_t launch_encode_residuals(const float *r, size_t n, int d,
+                                    const float *codebooks, int M, int ks,
+                                    uint8_t *codes, cudaStream_t s);
+
+// residual[i] = x[i] - cent[assign[i]]
+cudaError_t launch_residuals(const float *xn, size_t n, int d,
+                             const uint32_t *assign, const float *cent,
+                             float *out, cudaStream_t s);
+
+// Unpack argmin keys into u32 assignments and count reassignments against
+// prev (nullable); changed is a device counter.
+cudaError_t launch_keys_to_assign(const unsigned long long *best, size_t n,
+                                  uint32_t *assign, const uint32_t *prev,
+                                  unsigned int *changed, cudaStream_t s);
+
+// Gather list-ordered codes: for sorted position p (list l), copy
+// codes[sorted_ids[p]] to list_codes[code_off[l] + (p - list_off[l]) * M].
+cudaError_t launch_gather_list_codes(const uint8_t *codes, const uint32_t *sorted_ids,
+                                     const uint32_t *sorted_lists, size_t n,
+                                     int M, const uint64_t *list_off,
+                                     const uint64_t *code_off, uint8_t *list_codes,
+                                     cudaStream_t s);
+
+// 4-bit FastScan packing of every list with at least 16 vectors
+// (pq_simd.rs:426-486, search.rs:816-848).
+cudaError_t launch_pack_lists_4bit(const uint8_t *list_codes, const uint64_t *list_off,
+                                   const uint64_t *code_off, const uint64_t *pack_off,
+                                   size_t L, int M, uint8_t *packed, cudaStream_t s);
+
+// k-means update: for each cluster c with members sorted_ids[seg[c]..seg[c+1])
+// (ascending), new_cent[c] = mean of rows (sequential, deterministic), then
+// normalised when spherical != 0.  Empty clusters keep old_cent.
+cudaError_t launch_kmeans_update(const float *x, int d, const uint32_t *sorted_ids,
+                                 const uint32_t *seg, size_t k, const float *old_cent,
+                                 float *new_cent, int spherical, cudaStream_t s);
+
+// Per-subspace update for PQ codebooks: members of codeword (m, c) are the
+// rows with codes[i][m] == c; x holds residual rows [n][d].
+cudaError_t launch_pq_update(const float *x, size_t n, int d, int M, int ks,
+                             const uint32_t *sorted_rows, const uint32_t *seg,
+                             const float *old_cb, float *new_cb, cudaStream_t s);
+
+cudaError_t launch_gather_rows(const float *x, int d, const uint32_t *rows, size_t n,
+                               float *out, cudaStream_t s);
+
+cudaError_t launch_iota(uint32_t *out, size_t n, cudaStream_t s);
+
+// keys[row*M + m] = m*ks + codes[row][m], vals = row (PQ training segments).
+cudaError_t launch_pq_keys(const uint8_t *codes, size_t n, int M, int ks,
+                           uint32_t *keys, uint32_t *vals, cudaStream_t s);
+
+// seg[c] = lower bound of c in sorted_keys, for c in [0, nseg].
+cudaError_t launch_segments(const uint32_t *sorted_keys, size_t n, size_t nseg,
+                            uint32_t *seg, cudaStream_t s);
+
+// Stable LSD radix sort of (key, value) pairs on bits [0, end_bit); call
+// with temp == nullptr to size temp_bytes.
+cudaError_t sort_pairs_u32(void *temp, size_t &temp_bytes, const uint32_t *kin,
+                           uint32_t *kout, const uint32_t *vin, uint32_t *vout,
+                           size_t n, int end_bit, cudaStream_t s);
+
+}  // namespace vg

@@ -1,0 +1,498 @@
+// Search-side kernels: query normalisation, exact coarse distances, row
+// top-k selection, list-major pair grouping and the final merges.
+//
+// Reference behaviour restated here (vicinity 0.12.0):
+//   normalize_query            src/ivf_pq/search.rs:55-62
+//   find_nearest_centroids     src/ivf_pq/search.rs:1602-1617 (1 - dot,
+//                              select nprobe smallest, sort ascending)
+//   finish_top_k_by_distance   src/ivf_pq/search.rs:64-75
+//   doc-id mapping             src/ivf_pq/search.rs:1087-1093
+//   batch padding              src/python.rs:745-795 (-1 / +inf)
+#include "common.cuh"
+#include "kernels.h"
+#include "topk.cuh"
+
+namespace vg {
+
+// ---------------------------------------------------------------------------
+// Normalisation: 32 rows per block staged through shared memory (row stride
+// d+1 floats so the per-row sequential sums are bank-conflict free).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) normalize_rows_kernel(const float *__restrict__ x, size_t n,
+                                                             int d, float *__restrict__ out) {
+  extern __shared__ float tile[];  // [32][d+1]
+  __shared__ float norms[32];
+  __shared__ int do_div[32];
+  const size_t row0 = static_cast<size_t>(blockIdx.x) * 32;
+  const int rows = (n - row0) < 32 ? static_cast<int>(n - row0) : 32;
+  const int stride = d + 1;
+  for (int i = threadIdx.x; i < rows * d; i += blockDim.x) {
+    int r = i / d, j = i - r * d;
+    tile[r * stride + j] = x[(row0 + r) * d + j];
+  }
+  __syncthreads();
+  if (threadIdx.x < rows) {
+    const float *row = tile + threadIdx.x * stride;
+    float s = 0.0f;
+    for (int j = 0; j < d; ++j) s = __fadd_rn(s, __fmul_rn(row[j], row[j]));
+    float norm = __fsqrt_rn(s);
+    do_div[threadIdx.x] = norm > 1e-10f;
+    norms[threadIdx.x] = norm;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < rows * d; i += blockDim.x) {
+    int r = i / d, j = i - r * d;
+    float v = tile[r * stride + j];
+    out[(row0 + r) * d + j] = do_div[r] ? __fdiv_rn(v, norms[r]) : v;
+  }
+}
+
+cudaError_t launch_normalize_rows(const float *x, size_t n, int d, float *out, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  size_t smem = static_cast<size_t>(32) * (d + 1) * sizeof(float);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(normalize_rows_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  dim3 grid(static_cast<unsigned>((n + 31) / 32));
+  normalize_rows_kernel<<<grid, 256, smem, s>>>(x, n, d, out);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Exact dot-product tiles.  Each thread owns an 8x8 block of (row, column)
+// accumulators and walks the shared dimension in order, so every accumulator
+// is the reference's sequential sum sum_j a_j*b_j with separately rounded
+// multiply and add.  Zero padding beyond d adds +0 products, which leaves the
+// sum unchanged.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int kTileM = 128, kTileN = 128, kTileK = 16, kTileThreads = 256;
+enum DotMode { kWriteOneMinus = 0, kArgminOneMinus = 1, kWriteNeg = 2 };
+
+template <int MODE>
+__global__ void __launch_bounds__(kTileThreads)
+    dot_tile_kernel(const float *__restrict__ a, size_t rows, const float *__restrict__ b, size_t cols,
+                    int d, float *__restrict__ out, size_t ld, unsigned long long *__restrict__ best) {
+  __shared__ __align__(16) float as[kTileK][kTileM + 4];
+  __shared__ __align__(16) float bs[kTileK][kTileN + 4];
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const size_t row0 = static_cast<size_t>(blockIdx.y) * kTileM;
+  const size_t col0 = static_cast<size_t>(blockIdx.x) * kTileN;
+
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+
+  for (int k0 = 0; k0 < d; k0 += kTileK) {
+#pragma unroll
+    for (int t = 0; t < (kTileM * kTileK) / kTileThreads; ++t) {
+      int i = tid + t * kTileThreads;
+      int r = i >> 4, kk = i & 15;
+      size_t gr = row0 + r;
+      int gk = k0 + kk;
+      as[kk][r] = (gr < rows && gk < d) ? a[gr * d + gk] : 0.0f;
+      size_t gc = col0 + r;
+      bs[kk][r] = (gc < cols && gk < d) ? b[gc * d + gk] : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < kTileK; ++kk) {
+      float4 a0 = *reinterpret_cast<const float4 *>(&as[kk][ty * 8]);
+      float4 a1 = *reinterpret_cast<const float4 *>(&as[kk][ty * 8 + 4]);
+      float4 b0 = *reinterpret_cast<const float4 *>(&bs[kk][tx * 8]);
+      float4 b1 = *reinterpret_cast<const float4 *>(&bs[kk][tx * 8 + 4]);
+      float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(av[i], bv[j]));
+    }
+    __syncthreads();
+  }
+
+  if (MODE == kArgminOneMinus) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      size_t r = row0 + ty * 8 + i;
+      unsigned long long kbest = kEmptyKey;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        size_t c = col0 + tx * 8 + j;
+        if (c < cols) {
+          unsigned long long key = pack_key(__fsub_rn(1.0f, acc[i][j]), static_cast<uint32_t>(c));
+          kbest = key < kbest ? key : kbest;
+        }
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) {
+        unsigned long long o = __shfl_xor_sync(VG_FULL_MASK, kbest, off);
+        kbest = o < kbest ? o : kbest;
+      }
+      if (tx == 0 && r < rows && kbest != kEmptyKey) atomicMin(best + r, kbest);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      size_t r = row0 + ty * 8 + i;
+      if (r >= rows) continue;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        size_t c = col0 + tx * 8 + j;
+        if (c < cols)
+          out[r * ld + c] = (MODE == kWriteOneMinus) ? __fsub_rn(1.0f, acc[i][j]) : -acc[i][j];
+      }
+    }
+  }
+}
+
+template <int MODE>
+cudaError_t launch_dot(const float *a, size_t rows, const float *b, size_t cols, int d, float *out,
+                       size_t ld, unsigned long long *best, cudaStream_t s) {
+  if (rows == 0 || cols == 0) return cudaSuccess;
+  dim3 grid(static_cast<unsigned>((cols + kTileN - 1) / kTileN),
+            static_cast<unsigned>((rows + kTileM - 1) / kTileM));
+  if (grid.y > 65535) return cudaErrorInvalidValue;
+  dot_tile_kernel<MODE><<<grid, kTileThreads, 0, s>>>(a, rows, b, cols, d, out, ld, best);
+  return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_coarse_dist(const float *q, size_t B, const float *cent, size_t L, int d,
+                               float *dist, size_t ld, cudaStream_t s) {
+  return launch_dot<kWriteOneMinus>(q, B, cent, L, d, dist, ld, nullptr, s);
+}
+
+cudaError_t launch_coarse_argmin(const float *q, size_t B, const float *cent, size_t L, int d,
+                                 unsigned long long *best, cudaStream_t s) {
+  return launch_dot<kArgminOneMinus>(q, B, cent, L, d, nullptr, 0, best, s);
+}
+
+cudaError_t launch_neg_dot(const float *q, size_t B, const float *db, size_t n, int d, float *dist,
+                           size_t ld, cudaStream_t s) {
+  return launch_dot<kWriteNeg>(q, B, db, n, d, dist, ld, nullptr, s);
+}
+
+// ---------------------------------------------------------------------------
+// Row selection: one warp per row, WarpTopK over the row's columns.
+// ---------------------------------------------------------------------------
+namespace {
+template <int R>
+__global__ void __launch_bounds__(256)
+    select_rows_kernel(const float *__restrict__ dist, size_t rows, size_t cols, size_t ld, int k,
+                       uint32_t *__restrict__ out_ids, float *__restrict__ out_dist,
+                       unsigned long long *__restrict__ out_keys, size_t out_ld, uint32_t col_base) {
+  const size_t row = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (row >= rows) return;
+  const int lane = lane_id();
+  const float *drow = dist + row * ld;
+  WarpTopK<R> tk;
+  tk.init();
+  for (size_t c0 = 0; c0 < cols; c0 += 32) {
+    size_t c = c0 + lane;
+    uint64_t key = c < cols ? pack_key(drow[c], col_base + static_cast<uint32_t>(c)) : kEmptyKey;
+    tk.add(key);
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    int i = r * 32 + lane;
+    if (i < k) {
+      uint64_t key = tk.v[r];
+      if (out_keys) out_keys[row * out_ld + i] = key;
+      if (out_ids) {
+        bool real = key != kEmptyKey;
+        out_ids[row * out_ld + i] = real ? key_id(key) : 0xffffffffu;
+        out_dist[row * out_ld + i] = real ? key_dist(key) : __int_as_float(0x7f800000);
+      }
+    }
+  }
+}
+
+template <int R>
+cudaError_t launch_select_impl(const float *dist, size_t rows, size_t cols, size_t ld, int k,
+                               uint32_t *ids, float *dst, unsigned long long *keys, size_t out_ld,
+                               uint32_t col_base, cudaStream_t s) {
+  size_t threads = rows * 32;
+  dim3 grid(static_cast<unsigned>((threads + 255) / 256));
+  select_rows_kernel<R><<<grid, 256, 0, s>>>(dist, rows, cols, ld, k, ids, dst, keys, out_ld, col_base);
+  return cudaGetLastError();
+}
+
+cudaError_t select_dispatch(const float *dist, size_t rows, size_t cols, size_t ld, int k,
+                            uint32_t *ids, float *dst, unsigned long long *keys, size_t out_ld,
+                            uint32_t col_base, cudaStream_t s) {
+  if (rows == 0 || k <= 0) return cudaSuccess;
+  if (k <= 32) return launch_select_impl<1>(dist, rows, cols, ld, k, ids, dst, keys, out_ld, col_base, s);
+  if (k <= 64) return launch_select_impl<2>(dist, rows, cols, ld, k, ids, dst, keys, out_ld, col_base, s);
+  if (k <= 128) return launch_select_impl<4>(dist, rows, cols, ld, k, ids, dst, keys, out_ld, col_base, s);
+  if (k <= 256) return launch_select_impl<8>(dist, rows, cols, ld, k, ids, dst, keys, out_ld, col_base, s);
+  return cudaErrorInvalidValue;
+}
+}  // namespace
+
+cudaError_t launch_select_rows(const float *dist, size_t rows, size_t cols, size_t ld, int k,
+                               uint32_t *out_ids, float *out_dist, size_t out_ld, uint32_t col_base,
+                               cudaStream_t s) {
+  return select_dispatch(dist, rows, cols, ld, k, out_ids, out_dist, nullptr, out_ld, col_base, s);
+}
+
+cudaError_t launch_select_rows_keys(const float *dist, size_t rows, size_t cols, size_t ld, int k,
+                                    unsigned long long *out_keys, size_t out_ld, uint32_t col_base,
+                                    cudaStream_t s) {
+  return select_dispatch(dist, rows, cols, ld, k, nullptr, nullptr, out_keys, out_ld, col_base, s);
+}
+
+// ---------------------------------------------------------------------------
+// List-major pair grouping (counting sort by list id).
+// ---------------------------------------------------------------------------
+namespace {
+constexpr uint32_t kNoList = 0xffffffffu;
+
+__global__ void count_pairs_kernel(const uint32_t *__restrict__ probes, size_t total,
+                                   const uint8_t *__restrict__ owner, size_t L, uint32_t *counts,
+                                   const uint64_t *__restrict__ list_off, int M, bool four_bit,
+                                   unsigned long long *stats) {
+  size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  uint32_t l = probes[i];
+  if (l == kNoList || l >= L) return;
+  if (owner && !owner[l]) return;
+  atomicAdd(counts + l, 1u);
+  if (stats) {
+    unsigned long long len = list_off[l + 1] - list_off[l];
+    unsigned long long bytes = (four_bit && len >= 16) ? ((len + 31) / 32) * 16ull * M : len * M;
+    atomicAdd(stats + 0, 1ull);
+    atomicAdd(stats + 1, len);
+    atomicAdd(stats + 2, bytes);
+  }
+}
+
+// Exclusive scan of counts[0..L) into cursor, total into *d_total.  One block
+// of 1024 threads; each thread owns a contiguous chunk.
+__global__ void __launch_bounds__(1024) scan_counts_kernel(const uint32_t *__restrict__ counts,
+                                                           size_t L, uint32_t *__restrict__ cursor,
+                                                           uint32_t *__restrict__ d_total) {
+  __shared__ uint32_t warp_sums[32];
+  const int tid = threadIdx.x;
+  const size_t chunk = (L + 1023) / 1024;
+  const size_t beg = tid * chunk < L ? tid * chunk : L;
+  const size_t end = beg + chunk < L ? beg + chunk : L;
+  uint32_t local = 0;
+  for (size_t i = beg; i < end; ++i) local += counts[i];
+  // inclusive warp scan
+  uint32_t v = local;
+  const int lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    uint32_t o = __shfl_up_sync(VG_FULL_MASK, v, off);
+    if (lane >= off) v += o;
+  }
+  if (lane == 31) warp_sums[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = warp_sums[lane];
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      uint32_t o = __shfl_up_sync(VG_FULL_MASK, w, off);
+      if (lane >= off) w += o;
+    }
+    warp_sums[lane] = w;  // inclusive
+  }
+  __syncthreads();
+  uint32_t excl = v - local + (warp > 0 ? warp_sums[warp - 1] : 0u);
+  for (size_t i = beg; i < end; ++i) {
+    cursor[i] = excl;
+    excl += counts[i];
+  }
+  if (tid == 1023) *d_total = warp_sums[31];
+}
+
+__global__ void scatter_pairs_kernel(const uint32_t *__restrict__ probes, size_t total,
+                                     const uint8_t *__restrict__ owner, size_t L,
+                                     uint32_t *cursor, uint32_t *__restrict__ work) {
+  size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  uint32_t l = probes[i];
+  if (l == kNoList || l >= L) return;
+  if (owner && !owner[l]) return;
+  uint32_t pos = atomicAdd(cursor + l, 1u);
+  work[pos] = static_cast<uint32_t>(i);
+}
+}  // namespace
+
+cudaError_t launch_build_pairs(const uint32_t *probes, size_t B, int P, const uint8_t *owner, size_t L,
+                               uint32_t *counts, uint32_t *cursor, uint32_t *work, uint32_t *d_total,
+                               const uint64_t *list_off, int M, bool four_bit, unsigned long long *stats,
+                               cudaStream_t s) {
+  size_t total = B * static_cast<size_t>(P);
+  cudaError_t e = cudaMemsetAsync(counts, 0, L * sizeof(uint32_t), s);
+  if (e != cudaSuccess) return e;
+  if (total == 0) return cudaMemsetAsync(d_total, 0, sizeof(uint32_t), s);
+  dim3 grid(static_cast<unsigned>((total + 255) / 256));
+  count_pairs_kernel<<<grid, 256, 0, s>>>(probes, total, owner, L, counts, list_off, M, four_bit,
+                                          list_off ? stats : nullptr);
+  scan_counts_kernel<<<1, 1024, 0, s>>>(counts, L, cursor, d_total);
+  scatter_pairs_kernel<<<grid, 256, 0, s>>>(probes, total, owner, L, cursor, work);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Merges: warp per row over segmented key arrays.
+// Candidate j of row r lives at keys[(j / seg_len) * seg_stride + r * row_stride + j % seg_len].
+// ---------------------------------------------------------------------------
+namespace {
+template <int R>
+__global__ void __launch_bounds__(256)
+    merge_kernel(const unsigned long long *__restrict__ keys, size_t rows, size_t width,
+                 size_t seg_len, size_t seg_stride, size_t row_stride, int k,
+                 const uint32_t *__restrict__ ids_map, uint32_t *__restrict__ out_ids,
+                 float *__restrict__ out_dist, uint32_t *__restrict__ out_count,
+                 unsigned long long *__restrict__ out_keys) {
+  const size_t row = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (row >= rows) return;
+  const int lane = lane_id();
+  WarpTopK<R> tk;
+  tk.init();
+  for (size_t j0 = 0; j0 < width; j0 += 32) {
+    size_t j = j0 + lane;
+    uint64_t key = kEmptyKey;
+    if (j < width) {
+      size_t seg = j / seg_len, off = j - seg * seg_len;
+      key = keys[seg * seg_stride + row * row_stride + off];
+    }
+    tk.add(key);
+  }
+  uint32_t count = 0;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    int i = r * 32 + lane;
+    uint64_t key = tk.v[r];
+    bool real = (i < k) && key != kEmptyKey;
+    count += __popc(__ballot_sync(VG_FULL_MASK, real));
+    if (i < k) {
+      if (out_keys) out_keys[row * k + i] = key;
+      if (out_ids) {
+        out_ids[row * k + i] = real ? (ids_map ? ids_map[key_id(key)] : key_id(key)) : 0xffffffffu;
+        out_dist[row * k + i] = real ? key_dist(key) : __int_as_float(0x7f800000);
+      }
+    }
+  }
+  if (out_count && lane == 0) out_count[row] = count;
+}
+
+cudaError_t merge_dispatch(const unsigned long long *keys, size_t rows, size_t width, size_t seg_len,
+                           size_t seg_stride, size_t row_stride, int k, const uint32_t *ids_map,
+                           uint32_t *out_ids, float *out_dist, uint32_t *out_count,
+                           unsigned long long *out_keys, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  dim3 grid(static_cast<unsigned>((rows * 32 + 255) / 256));
+#define VG_MERGE(RR)                                                                               \
+  merge_kernel<RR><<<grid, 256, 0, s>>>(keys, rows, width, seg_len, seg_stride, row_stride, k,     \
+                                        ids_map, out_ids, out_dist, out_count, out_keys)
+  if (k <= 32)
+    VG_MERGE(1);
+  else if (k <= 64)
+    VG_MERGE(2);
+  else if (k <= 128)
+    VG_MERGE(4);
+  else if (k <= 256)
+    VG_MERGE(8);
+  else
+    return cudaErrorInvalidValue;
+#undef VG_MERGE
+  return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_merge_keys(const unsigned long long *keys, size_t rows, size_t width, size_t row_stride,
+                              int k, const uint32_t *ids_map, uint32_t *out_ids, float *out_dist,
+                              uint32_t *out_count, unsigned long long *out_keys, cudaStream_t s) {
+  size_t seg = width ? width : 1;
+  return merge_dispatch(keys, rows, width, seg, 0, row_stride, k, ids_map, out_ids, out_dist, out_count,
+                        out_keys, s);
+}
+
+cudaError_t launch_merge_shards(const unsigned long long *keys, int G, size_t rows, int k,
+                                const uint32_t *ids_map, uint32_t *out_ids, float *out_dist,
+                                uint32_t *out_count, unsigned long long *out_keys, cudaStream_t s) {
+  return merge_dispatch(keys, rows, static_cast<size_t>(G) * k, static_cast<size_t>(k), rows * k,
+                        static_cast<size_t>(k), k, ids_map, out_ids, out_dist, out_count, out_keys, s);
+}
+
+// ---------------------------------------------------------------------------
+// Exact rerank (search.rs:1117-1158): each approximate candidate is re-scored
+// with cosine_distance_normalized = 1 - dot(q, x) (distance.rs:104-109), the
+// dot summed in index order, then the k best are kept.  Warp per query; lane
+// i scores candidates i, i+32, ...
+// ---------------------------------------------------------------------------
+namespace {
+template <int R>
+__global__ void __launch_bounds__(256)
+    rerank_kernel(const float *__restrict__ qn, const float *__restrict__ vectors, int d,
+                  const unsigned long long *__restrict__ cand, size_t rows, int width, int k,
+                  const uint32_t *__restrict__ ids_map, uint32_t *__restrict__ out_ids,
+                  float *__restrict__ out_dist, uint32_t *__restrict__ out_count) {
+  const size_t row = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (row >= rows) return;
+  const int lane = lane_id();
+  const float *q = qn + row * d;
+  WarpTopK<R> tk;
+  tk.init();
+  for (int j0 = 0; j0 < width; j0 += 32) {
+    int j = j0 + lane;
+    uint64_t key = kEmptyKey;
+    if (j < width) {
+      uint64_t c = cand[row * width + j];
+      if (c != kEmptyKey) {
+        const float *x = vectors + static_cast<size_t>(key_id(c)) * d;
+        float dot = 0.0f;
+        for (int t = 0; t < d; ++t) dot = __fadd_rn(dot, __fmul_rn(q[t], x[t]));
+        key = pack_key(__fsub_rn(1.0f, dot), key_id(c));
+      }
+    }
+    tk.add(key);
+  }
+  uint32_t count = 0;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    int i = r * 32 + lane;
+    uint64_t key = tk.v[r];
+    bool real = (i < k) && key != kEmptyKey;
+    count += __popc(__ballot_sync(VG_FULL_MASK, real));
+    if (i < k) {
+      out_ids[row * k + i] = real ? ids_map[key_id(key)] : 0xffffffffu;
+      out_dist[row * k + i] = real ? key_dist(key) : __int_as_float(0x7f800000);
+    }
+  }
+  if (out_count && lane == 0) out_count[row] = count;
+}
+}  // namespace
+
+cudaError_t launch_rerank(const float *qn, const float *vectors, int d, const unsigned long long *cand,
+                          size_t rows, int width, int k, const uint32_t *ids_map, uint32_t *out_ids,
+                          float *out_dist, uint32_t *out_count, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  dim3 grid(static_cast<unsigned>((rows * 32 + 255) / 256));
+#define VG_RERANK(RR) \
+  rerank_kernel<RR><<<grid, 256, 0, s>>>(qn, vectors, d, cand, rows, width, k, ids_map, out_ids, out_dist, out_count)
+  if (k <= 32)
+    VG_RERANK(1);
+  else if (k <= 64)
+    VG_RERANK(2);
+  else if (k <= 128)
+    VG_RERANK(4);
+  else if (k <= 256)
+    VG_RERANK(8);
+  else
+    return cudaErrorInvalidValue;
+#undef VG_RERANK
+  return cudaGetLastError();
+}
+
+}  // namespace vg
