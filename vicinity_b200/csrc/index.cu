@@ -175,7 +175,7 @@ struct vg_index {
 
   // search workspace
   DevBuf ws_q, ws_qn, ws_dist, ws_probes, ws_pdist, ws_counts, ws_cursor, ws_work, ws_scalars,
-      ws_pair_out, ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count;
+      ws_pair_out, ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_tau;
   DevBuf stats;  // u64 [pairs, vectors, code bytes] accumulated while profiling
 
   // profiling
@@ -560,6 +560,8 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   VG_CU(ix->ws_pair_out.reserve(nq * P * kk * 8));
   VG_CU(cudaMemsetAsync(ix->ws_pair_out.p, 0xff, nq * P * kk * 8, s));
   VG_CU(cudaMemsetAsync(d_counter, 0, 4, s));
+  VG_CU(ix->ws_tau.reserve(nq * 8));
+  VG_CU(cudaMemsetAsync(ix->ws_tau.p, 0xff, nq * 8, s));
   mark(ix, 5);
 
   vg::ScanParams sp{};
@@ -583,6 +585,7 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   sp.P = static_cast<int>(P);
   sp.k = static_cast<int>(kk);
   sp.pair_out = ix->ws_pair_out.as<unsigned long long>();
+  sp.tau = ix->ws_tau.as<unsigned long long>();
   VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
   ix->launches += 1;
   mark(ix, 6);
@@ -746,7 +749,7 @@ int vg_ivfpq_destroy(vg_index *ix) {
                       &ix->owner, &ix->ws_q, &ix->ws_qn, &ix->ws_dist, &ix->ws_probes, &ix->ws_pdist,
                       &ix->ws_counts, &ix->ws_cursor, &ix->ws_work, &ix->ws_scalars, &ix->ws_pair_out,
                       &ix->ws_keys, &ix->ws_all_keys, &ix->ws_out_ids, &ix->ws_out_dist, &ix->ws_out_count,
-                      &ix->stats})
+                      &ix->ws_tau, &ix->stats})
       b->release();
     for (int i = 0; i < kPhaseEvents; ++i)
       if (ix->ev[i]) cudaEventDestroy(ix->ev[i]);

@@ -108,6 +108,7 @@ struct ScanParams {
   const uint32_t *list_ids; // internal vector ids, list order
   int d, M, ks, dsub, P, k;
   unsigned long long *pair_out;  // [B*P][k] keys
+  unsigned long long *tau;       // [B] per-query bound on the k-th key, preset to ~0
 };
 
 // Fused per-(query, list) kernel: query residual, ADC table in shared memory,
