@@ -174,8 +174,8 @@ struct vg_index {
   DevBuf owner;
 
   // search workspace
-  DevBuf ws_q, ws_qn, ws_dist, ws_probes, ws_pdist, ws_counts, ws_cursor, ws_work, ws_scalars,
-      ws_pair_out, ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_tau;
+  DevBuf ws_q, ws_qn, ws_dist, ws_probes, ws_pdist, ws_scalars,
+      ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count;
   DevBuf stats;  // u64 [pairs, vectors, code bytes] accumulated while profiling
 
   // profiling
@@ -544,51 +544,17 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
     }
   }
 
-  // list-major pair grouping
-  VG_CU(ix->ws_counts.reserve(Lc * 4));
-  VG_CU(ix->ws_cursor.reserve(Lc * 4));
-  VG_CU(ix->ws_work.reserve(nq * P * 4));
+  // per-query fused scan: probes -> (residual, table, scan, top-k) on chip
   VG_CU(ix->ws_scalars.reserve(64));
-  uint32_t *d_total = ix->ws_scalars.as<uint32_t>();
-  uint32_t *d_counter = d_total + 1;
-  VG_CU(launch_build_pairs(ix->ws_probes.as<uint32_t>(), nq, static_cast<int>(P),
-                           ix->world > 1 ? ix->owner.as<uint8_t>() : nullptr, Lc, ix->ws_counts.as<uint32_t>(),
-                           ix->ws_cursor.as<uint32_t>(), ix->ws_work.as<uint32_t>(), d_total,
-                           prof ? ix->list_off.as<uint64_t>() : nullptr, static_cast<int>(M),
-                           ix->params.codebook_size == 16, prof ? ix->stats.as<unsigned long long>() : nullptr, s));
-  ix->launches += 3;
-  VG_CU(ix->ws_pair_out.reserve(nq * P * kk * 8));
-  VG_CU(cudaMemsetAsync(ix->ws_pair_out.p, 0xff, nq * P * kk * 8, s));
+  uint32_t *d_counter = ix->ws_scalars.as<uint32_t>();
   VG_CU(cudaMemsetAsync(d_counter, 0, 4, s));
-  VG_CU(ix->ws_tau.reserve(nq * 8));
-  VG_CU(cudaMemsetAsync(ix->ws_tau.p, 0xff, nq * 8, s));
+  if (prof) {
+    VG_CU(launch_probe_stats(ix->ws_probes.as<uint32_t>(), nq, static_cast<int>(P),
+                             ix->world > 1 ? ix->owner.as<uint8_t>() : nullptr, Lc, ix->list_off.as<uint64_t>(),
+                             static_cast<int>(M), ix->params.codebook_size == 16,
+                             ix->stats.as<unsigned long long>(), s));
+  }
   mark(ix, 5);
-
-  vg::ScanParams sp{};
-  sp.qn = ix->ws_qn.as<float>();
-  sp.centroids = ix->centroids.as<float>();
-  sp.codebooks = ix->codebooks.as<float>();
-  sp.probes = ix->ws_probes.as<uint32_t>();
-  sp.work = ix->ws_work.as<uint32_t>();
-  sp.total = d_total;
-  sp.counter = d_counter;
-  sp.list_off = ix->list_off.as<uint64_t>();
-  sp.code_off = ix->code_off.as<uint64_t>();
-  sp.list_codes = ix->list_codes.as<uint8_t>();
-  sp.pack_off = ix->pack_off.as<uint64_t>();
-  sp.packed = ix->packed.as<uint8_t>();
-  sp.list_ids = ix->list_ids.as<uint32_t>();
-  sp.d = static_cast<int>(d);
-  sp.M = static_cast<int>(M);
-  sp.ks = static_cast<int>(ix->params.codebook_size);
-  sp.dsub = static_cast<int>(ix->dsub);
-  sp.P = static_cast<int>(P);
-  sp.k = static_cast<int>(kk);
-  sp.pair_out = ix->ws_pair_out.as<unsigned long long>();
-  sp.tau = ix->ws_tau.as<unsigned long long>();
-  VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
-  ix->launches += 1;
-  mark(ix, 6);
 
   // outputs: device pointers are written in place, host ones via staging
   const bool dev_out = is_device_ptr(out_ids) && is_device_ptr(out_dist) && (!out_count || is_device_ptr(out_count));
@@ -603,29 +569,49 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
     o_cnt = ix->ws_out_count.as<uint32_t>();
   }
   const uint32_t *doc_map = ix->doc_ids.as<uint32_t>();
-  const size_t width = P * kk;
-  if (ix->world == 1) {
-    if (rerank) {
-      VG_CU(ix->ws_keys.reserve(nq * kk * 8));
-      VG_CU(launch_merge_keys(ix->ws_pair_out.as<unsigned long long>(), nq, width, width, static_cast<int>(kk),
-                              nullptr, nullptr, nullptr, nullptr, ix->ws_keys.as<unsigned long long>(), s));
-      mark(ix, 7);
-      VG_CU(launch_rerank(ix->ws_qn.as<float>(), ix->vectors.as<float>(), static_cast<int>(d),
-                          ix->ws_keys.as<unsigned long long>(), nq, static_cast<int>(kk), static_cast<int>(k),
-                          doc_map, o_ids, o_dist, o_cnt, s));
-      ix->launches += 2;
-    } else {
-      VG_CU(launch_merge_keys(ix->ws_pair_out.as<unsigned long long>(), nq, width, width, static_cast<int>(k),
-                              doc_map, o_ids, o_dist, o_cnt, nullptr, s));
-      mark(ix, 7);
-      ix->launches += 1;
-    }
+  const bool direct = ix->world == 1 && !rerank;  // the kernel writes final results
+
+  vg::ScanParams sp{};
+  sp.qn = ix->ws_qn.as<float>();
+  sp.centroids = ix->centroids.as<float>();
+  sp.codebooks = ix->codebooks.as<float>();
+  sp.probes = ix->ws_probes.as<uint32_t>();
+  sp.owner = ix->world > 1 ? ix->owner.as<uint8_t>() : nullptr;
+  sp.counter = d_counter;
+  sp.list_off = ix->list_off.as<uint64_t>();
+  sp.code_off = ix->code_off.as<uint64_t>();
+  sp.list_codes = ix->list_codes.as<uint8_t>();
+  sp.pack_off = ix->pack_off.as<uint64_t>();
+  sp.packed = ix->packed.as<uint8_t>();
+  sp.list_ids = ix->list_ids.as<uint32_t>();
+  sp.doc_ids = doc_map;
+  sp.d = static_cast<int>(d);
+  sp.M = static_cast<int>(M);
+  sp.ks = static_cast<int>(ix->params.codebook_size);
+  sp.dsub = static_cast<int>(ix->dsub);
+  sp.P = static_cast<int>(P);
+  sp.k = static_cast<int>(kk);
+  sp.nq = static_cast<int>(nq);
+  if (direct) {
+    sp.out_ids = o_ids;
+    sp.out_dist = o_dist;
+    sp.out_count = o_cnt;
   } else {
     VG_CU(ix->ws_keys.reserve(nq * kk * 8));
-    VG_CU(ix->ws_all_keys.reserve(static_cast<size_t>(ix->world) * nq * kk * 8));
-    VG_CU(launch_merge_keys(ix->ws_pair_out.as<unsigned long long>(), nq, width, width, static_cast<int>(kk),
-                            nullptr, nullptr, nullptr, nullptr, ix->ws_keys.as<unsigned long long>(), s));
+    sp.out_keys = ix->ws_keys.as<unsigned long long>();
+  }
+  VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
+  ix->launches += 1;
+  mark(ix, 6);
+
+  if (!direct && ix->world == 1) {  // rerank on one device
+    mark(ix, 7);
+    VG_CU(launch_rerank(ix->ws_qn.as<float>(), ix->vectors.as<float>(), static_cast<int>(d),
+                        ix->ws_keys.as<unsigned long long>(), nq, static_cast<int>(kk), static_cast<int>(k),
+                        doc_map, o_ids, o_dist, o_cnt, s));
     ix->launches += 1;
+  } else if (ix->world > 1) {
+    VG_CU(ix->ws_all_keys.reserve(static_cast<size_t>(ix->world) * nq * kk * 8));
     mark(ix, 7);
     ncclResult_t r = ncclAllGather(ix->ws_keys.p, ix->ws_all_keys.p, nq * kk, ncclUint64, ix->comm, s);
     if (r == ncclInProgress) VG_TRY(nccl_wait_ready(ix->comm, ix->comm_timeout_ms));
@@ -643,6 +629,8 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
                                 doc_map, o_ids, o_dist, o_cnt, nullptr, s));
       ix->launches += 1;
     }
+  } else {
+    mark(ix, 7);
   }
   mark(ix, 9);
   if (!dev_out) {
@@ -670,7 +658,7 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
       p.merge_ms += el(6, 7) + el(8, 9);
       p.collective_ms += el(7, 8);
     } else {
-      p.merge_ms += el(6, 9);
+      p.merge_ms += el(6, 7) + el(7, 9);
     }
     p.d2h_ms += el(9, 10);
     p.total_ms += el(0, 10);
@@ -747,9 +735,8 @@ int vg_ivfpq_destroy(vg_index *ix) {
     for (DevBuf *b : {&ix->vectors, &ix->doc_ids, &ix->centroids, &ix->codebooks, &ix->assign, &ix->codes,
                       &ix->list_off, &ix->list_ids, &ix->code_off, &ix->list_codes, &ix->pack_off, &ix->packed,
                       &ix->owner, &ix->ws_q, &ix->ws_qn, &ix->ws_dist, &ix->ws_probes, &ix->ws_pdist,
-                      &ix->ws_counts, &ix->ws_cursor, &ix->ws_work, &ix->ws_scalars, &ix->ws_pair_out,
-                      &ix->ws_keys, &ix->ws_all_keys, &ix->ws_out_ids, &ix->ws_out_dist, &ix->ws_out_count,
-                      &ix->ws_tau, &ix->stats})
+                      &ix->ws_scalars, &ix->ws_keys, &ix->ws_all_keys, &ix->ws_out_ids, &ix->ws_out_dist,
+                      &ix->ws_out_count, &ix->stats})
       b->release();
     for (int i = 0; i < kPhaseEvents; ++i)
       if (ix->ev[i]) cudaEventDestroy(ix->ev[i]);

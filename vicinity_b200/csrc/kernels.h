@@ -63,6 +63,13 @@ cudaError_t launch_build_pairs(const uint32_t *probes, size_t B, int P,
                                const uint64_t *list_off, int M, bool four_bit,
                                unsigned long long *stats, cudaStream_t s);
 
+// Profiling counters: for every valid owned probe of [B][P], adds
+// (1 pair, list length, code bytes scanned) to stats[0..3).
+cudaError_t launch_probe_stats(const uint32_t *probes, size_t B, int P,
+                               const uint8_t *owner, size_t L,
+                               const uint64_t *list_off, int M, bool four_bit,
+                               unsigned long long *stats, cudaStream_t s);
+
 // Per row r: the k smallest of keys[r][0..width) (sentinel ~0 = none);
 // emits doc ids (ids_map[key id]) and distances, padded with 0xffffffff/+inf,
 // the real count, and optionally the raw keys [rows][k].
@@ -93,26 +100,29 @@ cudaError_t launch_count_diff_u8(const uint8_t *a, const uint8_t *b, size_t n,
 // ---- scan_kernels.cu ------------------------------------------------------
 
 struct ScanParams {
-  const float *qn;          // [B][d] normalised queries
+  const float *qn;          // [nq][d] normalised queries
   const float *centroids;   // [L][d]
   const float *codebooks;   // [M][ks][dsub]
-  const uint32_t *probes;   // [B][P]
-  const uint32_t *work;     // pair ids, list-major
-  const uint32_t *total;    // device scalar: number of pairs in work
-  uint32_t *counter;        // device scalar, zeroed before launch
+  const uint32_t *probes;   // [nq][P] list ids, nearest first (0xffffffff = none)
+  const uint8_t *owner;     // [L] nonzero for lists this device scans (nullable = all)
+  uint32_t *counter;        // device scalar, zeroed before launch (query counter)
   const uint64_t *list_off; // [L+1] vector offsets into list_ids
   const uint64_t *code_off; // [L] byte offsets into list_codes (16-aligned)
   const uint8_t *list_codes;
   const uint64_t *pack_off; // [L] byte offsets into packed (4-bit only)
   const uint8_t *packed;
   const uint32_t *list_ids; // internal vector ids, list order
-  int d, M, ks, dsub, P, k;
-  unsigned long long *pair_out;  // [B*P][k] keys
-  unsigned long long *tau;       // [B] per-query bound on the k-th key, preset to ~0
+  const uint32_t *doc_ids;  // internal id -> caller id (for out_ids)
+  int d, M, ks, dsub, P, k, nq;
+  unsigned long long *out_keys;  // [nq][k] keys (nullable)
+  uint32_t *out_ids;             // [nq][k] doc ids, padded 0xffffffff (nullable)
+  float *out_dist;               // [nq][k] distances, padded +inf
+  uint32_t *out_count;           // [nq] real result counts (nullable)
 };
 
-// Fused per-(query, list) kernel: query residual, ADC table in shared memory,
-// code scan (8-bit table sum or 4-bit FastScan), per-pair top-k.
+// Fused per-query kernel: for each probed list the query residual, the ADC
+// table in shared memory and the code scan (8-bit table sum or 4-bit
+// FastScan), with the query's top-k kept on chip.
 cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms,
                               cudaStream_t s);
 

@@ -1,4 +1,4 @@
-// Variant selection for the fused probe kernel (scan_kernel.cuh).
+// Variant selection for the fused search kernel (scan_kernel.cuh).
 //
 // Register-resident codebooks are used when the subvector has at most 8
 // dimensions and the whole codebook fits in EPT entries per thread with at
@@ -34,7 +34,7 @@ cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms, cudaStream_t s) 
 
 int ivfpq_scan_variant_name(const ScanParams &p, char *buf, size_t len) {
   const int ept = pick_ept(p);
-  return snprintf(buf, len, "ivfpq_scan<%d,%d,%d,%s>", ept ? p.dsub : 0, ept,
+  return snprintf(buf, len, "ivfpq_query_kernel<%d,%d,%d,%s>", ept ? p.dsub : 0, ept,
                   p.k <= 32 ? 1 : p.k <= 64 ? 2 : p.k <= 128 ? 4 : 8, p.ks == 16 ? "4bit" : "8bit");
 }
 

@@ -343,6 +343,56 @@ cudaError_t launch_build_pairs(const uint32_t *probes, size_t B, int P, const ui
 }
 
 // ---------------------------------------------------------------------------
+// Profiling counters of scanned work (block-reduced, three atomics per block).
+// ---------------------------------------------------------------------------
+namespace {
+__global__ void probe_stats_kernel(const uint32_t *__restrict__ probes, size_t total,
+                                   const uint8_t *__restrict__ owner, size_t L,
+                                   const uint64_t *__restrict__ list_off, int M, bool four_bit,
+                                   unsigned long long *stats) {
+  __shared__ unsigned long long part[3][8];
+  size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  unsigned long long pairs = 0, vecs = 0, bytes = 0;
+  if (i < total) {
+    uint32_t l = probes[i];
+    if (l != kNoList && l < L && (!owner || owner[l])) {
+      unsigned long long len = list_off[l + 1] - list_off[l];
+      pairs = 1;
+      vecs = len;
+      bytes = (four_bit && len >= 16) ? ((len + 31) / 32) * 16ull * M : len * M;
+    }
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    pairs += __shfl_xor_sync(VG_FULL_MASK, pairs, off);
+    vecs += __shfl_xor_sync(VG_FULL_MASK, vecs, off);
+    bytes += __shfl_xor_sync(VG_FULL_MASK, bytes, off);
+  }
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    part[0][w] = pairs;
+    part[1][w] = vecs;
+    part[2][w] = bytes;
+  }
+  __syncthreads();
+  if (threadIdx.x < 3) {
+    unsigned long long t = 0;
+    for (int j = 0; j < static_cast<int>(blockDim.x >> 5); ++j) t += part[threadIdx.x][j];
+    if (t) atomicAdd(stats + threadIdx.x, t);
+  }
+}
+}  // namespace
+
+cudaError_t launch_probe_stats(const uint32_t *probes, size_t B, int P, const uint8_t *owner, size_t L,
+                               const uint64_t *list_off, int M, bool four_bit, unsigned long long *stats,
+                               cudaStream_t s) {
+  size_t total = B * static_cast<size_t>(P);
+  if (total == 0 || !stats) return cudaSuccess;
+  probe_stats_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(probes, total, owner, L, list_off, M,
+                                                                              four_bit, stats);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
 // Merges: warp per row over segmented key arrays.
 // Candidate j of row r lives at keys[(j / seg_len) * seg_stride + r * row_stride + j % seg_len].
 // ---------------------------------------------------------------------------
