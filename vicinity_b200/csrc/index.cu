@@ -20,6 +20,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <numeric>
@@ -177,6 +178,9 @@ struct vg_index {
   DevBuf ws_q, ws_qn, ws_dist, ws_probes, ws_pdist, ws_scalars,
       ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count;
   DevBuf stats;  // u64 [pairs, vectors, code bytes] accumulated while profiling
+
+  // error flag of bounded device waits, in mapped pinned host memory
+  int *h_err = nullptr, *d_err = nullptr;
 
   // profiling
   bool profiling = false;
@@ -600,6 +604,8 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
     VG_CU(ix->ws_keys.reserve(nq * kk * 8));
     sp.out_keys = ix->ws_keys.as<unsigned long long>();
   }
+  *reinterpret_cast<volatile int *>(ix->h_err) = 0;
+  sp.error = ix->d_err;
   VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
   ix->launches += 1;
   mark(ix, 6);
@@ -640,6 +646,8 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   }
   mark(ix, 10);
   VG_TRY(sync_stream(ix));
+  if (const int code = *reinterpret_cast<volatile int *>(ix->h_err))
+    return fail(VG_ERR_CUDA, "search kernel gave up on a bounded pipeline wait (code " + std::to_string(code) + ")");
 
   if (prof) {
     auto el = [&](int a, int b) {
@@ -718,6 +726,12 @@ int vg_ivfpq_create(size_t dim, const vg_ivfpq_params *params, int device, vg_in
   cudaError_t e = cudaStreamCreateWithFlags(&ix->own_stream, cudaStreamNonBlocking);
   ix->stream = ix->own_stream;
   for (int i = 0; e == cudaSuccess && i < kPhaseEvents; ++i) e = cudaEventCreate(&ix->ev[i]);
+  if (e == cudaSuccess) e = cudaHostAlloc(reinterpret_cast<void **>(&ix->h_err), sizeof(int), cudaHostAllocMapped);
+  if (e == cudaSuccess) {
+    *ix->h_err = 0;
+    e = cudaHostGetDevicePointer(reinterpret_cast<void **>(&ix->d_err), ix->h_err, 0);
+  }
+  if (const char *fam = std::getenv("VICINITY_SCAN_KERNEL")) vg::set_scan_family(std::strcmp(fam, "pipeline") != 0);
   if (e != cudaSuccess) {
     vg_ivfpq_destroy(ix);
     return cuda_fail(e, "stream/event creation");
@@ -740,6 +754,7 @@ int vg_ivfpq_destroy(vg_index *ix) {
       b->release();
     for (int i = 0; i < kPhaseEvents; ++i)
       if (ix->ev[i]) cudaEventDestroy(ix->ev[i]);
+    if (ix->h_err) cudaFreeHost(ix->h_err);
     if (ix->own_stream) cudaStreamDestroy(ix->own_stream);
   }
   delete ix;

@@ -118,6 +118,7 @@ struct ScanParams {
   uint32_t *out_ids;             // [nq][k] doc ids, padded 0xffffffff (nullable)
   float *out_dist;               // [nq][k] distances, padded +inf
   uint32_t *out_count;           // [nq] real result counts (nullable)
+  int *error;                    // set nonzero when a bounded pipeline wait gives up
 };
 
 // Fused per-query kernel: for each probed list the query residual, the ADC
@@ -128,6 +129,10 @@ cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms,
 
 // Name of the kernel variant launch_ivfpq_scan would run for p.
 int ivfpq_scan_variant_name(const ScanParams &p, char *buf, size_t len);
+
+// Kernel family selection: 1 (default) = query-major kernel, 0 = the
+// warp-specialised pipeline where it applies.
+void set_scan_family(int family);
 
 // ---- build_kernels.cu -----------------------------------------------------
 

@@ -13,28 +13,47 @@ namespace vg {
 
 cudaError_t launch_scan_four(const ScanParams &p, int dsub, int ept, int num_sms, cudaStream_t s);
 cudaError_t launch_scan_eight(const ScanParams &p, int dsub, int ept, int num_sms, cudaStream_t s);
+cudaError_t launch_scan_ws(const ScanParams &p, int dsub, int ept, int num_sms, cudaStream_t s);
 
 namespace {
-int pick_ept(const ScanParams &p) {
-  if (p.dsub < 1 || p.dsub > 8 || p.k > 32) return 0;
+int g_family = 1;  // query-major kernel by default (measured faster at C1)
+
+// Entries per producer thread for the warp-specialised kernel (0 = n/a).
+int pick_ws_ept(const ScanParams &p) {
+  if (g_family == 1 || p.ks != 256 || p.dsub < 1 || p.dsub > 8 || p.k > 32 || p.P > 384) return 0;
   const int nent = p.M * p.ks;
-  const int max_ept = p.ks == 16 ? 4 : 16;
-  for (int ept = 1; ept <= max_ept; ept <<= 1)
-    if (ept * kScanThreads >= nent && ept * p.dsub <= 64) return ept;
+  for (int ept : {3, 6, 11, 22})
+    if (ept * 384 >= nent && ept * p.dsub <= 88) return ept;
+  return 0;
+}
+}  // namespace
+
+void set_scan_family(int family) { g_family = family; }
+
+namespace {
+int pick_gpt(const ScanParams &p) {
+  if (p.dsub < 1 || p.dsub > 8 || p.k > 32 || p.ks % 4 != 0) return 0;
+  const int ngroups = p.M * p.ks / 4;
+  for (int gpt = 1; gpt <= 4; gpt <<= 1)
+    if (gpt * kScanThreads >= ngroups && gpt * 4 * p.dsub <= 64) return gpt;
   return 0;
 }
 }  // namespace
 
 cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms, cudaStream_t s) {
   if (p.k < 1 || p.k > 256) return cudaErrorInvalidValue;
-  const int ept = pick_ept(p);
-  if (p.ks == 16) return launch_scan_four(p, ept ? p.dsub : 0, ept, num_sms, s);
-  return launch_scan_eight(p, ept ? p.dsub : 0, ept, num_sms, s);
+  const int ws = pick_ws_ept(p);
+  if (ws) return launch_scan_ws(p, p.dsub, ws, num_sms, s);
+  const int gpt = pick_gpt(p);
+  if (p.ks == 16) return launch_scan_four(p, gpt ? p.dsub : 0, gpt, num_sms, s);
+  return launch_scan_eight(p, gpt ? p.dsub : 0, gpt, num_sms, s);
 }
 
 int ivfpq_scan_variant_name(const ScanParams &p, char *buf, size_t len) {
-  const int ept = pick_ept(p);
-  return snprintf(buf, len, "ivfpq_query_kernel<%d,%d,%d,%s>", ept ? p.dsub : 0, ept,
+  const int ws = pick_ws_ept(p);
+  if (ws) return snprintf(buf, len, "ivfpq_ws_kernel<%d,%d,1,256>", p.dsub, ws);
+  const int gpt = pick_gpt(p);
+  return snprintf(buf, len, "ivfpq_query_kernel<%d,%d,%d,%s>", gpt ? p.dsub : 0, gpt,
                   p.k <= 32 ? 1 : p.k <= 64 ? 2 : p.k <= 128 ? 4 : 8, p.ks == 16 ? "4bit" : "8bit");
 }
 

@@ -8,11 +8,14 @@
 //      dist = sum * scale + min * M                    (pq_simd.rs:721-769)
 //   4. top-k by (distance, vector id)                  (search.rs:64-75)
 //
-// Persistent blocks (one per SM) take queries from an atomic counter and walk
-// the query's probes nearest-first, kMaxBatch lists at a time:
+// Persistent blocks (one per SM) take queries from an atomic counter, load
+// and compact the query's probe list in parallel, and walk it nearest-first,
+// kMaxBatch lists at a time:
 //   - every thread builds its fixed share of each list's table; when DSUB > 0
-//     the thread's EPT codewords live in registers for the whole kernel, so a
-//     table entry costs dsub subtract/multiply/add triples and one store;
+//     a thread owns GPT groups of 4 adjacent entries of one subspace and keeps
+//     their codewords in registers for the whole kernel, so a group costs one
+//     broadcast load of the residual subvector, 4 x dsub subtract/multiply/add
+//     triples and one 16-byte store;
 //   - the 512 threads score the batch's candidates, one candidate per thread
 //     with the reference's sequential sum over subspaces;
 //   - each warp keeps its own sorted top-k for the whole query and admits a
@@ -36,10 +39,12 @@ namespace vg {
 
 constexpr int kScanThreads = 512;
 constexpr int kScanWarps = kScanThreads / 32;
-constexpr int kMaxBatch = 4;
+constexpr int kMaxBatch = 4;  // lists per batch (the candidate prefix below is unrolled for 4)
 
+// Per-list shared memory: table (padded to 16 bytes), residual, and for
+// 16-entry codebooks the u8 table.
 __host__ __device__ inline size_t scan_pair_bytes(int d, int M, int ks, bool four) {
-  size_t b = static_cast<size_t>(M) * ks * 4 + static_cast<size_t>((d + 3) & ~3) * 4;
+  size_t b = static_cast<size_t>((M * ks + 3) & ~3) * 4 + static_cast<size_t>((d + 3) & ~3) * 4;
   if (four) b += (static_cast<size_t>(M) * 16 + 15) & ~static_cast<size_t>(15);
   return b;
 }
@@ -59,6 +64,32 @@ __device__ __forceinline__ void topk_insert_one(WarpTopK<R> &tk, uint64_t key) {
     tk.v[0] = lane < rank ? tk.v[0] : (lane == rank ? key : up);
   } else {
     tk.add(lane_id() == 0 ? key : kEmptyKey);
+  }
+}
+
+// Read a subvector of D floats from 16-byte aligned shared memory (the
+// start is aligned whenever D is a multiple of the vector width used).
+template <int D>
+__device__ __forceinline__ void load_subvector(const float *src, float (&v)[D]) {
+  if (D % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < D; j += 4) {
+      float4 t = *reinterpret_cast<const float4 *>(src + j);
+      v[j] = t.x;
+      v[j + 1] = t.y;
+      v[j + 2] = t.z;
+      v[j + 3] = t.w;
+    }
+  } else if (D % 2 == 0) {
+#pragma unroll
+    for (int j = 0; j < D; j += 2) {
+      float2 t = *reinterpret_cast<const float2 *>(src + j);
+      v[j] = t.x;
+      v[j + 1] = t.y;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < D; ++j) v[j] = src[j];
   }
 }
 
@@ -84,86 +115,109 @@ __device__ __forceinline__ float adc_row_sum(const uint8_t *cp, const float *lg,
   return acc;
 }
 
-template <int DSUB, int EPT, int R, bool FOUR, int KS>
+// Squared distance of one residual subvector to one codeword, summed in the
+// reference's order.  The first term is taken as is: for s >= +0 the
+// reference's 0.0 + s equals s exactly, and a square is never -0.
+template <int D>
+__device__ __forceinline__ float sq_dist(const float (&q)[D], const float (&c)[D]) {
+  float d0 = __fsub_rn(q[0], c[0]);
+  float acc = __fmul_rn(d0, d0);
+#pragma unroll
+  for (int j = 1; j < D; ++j) {
+    float dj = __fsub_rn(q[j], c[j]);
+    acc = __fadd_rn(acc, __fmul_rn(dj, dj));
+  }
+  return acc;
+}
+
+template <int DSUB, int GPT, int R, bool FOUR, int KS>
 __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const ScanParams p, const int batch) {
   extern __shared__ __align__(16) unsigned char smem[];
-  const int M = p.M, ks = p.ks, d = p.d, P = p.P, k = p.k;
+  const int M = p.M, ks = KS > 0 ? KS : p.ks, d = p.d, P = p.P, k = p.k;
   const int nent = M * ks;
+  const int tstride = (nent + 3) & ~3;  // table stride, keeps every region 16-byte aligned
   const int dpad = (d + 3) & ~3;
   unsigned long long *wl = reinterpret_cast<unsigned long long *>(smem);  // [warps][32R]
-  float *lut = reinterpret_cast<float *>(wl + kScanWarps * 32 * R);       // [batch][nent]
-  float *qres = lut + static_cast<size_t>(batch) * nent;                   // [batch][dpad]
+  float *lut = reinterpret_cast<float *>(wl + kScanWarps * 32 * R);       // [batch][tstride]
+  float *qres = lut + static_cast<size_t>(batch) * tstride;                // [batch][dpad]
   uint8_t *qlut = reinterpret_cast<uint8_t *>(qres + static_cast<size_t>(batch) * dpad);  // [batch][M*16]
   const int qlut_stride = (M * 16 + 15) & ~15;
 
   __shared__ uint32_t s_query;
-  __shared__ int s_nb, s_next;
-  __shared__ uint32_t s_list[kMaxBatch];
-  __shared__ uint64_t s_lbeg[kMaxBatch];
-  __shared__ uint32_t s_prefix[kMaxBatch + 1];
+  __shared__ int s_nvalid;
+  __shared__ int s_wcount[kScanWarps];
+  __shared__ uint32_t s_list[kScanThreads], s_len[kScanThreads];
+  __shared__ uint64_t s_lbeg[kScanThreads];
   __shared__ unsigned long long s_bound;
   __shared__ float s_rmin[kMaxBatch][kScanWarps], s_rmax[kMaxBatch][kScanWarps];
   __shared__ float s_scale[kMaxBatch], s_fbase[kMaxBatch];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
+  // register-resident codewords: groups G = tid + i*512 cover entries 4G..4G+3
   constexpr int kD = DSUB > 0 ? DSUB : 1;
-  constexpr int kE = EPT > 0 ? EPT : 1;
-  float cb[kE][kD];
+  constexpr int kG = GPT > 0 ? GPT : 1;
+  const int ngroups = nent >> 2;
+  float cb[kG][4][kD];
   if (DSUB > 0) {
 #pragma unroll
-    for (int i = 0; i < kE; ++i) {
-      int e = tid + i * kScanThreads;
+    for (int i = 0; i < kG; ++i) {
+      const int G = tid + i * kScanThreads;
 #pragma unroll
-      for (int j = 0; j < kD; ++j) cb[i][j] = e < nent ? p.codebooks[static_cast<size_t>(e) * kD + j] : 0.0f;
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int j = 0; j < kD; ++j)
+          cb[i][u][j] = G < ngroups ? p.codebooks[(static_cast<size_t>(4 * G + u)) * kD + j] : 0.0f;
     }
   }
-  // subspace offset of entry tid + i*512: an arithmetic progression in i
-  // when ks divides 512, otherwise one division per entry
-  const bool ks_divides = (kScanThreads % ks) == 0;
-  const int qoff0 = (tid / ks) * kD;
-  const int qstep = ks_divides ? (kScanThreads / ks) * kD : 0;
 
   for (;;) {
     if (tid == 0) {
       s_query = atomicAdd(p.counter, 1u);
-      s_next = 0;
       s_bound = kEmptyKey;
     }
     __syncthreads();
     const uint32_t q = s_query;
     if (q >= static_cast<uint32_t>(p.nq)) break;
-    const uint32_t *probes = p.probes + static_cast<size_t>(q) * P;
     const float *qv = p.qn + static_cast<size_t>(q) * d;
     WarpTopK<R> tk;
     tk.init();
 
-    for (;;) {
-      // next batch of probed lists (nearest first), skipping lists this
-      // device does not own
-      if (tid == 0) {
-        int nb = 0, i = s_next;
-        uint32_t acc = 0;
-        while (i < P && nb < batch) {
-          uint32_t l = probes[i++];
-          if (l == 0xffffffffu || (p.owner && !p.owner[l])) continue;
-          uint64_t b = p.list_off[l];
-          s_list[nb] = l;
-          s_lbeg[nb] = b;
-          s_prefix[nb] = acc;
-          acc += static_cast<uint32_t>(p.list_off[l + 1] - b);
-          ++nb;
-        }
-        for (int g = nb; g <= kMaxBatch; ++g) s_prefix[g] = acc;
-        s_nb = nb;
-        s_next = i;
+    // probe metadata of the query, compacted to valid owned lists in order
+    {
+      uint32_t l = 0xffffffffu;
+      bool valid = false;
+      if (tid < P) {
+        l = p.probes[static_cast<size_t>(q) * P + tid];
+        valid = l != 0xffffffffu && (!p.owner || p.owner[l]);
       }
+      const unsigned vm = __ballot_sync(VG_FULL_MASK, valid);
+      if (lane == 0) s_wcount[warp] = __popc(vm);
       __syncthreads();
-      const int nb = s_nb;
-      if (nb == 0) break;
+      int base = 0, total = 0;
+      for (int w = 0; w < kScanWarps; ++w) {
+        const int c = s_wcount[w];
+        base += w < warp ? c : 0;
+        total += c;
+      }
+      if (valid) {
+        const int pos = base + __popc(vm & ((1u << lane) - 1u));
+        const uint64_t b = p.list_off[l];
+        s_list[pos] = l;
+        s_lbeg[pos] = b;
+        s_len[pos] = static_cast<uint32_t>(p.list_off[l + 1] - b);
+      }
+      if (tid == 0) s_nvalid = total;
+      __syncthreads();
+    }
+    const int nvalid = s_nvalid;
+
+    for (int b0 = 0; b0 < nvalid; b0 += batch) {
+      const int nb = min(batch, nvalid - b0);
+      const uint32_t *blist = s_list + b0;
       for (int i = tid; i < nb * d; i += kScanThreads) {
         int g = i / d, j = i - g * d;
-        qres[g * dpad + j] = __fsub_rn(qv[j], p.centroids[static_cast<size_t>(s_list[g]) * d + j]);
+        qres[g * dpad + j] = __fsub_rn(qv[j], p.centroids[static_cast<size_t>(blist[g]) * d + j]);
       }
       __syncthreads();
 
@@ -171,24 +225,24 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
 #pragma unroll 1
       for (int g = 0; g < nb; ++g) {
         const float *qg = qres + g * dpad;
-        float *lg = lut + static_cast<size_t>(g) * nent;
+        float *lg = lut + static_cast<size_t>(g) * tstride;
         float lmin = __int_as_float(0x7f800000), lmax = -__int_as_float(0x7f800000);
         if (DSUB > 0) {
 #pragma unroll
-          for (int i = 0; i < kE; ++i) {
-            int e = tid + i * kScanThreads;
-            if (e < nent) {
-              const float *qs = qg + (ks_divides ? qoff0 + i * qstep : (e / ks) * kD);
-              float acc = 0.0f;
-#pragma unroll
-              for (int j = 0; j < kD; ++j) {
-                float diff = __fsub_rn(qs[j], cb[i][j]);
-                acc = __fadd_rn(acc, __fmul_rn(diff, diff));
-              }
-              lg[e] = acc;
+          for (int i = 0; i < kG; ++i) {
+            const int G = tid + i * kScanThreads;
+            if (G < ngroups) {
+              float qs[kD];
+              load_subvector<kD>(qg + ((4 * G) / ks) * kD, qs);
+              float4 out;
+              out.x = sq_dist<kD>(qs, cb[i][0]);
+              out.y = sq_dist<kD>(qs, cb[i][1]);
+              out.z = sq_dist<kD>(qs, cb[i][2]);
+              out.w = sq_dist<kD>(qs, cb[i][3]);
+              *reinterpret_cast<float4 *>(lg + 4 * G) = out;
               if (FOUR) {
-                lmin = fminf(lmin, acc);
-                lmax = fmaxf(lmax, acc);
+                lmin = fminf(lmin, fminf(fminf(out.x, out.y), fminf(out.z, out.w)));
+                lmax = fmaxf(lmax, fmaxf(fmaxf(out.x, out.y), fmaxf(out.z, out.w)));
               }
             }
           }
@@ -242,25 +296,33 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
         for (int i = tid; i < nb * nent; i += kScanThreads) {
           int g = i / nent, e = i - g * nent;
           // round half away from zero, clamp; NaN -> 0 (pq_simd.rs:607-609)
-          float t = roundf(__fmul_rn(__fsub_rn(lut[i], s_rmin[g][0]), s_rmax[g][0]));
+          float t = roundf(__fmul_rn(__fsub_rn(lut[g * tstride + e], s_rmin[g][0]), s_rmax[g][0]));
           t = fminf(fmaxf(t, 0.0f), 255.0f);
           qlut[g * qlut_stride + e] = static_cast<uint8_t>(t);
         }
       }
       __syncthreads();
 
+      // candidate prefix over the batch's lists (kMaxBatch == 4)
+      const uint32_t pre1 = s_len[b0];
+      const uint32_t pre2 = pre1 + (nb > 1 ? s_len[b0 + 1] : 0u);
+      const uint32_t pre3 = pre2 + (nb > 2 ? s_len[b0 + 2] : 0u);
+      const uint32_t pre4 = pre3 + (nb > 3 ? s_len[b0 + 3] : 0u);
+
       // ---- score and select ---------------------------------------------
-      const uint32_t ctotal = s_prefix[kMaxBatch];
+      const uint32_t ctotal = pre4;
       for (uint32_t x0 = warp * 32; x0 < ctotal; x0 += kScanThreads) {
         const uint32_t x = x0 + lane;
         float dist = 0.0f;
         int g = 0;
         uint32_t c = 0;
         if (x < ctotal) {
-          g = (x >= s_prefix[1]) + (x >= s_prefix[2]) + (x >= s_prefix[3]);
-          c = x - s_prefix[g];
-          const uint32_t list = s_list[g];
-          const uint32_t len = s_prefix[g + 1] - s_prefix[g];
+          g = (x >= pre1) + (x >= pre2) + (x >= pre3);
+          const uint32_t lo = g == 0 ? 0u : g == 1 ? pre1 : g == 2 ? pre2 : pre3;
+          const uint32_t hi = g == 0 ? pre1 : g == 1 ? pre2 : g == 2 ? pre3 : pre4;
+          c = x - lo;
+          const uint32_t list = blist[g];
+          const uint32_t len = hi - lo;
           if (FOUR && len >= 16) {  // search.rs:1261 (SIMD_BATCH_THRESHOLD)
             const uint8_t *bp = p.packed + p.pack_off[list] + static_cast<uint64_t>(c >> 5) * M * 16;
             const uint8_t *ql = qlut + g * qlut_stride;
@@ -271,7 +333,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
             dist = __fadd_rn(__fmul_rn(__uint2float_rn(acc), s_scale[g]), s_fbase[g]);
           } else {
             const uint8_t *cp = p.list_codes + p.code_off[list] + static_cast<uint64_t>(c) * M;
-            dist = adc_row_sum<KS>(cp, lut + static_cast<size_t>(g) * nent, M, ks);
+            dist = adc_row_sum<KS>(cp, lut + static_cast<size_t>(g) * tstride, M, ks);
           }
         }
         uint64_t thr = tk.worst();
@@ -281,7 +343,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
         const bool pass = x < ctotal && dk <= static_cast<uint32_t>(thr >> 32);
         unsigned mask = __ballot_sync(VG_FULL_MASK, pass);
         if (!mask) continue;
-        const uint64_t key = pass ? ((static_cast<uint64_t>(dk) << 32) | p.list_ids[s_lbeg[g] + c]) : kEmptyKey;
+        const uint64_t key = pass ? ((static_cast<uint64_t>(dk) << 32) | p.list_ids[s_lbeg[b0 + g] + c]) : kEmptyKey;
         if (__popc(mask) > 4) {
           tk.add(key < thr ? key : kEmptyKey);
         } else {
@@ -336,15 +398,15 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
   }
 }
 
-template <int DSUB, int EPT, int R, bool FOUR, int KS>
+template <int DSUB, int GPT, int R, bool FOUR, int KS>
 cudaError_t launch_scan_variant(const ScanParams &p, int num_sms, cudaStream_t s) {
-  auto kern = ivfpq_query_kernel<DSUB, EPT, R, FOUR, KS>;
+  auto kern = ivfpq_query_kernel<DSUB, GPT, R, FOUR, KS>;
   int dev = 0, optin = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if (e != cudaSuccess) return e;
-  const size_t reserve = 2048;  // static shared memory of the kernel
+  const size_t reserve = 12288;  // static shared memory of the kernel (8-9 KB)
   int batch = kMaxBatch;
   while (batch > 1 && scan_smem_bytes(p.d, p.M, p.ks, FOUR, batch, R) + reserve > static_cast<size_t>(optin)) --batch;
   const size_t smem = scan_smem_bytes(p.d, p.M, p.ks, FOUR, batch, R);
