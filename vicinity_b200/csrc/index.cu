@@ -731,7 +731,8 @@ int vg_ivfpq_create(size_t dim, const vg_ivfpq_params *params, int device, vg_in
     *ix->h_err = 0;
     e = cudaHostGetDevicePointer(reinterpret_cast<void **>(&ix->d_err), ix->h_err, 0);
   }
-  if (const char *fam = std::getenv("VICINITY_SCAN_KERNEL")) vg::set_scan_family(std::strcmp(fam, "pipeline") != 0);
+  if (const char *fam = std::getenv("VICINITY_SCAN_KERNEL"))
+    vg::set_scan_family(std::strcmp(fam, "pipeline") == 0 ? 0 : std::strcmp(fam, "query") == 0 ? 1 : 2);
   if (e != cudaSuccess) {
     vg_ivfpq_destroy(ix);
     return cuda_fail(e, "stream/event creation");

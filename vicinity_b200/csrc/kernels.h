@@ -130,8 +130,9 @@ cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms,
 // Name of the kernel variant launch_ivfpq_scan would run for p.
 int ivfpq_scan_variant_name(const ScanParams &p, char *buf, size_t len);
 
-// Kernel family selection: 1 (default) = query-major kernel, 0 = the
-// warp-specialised pipeline where it applies.
+// Kernel family selection: 2 (default) = double-buffered kernel where it
+// applies, 1 = single-buffered query-major kernel, 0 = the warp-specialised
+// pipeline where it applies.
 void set_scan_family(int family);
 
 // ---- build_kernels.cu -----------------------------------------------------

@@ -14,13 +14,14 @@ namespace vg {
 cudaError_t launch_scan_four(const ScanParams &p, int dsub, int ept, int num_sms, cudaStream_t s);
 cudaError_t launch_scan_eight(const ScanParams &p, int dsub, int ept, int num_sms, cudaStream_t s);
 cudaError_t launch_scan_ws(const ScanParams &p, int dsub, int ept, int num_sms, cudaStream_t s);
+cudaError_t launch_scan_pipe(const ScanParams &p, int dsub, int gpt, int num_sms, cudaStream_t s);
 
 namespace {
-int g_family = 1;  // query-major kernel by default (measured faster at C1)
+int g_family = 2;  // double-buffered kernel by default
 
 // Entries per producer thread for the warp-specialised kernel (0 = n/a).
 int pick_ws_ept(const ScanParams &p) {
-  if (g_family == 1 || p.ks != 256 || p.dsub < 1 || p.dsub > 8 || p.k > 32 || p.P > 384) return 0;
+  if (g_family != 0 || p.ks != 256 || p.dsub < 1 || p.dsub > 8 || p.k > 32 || p.P > 384) return 0;
   const int nent = p.M * p.ks;
   for (int ept : {3, 6, 11, 22})
     if (ept * 384 >= nent && ept * p.dsub <= 88) return ept;
@@ -45,6 +46,7 @@ cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms, cudaStream_t s) 
   const int ws = pick_ws_ept(p);
   if (ws) return launch_scan_ws(p, p.dsub, ws, num_sms, s);
   const int gpt = pick_gpt(p);
+  if (g_family == 2 && gpt && p.ks == 256) return launch_scan_pipe(p, p.dsub, gpt, num_sms, s);
   if (p.ks == 16) return launch_scan_four(p, gpt ? p.dsub : 0, gpt, num_sms, s);
   return launch_scan_eight(p, gpt ? p.dsub : 0, gpt, num_sms, s);
 }
@@ -53,6 +55,7 @@ int ivfpq_scan_variant_name(const ScanParams &p, char *buf, size_t len) {
   const int ws = pick_ws_ept(p);
   if (ws) return snprintf(buf, len, "ivfpq_ws_kernel<%d,%d,1,256>", p.dsub, ws);
   const int gpt = pick_gpt(p);
+  if (g_family == 2 && gpt && p.ks == 256) return snprintf(buf, len, "ivfpq_pipe_kernel<%d,%d,1,256>", p.dsub, gpt);
   return snprintf(buf, len, "ivfpq_query_kernel<%d,%d,%d,%s>", gpt ? p.dsub : 0, gpt,
                   p.k <= 32 ? 1 : p.k <= 64 ? 2 : p.k <= 128 ? 4 : 8, p.ks == 16 ? "4bit" : "8bit");
 }

@@ -1,0 +1,287 @@
+// Double-buffered variant of the fused IVF-PQ search kernel for 8-bit codes
+// (same computation and results as ivfpq_query_kernel in scan_kernel.cuh).
+//
+// Building a list's ADC table is FP32-issue bound and scoring its codes is
+// shared-memory bound; done one after the other they leave one of the two
+// pipes idle.  This kernel keeps two sets of `batch` tables: in each phase
+// every warp builds its share of the NEXT batch's tables and scores its share
+// of the CURRENT batch's candidates, even warps in that order and odd warps
+// in the other, so at any time half the warps feed the FP32 pipe and half the
+// shared-memory pipe.  One block barrier per phase separates the sets.
+//
+// The residuals of batch b + 2 are loaded from the centroid rows during phase
+// b and written into the residual buffer that batch b has finished with.
+#pragma once
+
+#include "scan_kernel.cuh"
+
+namespace vg {
+
+__host__ __device__ inline size_t pipe_smem_bytes(int d, int M, int ks, int batch, int R) {
+  const size_t table = static_cast<size_t>((M * ks + 3) & ~3) * 4;
+  const size_t vec = static_cast<size_t>((d + 3) & ~3) * 4;
+  return static_cast<size_t>(kScanWarps) * 32 * R * 8 + 2 * static_cast<size_t>(batch) * (table + vec);
+}
+
+template <int DSUB, int GPT, int R, int KS>
+__global__ void __launch_bounds__(kScanThreads, 1) ivfpq_pipe_kernel(const ScanParams p, const int batch) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int M = p.M, d = p.d, P = p.P, k = p.k;
+  constexpr int ks = KS;
+  const int nent = M * ks;
+  const int tstride = (nent + 3) & ~3;
+  const int dpad = (d + 3) & ~3;
+  unsigned long long *wl = reinterpret_cast<unsigned long long *>(smem);     // [warps][32R]
+  float *tables = reinterpret_cast<float *>(wl + kScanWarps * 32 * R);        // [2][batch][tstride]
+  float *qres = tables + 2 * static_cast<size_t>(batch) * tstride;            // [2][batch][dpad]
+
+  __shared__ uint32_t s_query;
+  __shared__ int s_nvalid;
+  __shared__ int s_wcount[kScanWarps];
+  __shared__ uint32_t s_list[kScanThreads], s_len[kScanThreads];
+  __shared__ uint64_t s_lbeg[kScanThreads], s_coff[kScanThreads];
+  __shared__ unsigned long long s_bound;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool build_first = (warp & 1) == 0;
+
+  const int ngroups = nent >> 2;
+  float cb[GPT][4][DSUB];
+#pragma unroll
+  for (int i = 0; i < GPT; ++i) {
+    const int G = tid + i * kScanThreads;
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int j = 0; j < DSUB; ++j)
+        cb[i][u][j] = G < ngroups ? p.codebooks[(static_cast<size_t>(4 * G + u)) * DSUB + j] : 0.0f;
+  }
+
+  for (;;) {
+    if (tid == 0) {
+      s_query = atomicAdd(p.counter, 1u);
+      s_bound = kEmptyKey;
+    }
+    __syncthreads();
+    const uint32_t q = s_query;
+    if (q >= static_cast<uint32_t>(p.nq)) break;
+    const float *qv = p.qn + static_cast<size_t>(q) * d;
+    WarpTopK<R> tk;
+    tk.init();
+
+    // probe metadata of the query, compacted to valid owned lists in order
+    {
+      uint32_t l = 0xffffffffu;
+      bool valid = false;
+      if (tid < P) {
+        l = p.probes[static_cast<size_t>(q) * P + tid];
+        valid = l != 0xffffffffu && (!p.owner || p.owner[l]);
+      }
+      const unsigned vm = __ballot_sync(VG_FULL_MASK, valid);
+      if (lane == 0) s_wcount[warp] = __popc(vm);
+      __syncthreads();
+      int base = 0, total = 0;
+      for (int w = 0; w < kScanWarps; ++w) {
+        const int c = s_wcount[w];
+        base += w < warp ? c : 0;
+        total += c;
+      }
+      if (valid) {
+        const int pos = base + __popc(vm & ((1u << lane) - 1u));
+        const uint64_t b = p.list_off[l];
+        s_list[pos] = l;
+        s_lbeg[pos] = b;
+        s_len[pos] = static_cast<uint32_t>(p.list_off[l + 1] - b);
+        s_coff[pos] = p.code_off[l];
+      }
+      if (tid == 0) s_nvalid = total;
+      __syncthreads();
+    }
+    const int nvalid = s_nvalid;
+    const int nbat = (nvalid + batch - 1) / batch;
+
+    // table of every list of batch b into table set `set` (residuals of batch
+    // b live in residual set b & 1)
+    auto build = [&](int b, int set) {
+      const int nb = min(batch, nvalid - b * batch);
+      const float *qset = qres + static_cast<size_t>(b & 1) * batch * dpad;
+      float *tset = tables + static_cast<size_t>(set) * batch * tstride;
+#pragma unroll 1
+      for (int g = 0; g < nb; ++g) {
+        const float *qg = qset + g * dpad;
+        float *lg = tset + static_cast<size_t>(g) * tstride;
+#pragma unroll
+        for (int i = 0; i < GPT; ++i) {
+          const int G = tid + i * kScanThreads;
+          if (G < ngroups) {
+            float qs[DSUB];
+            load_subvector<DSUB>(qg + ((4 * G) / ks) * DSUB, qs);
+            float4 out;
+            out.x = sq_dist<DSUB>(qs, cb[i][0]);
+            out.y = sq_dist<DSUB>(qs, cb[i][1]);
+            out.z = sq_dist<DSUB>(qs, cb[i][2]);
+            out.w = sq_dist<DSUB>(qs, cb[i][3]);
+            *reinterpret_cast<float4 *>(lg + 4 * G) = out;
+          }
+        }
+      }
+    };
+
+    // score and select the candidates of batch b against table set `set`
+    auto scan = [&](int b, int set) {
+      const int b0 = b * batch;
+      const int nb = min(batch, nvalid - b0);
+      const float *tset = tables + static_cast<size_t>(set) * batch * tstride;
+      const uint32_t pre1 = s_len[b0];
+      const uint32_t pre2 = pre1 + (nb > 1 ? s_len[b0 + 1] : 0u);
+      const uint32_t pre3 = pre2 + (nb > 2 ? s_len[b0 + 2] : 0u);
+      const uint32_t pre4 = pre3 + (nb > 3 ? s_len[b0 + 3] : 0u);
+      for (uint32_t x0 = warp * 32; x0 < pre4; x0 += kScanThreads) {
+        const uint32_t x = x0 + lane;
+        float dist = 0.0f;
+        int g = 0;
+        uint32_t c = 0;
+        if (x < pre4) {
+          g = (x >= pre1) + (x >= pre2) + (x >= pre3);
+          c = x - (g == 0 ? 0u : g == 1 ? pre1 : g == 2 ? pre2 : pre3);
+          const uint8_t *cp = p.list_codes + s_coff[b0 + g] + static_cast<uint64_t>(c) * M;
+          dist = adc_row_sum<KS>(cp, tset + static_cast<size_t>(g) * tstride, M, ks);
+        }
+        uint64_t thr = tk.worst();
+        const uint64_t bound = s_bound;
+        thr = bound < thr ? bound : thr;
+        const uint32_t dk = order_key(dist);
+        const bool pass = x < pre4 && dk <= static_cast<uint32_t>(thr >> 32);
+        unsigned mask = __ballot_sync(VG_FULL_MASK, pass);
+        if (!mask) continue;
+        const uint64_t key = pass ? ((static_cast<uint64_t>(dk) << 32) | p.list_ids[s_lbeg[b0 + g] + c]) : kEmptyKey;
+        if (__popc(mask) > 4) {
+          tk.add(key < thr ? key : kEmptyKey);
+        } else {
+          while (mask) {
+            const int src = __ffs(mask) - 1;
+            mask &= mask - 1;
+            const uint64_t kx = shfl64(key, src);
+            if (kx < thr) topk_insert_one(tk, kx);
+          }
+        }
+        const uint64_t kth = tk.get(k - 1);
+        if (lane == 0 && kth < bound) atomicMin(&s_bound, kth);
+      }
+    };
+
+    if (nbat > 0) {
+      // prologue: residuals of batches 0 and 1, tables of batch 0
+      for (int i = tid; i < min(2 * batch, nvalid) * d; i += kScanThreads) {
+        const int li = i / d, j = i - li * d;
+        qres[static_cast<size_t>(li / batch) * batch * dpad + (li % batch) * dpad + j] =
+            __fsub_rn(qv[j], p.centroids[static_cast<size_t>(s_list[li]) * d + j]);
+      }
+      __syncthreads();
+      build(0, 0);
+      __syncthreads();
+    }
+    for (int b = 0; b < nbat; ++b) {
+      const int set = b & 1;
+      const bool has_next = b + 1 < nbat;
+      // residuals of batch b + 2: centroid rows loaded now, written after the
+      // phase into residual set b & 1 (batch b's, no longer read)
+      const int l2 = (b + 2) * batch;
+      const int n2 = max(0, min(batch, nvalid - l2));
+      float cnext[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int i = tid + u * kScanThreads;
+        cnext[u] = 0.0f;
+        if (i < n2 * d) {
+          const int g = i / d, j = i - g * d;
+          cnext[u] = p.centroids[static_cast<size_t>(s_list[l2 + g]) * d + j];
+        }
+      }
+      if (build_first) {
+        if (has_next) build(b + 1, set ^ 1);
+        scan(b, set);
+      } else {
+        scan(b, set);
+        if (has_next) build(b + 1, set ^ 1);
+      }
+      float *qdst = qres + static_cast<size_t>(set) * batch * dpad;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int i = tid + u * kScanThreads;
+        if (i < n2 * d) {
+          const int g = i / d, j = i - g * d;
+          qdst[g * dpad + j] = __fsub_rn(qv[j], cnext[u]);
+        }
+      }
+      for (int i = tid + 2 * kScanThreads; i < n2 * d; i += kScanThreads) {  // batch * d > 1024 only
+        const int g = i / d, j = i - g * d;
+        qdst[g * dpad + j] = __fsub_rn(qv[j], p.centroids[static_cast<size_t>(s_list[l2 + g]) * d + j]);
+      }
+      __syncthreads();
+    }
+
+    // ---- merge the warp lists (binary tree) and emit -----------------------
+#pragma unroll
+    for (int r = 0; r < R; ++r) wl[warp * 32 * R + r * 32 + lane] = tk.v[r];
+    __syncthreads();
+    for (int stride = 1; stride < kScanWarps; stride <<= 1) {
+      if ((warp % (2 * stride)) == 0) {
+        const unsigned long long *other = wl + (warp + stride) * 32 * R;
+        if (other[0] < tk.worst()) {
+#pragma unroll
+          for (int r = 0; r < R; ++r) tk.merge_sorted_row(other[r * 32 + lane]);
+#pragma unroll
+          for (int r = 0; r < R; ++r) wl[warp * 32 * R + r * 32 + lane] = tk.v[r];
+        }
+      }
+      __syncthreads();
+    }
+    if (warp == 0) {
+      uint32_t count = 0;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int i = r * 32 + lane;
+        const uint64_t key = tk.v[r];
+        const bool real = i < k && key != kEmptyKey;
+        count += __popc(__ballot_sync(VG_FULL_MASK, real));
+        if (i < k) {
+          const size_t o = static_cast<size_t>(q) * k + i;
+          if (p.out_keys) p.out_keys[o] = key;
+          if (p.out_ids) {
+            p.out_ids[o] = real ? p.doc_ids[key_id(key)] : 0xffffffffu;
+            p.out_dist[o] = real ? key_dist(key) : __int_as_float(0x7f800000);
+          }
+        }
+      }
+      if (p.out_count && lane == 0) p.out_count[q] = count;
+    }
+  }
+}
+
+template <int DSUB, int GPT, int R, int KS>
+cudaError_t launch_pipe_variant(const ScanParams &p, int num_sms, cudaStream_t s) {
+  auto kern = ivfpq_pipe_kernel<DSUB, GPT, R, KS>;
+  int dev = 0, optin = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e != cudaSuccess) return e;
+  const size_t reserve = 16384;  // static shared memory of the kernel (~13 KB)
+  int batch = kMaxBatch;
+  while (batch > 1 && pipe_smem_bytes(p.d, p.M, KS, batch, R) + reserve > static_cast<size_t>(optin)) --batch;
+  const size_t smem = pipe_smem_bytes(p.d, p.M, KS, batch, R);
+  if (smem + reserve > static_cast<size_t>(optin)) return cudaErrorInvalidConfiguration;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kScanThreads, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  int grid = num_sms * per_sm;
+  if (grid > p.nq) grid = p.nq;
+  kern<<<grid, kScanThreads, smem, s>>>(p, batch);
+  return cudaGetLastError();
+}
+
+}  // namespace vg
