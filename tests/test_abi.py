@@ -33,6 +33,14 @@ def test_library_exports_every_declared_symbol():
     assert set(names) <= exported
 
 
+def test_torch_imports_after_the_engine_library():
+    # both link libnccl.so.2 by soname; loading the engine first must not pin
+    # an NCCL that torch cannot use
+    code = "from vicinity_b200 import _lib; _lib.load(); import torch; print('ok')"
+    out = subprocess.run(["python", "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0 and out.stdout.strip().endswith("ok"), out.stderr[-2000:]
+
+
 def test_version_string():
     assert b"sm_100a" in _lib.load().vg_version()
 

@@ -133,6 +133,28 @@ SIGNATURES = {
 _lib: C.CDLL | None = None
 
 
+def _preload_torch_nccl() -> None:
+    """Load the NCCL that PyTorch in this environment ships (the nvidia-nccl
+    wheel), when there is one, before the engine library.
+
+    The engine links libnccl.so.2 by soname.  Were the older system copy
+    loaded first, a later `import torch` would bind to it as well and fail
+    on symbols only torch's newer NCCL exports; with torch's copy loaded
+    first both share it (NCCL keeps its C API backward compatible).
+    """
+    import importlib.util
+
+    try:
+        spec = importlib.util.find_spec("nvidia.nccl")
+    except (ImportError, ValueError):
+        return
+    for base in (spec.submodule_search_locations or []) if spec else []:
+        path = Path(base) / "lib" / "libnccl.so.2"
+        if path.exists():
+            C.CDLL(os.fspath(path), mode=C.RTLD_GLOBAL)
+            return
+
+
 def load() -> C.CDLL:
     """Load (once) and return the engine library with typed signatures."""
     global _lib
@@ -143,6 +165,7 @@ def load() -> C.CDLL:
             f"{LIB_PATH} is missing; build it with `python -m vicinity_b200.build` "
             "(the engine has no CPU fallback)"
         )
+    _preload_torch_nccl()
     lib = C.CDLL(os.fspath(LIB_PATH))
     for name, (res, args) in SIGNATURES.items():
         fn = getattr(lib, name)
