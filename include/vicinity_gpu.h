@@ -204,6 +204,24 @@ int vg_flat_search_ip(const float *db, size_t n, const float *queries,
                       size_t nq, size_t dim, size_t k, int device,
                       uint32_t *out_ids, float *out_dist, uint32_t *out_count);
 
+/* No counterpart in the reference.  vg_flat_search_ip for callers that
+ * cannot allocate device memory at search time (memory handed out up front
+ * to another allocator or budget, loops that cannot take cudaMalloc's
+ * synchronisation, embedders that forbid allocation after start-up).  Same
+ * results; allocates nothing.  All pointers must be device memory of
+ * `device`; work runs on `stream` (a cudaStream_t, NULL = legacy default
+ * stream) and the call returns once it is done.  Scratch is one fixed
+ * 32 MiB device array per GPU, shared by every call: requests whose scratch
+ * would exceed it (nq > 32768, or nq * k * tiles too large) return
+ * VG_ERR_INVALID_PARAMETER -- split the batch.  The first call on a device
+ * resolves the array's address (cudaGetSymbolAddress); make it before any
+ * stream capture.  Calls whose GPU work overlaps race on the scratch and
+ * must be serialised by the caller. */
+int vg_flat_search_ip_noalloc(const float *db, size_t n, const float *queries,
+                              size_t nq, size_t dim, size_t k, int device,
+                              void *stream, uint32_t *out_ids, float *out_dist,
+                              uint32_t *out_count);
+
 #ifdef __cplusplus
 }
 #endif

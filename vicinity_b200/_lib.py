@@ -128,6 +128,7 @@ SIGNATURES = {
     "vg_ivfpq_shard": (_i, [_vp, _i, _i, _vp, _i]),
     "vg_shard_assign_lists": (_i, [_vp, _sz, _i, _vp]),
     "vg_flat_search_ip": (_i, [_vp, _sz, _vp, _sz, _sz, _sz, _i, _vp, _vp, _vp]),
+    "vg_flat_search_ip_noalloc": (_i, [_vp, _sz, _vp, _sz, _sz, _sz, _i, _vp, _vp, _vp, _vp]),
 }
 
 _lib: C.CDLL | None = None

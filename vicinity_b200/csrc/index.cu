@@ -680,6 +680,12 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
 
 }  // namespace
 
+namespace vg {
+// Sets the text vg_last_error reports, for entry points defined in other
+// translation units.
+void set_last_error(const char *msg) { g_last_error = msg; }
+}  // namespace vg
+
 // ===========================================================================
 // C ABI
 // ===========================================================================
