@@ -119,6 +119,7 @@ struct ScanParams {
   float *out_dist;               // [nq][k] distances, padded +inf
   uint32_t *out_count;           // [nq] real result counts (nullable)
   int *error;                    // set nonzero when a bounded pipeline wait gives up
+  float neg_zero;                // -0.0f; kernels take it as a run-time value (see f32x2.cuh)
 };
 
 // Fused per-query kernel: for each probed list the query residual, the ADC

@@ -13,6 +13,7 @@
 // b and written into the residual buffer that batch b has finished with.
 #pragma once
 
+#include "f32x2.cuh"
 #include "scan_kernel.cuh"
 
 namespace vg {
@@ -45,16 +46,20 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_pipe_kernel(const ScanP
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool build_first = (warp & 1) == 0;
 
+  // codewords of this thread's groups, lane-packed as entries (0,1), (2,3)
   const int ngroups = nent >> 2;
-  float cb[GPT][4][DSUB];
+  const f32x2 nz = f2_pack(p.neg_zero, p.neg_zero);
+  f32x2 cb[GPT][2][DSUB];
 #pragma unroll
   for (int i = 0; i < GPT; ++i) {
     const int G = tid + i * kScanThreads;
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int h = 0; h < 2; ++h)
 #pragma unroll
-      for (int j = 0; j < DSUB; ++j)
-        cb[i][u][j] = G < ngroups ? p.codebooks[(static_cast<size_t>(4 * G + u)) * DSUB + j] : 0.0f;
+      for (int j = 0; j < DSUB; ++j) {
+        const size_t e = static_cast<size_t>(4 * G + 2 * h);
+        cb[i][h][j] = G < ngroups ? f2_pack(p.codebooks[e * DSUB + j], p.codebooks[(e + 1) * DSUB + j]) : 0ull;
+      }
   }
 
   for (;;) {
@@ -116,12 +121,12 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_pipe_kernel(const ScanP
           if (G < ngroups) {
             float qs[DSUB];
             load_subvector<DSUB>(qg + ((4 * G) / ks) * DSUB, qs);
-            float4 out;
-            out.x = sq_dist<DSUB>(qs, cb[i][0]);
-            out.y = sq_dist<DSUB>(qs, cb[i][1]);
-            out.z = sq_dist<DSUB>(qs, cb[i][2]);
-            out.w = sq_dist<DSUB>(qs, cb[i][3]);
-            *reinterpret_cast<float4 *>(lg + 4 * G) = out;
+            f32x2 qq[DSUB];
+#pragma unroll
+            for (int j = 0; j < DSUB; ++j) qq[j] = f2_pack(qs[j], qs[j]);
+            const float2 e01 = f2_unpack(sq_dist_x2<DSUB>(qq, cb[i][0], nz));
+            const float2 e23 = f2_unpack(sq_dist_x2<DSUB>(qq, cb[i][1], nz));
+            *reinterpret_cast<float4 *>(lg + 4 * G) = make_float4(e01.x, e01.y, e23.x, e23.y);
           }
         }
       }
@@ -280,7 +285,9 @@ cudaError_t launch_pipe_variant(const ScanParams &p, int num_sms, cudaStream_t s
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
   int grid = num_sms * per_sm;
   if (grid > p.nq) grid = p.nq;
-  kern<<<grid, kScanThreads, smem, s>>>(p, batch);
+  ScanParams pp = p;
+  pp.neg_zero = -0.0f;
+  kern<<<grid, kScanThreads, smem, s>>>(pp, batch);
   return cudaGetLastError();
 }
 
