@@ -9,6 +9,7 @@
 //   doc-id mapping             src/ivf_pq/search.rs:1087-1093
 //   batch padding              src/python.rs:745-795 (-1 / +inf)
 #include "common.cuh"
+#include "f32x2.cuh"
 #include "kernels.h"
 #include "topk.cuh"
 
@@ -75,19 +76,27 @@ enum DotMode { kWriteOneMinus = 0, kArgminOneMinus = 1, kWriteNeg = 2 };
 template <int MODE>
 __global__ void __launch_bounds__(kTileThreads)
     dot_tile_kernel(const float *__restrict__ a, size_t rows, const float *__restrict__ b, size_t cols,
-                    int d, float *__restrict__ out, size_t ld, unsigned long long *__restrict__ best) {
-  __shared__ __align__(16) float as[kTileK][kTileM + 4];
+                    int d, float *__restrict__ out, size_t ld, unsigned long long *__restrict__ best,
+                    float neg_zero) {
+  // A is staged with every value in both halves of a pair ({a, a}), so one
+  // 16-byte load yields two ready operands for the packed products below.
+  __shared__ __align__(16) f32x2 as[kTileK][kTileM + 2];
   __shared__ __align__(16) float bs[kTileK][kTileN + 4];
   const int tid = threadIdx.x;
   const int tx = tid & 15, ty = tid >> 4;
   const size_t row0 = static_cast<size_t>(blockIdx.y) * kTileM;
   const size_t col0 = static_cast<size_t>(blockIdx.x) * kTileN;
+  const f32x2 nz = f2_pack(neg_zero, neg_zero);
 
-  float acc[8][8];
+  // acc2[i][h] holds columns (2h, 2h + 1) of row i of this thread's 8 x 8
+  // block; each lane sums its products in k order from 0, as the scalar
+  // __fadd_rn(acc, __fmul_rn(a, b)) does (the product is an FMA with a
+  // run-time -0 addend so it cannot be fused into the add).
+  f32x2 acc2[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+    for (int h = 0; h < 4; ++h) acc2[i][h] = 0ull;
 
   for (int k0 = 0; k0 < d; k0 += kTileK) {
 #pragma unroll
@@ -96,26 +105,40 @@ __global__ void __launch_bounds__(kTileThreads)
       int r = i >> 4, kk = i & 15;
       size_t gr = row0 + r;
       int gk = k0 + kk;
-      as[kk][r] = (gr < rows && gk < d) ? a[gr * d + gk] : 0.0f;
+      const float av = (gr < rows && gk < d) ? a[gr * d + gk] : 0.0f;
+      as[kk][r] = f2_pack(av, av);
       size_t gc = col0 + r;
       bs[kk][r] = (gc < cols && gk < d) ? b[gc * d + gk] : 0.0f;
     }
     __syncthreads();
 #pragma unroll
     for (int kk = 0; kk < kTileK; ++kk) {
-      float4 a0 = *reinterpret_cast<const float4 *>(&as[kk][ty * 8]);
-      float4 a1 = *reinterpret_cast<const float4 *>(&as[kk][ty * 8 + 4]);
-      float4 b0 = *reinterpret_cast<const float4 *>(&bs[kk][tx * 8]);
-      float4 b1 = *reinterpret_cast<const float4 *>(&bs[kk][tx * 8 + 4]);
-      float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      f32x2 av[8];
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        const ulonglong2 t2 = *reinterpret_cast<const ulonglong2 *>(&as[kk][ty * 8 + i]);
+        av[i] = t2.x;
+        av[i + 1] = t2.y;
+      }
+      const ulonglong2 b01 = *reinterpret_cast<const ulonglong2 *>(&bs[kk][tx * 8]);
+      const ulonglong2 b23 = *reinterpret_cast<const ulonglong2 *>(&bs[kk][tx * 8 + 4]);
+      const f32x2 bv[4] = {b01.x, b01.y, b23.x, b23.y};
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(av[i], bv[j]));
+        for (int h = 0; h < 4; ++h) acc2[i][h] = f2_add(acc2[i][h], f2_fma(av[i], bv[h], nz));
     }
     __syncthreads();
   }
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const float2 v = f2_unpack(acc2[i][h]);
+      acc[i][2 * h] = v.x;
+      acc[i][2 * h + 1] = v.y;
+    }
 
   if (MODE == kArgminOneMinus) {
 #pragma unroll
@@ -159,7 +182,7 @@ cudaError_t launch_dot(const float *a, size_t rows, const float *b, size_t cols,
   dim3 grid(static_cast<unsigned>((cols + kTileN - 1) / kTileN),
             static_cast<unsigned>((rows + kTileM - 1) / kTileM));
   if (grid.y > 65535) return cudaErrorInvalidValue;
-  dot_tile_kernel<MODE><<<grid, kTileThreads, 0, s>>>(a, rows, b, cols, d, out, ld, best);
+  dot_tile_kernel<MODE><<<grid, kTileThreads, 0, s>>>(a, rows, b, cols, d, out, ld, best, -0.0f);
   return cudaGetLastError();
 }
 }  // namespace
