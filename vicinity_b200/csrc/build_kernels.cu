@@ -134,25 +134,27 @@ __global__ void gather_list_codes_kernel(const uint8_t *__restrict__ codes, cons
   for (int m = 0; m < M; ++m) dst[m] = src[m];
 }
 
-// One block per list: byte (block b, subspace m, lane) = code(lane) | code(lane + 16) << 4.
-__global__ void pack_4bit_kernel(const uint8_t *__restrict__ list_codes, const uint64_t *__restrict__ list_off,
-                                 const uint64_t *__restrict__ code_off, const uint64_t *__restrict__ pack_off,
-                                 int M, uint8_t *__restrict__ packed) {
+// 4-bit codes of every list with at least 16 vectors (the lists the
+// reference scans with quantised tables, search.rs:816-848) repacked for the
+// GPU scan: vector-major, two codes per byte (code 2j in the low nibble,
+// 2j + 1 in the high one), ceil(M/2) bytes per vector, so one thread loads a
+// whole vector with a few wide loads.  Lists under 16 vectors keep no packed
+// copy (search.rs:824-828).
+__global__ void pack_nibbles_kernel(const uint8_t *__restrict__ list_codes, const uint64_t *__restrict__ list_off,
+                                    const uint64_t *__restrict__ code_off, const uint64_t *__restrict__ pack_off,
+                                    int M, uint8_t *__restrict__ packed) {
   const size_t l = blockIdx.x;
   const uint64_t len = list_off[l + 1] - list_off[l];
-  if (len < 16) return;  // search.rs:824-828: small lists keep no scan cache
-  const uint64_t blocks = (len + 31) / 32;
+  if (len < 16) return;
+  const int vs = (M + 1) / 2;
   const uint8_t *src = list_codes + code_off[l];
   uint8_t *dst = packed + pack_off[l];
-  const uint64_t per_block = static_cast<uint64_t>(M) * 16;
-  for (uint64_t i = threadIdx.x; i < blocks * per_block; i += blockDim.x) {
-    uint64_t b = i / per_block;
-    int rem = static_cast<int>(i - b * per_block);
-    int m = rem >> 4, lane = rem & 15;
-    uint64_t lo = b * 32 + lane, hi = lo + 16;
-    uint8_t clo = lo < len ? (src[lo * M + m] & 0x0f) : 0;
-    uint8_t chi = hi < len ? (src[hi * M + m] & 0x0f) : 0;
-    dst[i] = static_cast<uint8_t>(clo | (chi << 4));
+  for (uint64_t i = threadIdx.x; i < len * vs; i += blockDim.x) {
+    const uint64_t v = i / vs;
+    const int j = static_cast<int>(i - v * vs);
+    const uint8_t lo = src[v * M + 2 * j] & 0x0f;
+    const uint8_t hi = 2 * j + 1 < M ? (src[v * M + 2 * j + 1] & 0x0f) : 0;
+    dst[i] = static_cast<uint8_t>(lo | (hi << 4));
   }
 }
 
@@ -283,7 +285,7 @@ cudaError_t launch_pack_lists_4bit(const uint8_t *list_codes, const uint64_t *li
                                    const uint64_t *pack_off, size_t L, int M, uint8_t *packed,
                                    cudaStream_t s) {
   if (L == 0) return cudaSuccess;
-  pack_4bit_kernel<<<static_cast<unsigned>(L), 256, 0, s>>>(list_codes, list_off, code_off, pack_off, M, packed);
+  pack_nibbles_kernel<<<static_cast<unsigned>(L), 256, 0, s>>>(list_codes, list_off, code_off, pack_off, M, packed);
   return cudaGetLastError();
 }
 

@@ -13,8 +13,9 @@
 //   list_ids   u32 [n]             insertion indices, ascending within a list
 //   code_off   u64 [Lc]            16-byte aligned byte offset of each list's
 //   list_codes u8                  list-contiguous codes (list_codes.bin)
-//   pack_off   u64 [Lc]            (ks == 16) byte offset of each list's
-//   packed     u8                  32-vector FastScan blocks (pq_simd.rs:426)
+//   pack_off   u64 [Lc]            (ks == 16) 16-byte aligned byte offset of
+//   packed     u8                  each list's nibble-packed codes: vector-major,
+//                                  ceil(M/2) bytes per vector, lists >= 16 only
 #include <nccl.h>
 
 #include <algorithm>
@@ -451,7 +452,7 @@ int encode_and_layout(vg_index *ix) {
     h_code_off[l] = code_bytes;
     code_bytes += (len * M + 15) & ~uint64_t(15);
     h_pack_off[l] = pack_bytes;
-    if (ks == 16 && len >= 16) pack_bytes += ((len + 31) / 32) * M * 16;
+    if (ks == 16 && len >= 16) pack_bytes += (len * ((M + 1) / 2) + 15) & ~uint64_t(15);
   }
   VG_CU(ix->list_off.reserve((Lc + 1) * 8));
   VG_CU(ix->code_off.reserve(Lc * 8));

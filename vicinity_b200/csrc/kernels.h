@@ -169,8 +169,10 @@ cudaError_t launch_gather_list_codes(const uint8_t *codes, const uint32_t *sorte
                                      const uint64_t *code_off, uint8_t *list_codes,
                                      cudaStream_t s);
 
-// 4-bit FastScan packing of every list with at least 16 vectors
-// (pq_simd.rs:426-486, search.rs:816-848).
+// 4-bit scan layout of every list with at least 16 vectors (the lists the
+// reference scans with quantised tables, search.rs:816-848): vector-major,
+// code 2j | code 2j+1 << 4 per byte, ceil(M/2) bytes per vector, at
+// pack_off[l].
 cudaError_t launch_pack_lists_4bit(const uint8_t *list_codes, const uint64_t *list_off,
                                    const uint64_t *code_off, const uint64_t *pack_off,
                                    size_t L, int M, uint8_t *packed, cudaStream_t s);

@@ -5,7 +5,9 @@
 //   3. code scan       dist = sum_m T[m][code_m]       (pq_simd.rs:314-369),
 //      or for 16-entry codebooks on lists of >= 16 vectors the FastScan
 //      path: u8-quantised table (pq_simd.rs:576-611), integer sums and
-//      dist = sum * scale + min * M                    (pq_simd.rs:721-769)
+//      dist = sum * scale + min * M                    (pq_simd.rs:721-769);
+//      the integer sum is order-free, so the codes are read from a
+//      vector-major nibble layout instead of the reference's 32-vector blocks
 //   4. top-k by (distance, vector id)                  (search.rs:64-75)
 //
 // Persistent blocks (one per SM) take queries from an atomic counter, load
@@ -111,6 +113,37 @@ __device__ __forceinline__ float adc_row_sum(const uint8_t *cp, const float *lg,
     }
   } else {
     for (int m = 0; m < M; ++m) acc = __fadd_rn(acc, lg[m * row_len + cp[m]]);
+  }
+  return acc;
+}
+
+// Integer sum of a quantised 4-bit table ql [M][16] (u8) over one vector's
+// nibble-packed codes vp (code 2j low nibble, 2j + 1 high nibble of byte j).
+// The sum is exact in any order.  When M is a multiple of 16 the vector is
+// fetched with 8-byte loads (up to four in flight before the lookups; the
+// vector start is 8-byte aligned), else byte by byte.
+__device__ __forceinline__ uint32_t nibble_lut_sum(const uint8_t *vp, const uint8_t *ql, int M) {
+  uint32_t acc = 0;
+  if ((M & 15) == 0) {
+    for (int m0 = 0; m0 < M; m0 += 64) {
+      uint2 w[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        w[u] = m0 + 16 * u < M ? *reinterpret_cast<const uint2 *>(vp + (m0 >> 1) + 8 * u) : make_uint2(0u, 0u);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (m0 + 16 * u < M) {
+          const uint8_t *row = ql + (m0 + 16 * u) * 16;
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            const uint32_t word = t < 8 ? w[u].x : w[u].y;
+            acc += row[t * 16 + ((word >> (4 * (t & 7))) & 15u)];
+          }
+        }
+      }
+    }
+  } else {
+    for (int m = 0; m < M; ++m) acc += ql[m * 16 + ((vp[m >> 1] >> ((m & 1) * 4)) & 15u)];
   }
   return acc;
 }
@@ -324,12 +357,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
           const uint32_t list = blist[g];
           const uint32_t len = hi - lo;
           if (FOUR && len >= 16) {  // search.rs:1261 (SIMD_BATCH_THRESHOLD)
-            const uint8_t *bp = p.packed + p.pack_off[list] + static_cast<uint64_t>(c >> 5) * M * 16;
-            const uint8_t *ql = qlut + g * qlut_stride;
-            const int col = c & 15;
-            const int sh = (c & 31) >= 16 ? 4 : 0;
-            uint32_t acc = 0;
-            for (int m = 0; m < M; ++m) acc += ql[m * 16 + ((bp[m * 16 + col] >> sh) & 15u)];
+            const uint8_t *vp = p.packed + p.pack_off[list] + static_cast<uint64_t>(c) * ((M + 1) >> 1);
+            const uint32_t acc = nibble_lut_sum(vp, qlut + g * qlut_stride, M);
             dist = __fadd_rn(__fmul_rn(__uint2float_rn(acc), s_scale[g]), s_fbase[g]);
           } else {
             const uint8_t *cp = p.list_codes + p.code_off[list] + static_cast<uint64_t>(c) * M;
