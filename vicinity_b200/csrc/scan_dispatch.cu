@@ -56,6 +56,7 @@ int ivfpq_scan_variant_name(const ScanParams &p, char *buf, size_t len) {
   if (ws) return snprintf(buf, len, "ivfpq_ws_kernel<%d,%d,1,256>", p.dsub, ws);
   const int gpt = pick_gpt(p);
   if (g_family == 2 && gpt && p.ks == 256) return snprintf(buf, len, "ivfpq_pipe_kernel<%d,%d,1,256>", p.dsub, gpt);
+  if (p.ks == 16) return snprintf(buf, len, "ivfpq_four_kernel<%d>", p.k <= 32 ? 1 : p.k <= 64 ? 2 : p.k <= 128 ? 4 : 8);
   return snprintf(buf, len, "ivfpq_query_kernel<%d,%d,%d,%s>", gpt ? p.dsub : 0, gpt,
                   p.k <= 32 ? 1 : p.k <= 64 ? 2 : p.k <= 128 ? 4 : 8, p.ks == 16 ? "4bit" : "8bit");
 }

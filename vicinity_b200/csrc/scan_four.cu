@@ -1,42 +1,39 @@
-// Instantiations of the fused search kernel for 16-entry (FastScan) codebooks.
-// One case per (subvector dimensions, 4-entry groups per thread) the dispatcher can pick.
-#include "scan_kernel.cuh"
+// Launcher of the 4-bit (16-entry codebook) search kernel, scan_fourbit.cuh.
+#include "scan_fourbit.cuh"
 
 namespace vg {
 
-cudaError_t launch_scan_four(const ScanParams &p, int dsub, int gpt, int num_sms, cudaStream_t s) {
-  if (gpt == 0) {
-    if (p.k <= 32) return launch_scan_variant<0, 0, 1, true, 0>(p, num_sms, s);
-    if (p.k <= 64) return launch_scan_variant<0, 0, 2, true, 0>(p, num_sms, s);
-    if (p.k <= 128) return launch_scan_variant<0, 0, 4, true, 0>(p, num_sms, s);
-    return launch_scan_variant<0, 0, 8, true, 0>(p, num_sms, s);
-  }
-  if (p.ks == 16) {
-    switch (dsub * 100 + gpt) {
-      case 101: return launch_scan_variant<1, 1, 1, true, 16>(p, num_sms, s);
-      case 102: return launch_scan_variant<1, 2, 1, true, 16>(p, num_sms, s);
-      case 104: return launch_scan_variant<1, 4, 1, true, 16>(p, num_sms, s);
-      case 201: return launch_scan_variant<2, 1, 1, true, 16>(p, num_sms, s);
-      case 202: return launch_scan_variant<2, 2, 1, true, 16>(p, num_sms, s);
-      case 204: return launch_scan_variant<2, 4, 1, true, 16>(p, num_sms, s);
-      case 301: return launch_scan_variant<3, 1, 1, true, 16>(p, num_sms, s);
-      case 302: return launch_scan_variant<3, 2, 1, true, 16>(p, num_sms, s);
-      case 304: return launch_scan_variant<3, 4, 1, true, 16>(p, num_sms, s);
-      case 401: return launch_scan_variant<4, 1, 1, true, 16>(p, num_sms, s);
-      case 402: return launch_scan_variant<4, 2, 1, true, 16>(p, num_sms, s);
-      case 404: return launch_scan_variant<4, 4, 1, true, 16>(p, num_sms, s);
-      case 501: return launch_scan_variant<5, 1, 1, true, 16>(p, num_sms, s);
-      case 502: return launch_scan_variant<5, 2, 1, true, 16>(p, num_sms, s);
-      case 601: return launch_scan_variant<6, 1, 1, true, 16>(p, num_sms, s);
-      case 602: return launch_scan_variant<6, 2, 1, true, 16>(p, num_sms, s);
-      case 701: return launch_scan_variant<7, 1, 1, true, 16>(p, num_sms, s);
-      case 702: return launch_scan_variant<7, 2, 1, true, 16>(p, num_sms, s);
-      case 801: return launch_scan_variant<8, 1, 1, true, 16>(p, num_sms, s);
-      case 802: return launch_scan_variant<8, 2, 1, true, 16>(p, num_sms, s);
-      default: break;
-    }
-  }
-  return cudaErrorInvalidValue;
+namespace {
+template <int R>
+cudaError_t launch_four_variant(const ScanParams &p, int num_sms, cudaStream_t s) {
+  auto kern = ivfpq_four_kernel<R>;
+  int dev = 0, optin = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e != cudaSuccess) return e;
+  const size_t reserve = 10240;  // static shared memory of the kernel (~8.5 KB)
+  const size_t smem = four_smem_bytes(p.M, p.dsub, R);
+  if (smem + reserve > static_cast<size_t>(optin)) return cudaErrorInvalidConfiguration;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kScanThreads, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  int grid = num_sms * per_sm;
+  if (grid > p.nq) grid = p.nq;
+  kern<<<grid, kScanThreads, smem, s>>>(p);
+  return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_scan_four(const ScanParams &p, int, int, int num_sms, cudaStream_t s) {
+  if (p.ks != 16) return cudaErrorInvalidValue;
+  if (p.k <= 32) return launch_four_variant<1>(p, num_sms, s);
+  if (p.k <= 64) return launch_four_variant<2>(p, num_sms, s);
+  if (p.k <= 128) return launch_four_variant<4>(p, num_sms, s);
+  return launch_four_variant<8>(p, num_sms, s);
 }
 
 }  // namespace vg
