@@ -2,12 +2,8 @@
 // the reference's per-query loop (search.rs:1175-1391) over its probed lists:
 //   1. query residual  q - c_list                      (search.rs:1239-1245)
 //   2. ADC table       T[m][c] = sum_j (r_mj - cw_mcj)^2 (pq.rs:573-643)
-//   3. code scan       dist = sum_m T[m][code_m]       (pq_simd.rs:314-369),
-//      or for 16-entry codebooks on lists of >= 16 vectors the FastScan
-//      path: u8-quantised table (pq_simd.rs:576-611), integer sums and
-//      dist = sum * scale + min * M                    (pq_simd.rs:721-769);
-//      the integer sum is order-free, so the codes are read from a
-//      vector-major nibble layout instead of the reference's 32-vector blocks
+//   3. code scan       dist = sum_m T[m][code_m]       (pq_simd.rs:314-369)
+//      (16-entry codebooks run ivfpq_four_kernel, scan_fourbit.cuh)
 //   4. top-k by (distance, vector id)                  (search.rs:64-75)
 //
 // Persistent blocks (one per SM) take queries from an atomic counter, load
@@ -43,16 +39,13 @@ constexpr int kScanThreads = 512;
 constexpr int kScanWarps = kScanThreads / 32;
 constexpr int kMaxBatch = 4;  // lists per batch (the candidate prefix below is unrolled for 4)
 
-// Per-list shared memory: table (padded to 16 bytes), residual, and for
-// 16-entry codebooks the u8 table.
-__host__ __device__ inline size_t scan_pair_bytes(int d, int M, int ks, bool four) {
-  size_t b = static_cast<size_t>((M * ks + 3) & ~3) * 4 + static_cast<size_t>((d + 3) & ~3) * 4;
-  if (four) b += (static_cast<size_t>(M) * 16 + 15) & ~static_cast<size_t>(15);
-  return b;
+// Per-list shared memory: table (padded to 16 bytes) and residual.
+__host__ __device__ inline size_t scan_pair_bytes(int d, int M, int ks) {
+  return static_cast<size_t>((M * ks + 3) & ~3) * 4 + static_cast<size_t>((d + 3) & ~3) * 4;
 }
 
-__host__ __device__ inline size_t scan_smem_bytes(int d, int M, int ks, bool four, int batch, int R) {
-  return static_cast<size_t>(kScanWarps) * 32 * R * 8 + static_cast<size_t>(batch) * scan_pair_bytes(d, M, ks, four);
+__host__ __device__ inline size_t scan_smem_bytes(int d, int M, int ks, int batch, int R) {
+  return static_cast<size_t>(kScanWarps) * 32 * R * 8 + static_cast<size_t>(batch) * scan_pair_bytes(d, M, ks);
 }
 
 template <int R>
@@ -117,37 +110,6 @@ __device__ __forceinline__ float adc_row_sum(const uint8_t *cp, const float *lg,
   return acc;
 }
 
-// Integer sum of a quantised 4-bit table ql [M][16] (u8) over one vector's
-// nibble-packed codes vp (code 2j low nibble, 2j + 1 high nibble of byte j).
-// The sum is exact in any order.  When M is a multiple of 16 the vector is
-// fetched with 8-byte loads (up to four in flight before the lookups; the
-// vector start is 8-byte aligned), else byte by byte.
-__device__ __forceinline__ uint32_t nibble_lut_sum(const uint8_t *vp, const uint8_t *ql, int M) {
-  uint32_t acc = 0;
-  if ((M & 15) == 0) {
-    for (int m0 = 0; m0 < M; m0 += 64) {
-      uint2 w[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        w[u] = m0 + 16 * u < M ? *reinterpret_cast<const uint2 *>(vp + (m0 >> 1) + 8 * u) : make_uint2(0u, 0u);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (m0 + 16 * u < M) {
-          const uint8_t *row = ql + (m0 + 16 * u) * 16;
-#pragma unroll
-          for (int t = 0; t < 16; ++t) {
-            const uint32_t word = t < 8 ? w[u].x : w[u].y;
-            acc += row[t * 16 + ((word >> (4 * (t & 7))) & 15u)];
-          }
-        }
-      }
-    }
-  } else {
-    for (int m = 0; m < M; ++m) acc += ql[m * 16 + ((vp[m >> 1] >> ((m & 1) * 4)) & 15u)];
-  }
-  return acc;
-}
-
 // Squared distance of one residual subvector to one codeword, summed in the
 // reference's order.  The first term is taken as is: for s >= +0 the
 // reference's 0.0 + s equals s exactly, and a square is never -0.
@@ -163,7 +125,7 @@ __device__ __forceinline__ float sq_dist(const float (&q)[D], const float (&c)[D
   return acc;
 }
 
-template <int DSUB, int GPT, int R, bool FOUR, int KS>
+template <int DSUB, int GPT, int R, int KS>
 __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const ScanParams p, const int batch) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int M = p.M, ks = KS > 0 ? KS : p.ks, d = p.d, P = p.P, k = p.k;
@@ -173,8 +135,6 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
   unsigned long long *wl = reinterpret_cast<unsigned long long *>(smem);  // [warps][32R]
   float *lut = reinterpret_cast<float *>(wl + kScanWarps * 32 * R);       // [batch][tstride]
   float *qres = lut + static_cast<size_t>(batch) * tstride;                // [batch][dpad]
-  uint8_t *qlut = reinterpret_cast<uint8_t *>(qres + static_cast<size_t>(batch) * dpad);  // [batch][M*16]
-  const int qlut_stride = (M * 16 + 15) & ~15;
 
   __shared__ uint32_t s_query;
   __shared__ int s_nvalid;
@@ -182,8 +142,6 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
   __shared__ uint32_t s_list[kScanThreads], s_len[kScanThreads];
   __shared__ uint64_t s_lbeg[kScanThreads];
   __shared__ unsigned long long s_bound;
-  __shared__ float s_rmin[kMaxBatch][kScanWarps], s_rmax[kMaxBatch][kScanWarps];
-  __shared__ float s_scale[kMaxBatch], s_fbase[kMaxBatch];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
@@ -259,7 +217,6 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
       for (int g = 0; g < nb; ++g) {
         const float *qg = qres + g * dpad;
         float *lg = lut + static_cast<size_t>(g) * tstride;
-        float lmin = __int_as_float(0x7f800000), lmax = -__int_as_float(0x7f800000);
         if (DSUB > 0) {
 #pragma unroll
           for (int i = 0; i < kG; ++i) {
@@ -273,10 +230,6 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
               out.z = sq_dist<kD>(qs, cb[i][2]);
               out.w = sq_dist<kD>(qs, cb[i][3]);
               *reinterpret_cast<float4 *>(lg + 4 * G) = out;
-              if (FOUR) {
-                lmin = fminf(lmin, fminf(fminf(out.x, out.y), fminf(out.z, out.w)));
-                lmax = fmaxf(lmax, fmaxf(fmaxf(out.x, out.y), fmaxf(out.z, out.w)));
-              }
             }
           }
         } else {
@@ -289,49 +242,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
               acc = __fadd_rn(acc, __fmul_rn(diff, diff));
             }
             lg[e] = acc;
-            if (FOUR) {
-              lmin = fminf(lmin, acc);
-              lmax = fmaxf(lmax, acc);
-            }
           }
-        }
-        if (FOUR) {
-          // global min/max of the table (pq_simd.rs:587-598); fminf/fmaxf
-          // skip NaNs as the reference's `<` / `>` comparisons do
-#pragma unroll
-          for (int off = 16; off > 0; off >>= 1) {
-            lmin = fminf(lmin, __shfl_xor_sync(VG_FULL_MASK, lmin, off));
-            lmax = fmaxf(lmax, __shfl_xor_sync(VG_FULL_MASK, lmax, off));
-          }
-          if (lane == 0) {
-            s_rmin[g][warp] = lmin;
-            s_rmax[g][warp] = lmax;
-          }
-        }
-      }
-      if (FOUR) {
-        __syncthreads();
-        if (tid < nb) {
-          const int g = tid;
-          float gmin = s_rmin[g][0], gmax = s_rmax[g][0];
-          for (int w = 1; w < kScanWarps; ++w) {
-            gmin = fminf(gmin, s_rmin[g][w]);
-            gmax = fmaxf(gmax, s_rmax[g][w]);
-          }
-          float range = __fsub_rn(gmax, gmin);
-          bool flat = range < FLT_EPSILON;
-          s_rmin[g][0] = gmin;                                    // offset
-          s_rmax[g][0] = flat ? 0.0f : __fdiv_rn(255.0f, range);  // inverse scale
-          s_scale[g] = flat ? 1.0f : __fdiv_rn(range, 255.0f);
-          s_fbase[g] = __fmul_rn(gmin, static_cast<float>(M));
-        }
-        __syncthreads();
-        for (int i = tid; i < nb * nent; i += kScanThreads) {
-          int g = i / nent, e = i - g * nent;
-          // round half away from zero, clamp; NaN -> 0 (pq_simd.rs:607-609)
-          float t = roundf(__fmul_rn(__fsub_rn(lut[g * tstride + e], s_rmin[g][0]), s_rmax[g][0]));
-          t = fminf(fmaxf(t, 0.0f), 255.0f);
-          qlut[g * qlut_stride + e] = static_cast<uint8_t>(t);
         }
       }
       __syncthreads();
@@ -352,18 +263,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
         if (x < ctotal) {
           g = (x >= pre1) + (x >= pre2) + (x >= pre3);
           const uint32_t lo = g == 0 ? 0u : g == 1 ? pre1 : g == 2 ? pre2 : pre3;
-          const uint32_t hi = g == 0 ? pre1 : g == 1 ? pre2 : g == 2 ? pre3 : pre4;
           c = x - lo;
           const uint32_t list = blist[g];
-          const uint32_t len = hi - lo;
-          if (FOUR && len >= 16) {  // search.rs:1261 (SIMD_BATCH_THRESHOLD)
-            const uint8_t *vp = p.packed + p.pack_off[list] + static_cast<uint64_t>(c) * ((M + 1) >> 1);
-            const uint32_t acc = nibble_lut_sum(vp, qlut + g * qlut_stride, M);
-            dist = __fadd_rn(__fmul_rn(__uint2float_rn(acc), s_scale[g]), s_fbase[g]);
-          } else {
-            const uint8_t *cp = p.list_codes + p.code_off[list] + static_cast<uint64_t>(c) * M;
-            dist = adc_row_sum<KS>(cp, lut + static_cast<size_t>(g) * tstride, M, ks);
-          }
+          const uint8_t *cp = p.list_codes + p.code_off[list] + static_cast<uint64_t>(c) * M;
+          dist = adc_row_sum<KS>(cp, lut + static_cast<size_t>(g) * tstride, M, ks);
         }
         uint64_t thr = tk.worst();
         const uint64_t bound = s_bound;
@@ -427,9 +330,9 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
   }
 }
 
-template <int DSUB, int GPT, int R, bool FOUR, int KS>
+template <int DSUB, int GPT, int R, int KS>
 cudaError_t launch_scan_variant(const ScanParams &p, int num_sms, cudaStream_t s) {
-  auto kern = ivfpq_query_kernel<DSUB, GPT, R, FOUR, KS>;
+  auto kern = ivfpq_query_kernel<DSUB, GPT, R, KS>;
   int dev = 0, optin = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -437,8 +340,8 @@ cudaError_t launch_scan_variant(const ScanParams &p, int num_sms, cudaStream_t s
   if (e != cudaSuccess) return e;
   const size_t reserve = 12288;  // static shared memory of the kernel (8-9 KB)
   int batch = kMaxBatch;
-  while (batch > 1 && scan_smem_bytes(p.d, p.M, p.ks, FOUR, batch, R) + reserve > static_cast<size_t>(optin)) --batch;
-  const size_t smem = scan_smem_bytes(p.d, p.M, p.ks, FOUR, batch, R);
+  while (batch > 1 && scan_smem_bytes(p.d, p.M, p.ks, batch, R) + reserve > static_cast<size_t>(optin)) --batch;
+  const size_t smem = scan_smem_bytes(p.d, p.M, p.ks, batch, R);
   if (smem + reserve > static_cast<size_t>(optin)) return cudaErrorInvalidConfiguration;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
