@@ -44,7 +44,8 @@ typedef enum vg_status {
   VG_ERR_CUDA = -10,              /* device failure (no reference variant) */
   VG_ERR_NCCL = -11,              /* collective failure (no reference variant) */
   VG_ERR_OUT_OF_MEMORY = -12,     /* device allocation failed */
-  VG_ERR_OTHER = -13              /* RetrieveError::Other */
+  VG_ERR_OTHER = -13,             /* RetrieveError::Other */
+  VG_ERR_NOT_FOUND = -14          /* RetrieveError::Io of kind NotFound */
 } vg_status;
 
 /* src/ivf_pq/search.rs:286-329 (IVFPQParams). */
@@ -147,6 +148,17 @@ int vg_ivfpq_reconstruct(const vg_index *ix, size_t idx, float *out);
 
 /* src/ivf_pq/search.rs:901-904 (compact): drop the raw vectors. */
 int vg_ivfpq_compact(vg_index *ix);
+
+/* src/ivf_pq/search.rs:912-1015 (save_to_dir): write the index as a
+ * directory snapshot in the reference's format (manifest.json, centroids.bin,
+ * doc_ids.bin, codes.bin, list_offsets.bin, list_codes.bin, clusters.bin and,
+ * unless compacted, raw_vectors.bin).  VG_ERR_NOT_BUILT before build. */
+int vg_ivfpq_save(const vg_index *ix, const char *dir);
+
+/* src/ivf_pq/search.rs:1034-1084 (load_from_dir): create a built index on
+ * `device` from a directory snapshot.  Missing files give VG_ERR_NOT_FOUND,
+ * malformed ones VG_ERR_FORMAT. */
+int vg_ivfpq_load(const char *dir, int device, vg_index **out);
 
 /* Copies of index state for parity checks and persistence (host or device
  * destination, `bytes` must match):

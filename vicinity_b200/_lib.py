@@ -25,6 +25,7 @@ VG_ERR_CUDA = -10
 VG_ERR_NCCL = -11
 VG_ERR_OUT_OF_MEMORY = -12
 VG_ERR_OTHER = -13
+VG_ERR_NOT_FOUND = -14
 
 EXPORT_CENTROIDS = 0
 EXPORT_CODEBOOKS = 1
@@ -128,6 +129,8 @@ SIGNATURES = {
     "vg_ivfpq_shard": (_i, [_vp, _i, _i, _vp, _i]),
     "vg_shard_assign_lists": (_i, [_vp, _sz, _i, _vp]),
     "vg_flat_search_ip": (_i, [_vp, _sz, _vp, _sz, _sz, _sz, _i, _vp, _vp, _vp]),
+    "vg_ivfpq_save": (_i, [_vp, C.c_char_p]),
+    "vg_ivfpq_load": (_i, [C.c_char_p, _i, C.POINTER(_vp)]),
     "vg_flat_search_ip_noalloc": (_i, [_vp, _sz, _vp, _sz, _sz, _sz, _i, _vp, _vp, _vp, _vp]),
 }
 
@@ -191,8 +194,12 @@ def check(status: int) -> None:
     if status == VG_OK:
         return
     msg = last_error()
+    if status == VG_ERR_NOT_FOUND:
+        raise FileNotFoundError(msg)
     if status == VG_ERR_IO:
         raise OSError(msg)
+    if status == VG_ERR_FORMAT:  # persistence format errors (python.rs:67-70)
+        raise RuntimeError(msg)
     if status in (VG_ERR_CUDA, VG_ERR_NCCL, VG_ERR_OUT_OF_MEMORY):
         raise VicinityError(f"[{status}] {msg}")
     raise ValueError(msg)

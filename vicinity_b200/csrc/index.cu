@@ -31,6 +31,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "snapshot.h"
 #include "vicinity_gpu.h"
 
 using namespace vg;
@@ -168,6 +169,19 @@ struct vg_index {
   DevBuf list_off, list_ids, code_off, list_codes, pack_off, packed;
   std::vector<uint64_t> h_list_off;
   std::vector<uint32_t> h_doc_ids;
+
+  // quantizer kind and OPQ rotation (opq.rs): rotation [d][d] row-major when set
+  bool optimized = false;
+  DevBuf rotation;
+  std::vector<float> h_rotation;
+
+  // metadata filtering (search.rs:414-470, 626-651): the filter field, every
+  // document's metadata in the reference's serialised form, and per list the
+  // bitmask of the filter categories present
+  bool has_filter_field = false;
+  std::string filter_field;
+  std::vector<std::pair<uint32_t, std::string>> metadata;
+  std::vector<uint64_t> h_bitmask;
 
   // sharding
   int rank = 0, world = 1;
@@ -406,6 +420,8 @@ int train(vg_index *ix, size_t n_train, size_t max_iter) {
 
 // ---- encode and list layout (search.rs:620-848) ---------------------------
 
+int build_list_storage(vg_index *ix, const uint32_t *sorted_lists);
+
 int encode_and_layout(vg_index *ix) {
   cudaStream_t s = ix->stream;
   const size_t n = ix->n, d = ix->d, M = ix->params.num_codebooks, ks = ix->params.codebook_size;
@@ -445,6 +461,17 @@ int encode_and_layout(vg_index *ix) {
   VG_CU(cudaStreamSynchronize(s));
 
   ix->h_list_off.assign(hseg.begin(), hseg.end());
+  return build_list_storage(ix, sorted_lists.as<uint32_t>());
+}
+
+// List-contiguous code storage from the list layout: ix->h_list_off (host
+// CSR offsets), ix->list_ids (device, vector ids in list order) and
+// sorted_lists (device, the list of every position).  Gathers list_codes and,
+// for 16-entry codebooks, the nibble-packed scan copy.
+int build_list_storage(vg_index *ix, const uint32_t *sorted_lists) {
+  cudaStream_t s = ix->stream;
+  const size_t n = ix->n, M = ix->params.num_codebooks, ks = ix->params.codebook_size;
+  const size_t Lc = ix->num_centroids;
   std::vector<uint64_t> h_code_off(Lc), h_pack_off(Lc);
   uint64_t code_bytes = 0, pack_bytes = 0;
   for (size_t l = 0; l < Lc; ++l) {
@@ -461,7 +488,7 @@ int encode_and_layout(vg_index *ix) {
   VG_CU(cudaMemcpyAsync(ix->list_off.p, ix->h_list_off.data(), (Lc + 1) * 8, cudaMemcpyHostToDevice, s));
   VG_CU(cudaMemcpyAsync(ix->code_off.p, h_code_off.data(), Lc * 8, cudaMemcpyHostToDevice, s));
   VG_CU(cudaMemcpyAsync(ix->pack_off.p, h_pack_off.data(), Lc * 8, cudaMemcpyHostToDevice, s));
-  VG_CU(launch_gather_list_codes(ix->codes.as<uint8_t>(), ix->list_ids.as<uint32_t>(), sorted_lists.as<uint32_t>(),
+  VG_CU(launch_gather_list_codes(ix->codes.as<uint8_t>(), ix->list_ids.as<uint32_t>(), sorted_lists,
                                  n, static_cast<int>(M), ix->list_off.as<uint64_t>(), ix->code_off.as<uint64_t>(),
                                  ix->list_codes.as<uint8_t>(), s));
   if (ks == 16) {
@@ -685,6 +712,118 @@ namespace vg {
 // Sets the text vg_last_error reports, for entry points defined in other
 // translation units.
 void set_last_error(const char *msg) { g_last_error = msg; }
+
+// ---- snapshot image (search.rs:945-1084) -----------------------------------
+
+int snapshot_export(const vg_index *ix, SnapshotState &st) {
+  if (!ix->built) return fail(VG_ERR_NOT_BUILT, "IVF-PQ index is not built: cannot save");
+  DeviceGuard g(ix->device);
+  const size_t n = ix->n, d = ix->d, M = ix->params.num_codebooks, ks = ix->params.codebook_size;
+  const size_t Lc = ix->num_centroids, L = ix->params.num_clusters;
+  st = SnapshotState{};
+  st.dim = d;
+  st.num_vectors = n;
+  st.num_centroids = Lc;
+  st.params = ix->params;
+  st.centroids.resize(Lc * d);
+  st.codebooks.resize(M * ks * ix->dsub);
+  st.codes.resize(n * M);
+  st.list_ids.resize(n);
+  VG_CU(cudaMemcpy(st.centroids.data(), ix->centroids.p, st.centroids.size() * 4, cudaMemcpyDeviceToHost));
+  VG_CU(cudaMemcpy(st.codebooks.data(), ix->codebooks.p, st.codebooks.size() * 4, cudaMemcpyDeviceToHost));
+  VG_CU(cudaMemcpy(st.codes.data(), ix->codes.p, st.codes.size(), cudaMemcpyDeviceToHost));
+  VG_CU(cudaMemcpy(st.list_ids.data(), ix->list_ids.p, n * 4, cudaMemcpyDeviceToHost));
+  st.optimized = ix->optimized;
+  st.rotation = ix->h_rotation;
+  st.doc_ids = ix->h_doc_ids;
+  // the reference keeps num_clusters clusters; those past the trained
+  // centroids are empty
+  st.list_offsets.assign(ix->h_list_off.begin(), ix->h_list_off.end());
+  st.list_offsets.resize(L + 1, st.list_offsets.back());
+  st.bitmasks = ix->h_bitmask;
+  st.bitmasks.resize(L, 0);
+  if (!ix->compacted) {
+    st.vectors.resize(n * d);
+    VG_CU(cudaMemcpy(st.vectors.data(), ix->vectors.p, n * d * 4, cudaMemcpyDeviceToHost));
+  }
+  st.has_filter_field = ix->has_filter_field;
+  st.filter_field = ix->filter_field;
+  st.metadata = ix->metadata;
+  return VG_OK;
+}
+
+int snapshot_adopt(vg_index *ix, SnapshotState &st) {
+  const size_t n = st.num_vectors, d = ix->d, M = ix->params.num_codebooks, ks = ix->params.codebook_size;
+  const size_t L = ix->params.num_clusters, Lc = st.num_centroids;
+  auto bad = [](const std::string &what) { return fail(VG_ERR_FORMAT, "IVF-PQ snapshot: " + what); };
+  if (st.dim != d) return bad("dimension does not match the index");
+  if (n == 0 || n > 0xffffffffull) return bad("vector count out of range");
+  if (Lc == 0 || Lc > L) return bad("num_centroids must be in 1..=num_clusters");
+  if (st.centroids.size() != Lc * d) return bad("centroid array has the wrong length");
+  if (st.codebooks.size() != M * ks * ix->dsub) return bad("codebook array has the wrong length");
+  if (!st.rotation.empty() && st.rotation.size() != d * d) return bad("rotation is not dimension x dimension");
+  if (st.doc_ids.size() != n || st.codes.size() != n * M) return bad("doc ids or codes have the wrong length");
+  if (!st.vectors.empty() && st.vectors.size() != n * d) return bad("raw vectors have the wrong length");
+  if (st.list_offsets.size() != L + 1 || st.list_offsets.front() != 0 || st.list_offsets.back() != n ||
+      st.list_ids.size() != n || st.bitmasks.size() != L)
+    return bad("cluster table does not match num_clusters and num_vectors");
+  for (size_t i = 0; i < n * M; ++i)
+    if (st.codes[i] >= ks) return bad("code " + std::to_string(st.codes[i]) + " out of range for codebook_size");
+  // the clusters must partition the vectors; clusters past the centroids are
+  // never probed and must be empty
+  std::vector<uint32_t> assign(n, 0xffffffffu), sorted_lists(n);
+  for (size_t l = 0; l < L; ++l) {
+    if (st.list_offsets[l + 1] < st.list_offsets[l]) return bad("cluster offsets decrease");
+    if (l >= Lc && st.list_offsets[l + 1] != st.list_offsets[l]) return bad("a cluster past num_centroids is not empty");
+    for (uint64_t p = st.list_offsets[l]; p < st.list_offsets[l + 1]; ++p) {
+      const uint32_t id = st.list_ids[p];
+      if (id >= n) return bad("cluster id " + std::to_string(id) + " exceeds vector count " + std::to_string(n));
+      if (assign[id] != 0xffffffffu) return bad("vector " + std::to_string(id) + " is in more than one cluster");
+      assign[id] = static_cast<uint32_t>(l);
+      sorted_lists[p] = static_cast<uint32_t>(l);
+    }
+  }
+  DeviceGuard g(ix->device);
+  cudaStream_t s = ix->stream;
+  VG_CU(ix->centroids.reserve(Lc * d * 4));
+  VG_CU(ix->codebooks.reserve(st.codebooks.size() * 4));
+  VG_CU(ix->doc_ids.reserve(n * 4));
+  VG_CU(ix->codes.reserve(n * M));
+  VG_CU(ix->assign.reserve(n * 4));
+  VG_CU(ix->list_ids.reserve(n * 4));
+  DevBuf d_sorted;
+  VG_CU(d_sorted.reserve(n * 4));
+  VG_CU(cudaMemcpyAsync(ix->centroids.p, st.centroids.data(), Lc * d * 4, cudaMemcpyHostToDevice, s));
+  VG_CU(cudaMemcpyAsync(ix->codebooks.p, st.codebooks.data(), st.codebooks.size() * 4, cudaMemcpyHostToDevice, s));
+  VG_CU(cudaMemcpyAsync(ix->doc_ids.p, st.doc_ids.data(), n * 4, cudaMemcpyHostToDevice, s));
+  VG_CU(cudaMemcpyAsync(ix->codes.p, st.codes.data(), n * M, cudaMemcpyHostToDevice, s));
+  VG_CU(cudaMemcpyAsync(ix->assign.p, assign.data(), n * 4, cudaMemcpyHostToDevice, s));
+  VG_CU(cudaMemcpyAsync(ix->list_ids.p, st.list_ids.data(), n * 4, cudaMemcpyHostToDevice, s));
+  VG_CU(cudaMemcpyAsync(d_sorted.p, sorted_lists.data(), n * 4, cudaMemcpyHostToDevice, s));
+  if (!st.vectors.empty()) {
+    VG_CU(ix->vectors.reserve(n * d * 4));
+    VG_CU(cudaMemcpyAsync(ix->vectors.p, st.vectors.data(), n * d * 4, cudaMemcpyHostToDevice, s));
+  }
+  if (!st.rotation.empty()) {
+    VG_CU(ix->rotation.reserve(d * d * 4));
+    VG_CU(cudaMemcpyAsync(ix->rotation.p, st.rotation.data(), d * d * 4, cudaMemcpyHostToDevice, s));
+  }
+  VG_CU(cudaStreamSynchronize(s));
+  ix->n = ix->cap = n;
+  ix->num_centroids = Lc;
+  ix->h_doc_ids = std::move(st.doc_ids);
+  ix->h_list_off.assign(st.list_offsets.begin(), st.list_offsets.begin() + Lc + 1);
+  ix->h_bitmask = std::move(st.bitmasks);
+  ix->optimized = st.optimized;
+  ix->h_rotation = std::move(st.rotation);
+  ix->compacted = st.vectors.empty();
+  ix->has_filter_field = st.has_filter_field;
+  ix->filter_field = std::move(st.filter_field);
+  ix->metadata = std::move(st.metadata);
+  ix->trained = true;
+  VG_TRY(build_list_storage(ix, d_sorted.as<uint32_t>()));
+  return VG_OK;
+}
 }  // namespace vg
 
 // ===========================================================================

@@ -8,6 +8,7 @@ method is a thin call into the C ABI of ``libvicinity_gpu.so``.
 from __future__ import annotations
 
 import ctypes as C
+import os
 
 import numpy as np
 
@@ -98,6 +99,27 @@ class IVFPQIndex:
     @property
     def handle(self) -> C.c_void_p:
         return self._h
+
+    # -- persistence (src/python.rs:654-681) ------------------------------
+    def save(self, path) -> None:
+        """Write a directory snapshot in the reference's format
+        (IVFPQIndex::save_to_dir): ValueError before build, OSError on I/O."""
+        _lib.check(self._lib.vg_ivfpq_save(self._h, os.fsencode(os.fspath(path))))
+
+    @staticmethod
+    def load(path, device: int = 0) -> "IVFPQIndex":
+        """Load a directory snapshot written by ``save`` or by the reference
+        (IVFPQIndex::load_from_dir): FileNotFoundError when it is missing,
+        RuntimeError when it is malformed."""
+        lib = _lib.load()
+        handle = C.c_void_p()
+        _lib.check(lib.vg_ivfpq_load(os.fsencode(os.fspath(path)), device, C.byref(handle)))
+        ix = IVFPQIndex.__new__(IVFPQIndex)
+        ix._lib = lib
+        ix._h = handle
+        ix._used_ids = set()
+        ix._dim = int(ix.info().dimension)
+        return ix
 
     # -- construction --------------------------------------------------------
     def add_items(self, vectors, ids=None) -> None:
