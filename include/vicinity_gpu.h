@@ -54,7 +54,7 @@ typedef struct vg_ivfpq_params {
   uint64_t nprobe;        /* default 100 */
   uint64_t num_codebooks; /* default 8 */
   uint64_t codebook_size; /* default 256, at most 256 */
-  int32_t use_opq;        /* must be 0: OPQ is not built by this engine */
+  int32_t use_opq;        /* OPQ: build trains a rotation (opq.rs:65-105) */
   int32_t reserved;
   uint64_t seed;          /* default 42 */
 } vg_ivfpq_params;
@@ -107,6 +107,12 @@ int vg_ivfpq_add(vg_index *ix, const uint32_t *doc_ids, const float *x,
  * encoding; also the parity hook for identical codebooks). */
 int vg_ivfpq_set_trained(vg_index *ix, const float *centroids,
                          size_t num_centroids, const float *codebooks);
+
+/* Adopt an OPQ rotation [dim][dim] row-major (OptimizedProductQuantizer's
+ * `rotation`, src/ivf_pq/opq.rs:31-41) before build: residuals are rotated
+ * before encoding and query residuals before every table; NULL removes it.
+ * With set_trained this is the state a trained OPQ quantizer holds. */
+int vg_ivfpq_set_rotation(vg_index *ix, const float *rotation);
 
 /* src/ivf_pq/search.rs:515-787 (build, build_with_training_sample,
  * build_with_training_options): training_sample_size 0 trains on every
@@ -169,7 +175,8 @@ int vg_ivfpq_load(const char *dir, int device, vg_index **out);
  *   VG_EXPORT_LIST_OFFSETS u64 [num_centroids+1] vector offsets
  *   VG_EXPORT_LIST_IDS     u32 [n]       insertion indices, list order
  *   VG_EXPORT_DOC_IDS      u32 [n]
- *   VG_EXPORT_VECTORS      f32 [n][dim]  normalised rows (until compact) */
+ *   VG_EXPORT_VECTORS      f32 [n][dim]  normalised rows (until compact)
+ *   VG_EXPORT_ROTATION     f32 [dim][dim] OPQ rotation, row-major (when set) */
 enum {
   VG_EXPORT_CENTROIDS = 0,
   VG_EXPORT_CODEBOOKS = 1,
@@ -178,7 +185,8 @@ enum {
   VG_EXPORT_LIST_OFFSETS = 4,
   VG_EXPORT_LIST_IDS = 5,
   VG_EXPORT_DOC_IDS = 6,
-  VG_EXPORT_VECTORS = 7
+  VG_EXPORT_VECTORS = 7,
+  VG_EXPORT_ROTATION = 8
 };
 int vg_ivfpq_export(const vg_index *ix, int what, void *dst, size_t bytes);
 

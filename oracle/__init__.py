@@ -41,6 +41,9 @@ _SIGS = {
     "or_index_finalize": (_i, [_vp]),
     "or_index_adopt_codes": (_i, [_vp, _vp, _vp]),
     "or_index_set_nprobe": (None, [_vp, _sz]),
+    "or_index_set_rotation": (None, [_vp, _vp]),
+    "or_rotate": (None, [_vp, _vp, _sz, _vp]),
+    "or_rotate_t": (None, [_vp, _vp, _sz, _vp]),
     "or_index_num_vectors": (_sz, [_vp]),
     "or_index_get_assignments": (None, [_vp, _vp]),
     "or_index_get_codes": (None, [_vp, _vp]),
@@ -160,6 +163,16 @@ def fastscan_batch_flat(packed, n: int, num_codebooks: int, lut) -> np.ndarray:
     return out
 
 
+def rotate(r, v, transpose: bool = False) -> np.ndarray:
+    """opq.rs:181-205: R v (or R^T v) with R [d][d] row-major."""
+    v = f32(v)
+    d = v.shape[0]
+    r = f32(r).reshape(d, d)
+    out = np.empty(d, np.float32)
+    (load().or_rotate_t if transpose else load().or_rotate)(_p(r), _p(v), d, _p(out))
+    return out
+
+
 def find_nearest_centroids(query, centroids, nprobe: int):
     q = f32(query)
     c = f32(centroids)
@@ -235,6 +248,14 @@ class OracleIndex:
         a = np.ascontiguousarray(assignments, dtype=np.uint32)
         c = np.ascontiguousarray(codes, dtype=np.uint8)
         assert self._lib.or_index_adopt_codes(self._h, _p(a), _p(c)) == 0
+
+    def set_rotation(self, rotation):
+        """OPQ rotation [d][d] (None clears); set before finalize/adopt."""
+        if rotation is None:
+            self._lib.or_index_set_rotation(self._h, None)
+        else:
+            self._rot = f32(rotation).reshape(self.d, self.d)
+            self._lib.or_index_set_rotation(self._h, _p(self._rot))
 
     def set_nprobe(self, nprobe: int):
         self._lib.or_index_set_nprobe(self._h, nprobe)

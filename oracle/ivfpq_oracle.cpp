@@ -366,9 +366,29 @@ struct or_index {
   std::vector<std::vector<uint32_t>> lists;
   std::vector<std::vector<uint8_t>> adc_codes;  // list order, |l| >= 16
   std::vector<std::vector<uint8_t>> packed;     // 4-bit blocks, |l| >= 16
+  std::vector<float> rotation;  // OPQ rotation [d][d] row-major (empty: plain PQ)
 };
 
 namespace {
+
+// opq.rs:181-192 (matrix_vector_multiply): out = R v, every row summed from
+// 0.0 in column order.
+void rotate(const float *r, const float *v, size_t d, float *out) {
+  for (size_t i = 0; i < d; ++i) {
+    float s = 0.0f;
+    for (size_t j = 0; j < d; ++j) s += r[i * d + j] * v[j];
+    out[i] = s;
+  }
+}
+
+// opq.rs:194-205 (transpose_matrix_vector_multiply): out = R^T v.
+void rotate_t(const float *r, const float *v, size_t d, float *out) {
+  for (size_t i = 0; i < d; ++i) {
+    float s = 0.0f;
+    for (size_t j = 0; j < d; ++j) s += r[j * d + i] * v[j];
+    out[i] = s;
+  }
+}
 
 // search.rs:623-718 (lists in vector order) and 816-848 (build_scan_caches).
 void build_lists(or_index *ix) {
@@ -402,13 +422,18 @@ void search_one(const or_index *ix, const float *qn, size_t k, size_t nprobe,
   std::vector<float> pdist(p);
   p = or_find_nearest_centroids(qn, ix->d, ix->centroids.data(), ix->L, p,
                                 pid.data(), pdist.data());
-  std::vector<float> qres(ix->d), table(ix->M * ix->ks), dist;
+  std::vector<float> qres(ix->d), qrot(ix->d), table(ix->M * ix->ks), dist;
   for (size_t pi = 0; pi < p; ++pi) {
     uint32_t l = pid[pi];
     const auto &ids = ix->lists[l];
     const float *c = &ix->centroids[static_cast<size_t>(l) * ix->d];
     for (size_t j = 0; j < ix->d; ++j) qres[j] = qn[j] - c[j];  // 1239-1245
-    or_adc_table(qres.data(), ix->d, ix->M, ix->ks, ix->codebooks.data(), table.data());
+    const float *tq = qres.data();
+    if (!ix->rotation.empty()) {  // opq.rs:115-121: table of the rotated residual
+      rotate(ix->rotation.data(), qres.data(), ix->d, qrot.data());
+      tq = qrot.data();
+    }
+    or_adc_table(tq, ix->d, ix->M, ix->ks, ix->codebooks.data(), table.data());
     if (ids.size() >= kSimdBatchThreshold) {
       dist.resize(ids.size());
       if (ix->ks == 16) {  // 1277-1316 (FastScan over prepacked blocks)
@@ -483,14 +508,18 @@ int or_index_finalize(or_index *ix) {
   if (n == 0) return -1;  // EmptyIndex
   ix->assign.resize(n);
   or_assign(ix->vectors.data(), n, ix->d, ix->centroids.data(), ix->L, ix->assign.data());
-  std::vector<float> residual(ix->d);
+  std::vector<float> residual(ix->d), rotated(ix->d);
   ix->codes.resize(n * ix->M);
   for (size_t i = 0; i < n; ++i) {  // 720-729 then 776-781
     const float *v = &ix->vectors[i * ix->d];
     const float *c = &ix->centroids[static_cast<size_t>(ix->assign[i]) * ix->d];
     for (size_t j = 0; j < ix->d; ++j) residual[j] = v[j] - c[j];
-    or_pq_quantize(residual.data(), 1, ix->d, ix->M, ix->ks, ix->codebooks.data(),
-                   &ix->codes[i * ix->M]);
+    const float *enc = residual.data();
+    if (!ix->rotation.empty()) {  // opq.rs:107-113: encode the rotated residual
+      rotate(ix->rotation.data(), residual.data(), ix->d, rotated.data());
+      enc = rotated.data();
+    }
+    or_pq_quantize(enc, 1, ix->d, ix->M, ix->ks, ix->codebooks.data(), &ix->codes[i * ix->M]);
   }
   build_lists(ix);
   return 0;
@@ -507,6 +536,14 @@ int or_index_adopt_codes(or_index *ix, const uint32_t *assignments, const uint8_
 }
 
 void or_index_set_nprobe(or_index *ix, size_t nprobe) { ix->nprobe = nprobe; }
+
+void or_rotate(const float *r, const float *v, size_t d, float *out) { rotate(r, v, d, out); }
+void or_rotate_t(const float *r, const float *v, size_t d, float *out) { rotate_t(r, v, d, out); }
+
+void or_index_set_rotation(or_index *ix, const float *rotation) {
+  if (rotation) ix->rotation.assign(rotation, rotation + ix->d * ix->d);
+  else ix->rotation.clear();
+}
 size_t or_index_num_vectors(const or_index *ix) { return ix->doc_ids.size(); }
 
 void or_index_get_assignments(const or_index *ix, uint32_t *out) {
@@ -531,6 +568,10 @@ void or_index_get_vectors(const or_index *ix, float *out) {
 int or_index_reconstruct(const or_index *ix, size_t idx, float *out) {
   if (!ix->built || idx >= ix->doc_ids.size()) return -2;
   or_pq_reconstruct(&ix->codes[idx * ix->M], ix->d, ix->M, ix->ks, ix->codebooks.data(), out);
+  if (!ix->rotation.empty()) {  // opq.rs:126-136: back to the original space
+    std::vector<float> rec(out, out + ix->d);
+    rotate_t(ix->rotation.data(), rec.data(), ix->d, out);
+  }
   const float *c = &ix->centroids[static_cast<size_t>(ix->assign[idx]) * ix->d];
   for (size_t j = 0; j < ix->d; ++j) out[j] += c[j];
   return 0;

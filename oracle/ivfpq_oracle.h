@@ -128,6 +128,15 @@ int or_index_adopt_codes(or_index *ix, const uint32_t *assignments,
                          const uint8_t *codes);
 
 void or_index_set_nprobe(or_index *ix, size_t nprobe);
+/* opq.rs:181-192 (matrix_vector_multiply) and 194-205 (transpose): out = R v
+ * and out = R^T v with R [d][d] row-major, each output summed from 0.0. */
+void or_rotate(const float *r, const float *v, size_t d, float *out);
+void or_rotate_t(const float *r, const float *v, size_t d, float *out);
+
+/* OPQ rotation [d][d] row-major (opq.rs:31-41), applied to residuals before
+ * encoding (opq.rs:107-113) and to query residuals before each table
+ * (opq.rs:115-121); NULL clears it.  Set it before or_index_finalize. */
+void or_index_set_rotation(or_index *ix, const float *rotation);
 size_t or_index_num_vectors(const or_index *ix);
 
 /* Export views (sizes: n, n*M, num_clusters+1, n). list_offsets counts

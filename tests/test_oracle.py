@@ -230,3 +230,43 @@ def test_query_scale_invariance_and_padding():
     ids, dists, cnt = ix.search_batch(q, 300, nprobe=32)
     assert (cnt == 256).all()
     assert (ids[:, 256:] == 0xFFFFFFFF).all() and np.isinf(dists[:, 256:]).all()
+
+
+# ---- OPQ rotation (opq.rs) ---------------------------------------------------
+
+def test_opq_matrix_vector_multiply(kats):
+    for case in kats["opq_matrix_vector_multiply"]["cases"]:
+        got = orc.rotate(case["matrix"], case["vector"])
+        np.testing.assert_allclose(got, case["expected"], atol=case["tolerance"], rtol=0)
+
+
+def test_opq_identity_rotation_is_a_no_op(kats):
+    kat = kats["opq_identity_rotation"]
+    v = np.asarray(kat["vector"], np.float32)
+    assert np.array_equal(orc.rotate(np.eye(kat["dimension"]), v), v)
+
+
+def test_opq_encode_rotates_and_decode_applies_the_transpose(kats):
+    kat = kats["opq_decode_applies_transpose"]
+    d, m, ks = kat["dimension"], kat["num_codebooks"], kat["codebook_size"]
+    rot = np.asarray(kat["rotation"], np.float32).reshape(d, d)
+    g = np.random.default_rng(11)
+    cb = g.uniform(-1, 1, (m, ks, d // m)).astype(np.float32)
+    x = g.uniform(-1, 0.9, (5, d)).astype(np.float32)
+    ix = orc.OracleIndex(d, 1, m, ks, 1)
+    ix.set_trained(np.zeros((1, d), np.float32), cb)
+    ix.set_rotation(rot)
+    ix.add(np.arange(5, dtype=np.uint32), x)
+    ix.finalize()
+    xn = ix.vectors()
+    for i in range(5):
+        codes = ix.codes()[i]
+        # encoding quantises the rotated residual (opq.rs:107-113)
+        assert np.array_equal(codes, orc.pq_quantize(orc.rotate(rot, xn[i]), m, ks, cb)[0])
+        rotated_space = orc.pq_reconstruct(codes, d, m, ks, cb)
+        decoded = ix.reconstruct(i)
+        expected = orc.rotate(rot, rotated_space, transpose=True)
+        np.testing.assert_allclose(decoded, expected, atol=kat["tolerance"], rtol=0)
+        err = np.linalg.norm(xn[i] - decoded)
+        forgot = np.linalg.norm(xn[i] - rotated_space)
+        assert err <= forgot + 1e-6

@@ -35,6 +35,7 @@ EXPORT_LIST_OFFSETS = 4
 EXPORT_LIST_IDS = 5
 EXPORT_DOC_IDS = 6
 EXPORT_VECTORS = 7
+EXPORT_ROTATION = 8
 
 
 class VgParams(C.Structure):
@@ -113,6 +114,7 @@ SIGNATURES = {
     "vg_ivfpq_destroy": (_i, [_vp]),
     "vg_ivfpq_add": (_i, [_vp, _vp, _vp, _sz]),
     "vg_ivfpq_set_trained": (_i, [_vp, _vp, _sz, _vp]),
+    "vg_ivfpq_set_rotation": (_i, [_vp, _vp]),
     "vg_ivfpq_build": (_i, [_vp, _sz, _sz]),
     "vg_ivfpq_set_nprobe": (_i, [_vp, _sz]),
     "vg_ivfpq_set_stream": (_i, [_vp, _vp]),

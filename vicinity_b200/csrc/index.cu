@@ -19,6 +19,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <cmath>
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
@@ -31,6 +32,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "opq.h"
 #include "snapshot.h"
 #include "vicinity_gpu.h"
 
@@ -172,7 +174,7 @@ struct vg_index {
 
   // quantizer kind and OPQ rotation (opq.rs): rotation [d][d] row-major when set
   bool optimized = false;
-  DevBuf rotation;
+  DevBuf rotation, rotation_t;  // row-major (encode) and transposed (scan kernels)
   std::vector<float> h_rotation;
 
   // metadata filtering (search.rs:414-470, 626-651): the filter field, every
@@ -206,7 +208,7 @@ struct vg_index {
   size_t device_bytes() const {
     return vectors.cap + doc_ids.cap + centroids.cap + codebooks.cap + assign.cap + codes.cap +
            list_off.cap + list_ids.cap + code_off.cap + list_codes.cap + pack_off.cap + packed.cap +
-           owner.cap;
+           owner.cap + rotation.cap + rotation_t.cap;
   }
 };
 
@@ -222,8 +224,6 @@ int validate_shape(size_t dim, const vg_ivfpq_params &p) {
                 "invalid config `num_clusters, num_codebooks, codebook_size`: must all be greater than 0");
   if (dim % p.num_codebooks != 0)
     return fail(VG_ERR_INVALID_CONFIG, "invalid config `dimension`: must be divisible by num_codebooks");
-  if (p.use_opq)
-    return fail(VG_ERR_UNSUPPORTED, "unsupported: OPQ rotation is not built by the B200 engine");
   if (p.codebook_size == 16 && p.num_codebooks > 65535 / 255)
     return fail(VG_ERR_INVALID_PARAMETER,
                 "FastScan accumulates LUT terms in u16: at most 257 codebooks are supported");
@@ -278,6 +278,8 @@ void mark(vg_index *ix, int i) {
 
 // ---- training (device Lloyd iterations; not bit-pinned to the reference's
 // third-party k-means, see src/partitioning/kmeans.rs:64-90) --------------
+
+int upload_rotation(vg_index *ix);
 
 int train(vg_index *ix, size_t n_train, size_t max_iter) {
   cudaStream_t s = ix->stream;
@@ -364,25 +366,6 @@ int train(vg_index *ix, size_t n_train, size_t max_iter) {
                          resid.as<float>(), s));
   const size_t dsub = d / M;
   VG_CU(ix->codebooks.reserve(M * ks * dsub * 4));
-  {
-    std::vector<float> cb_init(M * ks * dsub);
-    std::vector<float> host_res;  // gather the seeded rows per subspace on the host
-    for (size_t m = 0; m < M; ++m) {
-      std::vector<uint32_t> pick = seeded_prefix(n_train, ks, ix->params.seed + m);
-      DevBuf pick_d, rows_out;
-      VG_CU(pick_d.reserve(ks * 4));
-      VG_CU(rows_out.reserve(ks * d * 4));
-      VG_CU(cudaMemcpyAsync(pick_d.p, pick.data(), ks * 4, cudaMemcpyHostToDevice, s));
-      VG_CU(launch_gather_rows(resid.as<float>(), static_cast<int>(d), pick_d.as<uint32_t>(), ks,
-                               rows_out.as<float>(), s));
-      host_res.resize(ks * d);
-      VG_CU(cudaMemcpyAsync(host_res.data(), rows_out.p, ks * d * 4, cudaMemcpyDeviceToHost, s));
-      VG_CU(cudaStreamSynchronize(s));
-      for (size_t c = 0; c < ks; ++c)
-        std::memcpy(&cb_init[(m * ks + c) * dsub], &host_res[c * d + m * dsub], dsub * 4);
-    }
-    VG_CU(cudaMemcpyAsync(ix->codebooks.p, cb_init.data(), cb_init.size() * 4, cudaMemcpyHostToDevice, s));
-  }
   VG_CU(codes_t.reserve(n_train * M));
   VG_CU(codes_prev.reserve(n_train * M));
   VG_CU(pkeys.reserve(n_train * M * 4));
@@ -391,30 +374,129 @@ int train(vg_index *ix, size_t n_train, size_t max_iter) {
   VG_CU(pkeys_sorted.reserve(n_train * M * 4));
   int end_bit = 1;
   while ((size_t(1) << end_bit) < M * ks) ++end_bit;
-  changed = 1;
-  for (size_t it = 0; it < max_iter && changed; ++it) {
-    VG_CU(launch_encode_residuals(resid.as<float>(), n_train, static_cast<int>(d), ix->codebooks.as<float>(),
-                                  static_cast<int>(M), static_cast<int>(ks), codes_t.as<uint8_t>(), s));
-    VG_CU(cudaMemsetAsync(scal.p, 0, 4, s));
-    if (it) VG_CU(launch_count_diff_u8(codes_t.as<uint8_t>(), codes_prev.as<uint8_t>(), n_train * M,
-                                       scal.as<unsigned int>(), s));
-    VG_CU(launch_pq_keys(codes_t.as<uint8_t>(), n_train, static_cast<int>(M), static_cast<int>(ks),
-                         pkeys.as<uint32_t>(), pvals.as<uint32_t>(), s));
-    size_t tb = temp_bytes;
-    VG_CU(sort_pairs_u32(temp.p, tb, pkeys.as<uint32_t>(), pkeys_sorted.as<uint32_t>(), pvals.as<uint32_t>(),
-                         ids_sorted.as<uint32_t>(), n_train * M, end_bit, s));
-    VG_CU(launch_segments(pkeys_sorted.as<uint32_t>(), n_train * M, M * ks, seg.as<uint32_t>(), s));
-    VG_CU(launch_pq_update(resid.as<float>(), n_train, static_cast<int>(d), static_cast<int>(M),
-                           static_cast<int>(ks), ids_sorted.as<uint32_t>(), seg.as<uint32_t>(),
-                           ix->codebooks.as<float>(), newc.as<float>(), s));
-    VG_CU(cudaMemcpyAsync(ix->codebooks.p, newc.p, M * ks * dsub * 4, cudaMemcpyDeviceToDevice, s));
-    VG_CU(cudaMemcpyAsync(codes_prev.p, codes_t.p, n_train * M, cudaMemcpyDeviceToDevice, s));
-    VG_CU(cudaMemcpyAsync(&changed, scal.p, 4, cudaMemcpyDeviceToHost, s));
+
+  // Lloyd iterations of the M codebooks on the rows of `data` (training
+  // residuals, rotated when OPQ is on), from seeded rows per subspace
+  auto fit_pq = [&](const float *data) -> int {
+    std::vector<float> cb_init(M * ks * dsub);
+    std::vector<float> host_res;  // gather the seeded rows per subspace on the host
+    for (size_t m = 0; m < M; ++m) {
+      std::vector<uint32_t> pick = seeded_prefix(n_train, ks, ix->params.seed + m);
+      DevBuf pick_d, rows_out;
+      VG_CU(pick_d.reserve(ks * 4));
+      VG_CU(rows_out.reserve(ks * d * 4));
+      VG_CU(cudaMemcpyAsync(pick_d.p, pick.data(), ks * 4, cudaMemcpyHostToDevice, s));
+      VG_CU(launch_gather_rows(data, static_cast<int>(d), pick_d.as<uint32_t>(), ks, rows_out.as<float>(), s));
+      host_res.resize(ks * d);
+      VG_CU(cudaMemcpyAsync(host_res.data(), rows_out.p, ks * d * 4, cudaMemcpyDeviceToHost, s));
+      VG_CU(cudaStreamSynchronize(s));
+      for (size_t c = 0; c < ks; ++c)
+        std::memcpy(&cb_init[(m * ks + c) * dsub], &host_res[c * d + m * dsub], dsub * 4);
+    }
+    VG_CU(cudaMemcpyAsync(ix->codebooks.p, cb_init.data(), cb_init.size() * 4, cudaMemcpyHostToDevice, s));
+    changed = 1;
+    for (size_t it = 0; it < max_iter && changed; ++it) {
+      VG_CU(launch_encode_residuals(data, n_train, static_cast<int>(d), ix->codebooks.as<float>(),
+                                    static_cast<int>(M), static_cast<int>(ks), codes_t.as<uint8_t>(), s));
+      VG_CU(cudaMemsetAsync(scal.p, 0, 4, s));
+      if (it) VG_CU(launch_count_diff_u8(codes_t.as<uint8_t>(), codes_prev.as<uint8_t>(), n_train * M,
+                                         scal.as<unsigned int>(), s));
+      VG_CU(launch_pq_keys(codes_t.as<uint8_t>(), n_train, static_cast<int>(M), static_cast<int>(ks),
+                           pkeys.as<uint32_t>(), pvals.as<uint32_t>(), s));
+      size_t tb = temp_bytes;
+      VG_CU(sort_pairs_u32(temp.p, tb, pkeys.as<uint32_t>(), pkeys_sorted.as<uint32_t>(), pvals.as<uint32_t>(),
+                           ids_sorted.as<uint32_t>(), n_train * M, end_bit, s));
+      VG_CU(launch_segments(pkeys_sorted.as<uint32_t>(), n_train * M, M * ks, seg.as<uint32_t>(), s));
+      VG_CU(launch_pq_update(data, n_train, static_cast<int>(d), static_cast<int>(M), static_cast<int>(ks),
+                             ids_sorted.as<uint32_t>(), seg.as<uint32_t>(), ix->codebooks.as<float>(),
+                             newc.as<float>(), s));
+      VG_CU(cudaMemcpyAsync(ix->codebooks.p, newc.p, M * ks * dsub * 4, cudaMemcpyDeviceToDevice, s));
+      VG_CU(cudaMemcpyAsync(codes_prev.p, codes_t.p, n_train * M, cudaMemcpyDeviceToDevice, s));
+      VG_CU(cudaMemcpyAsync(&changed, scal.p, 4, cudaMemcpyDeviceToHost, s));
+      VG_CU(cudaStreamSynchronize(s));
+      if (it == 0) changed = 1;
+    }
+    return VG_OK;
+  };
+
+  if (!ix->h_rotation.empty()) {
+    // a rotation given by the caller: codebooks of the rotated residuals
+    DevBuf rot;
+    VG_CU(rot.reserve(n_train * d * 4));
+    VG_CU(launch_rotate_rows(resid.as<float>(), n_train, static_cast<int>(d), ix->rotation.as<float>(),
+                             rot.as<float>(), s));
+    VG_TRY(fit_pq(rot.as<float>()));
+  } else if (!ix->params.use_opq) {
+    VG_TRY(fit_pq(resid.as<float>()));
+  } else {
+    // OPQ (opq.rs:65-105): ten alternations of fitting the codebooks on the
+    // rotated residuals and re-solving the rotation by Procrustes on the
+    // first min(n, 5000) residuals (opq.rs:207-290)
+    std::vector<float> rmat(d * d, 0.0f);
+    for (size_t i = 0; i < d; ++i) rmat[i * d + i] = 1.0f;
+    const size_t S = std::min<size_t>(n_train, 5000);
+    DevBuf rot, rdev;
+    VG_CU(rot.reserve(n_train * d * 4));
+    VG_CU(rdev.reserve(d * d * 4));
+    std::vector<float> xs(S * d), cbh(M * ks * dsub);
+    std::vector<uint8_t> cs(S * M);
+    VG_CU(cudaMemcpyAsync(xs.data(), resid.p, S * d * 4, cudaMemcpyDeviceToHost, s));
     VG_CU(cudaStreamSynchronize(s));
-    if (it == 0) changed = 1;
+    std::vector<double> cov(d * d), rec(d);
+    for (int iter = 0; iter < 10; ++iter) {
+      VG_CU(cudaMemcpyAsync(rdev.p, rmat.data(), d * d * 4, cudaMemcpyHostToDevice, s));
+      const float *data = resid.as<float>();
+      if (iter > 0) {
+        VG_CU(launch_rotate_rows(resid.as<float>(), n_train, static_cast<int>(d), rdev.as<float>(),
+                                 rot.as<float>(), s));
+        data = rot.as<float>();
+      }
+      VG_TRY(fit_pq(data));
+      // M = sum_k recon(quantize(R x_k)) x_k^T over the sample
+      VG_CU(launch_rotate_rows(resid.as<float>(), S, static_cast<int>(d), rdev.as<float>(), rot.as<float>(), s));
+      VG_CU(launch_encode_residuals(rot.as<float>(), S, static_cast<int>(d), ix->codebooks.as<float>(),
+                                    static_cast<int>(M), static_cast<int>(ks), codes_t.as<uint8_t>(), s));
+      VG_CU(cudaMemcpyAsync(cs.data(), codes_t.p, S * M, cudaMemcpyDeviceToHost, s));
+      VG_CU(cudaMemcpyAsync(cbh.data(), ix->codebooks.p, cbh.size() * 4, cudaMemcpyDeviceToHost, s));
+      VG_CU(cudaStreamSynchronize(s));
+      std::fill(cov.begin(), cov.end(), 0.0);
+      for (size_t k = 0; k < S; ++k) {
+        for (size_t m = 0; m < M; ++m)
+          for (size_t j = 0; j < dsub; ++j) rec[m * dsub + j] = cbh[(m * ks + cs[k * M + m]) * dsub + j];
+        const float *x = &xs[k * d];
+        for (size_t i = 0; i < d; ++i) {
+          const double ri = rec[i];
+          double *row = &cov[i * d];
+          for (size_t j = 0; j < d; ++j) row[j] += ri * x[j];
+        }
+      }
+      rmat = procrustes_rotation(cov, d);
+    }
+    ix->h_rotation = std::move(rmat);
+    ix->optimized = true;
+    VG_TRY(upload_rotation(ix));
   }
   ix->num_centroids = Lc;
   ix->trained = true;
+  return VG_OK;
+}
+
+// Device copies of the host rotation: row-major for the encode GEMM and
+// transposed for the scan kernels (coalesced loads of one column).
+int upload_rotation(vg_index *ix) {
+  const size_t d = ix->d;
+  if (ix->h_rotation.empty()) {
+    ix->rotation.release();
+    ix->rotation_t.release();
+    return VG_OK;
+  }
+  std::vector<float> rt(d * d);
+  for (size_t i = 0; i < d; ++i)
+    for (size_t j = 0; j < d; ++j) rt[j * d + i] = ix->h_rotation[i * d + j];
+  VG_CU(ix->rotation.reserve(d * d * 4));
+  VG_CU(ix->rotation_t.reserve(d * d * 4));
+  VG_CU(cudaMemcpy(ix->rotation.p, ix->h_rotation.data(), d * d * 4, cudaMemcpyHostToDevice));
+  VG_CU(cudaMemcpy(ix->rotation_t.p, rt.data(), d * d * 4, cudaMemcpyHostToDevice));
   return VG_OK;
 }
 
@@ -439,9 +521,28 @@ int encode_and_layout(vg_index *ix) {
   }
   best.release();
   VG_CU(ix->codes.reserve(n * M));
-  VG_CU(launch_encode(ix->vectors.as<float>(), n, static_cast<int>(d), ix->assign.as<uint32_t>(),
-                      ix->centroids.as<float>(), ix->codebooks.as<float>(), static_cast<int>(M),
-                      static_cast<int>(ks), ix->codes.as<uint8_t>(), s));
+  if (ix->h_rotation.empty()) {
+    VG_CU(launch_encode(ix->vectors.as<float>(), n, static_cast<int>(d), ix->assign.as<uint32_t>(),
+                        ix->centroids.as<float>(), ix->codebooks.as<float>(), static_cast<int>(M),
+                        static_cast<int>(ks), ix->codes.as<uint8_t>(), s));
+  } else {
+    // OPQ (opq.rs:107-113): quantise the rotated residual R (x - c)
+    const size_t chunk = std::min(n, size_t(1) << 20);
+    DevBuf res, rot;
+    VG_CU(res.reserve(chunk * d * 4));
+    VG_CU(rot.reserve(chunk * d * 4));
+    for (size_t r0 = 0; r0 < n; r0 += chunk) {
+      const size_t rows = std::min(chunk, n - r0);
+      VG_CU(launch_residuals(ix->vectors.as<float>() + r0 * d, rows, static_cast<int>(d),
+                             ix->assign.as<uint32_t>() + r0, ix->centroids.as<float>(), res.as<float>(), s));
+      VG_CU(launch_rotate_rows(res.as<float>(), rows, static_cast<int>(d), ix->rotation.as<float>(),
+                               rot.as<float>(), s));
+      VG_CU(launch_encode_residuals(rot.as<float>(), rows, static_cast<int>(d), ix->codebooks.as<float>(),
+                                    static_cast<int>(M), static_cast<int>(ks),
+                                    ix->codes.as<uint8_t>() + r0 * M, s));
+    }
+    VG_CU(cudaStreamSynchronize(s));
+  }
 
   // stable sort by list keeps insertion order inside each list
   DevBuf iota, sorted_lists, temp, seg;
@@ -617,6 +718,7 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   sp.packed = ix->packed.as<uint8_t>();
   sp.list_ids = ix->list_ids.as<uint32_t>();
   sp.doc_ids = doc_map;
+  sp.rot_t = ix->h_rotation.empty() ? nullptr : ix->rotation_t.as<float>();
   sp.d = static_cast<int>(d);
   sp.M = static_cast<int>(M);
   sp.ks = static_cast<int>(ix->params.codebook_size);
@@ -804,10 +906,6 @@ int snapshot_adopt(vg_index *ix, SnapshotState &st) {
     VG_CU(ix->vectors.reserve(n * d * 4));
     VG_CU(cudaMemcpyAsync(ix->vectors.p, st.vectors.data(), n * d * 4, cudaMemcpyHostToDevice, s));
   }
-  if (!st.rotation.empty()) {
-    VG_CU(ix->rotation.reserve(d * d * 4));
-    VG_CU(cudaMemcpyAsync(ix->rotation.p, st.rotation.data(), d * d * 4, cudaMemcpyHostToDevice, s));
-  }
   VG_CU(cudaStreamSynchronize(s));
   ix->n = ix->cap = n;
   ix->num_centroids = Lc;
@@ -816,6 +914,7 @@ int snapshot_adopt(vg_index *ix, SnapshotState &st) {
   ix->h_bitmask = std::move(st.bitmasks);
   ix->optimized = st.optimized;
   ix->h_rotation = std::move(st.rotation);
+  VG_TRY(upload_rotation(ix));
   ix->compacted = st.vectors.empty();
   ix->has_filter_field = st.has_filter_field;
   ix->filter_field = std::move(st.filter_field);
@@ -867,6 +966,7 @@ int vg_ivfpq_create(size_t dim, const vg_ivfpq_params *params, int device, vg_in
   ix->device = device;
   ix->d = dim;
   ix->params = *params;
+  ix->optimized = params->use_opq != 0;
   ix->dsub = dim / params->num_codebooks;
   cudaDeviceGetAttribute(&ix->num_sms, cudaDevAttrMultiProcessorCount, device);
   cudaError_t e = cudaStreamCreateWithFlags(&ix->own_stream, cudaStreamNonBlocking);
@@ -965,6 +1065,25 @@ int vg_ivfpq_set_trained(vg_index *ix, const float *centroids, size_t num_centro
   return VG_OK;
 }
 
+int vg_ivfpq_set_rotation(vg_index *ix, const float *rotation) {
+  if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
+  if (ix->built) return fail(VG_ERR_ALREADY_BUILT, "IVF-PQ index is already built: cannot replace its rotation");
+  DeviceGuard g(ix->device);
+  const size_t d = ix->d;
+  if (!rotation) {
+    ix->h_rotation.clear();
+    ix->optimized = ix->params.use_opq != 0;
+    return upload_rotation(ix);
+  }
+  std::vector<float> r(d * d);
+  VG_CU(cudaMemcpy(r.data(), rotation, d * d * 4, cudaMemcpyDefault));
+  for (float v : r)
+    if (!std::isfinite(v)) return fail(VG_ERR_INVALID_PARAMETER, "rotation holds a non-finite value");
+  ix->h_rotation = std::move(r);
+  ix->optimized = true;
+  return upload_rotation(ix);
+}
+
 int vg_ivfpq_build(vg_index *ix, size_t training_sample_size, size_t kmeans_max_iter) {
   if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
   if (ix->built) return VG_OK;  // search.rs:550-552
@@ -1052,9 +1171,19 @@ int vg_ivfpq_reconstruct(const vg_index *ix, size_t idx, float *out) {
   VG_CU(cudaMemcpy(code.data(), ix->codes.as<uint8_t>() + idx * M, M, cudaMemcpyDeviceToHost));
   VG_CU(cudaMemcpy(cent.data(), ix->centroids.as<float>() + static_cast<size_t>(a) * d, d * 4, cudaMemcpyDeviceToHost));
   VG_CU(cudaMemcpy(cb.data(), ix->codebooks.p, cb.size() * 4, cudaMemcpyDeviceToHost));
-  std::vector<float> res(d);
+  std::vector<float> res(d), dec(d);
   for (size_t m = 0; m < M; ++m)
-    for (size_t j = 0; j < dsub; ++j) res[m * dsub + j] = cb[(m * ks + code[m]) * dsub + j] + cent[m * dsub + j];
+    for (size_t j = 0; j < dsub; ++j) dec[m * dsub + j] = cb[(m * ks + code[m]) * dsub + j];
+  if (!ix->h_rotation.empty()) {  // opq.rs:126-136: decode applies R^T
+    const std::vector<float> &r = ix->h_rotation;
+    std::vector<float> rot(dec);
+    for (size_t i = 0; i < d; ++i) {
+      float s = 0.0f;
+      for (size_t j = 0; j < d; ++j) s += r[j * d + i] * rot[j];
+      dec[i] = s;
+    }
+  }
+  for (size_t j = 0; j < d; ++j) res[j] = dec[j] + cent[j];  // search.rs:878-881
   VG_CU(cudaMemcpy(out, res.data(), d * 4, cudaMemcpyDefault));
   return VG_OK;
 }
@@ -1083,6 +1212,8 @@ int vg_ivfpq_export(const vg_index *ix, int what, void *dst, size_t bytes) {
     case VG_EXPORT_LIST_OFFSETS: src = ix->list_off.p; need = (ix->num_centroids + 1) * 8; break;
     case VG_EXPORT_LIST_IDS: src = ix->list_ids.p; need = n * 4; break;
     case VG_EXPORT_DOC_IDS: src = ix->doc_ids.p; need = n * 4; needs_build = false; break;
+    case VG_EXPORT_ROTATION:
+      src = ix->rotation.p; need = ix->h_rotation.empty() ? 0 : d * d * 4; needs_build = false; break;
     case VG_EXPORT_VECTORS:
       if (ix->compacted) return fail(VG_ERR_UNSUPPORTED, "raw vectors were dropped by compact()");
       src = ix->vectors.p; need = n * d * 4; needs_build = false; break;

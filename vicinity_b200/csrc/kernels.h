@@ -34,6 +34,12 @@ cudaError_t launch_coarse_argmin(const float *q, size_t B, const float *cent,
 cudaError_t launch_neg_dot(const float *q, size_t B, const float *db, size_t n,
                            int d, float *dist, size_t ld, cudaStream_t s);
 
+// OPQ rotation of rows (opq.rs:181-192, 207-222): out[i] = R x[i] with R
+// [d][d] row-major, every output summed from 0.0 in column order with
+// separately rounded products.
+cudaError_t launch_rotate_rows(const float *x, size_t n, int d, const float *rotation,
+                               float *out, cudaStream_t s);
+
 // Per row: the k smallest (value, column) of a row-major [rows][cols]
 // matrix, ascending, ties to the lower column.  Rows with fewer than k
 // columns are padded with id 0xffffffff and +inf.  k <= 256.
@@ -120,6 +126,7 @@ struct ScanParams {
   uint32_t *out_count;           // [nq] real result counts (nullable)
   int *error;                    // set nonzero when a bounded pipeline wait gives up
   float neg_zero;                // -0.0f; kernels take it as a run-time value (see f32x2.cuh)
+  const float *rot_t;            // OPQ rotation transposed, [d][d] (nullable: plain PQ)
 };
 
 // Fused per-query kernel: for each probed list the query residual, the ADC

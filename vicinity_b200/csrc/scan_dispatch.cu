@@ -43,19 +43,20 @@ int pick_gpt(const ScanParams &p) {
 
 cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms, cudaStream_t s) {
   if (p.k < 1 || p.k > 256) return cudaErrorInvalidValue;
-  const int ws = pick_ws_ept(p);
+  // an OPQ rotation is applied by the query-major and 4-bit kernels only
+  const int ws = p.rot_t ? 0 : pick_ws_ept(p);
   if (ws) return launch_scan_ws(p, p.dsub, ws, num_sms, s);
   const int gpt = pick_gpt(p);
-  if (g_family == 2 && gpt && p.ks == 256) return launch_scan_pipe(p, p.dsub, gpt, num_sms, s);
+  if (g_family == 2 && gpt && p.ks == 256 && !p.rot_t) return launch_scan_pipe(p, p.dsub, gpt, num_sms, s);
   if (p.ks == 16) return launch_scan_four(p, gpt ? p.dsub : 0, gpt, num_sms, s);
   return launch_scan_eight(p, gpt ? p.dsub : 0, gpt, num_sms, s);
 }
 
 int ivfpq_scan_variant_name(const ScanParams &p, char *buf, size_t len) {
-  const int ws = pick_ws_ept(p);
+  const int ws = p.rot_t ? 0 : pick_ws_ept(p);
   if (ws) return snprintf(buf, len, "ivfpq_ws_kernel<%d,%d,1,256>", p.dsub, ws);
   const int gpt = pick_gpt(p);
-  if (g_family == 2 && gpt && p.ks == 256) return snprintf(buf, len, "ivfpq_pipe_kernel<%d,%d,1,256>", p.dsub, gpt);
+  if (g_family == 2 && gpt && p.ks == 256 && !p.rot_t) return snprintf(buf, len, "ivfpq_pipe_kernel<%d,%d,1,256>", p.dsub, gpt);
   if (p.ks == 16) return snprintf(buf, len, "ivfpq_four_kernel<%d>", p.k <= 32 ? 1 : p.k <= 64 ? 2 : p.k <= 128 ? 4 : 8);
   return snprintf(buf, len, "ivfpq_query_kernel<%d,%d,%d,%s>", gpt ? p.dsub : 0, gpt,
                   p.k <= 32 ? 1 : p.k <= 64 ? 2 : p.k <= 128 ? 4 : 8, p.ks == 16 ? "4bit" : "8bit");

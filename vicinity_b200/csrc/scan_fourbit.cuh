@@ -33,10 +33,12 @@ constexpr int kFourGroup = 128;  // threads that build one list's table
 __host__ __device__ inline size_t four_float_stride(int M) { return (static_cast<size_t>(M) * 16 + 3) & ~size_t(3); }
 __host__ __device__ inline size_t four_u8_stride(int M) { return (static_cast<size_t>(M) * 16 + 15) & ~size_t(15); }
 
-__host__ __device__ inline size_t four_smem_bytes(int M, int dsub, int R) {
+__host__ __device__ inline size_t four_smem_bytes(int M, int dsub, int R, bool rot = false) {
   const size_t nent = static_cast<size_t>(M) * 16;
+  const size_t dpad = (static_cast<size_t>(M) * dsub + 3) & ~size_t(3);
   return static_cast<size_t>(kScanWarps) * 32 * R * 8 + ((nent * dsub + 3) & ~size_t(3)) * 4 +
-         2 * kMaxBatch * (four_float_stride(M) * 4 + four_u8_stride(M));
+         2 * kMaxBatch * (four_float_stride(M) * 4 + four_u8_stride(M)) +
+         (rot ? kMaxBatch * 2 * dpad * 4 : 0);
 }
 
 template <int OFF>
@@ -83,6 +85,8 @@ __global__ void __launch_bounds__(kScanThreads, 2) ivfpq_four_kernel(const ScanP
   float *cbs = reinterpret_cast<float *>(wl + kScanWarps * 32 * R);                   // [nent][dsub]
   float *flut = cbs + ((static_cast<size_t>(nent) * dsub + 3) & ~size_t(3));          // [2][batch][fstride]
   uint8_t *qlut = reinterpret_cast<uint8_t *>(flut + 2 * kMaxBatch * fstride);        // [2][batch][qstride]
+  const int dpad = (d + 3) & ~3;
+  float *qbuf = reinterpret_cast<float *>(qlut + 2 * kMaxBatch * qstride);           // [batch][2][dpad] (OPQ)
 
   __shared__ uint32_t s_query;
   __shared__ int s_nvalid;
@@ -148,15 +152,32 @@ __global__ void __launch_bounds__(kScanThreads, 2) ivfpq_four_kernel(const ScanP
       if (grp < nb) {
         const float *cent = p.centroids + static_cast<size_t>(s_list[b0 + grp]) * d;
         float *fl = fset + static_cast<size_t>(grp) * fstride;
+        // OPQ: the table is built from the rotated residual R r (opq.rs:115-121),
+        // kept in shared memory; output i is sum_j R[i][j] r_j from 0.0
+        const float *rres = nullptr;
+        if (p.rot_t) {
+          float *res = qbuf + static_cast<size_t>(grp) * 2 * dpad, *rot = res + dpad;
+          for (int j = gt; j < d; j += kFourGroup) res[j] = __fsub_rn(qv[j], cent[j]);
+          named_sync(1 + grp, kFourGroup);
+          for (int r = gt; r < d; r += kFourGroup) {
+            float s = 0.0f;
+            for (int j = 0; j < d; ++j) s = __fadd_rn(s, __fmul_rn(p.rot_t[static_cast<size_t>(j) * d + r], res[j]));
+            rot[r] = s;
+          }
+          named_sync(1 + grp, kFourGroup);
+          rres = rot;
+        }
         float lmin = __int_as_float(0x7f800000), lmax = -__int_as_float(0x7f800000);
         for (int e = gt; e < nent; e += kFourGroup) {
           const int m = e >> 4;
           const float *cw = cbs + static_cast<size_t>(e) * dsub;
-          // residual r_j = q_j - c_j, then sum_j (r_j - cw_j)^2 in j order
-          float diff = __fsub_rn(__fsub_rn(qv[m * dsub], cent[m * dsub]), cw[0]);
+          // residual r_j = q_j - c_j (or its rotation), then sum_j (r_j - cw_j)^2 in j order
+          float rj = rres ? rres[m * dsub] : __fsub_rn(qv[m * dsub], cent[m * dsub]);
+          float diff = __fsub_rn(rj, cw[0]);
           float acc = __fmul_rn(diff, diff);
           for (int j = 1; j < dsub; ++j) {
-            diff = __fsub_rn(__fsub_rn(qv[m * dsub + j], cent[m * dsub + j]), cw[j]);
+            rj = rres ? rres[m * dsub + j] : __fsub_rn(qv[m * dsub + j], cent[m * dsub + j]);
+            diff = __fsub_rn(rj, cw[j]);
             acc = __fadd_rn(acc, __fmul_rn(diff, diff));
           }
           fl[e] = acc;

@@ -44,8 +44,9 @@ __host__ __device__ inline size_t scan_pair_bytes(int d, int M, int ks) {
   return static_cast<size_t>((M * ks + 3) & ~3) * 4 + static_cast<size_t>((d + 3) & ~3) * 4;
 }
 
-__host__ __device__ inline size_t scan_smem_bytes(int d, int M, int ks, int batch, int R) {
-  return static_cast<size_t>(kScanWarps) * 32 * R * 8 + static_cast<size_t>(batch) * scan_pair_bytes(d, M, ks);
+__host__ __device__ inline size_t scan_smem_bytes(int d, int M, int ks, int batch, int R, bool rot = false) {
+  return static_cast<size_t>(kScanWarps) * 32 * R * 8 + static_cast<size_t>(batch) * scan_pair_bytes(d, M, ks) +
+         (rot ? static_cast<size_t>(batch) * ((d + 3) & ~3) * 4 : 0);
 }
 
 template <int R>
@@ -135,6 +136,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
   unsigned long long *wl = reinterpret_cast<unsigned long long *>(smem);  // [warps][32R]
   float *lut = reinterpret_cast<float *>(wl + kScanWarps * 32 * R);       // [batch][tstride]
   float *qres = lut + static_cast<size_t>(batch) * tstride;                // [batch][dpad]
+  float *qrot = qres + static_cast<size_t>(batch) * dpad;                  // [batch][dpad] (OPQ only)
 
   __shared__ uint32_t s_query;
   __shared__ int s_nvalid;
@@ -211,11 +213,26 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
         qres[g * dpad + j] = __fsub_rn(qv[j], p.centroids[static_cast<size_t>(blist[g]) * d + j]);
       }
       __syncthreads();
+      // OPQ: tables are built from the rotated residual R r (opq.rs:115-121);
+      // output i is sum_j R[i][j] r_j from 0.0, read through R^T so that a
+      // warp's loads of one j are contiguous
+      const float *tq = qres;
+      if (p.rot_t) {
+        for (int i = tid; i < nb * d; i += kScanThreads) {
+          const int g = i / d, r = i - g * d;
+          const float *res = qres + g * dpad;
+          float s = 0.0f;
+          for (int j = 0; j < d; ++j) s = __fadd_rn(s, __fmul_rn(p.rot_t[static_cast<size_t>(j) * d + r], res[j]));
+          qrot[g * dpad + r] = s;
+        }
+        __syncthreads();
+        tq = qrot;
+      }
 
       // ---- ADC tables: sequential sum over the subvector, no FMA --------
 #pragma unroll 1
       for (int g = 0; g < nb; ++g) {
-        const float *qg = qres + g * dpad;
+        const float *qg = tq + g * dpad;
         float *lg = lut + static_cast<size_t>(g) * tstride;
         if (DSUB > 0) {
 #pragma unroll
@@ -340,8 +357,8 @@ cudaError_t launch_scan_variant(const ScanParams &p, int num_sms, cudaStream_t s
   if (e != cudaSuccess) return e;
   const size_t reserve = 12288;  // static shared memory of the kernel (8-9 KB)
   int batch = kMaxBatch;
-  while (batch > 1 && scan_smem_bytes(p.d, p.M, p.ks, batch, R) + reserve > static_cast<size_t>(optin)) --batch;
-  const size_t smem = scan_smem_bytes(p.d, p.M, p.ks, batch, R);
+  while (batch > 1 && scan_smem_bytes(p.d, p.M, p.ks, batch, R, p.rot_t != nullptr) + reserve > static_cast<size_t>(optin)) --batch;
+  const size_t smem = scan_smem_bytes(p.d, p.M, p.ks, batch, R, p.rot_t != nullptr);
   if (smem + reserve > static_cast<size_t>(optin)) return cudaErrorInvalidConfiguration;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;

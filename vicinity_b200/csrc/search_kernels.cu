@@ -71,7 +71,7 @@ cudaError_t launch_normalize_rows(const float *x, size_t n, int d, float *out, c
 // ---------------------------------------------------------------------------
 namespace {
 constexpr int kTileM = 128, kTileN = 128, kTileK = 16, kTileThreads = 256;
-enum DotMode { kWriteOneMinus = 0, kArgminOneMinus = 1, kWriteNeg = 2 };
+enum DotMode { kWriteOneMinus = 0, kArgminOneMinus = 1, kWriteNeg = 2, kWriteDot = 3 };
 
 template <int MODE>
 __global__ void __launch_bounds__(kTileThreads)
@@ -169,7 +169,9 @@ __global__ void __launch_bounds__(kTileThreads)
       for (int j = 0; j < 8; ++j) {
         size_t c = col0 + tx * 8 + j;
         if (c < cols)
-          out[r * ld + c] = (MODE == kWriteOneMinus) ? __fsub_rn(1.0f, acc[i][j]) : -acc[i][j];
+          out[r * ld + c] = MODE == kWriteOneMinus ? __fsub_rn(1.0f, acc[i][j])
+                            : MODE == kWriteNeg    ? -acc[i][j]
+                                                   : acc[i][j];
       }
     }
   }
@@ -200,6 +202,12 @@ cudaError_t launch_coarse_argmin(const float *q, size_t B, const float *cent, si
 cudaError_t launch_neg_dot(const float *q, size_t B, const float *db, size_t n, int d, float *dist,
                            size_t ld, cudaStream_t s) {
   return launch_dot<kWriteNeg>(q, B, db, n, d, dist, ld, nullptr, s);
+}
+
+cudaError_t launch_rotate_rows(const float *x, size_t n, int d, const float *rotation, float *out,
+                               cudaStream_t s) {
+  // out[i][r] = sum_j x[i][j] * R[r][j]: the rows of R are the columns of the tile
+  return launch_dot<kWriteDot>(x, n, rotation, static_cast<size_t>(d), d, out, static_cast<size_t>(d), nullptr, s);
 }
 
 // ---------------------------------------------------------------------------

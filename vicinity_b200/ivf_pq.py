@@ -165,8 +165,11 @@ class IVFPQIndex:
         _lib.check(self._lib.vg_ivfpq_add(self._h, _ptr(id_u32), _ptr(x), n))
         self._used_ids.update(id_u32.tolist())
 
-    def set_trained(self, centroids, codebooks) -> None:
-        """Adopt coarse centroids [nc][dim] and PQ codebooks [M][ks][dsub]."""
+    def set_trained(self, centroids, codebooks, rotation=None) -> None:
+        """Adopt coarse centroids [nc][dim] and PQ codebooks [M][ks][dsub]
+        (and, for OPQ, the rotation [dim][dim])."""
+        if rotation is not None:
+            self.set_rotation(rotation)
         c = np.ascontiguousarray(centroids, dtype=np.float32)
         cb = np.ascontiguousarray(codebooks, dtype=np.float32)
         info = self.info()
@@ -176,6 +179,16 @@ class IVFPQIndex:
         if c.ndim != 2 or c.shape[1] != self._dim:
             raise ValueError("centroids must be [num_centroids, dim]")
         _lib.check(self._lib.vg_ivfpq_set_trained(self._h, _ptr(c), c.shape[0], _ptr(cb)))
+
+    def set_rotation(self, rotation) -> None:
+        """OPQ rotation [dim][dim], row-major (opq.rs:31-41); None removes it."""
+        if rotation is None:
+            _lib.check(self._lib.vg_ivfpq_set_rotation(self._h, None))
+            return
+        r = np.ascontiguousarray(rotation, dtype=np.float32)
+        if r.shape != (self._dim, self._dim):
+            raise ValueError(f"rotation must be [{self._dim}, {self._dim}]")
+        _lib.check(self._lib.vg_ivfpq_set_rotation(self._h, _ptr(r)))
 
     def build(self, training_sample_size: int | None = None, kmeans_max_iter: int = 100) -> None:
         """src/python.rs:622-637 (build_with_training_options)."""
@@ -272,6 +285,13 @@ class IVFPQIndex:
         return self._export(
             _lib.EXPORT_CODEBOOKS, np.float32, (i.num_codebooks, i.codebook_size, i.subvector_dim)
         )
+
+    def rotation(self) -> np.ndarray | None:
+        """OPQ rotation [dim][dim] (None for plain PQ)."""
+        try:
+            return self._export(_lib.EXPORT_ROTATION, np.float32, (self._dim, self._dim))
+        except ValueError:
+            return None
 
     def assignments(self) -> np.ndarray:
         return self._export(_lib.EXPORT_ASSIGNMENTS, np.uint32, (len(self),))
