@@ -149,6 +149,28 @@ int vg_ivfpq_search_batch_reranked(vg_index *ix, const float *queries,
                                    size_t nprobe, uint32_t *out_ids,
                                    float *out_dist, uint32_t *out_count);
 
+/* src/ivf_pq/search.rs:414-434 (with_filtering): enable metadata filtering
+ * on `field` (before build).  Builds then record, per inverted list, the
+ * bitmask of the field's categories among its vectors. */
+int vg_ivfpq_set_filter_field(vg_index *ix, const char *field);
+
+/* src/ivf_pq/search.rs:436-475 (add_metadata): metadata of a document as a
+ * JSON object in the reference's serde form, e.g.
+ * {"category": {"Int": 3}, "label": {"Str": "x"}}; the filter field's value
+ * must be an Int in 0..63.  Replaces earlier metadata of doc_id.  Unsupported
+ * unless filtering is enabled. */
+int vg_ivfpq_add_metadata(vg_index *ix, uint32_t doc_id, const char *metadata_json);
+
+/* src/ivf_pq/search.rs:1407-1549 (search_with_filter) over nq rows with the
+ * equality filter field == value (value_json in serde form, {"Int": 3}):
+ * the nprobe nearest lists whose bitmask holds the category, then every list
+ * when they hold fewer than k matching documents.  Outputs as
+ * vg_ivfpq_search_batch.  Unsupported on a sharded index. */
+int vg_ivfpq_search_filtered_batch(vg_index *ix, const float *queries,
+                                   size_t nq, size_t k, const char *field,
+                                   const char *value_json, uint32_t *out_ids,
+                                   float *out_dist, uint32_t *out_count);
+
 /* src/ivf_pq/search.rs:857-884 (reconstruct) of insertion index idx. */
 int vg_ivfpq_reconstruct(const vg_index *ix, size_t idx, float *out);
 

@@ -42,6 +42,8 @@ _SIGS = {
     "or_index_adopt_codes": (_i, [_vp, _vp, _vp]),
     "or_index_set_nprobe": (None, [_vp, _sz]),
     "or_index_set_rotation": (None, [_vp, _vp]),
+    "or_index_set_filter": (_i, [_vp, _vp, _vp]),
+    "or_index_search_filtered_batch": (_i, [_vp, _vp, _sz, _sz, _i, _i, _vp, _vp, _vp]),
     "or_rotate": (None, [_vp, _vp, _sz, _vp]),
     "or_rotate_t": (None, [_vp, _vp, _sz, _vp]),
     "or_index_num_vectors": (_sz, [_vp]),
@@ -248,6 +250,27 @@ class OracleIndex:
         a = np.ascontiguousarray(assignments, dtype=np.uint32)
         c = np.ascontiguousarray(codes, dtype=np.uint8)
         assert self._lib.or_index_adopt_codes(self._h, _p(a), _p(c)) == 0
+
+    def set_filter(self, category, bitmask=None):
+        """Per-vector filter categories (255: none) and per-list bitmasks
+        (None: from the categories, as at build); call after finalize."""
+        self._cat = np.ascontiguousarray(category, dtype=np.uint8)
+        self._mask = None if bitmask is None else np.ascontiguousarray(bitmask, dtype=np.uint64)
+        st = self._lib.or_index_set_filter(self._h, _p(self._cat), None if self._mask is None else _p(self._mask))
+        if st:
+            raise RuntimeError(f"or_index_set_filter failed ({st})")
+
+    def search_filtered_batch(self, queries, k: int, want: int, threads: int = 1):
+        q = f32(queries)
+        nq = q.shape[0]
+        ids = np.empty((nq, k), np.uint32)
+        dists = np.empty((nq, k), np.float32)
+        counts = np.empty(nq, np.uint32)
+        st = self._lib.or_index_search_filtered_batch(self._h, _p(q), nq, k, want, threads, _p(ids), _p(dists),
+                                                      _p(counts))
+        if st:
+            raise RuntimeError(f"or_index_search_filtered_batch failed ({st})")
+        return ids, dists, counts
 
     def set_rotation(self, rotation):
         """OPQ rotation [d][d] (None clears); set before finalize/adopt."""

@@ -367,6 +367,8 @@ struct or_index {
   std::vector<std::vector<uint8_t>> adc_codes;  // list order, |l| >= 16
   std::vector<std::vector<uint8_t>> packed;     // 4-bit blocks, |l| >= 16
   std::vector<float> rotation;  // OPQ rotation [d][d] row-major (empty: plain PQ)
+  std::vector<uint8_t> category;   // filter category per vector (255: none)
+  std::vector<uint64_t> bitmask;   // filter categories per list (at build)
 };
 
 namespace {
@@ -449,6 +451,43 @@ void search_one(const or_index *ix, const float *qn, size_t k, size_t nprobe,
         out.push_back(make_cand(
             id, or_distance_with_table(table.data(), ix->M, ix->ks, &ix->codes[id * ix->M])));
     }
+  }
+  finish_top_k(out, k);
+}
+
+// search.rs:1407-1549 (search_with_filter) for one normalised query.
+void search_filtered_one(const or_index *ix, const float *qn, size_t k, int want,
+                         std::vector<Cand> &out) {
+  out.clear();
+  const uint64_t bit = uint64_t(1) << want;
+  size_t p = std::min(ix->nprobe, ix->L);
+  std::vector<uint32_t> order(p);
+  std::vector<float> pdist(p);
+  p = or_find_nearest_centroids(qn, ix->d, ix->centroids.data(), ix->L, p, order.data(), pdist.data());
+  order.resize(p);
+  std::vector<bool> scanned(ix->L, false);
+  std::vector<float> qres(ix->d), qrot(ix->d), table(ix->M * ix->ks);
+  for (;;) {
+    for (uint32_t l : order) {
+      if (scanned[l]) continue;
+      scanned[l] = true;
+      if ((ix->bitmask[l] & bit) == 0) continue;  // 1502-1505
+      const float *c = &ix->centroids[static_cast<size_t>(l) * ix->d];
+      for (size_t j = 0; j < ix->d; ++j) qres[j] = qn[j] - c[j];
+      const float *tq = qres.data();
+      if (!ix->rotation.empty()) {
+        rotate(ix->rotation.data(), qres.data(), ix->d, qrot.data());
+        tq = qrot.data();
+      }
+      or_adc_table(tq, ix->d, ix->M, ix->ks, ix->codebooks.data(), table.data());
+      for (uint32_t id : ix->lists[l])  // 1512-1530: matching documents, float table
+        if (ix->category[id] == static_cast<uint8_t>(want))
+          out.push_back(make_cand(
+              id, or_distance_with_table(table.data(), ix->M, ix->ks, &ix->codes[id * ix->M])));
+    }
+    if (out.size() >= k || order.size() == ix->L) break;  // 1539-1546: widen once
+    order.resize(ix->L);
+    for (size_t l = 0; l < ix->L; ++l) order[l] = static_cast<uint32_t>(l);
   }
   finish_top_k(out, k);
 }
@@ -539,6 +578,35 @@ void or_index_set_nprobe(or_index *ix, size_t nprobe) { ix->nprobe = nprobe; }
 
 void or_rotate(const float *r, const float *v, size_t d, float *out) { rotate(r, v, d, out); }
 void or_rotate_t(const float *r, const float *v, size_t d, float *out) { rotate_t(r, v, d, out); }
+
+int or_index_set_filter(or_index *ix, const uint8_t *category, const uint64_t *bitmask) {
+  const size_t n = ix->doc_ids.size();
+  ix->category.assign(category, category + n);
+  if (bitmask) {
+    ix->bitmask.assign(bitmask, bitmask + ix->L);
+  } else {  // search.rs:626-651: categories of each list's vectors
+    if (!ix->built) return -4;
+    ix->bitmask.assign(ix->L, 0);
+    for (size_t i = 0; i < n; ++i)
+      if (ix->category[i] < 64) ix->bitmask[ix->assign[i]] |= uint64_t(1) << ix->category[i];
+  }
+  return 0;
+}
+
+int or_index_search_filtered_batch(const or_index *ix, const float *queries, size_t nq, size_t k,
+                                   int want, int threads, uint32_t *out_ids, float *out_dists,
+                                   uint32_t *out_count) {
+  if (!ix->built) return -4;
+  if (want < 0 || want >= 64 || ix->category.size() != ix->doc_ids.size()) return -2;
+  parallel_for(nq, threads, [&](size_t qi) {
+    std::vector<float> qn(ix->d);
+    or_normalize(queries + qi * ix->d, 1, ix->d, qn.data());
+    std::vector<Cand> res;
+    search_filtered_one(ix, qn.data(), k, want, res);
+    write_row(ix, res, k, qi, out_ids, out_dists, out_count);
+  });
+  return 0;
+}
 
 void or_index_set_rotation(or_index *ix, const float *rotation) {
   if (rotation) ix->rotation.assign(rotation, rotation + ix->d * ix->d);

@@ -128,6 +128,16 @@ int or_index_adopt_codes(or_index *ix, const uint32_t *assignments,
                          const uint8_t *codes);
 
 void or_index_set_nprobe(or_index *ix, size_t nprobe);
+/* Filter state of search.rs:1407-1549: category [n] per vector (255: none)
+ * and bitmask [L] per list (NULL: computed from the categories as
+ * search.rs:626-651 does at build).  Call after finalize. */
+int or_index_set_filter(or_index *ix, const uint8_t *category, const uint64_t *bitmask);
+
+/* search.rs:1407-1549 (search_with_filter) for category `want` (0..63). */
+int or_index_search_filtered_batch(const or_index *ix, const float *queries, size_t nq,
+                                   size_t k, int want, int threads, uint32_t *out_ids,
+                                   float *out_dists, uint32_t *out_count);
+
 /* opq.rs:181-192 (matrix_vector_multiply) and 194-205 (transpose): out = R v
  * and out = R^T v with R [d][d] row-major, each output summed from 0.0. */
 void or_rotate(const float *r, const float *v, size_t d, float *out);

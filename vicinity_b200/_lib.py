@@ -121,6 +121,9 @@ SIGNATURES = {
     "vg_ivfpq_get_info": (_i, [_vp, C.POINTER(VgInfo)]),
     "vg_ivfpq_search_batch": (_i, [_vp, _vp, _sz, _sz, _sz, _vp, _vp, _vp]),
     "vg_ivfpq_search_batch_reranked": (_i, [_vp, _vp, _sz, _sz, _sz, _sz, _vp, _vp, _vp]),
+    "vg_ivfpq_set_filter_field": (_i, [_vp, C.c_char_p]),
+    "vg_ivfpq_add_metadata": (_i, [_vp, C.c_uint32, C.c_char_p]),
+    "vg_ivfpq_search_filtered_batch": (_i, [_vp, _vp, _sz, _sz, C.c_char_p, C.c_char_p, _vp, _vp, _vp]),
     "vg_ivfpq_reconstruct": (_i, [_vp, _sz, _vp]),
     "vg_ivfpq_compact": (_i, [_vp]),
     "vg_ivfpq_export": (_i, [_vp, _i, _vp, _sz]),

@@ -24,7 +24,9 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <unordered_map>
 #include <numeric>
 #include <string>
 #include <thread>
@@ -182,8 +184,11 @@ struct vg_index {
   // bitmask of the filter categories present
   bool has_filter_field = false;
   std::string filter_field;
-  std::vector<std::pair<uint32_t, std::string>> metadata;
-  std::vector<uint64_t> h_bitmask;
+  std::map<uint32_t, std::string> metadata;      // doc id -> metadata object (serde JSON)
+  std::unordered_map<uint32_t, int> doc_category;  // doc id -> filter category 0..63 (-1: none)
+  std::vector<uint64_t> h_bitmask;                 // [num_clusters], fixed at build
+  DevBuf category_d, bitmask_d, cat_counts;        // [n] u8, [num_clusters] u64, [Lc][64] u32
+  bool cat_dirty = true;                           // categories changed since the last upload
 
   // sharding
   int rank = 0, world = 1;
@@ -208,7 +213,7 @@ struct vg_index {
   size_t device_bytes() const {
     return vectors.cap + doc_ids.cap + centroids.cap + codebooks.cap + assign.cap + codes.cap +
            list_off.cap + list_ids.cap + code_off.cap + list_codes.cap + pack_off.cap + packed.cap +
-           owner.cap + rotation.cap + rotation_t.cap;
+           owner.cap + rotation.cap + rotation_t.cap + category_d.cap + bitmask_d.cap + cat_counts.cap;
   }
 };
 
@@ -808,6 +813,174 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   return VG_OK;
 }
 
+// ---- filtered search (search.rs:1407-1549) --------------------------------
+
+// Device per-vector categories and per-list category counts from the current
+// metadata (metadata may change after build; list bitmasks do not).
+int refresh_categories(vg_index *ix) {
+  if (!ix->cat_dirty) return VG_OK;
+  cudaStream_t s = ix->stream;
+  const size_t n = ix->n, Lc = ix->num_centroids;
+  std::vector<uint8_t> cat(n, 0xff);
+  for (size_t i = 0; i < n; ++i) {
+    auto it = ix->doc_category.find(ix->h_doc_ids[i]);
+    if (it != ix->doc_category.end() && it->second >= 0) cat[i] = static_cast<uint8_t>(it->second);
+  }
+  VG_CU(ix->category_d.reserve(std::max<size_t>(n, 1)));
+  VG_CU(ix->cat_counts.reserve(Lc * 64 * 4));
+  VG_CU(cudaMemcpyAsync(ix->category_d.p, cat.data(), n, cudaMemcpyHostToDevice, s));
+  VG_CU(cudaMemsetAsync(ix->cat_counts.p, 0, Lc * 64 * 4, s));
+  VG_CU(launch_category_counts(ix->category_d.as<uint8_t>(), ix->assign.as<uint32_t>(), n,
+                               ix->cat_counts.as<uint32_t>(), s));
+  VG_CU(cudaStreamSynchronize(s));
+  ix->cat_dirty = false;
+  return VG_OK;
+}
+
+// Per-list category bitmasks at build time (search.rs:626-651).
+int build_filter_bitmasks(vg_index *ix) {
+  const size_t n = ix->n, L = ix->params.num_clusters;
+  std::vector<uint32_t> assign(n);
+  VG_CU(cudaMemcpy(assign.data(), ix->assign.p, n * 4, cudaMemcpyDeviceToHost));
+  ix->h_bitmask.assign(L, 0);
+  for (size_t i = 0; i < n; ++i) {
+    auto it = ix->doc_category.find(ix->h_doc_ids[i]);
+    if (it != ix->doc_category.end() && it->second >= 0) ix->h_bitmask[assign[i]] |= uint64_t(1) << it->second;
+  }
+  VG_CU(ix->bitmask_d.reserve(L * 8));
+  VG_CU(cudaMemcpy(ix->bitmask_d.p, ix->h_bitmask.data(), L * 8, cudaMemcpyHostToDevice));
+  ix->cat_dirty = true;
+  return VG_OK;
+}
+
+int search_filtered_impl(vg_index *ix, const float *queries, size_t nq, size_t k, const char *field,
+                         const char *value_json, uint32_t *out_ids, float *out_dist, uint32_t *out_count) {
+  if (!ix->built) return fail(VG_ERR_NOT_BUILT, "IVF-PQ index is not built: cannot search");
+  if (!field) return fail(VG_ERR_INVALID_PARAMETER, "null filter field");
+  if (!ix->has_filter_field || ix->filter_field != field)  // search.rs:1428-1435
+    return fail(VG_ERR_INVALID_PARAMETER,
+                std::string("filter field '") + field + "' doesn't match index filter field '" +
+                    (ix->has_filter_field ? "Some(\"" + ix->filter_field + "\")" : std::string("None")) + "'");
+  int want = -1;
+  VG_TRY(parse_filter_category(value_json, &want));
+  if (k > 256) return fail(VG_ERR_INVALID_PARAMETER, "k must be at most 256");
+  if (ix->world > 1) return fail(VG_ERR_UNSUPPORTED, "unsupported: filtered search on a sharded index");
+  if (nq == 0 || k == 0) return write_padding(ix, nq, k, out_ids, out_dist, out_count);
+  if (!queries || !out_ids || !out_dist) return fail(VG_ERR_INVALID_PARAMETER, "null query or output buffer");
+  const size_t Lc = ix->num_centroids, d = ix->d;
+  const size_t P = std::min(static_cast<size_t>(ix->params.nprobe), Lc);
+  if (P == 0) return write_padding(ix, nq, k, out_ids, out_dist, out_count);
+  if (nq * std::max(P, Lc) > 0xffffffffull) return fail(VG_ERR_INVALID_PARAMETER, "too many queries in one call");
+  VG_TRY(refresh_categories(ix));
+  cudaStream_t s = ix->stream;
+
+  // normalise, coarse distances and the nprobe nearest lists (search.rs:1460-1471)
+  const float *dq = queries;
+  if (!is_device_ptr(queries)) {
+    VG_CU(ix->ws_q.reserve(nq * d * 4));
+    VG_CU(cudaMemcpyAsync(ix->ws_q.p, queries, nq * d * 4, cudaMemcpyHostToDevice, s));
+    dq = ix->ws_q.as<float>();
+  }
+  VG_CU(ix->ws_qn.reserve(nq * d * 4));
+  VG_CU(launch_normalize_rows(dq, nq, static_cast<int>(d), ix->ws_qn.as<float>(), s));
+  const size_t tile = std::max<size_t>(1, std::min(nq, kDistBudgetBytes / (Lc * 4)));
+  VG_CU(ix->ws_dist.reserve(tile * Lc * 4));
+  VG_CU(ix->ws_probes.reserve(nq * P * 4));
+  VG_CU(ix->ws_pdist.reserve(nq * P * 4));
+  for (size_t r0 = 0; r0 < nq; r0 += tile) {
+    const size_t rows = std::min(tile, nq - r0);
+    VG_CU(launch_coarse_dist(ix->ws_qn.as<float>() + r0 * d, rows, ix->centroids.as<float>(), Lc,
+                             static_cast<int>(d), ix->ws_dist.as<float>(), Lc, s));
+    VG_CU(launch_select_rows(ix->ws_dist.as<float>(), rows, Lc, Lc, static_cast<int>(P),
+                             ix->ws_probes.as<uint32_t>() + r0 * P, ix->ws_pdist.as<float>() + r0 * P, P, 0, s));
+  }
+
+  // which queries find fewer than k matches in their probed lists
+  std::vector<uint8_t> widen(nq, 0);
+  if (P < Lc) {
+    VG_CU(ix->ws_scalars.reserve(std::max<size_t>(64, nq)));
+    VG_CU(launch_filter_widen(ix->ws_probes.as<uint32_t>(), nq, static_cast<int>(P), ix->bitmask_d.as<uint64_t>(),
+                              ix->cat_counts.as<uint32_t>(), want, k, ix->ws_scalars.as<uint8_t>(), s));
+    VG_CU(cudaMemcpyAsync(widen.data(), ix->ws_scalars.p, nq, cudaMemcpyDeviceToHost, s));
+    VG_CU(cudaStreamSynchronize(s));
+  }
+  std::vector<uint32_t> narrow_q, wide_q;
+  for (size_t q = 0; q < nq; ++q) (widen[q] ? wide_q : narrow_q).push_back(static_cast<uint32_t>(q));
+
+  const bool dev_out = is_device_ptr(out_ids) && is_device_ptr(out_dist) && (!out_count || is_device_ptr(out_count));
+  uint32_t *o_ids = out_ids, *o_cnt = out_count;
+  float *o_dist = out_dist;
+  if (!dev_out) {
+    VG_CU(ix->ws_out_ids.reserve(nq * k * 4));
+    VG_CU(ix->ws_out_dist.reserve(nq * k * 4));
+    VG_CU(ix->ws_out_count.reserve(nq * 4));
+    o_ids = ix->ws_out_ids.as<uint32_t>();
+    o_dist = ix->ws_out_dist.as<float>();
+    o_cnt = ix->ws_out_count.as<uint32_t>();
+  }
+  DevBuf qmap, all_lists, counter, cnt_tmp;
+  VG_CU(qmap.reserve(nq * 4));
+  VG_CU(counter.reserve(16));
+  if (!o_cnt) {
+    VG_CU(cnt_tmp.reserve(nq * 4));
+    o_cnt = cnt_tmp.as<uint32_t>();
+  }
+  vg::ScanParams sp{};
+  sp.qn = ix->ws_qn.as<float>();
+  sp.centroids = ix->centroids.as<float>();
+  sp.codebooks = ix->codebooks.as<float>();
+  sp.counter = counter.as<uint32_t>();
+  sp.list_off = ix->list_off.as<uint64_t>();
+  sp.code_off = ix->code_off.as<uint64_t>();
+  sp.list_codes = ix->list_codes.as<uint8_t>();
+  sp.list_ids = ix->list_ids.as<uint32_t>();
+  sp.doc_ids = ix->doc_ids.as<uint32_t>();
+  sp.rot_t = ix->h_rotation.empty() ? nullptr : ix->rotation_t.as<float>();
+  sp.d = static_cast<int>(d);
+  sp.M = static_cast<int>(ix->params.num_codebooks);
+  sp.ks = static_cast<int>(ix->params.codebook_size);
+  sp.dsub = static_cast<int>(ix->dsub);
+  sp.k = static_cast<int>(k);
+  sp.out_ids = o_ids;
+  sp.out_dist = o_dist;
+  sp.out_count = o_cnt;
+  sp.error = ix->d_err;
+  sp.qmap = qmap.as<uint32_t>();
+  sp.category = ix->category_d.as<uint8_t>();
+  sp.bitmask = ix->bitmask_d.as<uint64_t>();
+  sp.want_cat = want;
+  // every list scored with the float table, as distance_with_table does
+  // (search.rs:1523-1528), also for 16-entry codebooks
+  auto run = [&](const std::vector<uint32_t> &qs, const uint32_t *probes, int np, int shared) -> int {
+    if (qs.empty()) return VG_OK;
+    VG_CU(cudaMemcpyAsync(qmap.p, qs.data(), qs.size() * 4, cudaMemcpyHostToDevice, s));
+    VG_CU(cudaMemsetAsync(counter.p, 0, 4, s));
+    sp.probes = probes;
+    sp.P = np;
+    sp.probes_shared = shared;
+    sp.nq = static_cast<int>(qs.size());
+    VG_CU(launch_ivfpq_scan_generic(sp, ix->num_sms, s));
+    VG_CU(cudaStreamSynchronize(s));
+    ix->launches += 1;
+    return VG_OK;
+  };
+  VG_TRY(run(narrow_q, ix->ws_probes.as<uint32_t>(), static_cast<int>(P), 0));
+  if (!wide_q.empty()) {  // widen: every list, nearest-first order is immaterial to the top-k
+    std::vector<uint32_t> iota(Lc);
+    std::iota(iota.begin(), iota.end(), 0u);
+    VG_CU(all_lists.reserve(Lc * 4));
+    VG_CU(cudaMemcpyAsync(all_lists.p, iota.data(), Lc * 4, cudaMemcpyHostToDevice, s));
+    VG_TRY(run(wide_q, all_lists.as<uint32_t>(), static_cast<int>(Lc), 1));
+  }
+  if (!dev_out) {
+    VG_CU(cudaMemcpyAsync(out_ids, o_ids, nq * k * 4, cudaMemcpyDeviceToHost, s));
+    VG_CU(cudaMemcpyAsync(out_dist, o_dist, nq * k * 4, cudaMemcpyDeviceToHost, s));
+    if (out_count) VG_CU(cudaMemcpyAsync(out_count, o_cnt, nq * 4, cudaMemcpyDeviceToHost, s));
+  }
+  VG_TRY(sync_stream(ix));
+  return VG_OK;
+}
+
 }  // namespace
 
 namespace vg {
@@ -850,7 +1023,7 @@ int snapshot_export(const vg_index *ix, SnapshotState &st) {
   }
   st.has_filter_field = ix->has_filter_field;
   st.filter_field = ix->filter_field;
-  st.metadata = ix->metadata;
+  st.metadata.assign(ix->metadata.begin(), ix->metadata.end());
   return VG_OK;
 }
 
@@ -918,7 +1091,19 @@ int snapshot_adopt(vg_index *ix, SnapshotState &st) {
   ix->compacted = st.vectors.empty();
   ix->has_filter_field = st.has_filter_field;
   ix->filter_field = std::move(st.filter_field);
-  ix->metadata = std::move(st.metadata);
+  for (auto &e : st.metadata) {
+    int cat = -1;
+    std::string canon;
+    if (parse_metadata(e.second.c_str(), ix->filter_field, &cat, &canon) != VG_OK)
+      return fail(VG_ERR_FORMAT, "IVF-PQ snapshot: metadata of document " + std::to_string(e.first) + ": " + g_last_error);
+    ix->metadata[e.first] = std::move(canon);
+    ix->doc_category[e.first] = cat;
+  }
+  if (ix->has_filter_field) {
+    VG_CU(ix->bitmask_d.reserve(ix->h_bitmask.size() * 8));
+    VG_CU(cudaMemcpy(ix->bitmask_d.p, ix->h_bitmask.data(), ix->h_bitmask.size() * 8, cudaMemcpyHostToDevice));
+  }
+  ix->cat_dirty = true;
   ix->trained = true;
   VG_TRY(build_list_storage(ix, d_sorted.as<uint32_t>()));
   return VG_OK;
@@ -1103,7 +1288,39 @@ int vg_ivfpq_build(vg_index *ix, size_t training_sample_size, size_t kmeans_max_
                                               std::to_string(min_train) + ")");
   DeviceGuard g(ix->device);
   if (!ix->trained) VG_TRY(train(ix, n_train, kmeans_max_iter));
-  return encode_and_layout(ix);
+  VG_TRY(encode_and_layout(ix));
+  if (ix->has_filter_field) VG_TRY(build_filter_bitmasks(ix));
+  return VG_OK;
+}
+
+int vg_ivfpq_set_filter_field(vg_index *ix, const char *field) {
+  if (!ix || !field) return fail(VG_ERR_INVALID_PARAMETER, "null index or field");
+  if (ix->built) return fail(VG_ERR_ALREADY_BUILT, "IVF-PQ index is already built: cannot enable filtering");
+  ix->has_filter_field = true;
+  ix->filter_field = field;
+  return VG_OK;
+}
+
+int vg_ivfpq_add_metadata(vg_index *ix, uint32_t doc_id, const char *metadata_json) {
+  if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
+  if (!ix->has_filter_field)  // search.rs:469-474
+    return fail(VG_ERR_UNSUPPORTED,
+                "unsupported: filtered search; rebuild the index with IVFPQIndex::with_filtering()");
+  int cat = -1;
+  std::string canon;
+  VG_TRY(parse_metadata(metadata_json, ix->filter_field, &cat, &canon));
+  ix->metadata[doc_id] = std::move(canon);  // MetadataStore::add replaces (filtering/mod.rs:206-208)
+  ix->doc_category[doc_id] = cat;
+  ix->cat_dirty = true;
+  return VG_OK;
+}
+
+int vg_ivfpq_search_filtered_batch(vg_index *ix, const float *queries, size_t nq, size_t k, const char *field,
+                                   const char *value_json, uint32_t *out_ids, float *out_dist,
+                                   uint32_t *out_count) {
+  if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
+  DeviceGuard g(ix->device);
+  return search_filtered_impl(ix, queries, nq, k, field, value_json, out_ids, out_dist, out_count);
 }
 
 int vg_ivfpq_set_nprobe(vg_index *ix, size_t nprobe) {

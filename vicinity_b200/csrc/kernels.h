@@ -99,6 +99,18 @@ cudaError_t launch_rerank(const float *qn, const float *vectors, int d,
                           int k, const uint32_t *ids_map, uint32_t *out_ids,
                           float *out_dist, uint32_t *out_count, cudaStream_t s);
 
+// Filtered search (search.rs:1407-1549): counts[l * 64 + c] = number of
+// vectors of list l (assign) with category c (< 64).  counts must be zeroed.
+cudaError_t launch_category_counts(const uint8_t *category, const uint32_t *assign, size_t n,
+                                   uint32_t *counts, cudaStream_t s);
+
+// widen[q] = 1 when the lists query q probes (probes [nq][P]) that carry
+// category want hold fewer than k vectors of that category: the reference
+// then scans every remaining list (search.rs:1489-1547).
+cudaError_t launch_filter_widen(const uint32_t *probes, size_t nq, int P, const uint64_t *bitmask,
+                                const uint32_t *counts, int want, size_t k, uint8_t *widen,
+                                cudaStream_t s);
+
 // Number of positions where a[i] != b[i] added to *changed.
 cudaError_t launch_count_diff_u8(const uint8_t *a, const uint8_t *b, size_t n,
                                  unsigned int *changed, cudaStream_t s);
@@ -127,6 +139,12 @@ struct ScanParams {
   int *error;                    // set nonzero when a bounded pipeline wait gives up
   float neg_zero;                // -0.0f; kernels take it as a run-time value (see f32x2.cuh)
   const float *rot_t;            // OPQ rotation transposed, [d][d] (nullable: plain PQ)
+  // filtered search (query-major kernel only; zero-initialised = off):
+  const uint32_t *qmap;          // work item -> query row (nullable: identity)
+  int probes_shared;             // nonzero: every query reads probe row 0 (P entries)
+  const uint8_t *category;       // [n] filter category per vector id, 255 = none (nullable: no filter)
+  const uint64_t *bitmask;       // [L] categories present per list (at build)
+  int want_cat;                  // category to keep, 0..63
 };
 
 // Fused per-query kernel: for each probed list the query residual, the ADC
@@ -134,6 +152,10 @@ struct ScanParams {
 // FastScan), with the query's top-k kept on chip.
 cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms,
                               cudaStream_t s);
+
+// The query-major kernel for any shape: the path of filtered search, whose
+// probe lists, query map and filter only that kernel reads.
+cudaError_t launch_ivfpq_scan_generic(const ScanParams &p, int num_sms, cudaStream_t s);
 
 // Name of the kernel variant launch_ivfpq_scan would run for p.
 int ivfpq_scan_variant_name(const ScanParams &p, char *buf, size_t len);

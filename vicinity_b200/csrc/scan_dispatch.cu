@@ -52,6 +52,12 @@ cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms, cudaStream_t s) 
   return launch_scan_eight(p, gpt ? p.dsub : 0, gpt, num_sms, s);
 }
 
+cudaError_t launch_ivfpq_scan_generic(const ScanParams &p, int num_sms, cudaStream_t s) {
+  if (p.k < 1 || p.k > 256) return cudaErrorInvalidValue;
+  const int gpt = p.ks == 256 ? pick_gpt(p) : 0;
+  return launch_scan_eight(p, gpt ? p.dsub : 0, gpt, num_sms, s);
+}
+
 int ivfpq_scan_variant_name(const ScanParams &p, char *buf, size_t len) {
   const int ws = p.rot_t ? 0 : pick_ws_ept(p);
   if (ws) return snprintf(buf, len, "ivfpq_ws_kernel<%d,%d,1,256>", p.dsub, ws);

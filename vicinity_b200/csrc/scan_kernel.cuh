@@ -170,19 +170,24 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
       s_bound = kEmptyKey;
     }
     __syncthreads();
-    const uint32_t q = s_query;
-    if (q >= static_cast<uint32_t>(p.nq)) break;
+    if (s_query >= static_cast<uint32_t>(p.nq)) break;
+    const uint32_t q = p.qmap ? p.qmap[s_query] : s_query;
     const float *qv = p.qn + static_cast<size_t>(q) * d;
+    const uint32_t *prow = p.probes + (p.probes_shared ? 0 : static_cast<size_t>(q) * P);
     WarpTopK<R> tk;
     tk.init();
 
-    // probe metadata of the query, compacted to valid owned lists in order
+    // probe lists in chunks of one per thread (P may exceed the block size)
+    for (int pc = 0; pc < P; pc += kScanThreads) {
+    // probe metadata of the chunk, compacted to valid owned lists in order;
+    // a filter also drops lists without its category (search.rs:1502-1505)
     {
       uint32_t l = 0xffffffffu;
       bool valid = false;
-      if (tid < P) {
-        l = p.probes[static_cast<size_t>(q) * P + tid];
-        valid = l != 0xffffffffu && (!p.owner || p.owner[l]);
+      if (pc + tid < P) {
+        l = prow[pc + tid];
+        valid = l != 0xffffffffu && (!p.owner || p.owner[l]) &&
+                (!p.category || ((p.bitmask[l] >> p.want_cat) & 1ull));
       }
       const unsigned vm = __ballot_sync(VG_FULL_MASK, valid);
       if (lane == 0) s_wcount[warp] = __popc(vm);
@@ -276,23 +281,31 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
         const uint32_t x = x0 + lane;
         float dist = 0.0f;
         int g = 0;
-        uint32_t c = 0;
-        if (x < ctotal) {
+        uint32_t c = 0, vid = 0;
+        bool live = x < ctotal;
+        if (live) {
           g = (x >= pre1) + (x >= pre2) + (x >= pre3);
           const uint32_t lo = g == 0 ? 0u : g == 1 ? pre1 : g == 2 ? pre2 : pre3;
           c = x - lo;
-          const uint32_t list = blist[g];
-          const uint8_t *cp = p.list_codes + p.code_off[list] + static_cast<uint64_t>(c) * M;
-          dist = adc_row_sum<KS>(cp, lut + static_cast<size_t>(g) * tstride, M, ks);
+          if (p.category) {  // only documents whose metadata matches (search.rs:1515-1520)
+            vid = p.list_ids[s_lbeg[b0 + g] + c];
+            live = p.category[vid] == static_cast<uint8_t>(p.want_cat);
+          }
+          if (live) {
+            const uint32_t list = blist[g];
+            const uint8_t *cp = p.list_codes + p.code_off[list] + static_cast<uint64_t>(c) * M;
+            dist = adc_row_sum<KS>(cp, lut + static_cast<size_t>(g) * tstride, M, ks);
+          }
         }
         uint64_t thr = tk.worst();
         const uint64_t bound = s_bound;
         thr = bound < thr ? bound : thr;
         const uint32_t dk = order_key(dist);
-        const bool pass = x < ctotal && dk <= static_cast<uint32_t>(thr >> 32);
+        const bool pass = live && dk <= static_cast<uint32_t>(thr >> 32);
         unsigned mask = __ballot_sync(VG_FULL_MASK, pass);
         if (!mask) continue;
-        const uint64_t key = pass ? ((static_cast<uint64_t>(dk) << 32) | p.list_ids[s_lbeg[b0 + g] + c]) : kEmptyKey;
+        const uint64_t key =
+            pass ? ((static_cast<uint64_t>(dk) << 32) | (p.category ? vid : p.list_ids[s_lbeg[b0 + g] + c])) : kEmptyKey;
         if (__popc(mask) > 4) {
           tk.add(key < thr ? key : kEmptyKey);
         } else {
@@ -308,6 +321,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
       }
       __syncthreads();  // tables and batch metadata are rewritten next
     }
+    }  // probe chunks
 
     // ---- merge the warp lists (binary tree) and emit -----------------------
 #pragma unroll

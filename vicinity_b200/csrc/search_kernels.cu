@@ -507,6 +507,47 @@ cudaError_t launch_merge_shards(const unsigned long long *keys, int G, size_t ro
 }
 
 // ---------------------------------------------------------------------------
+// Filtered search helpers.
+// ---------------------------------------------------------------------------
+namespace {
+__global__ void category_counts_kernel(const uint8_t *__restrict__ category, const uint32_t *__restrict__ assign,
+                                       size_t n, uint32_t *counts) {
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint8_t c = category[i];
+  if (c < 64) atomicAdd(counts + static_cast<size_t>(assign[i]) * 64 + c, 1u);
+}
+
+__global__ void filter_widen_kernel(const uint32_t *__restrict__ probes, size_t nq, int P,
+                                    const uint64_t *__restrict__ bitmask, const uint32_t *__restrict__ counts,
+                                    int want, size_t k, uint8_t *__restrict__ widen) {
+  const size_t q = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  uint64_t found = 0;
+  for (int i = 0; i < P; ++i) {
+    const uint32_t l = probes[q * P + i];
+    if (l != 0xffffffffu && ((bitmask[l] >> want) & 1ull)) found += counts[static_cast<size_t>(l) * 64 + want];
+  }
+  widen[q] = found < k ? 1 : 0;
+}
+}  // namespace
+
+cudaError_t launch_category_counts(const uint8_t *category, const uint32_t *assign, size_t n, uint32_t *counts,
+                                   cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  category_counts_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(category, assign, n, counts);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_filter_widen(const uint32_t *probes, size_t nq, int P, const uint64_t *bitmask,
+                                const uint32_t *counts, int want, size_t k, uint8_t *widen, cudaStream_t s) {
+  if (nq == 0) return cudaSuccess;
+  filter_widen_kernel<<<static_cast<unsigned>((nq + 127) / 128), 128, 0, s>>>(probes, nq, P, bitmask, counts, want,
+                                                                            k, widen);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
 // Exact rerank (search.rs:1117-1158): each approximate candidate is re-scored
 // with cosine_distance_normalized = 1 - dot(q, x) (distance.rs:104-109), the
 // dot summed in index order, then the k best are kept.  Warp per query; lane

@@ -665,7 +665,65 @@ int parse_manifest(const std::string &text, SnapshotState &st) {
   return VG_OK;
 }
 
+// A MetadataValue in serde form: one of {"Int": i64}, {"Float": f64},
+// {"Str": string}, {"Bool": bool}.
+bool metadata_value(const JVal &v, std::string &tag) {
+  if (v.kind != JVal::Obj || v.obj.size() != 1) return false;
+  tag = v.obj[0].first;
+  const JVal &x = v.obj[0].second;
+  if (tag == "Int") return x.kind == JVal::Num && x.text.find_first_of(".eE") == std::string::npos;
+  if (tag == "Float") return x.kind == JVal::Num;
+  if (tag == "Str") return x.kind == JVal::Str;
+  if (tag == "Bool") return x.kind == JVal::Bool;
+  return false;
+}
+
+// Category of an Int value: 0..63, else the reference's error.
+int int_category(const JVal &v, const std::string &tag, int *category, bool at_search) {
+  if (tag != "Int")
+    return fail(VG_ERR_INVALID_PARAMETER, "category ID must be an integer in 0..63 for bitmask filtering");
+  errno = 0;
+  const long long n = std::strtoll(v.obj[0].second.text.c_str(), nullptr, 10);
+  if (errno == ERANGE || n < 0 || n >= 64)
+    return fail(VG_ERR_INVALID_PARAMETER,
+                "category ID " + v.obj[0].second.text + " exceeds bitmask limit of 63" +
+                    (at_search ? std::string() : std::string("; use an integer in 0..63")));
+  *category = static_cast<int>(n);
+  return VG_OK;
+}
+
 }  // namespace
+
+namespace vg {
+
+int parse_metadata(const char *json, const std::string &field, int *category, std::string *canonical) {
+  JVal root;
+  std::string err;
+  if (!json || !parse_json(json, root, err)) return fail(VG_ERR_INVALID_PARAMETER, "metadata is not valid JSON: " + err);
+  if (root.kind != JVal::Obj) return fail(VG_ERR_INVALID_PARAMETER, "metadata must be a JSON object");
+  *category = -1;
+  for (const auto &kv : root.obj) {
+    std::string tag;
+    if (!metadata_value(kv.second, tag))
+      return fail(VG_ERR_INVALID_PARAMETER, "metadata value of `" + kv.first +
+                                                "` must be {\"Int\"|\"Float\"|\"Str\"|\"Bool\": value}");
+    if (kv.first == field)
+      if (int s = int_category(kv.second, tag, category, false)) return s;
+  }
+  canonical->clear();
+  json_dump(*canonical, root);
+  return VG_OK;
+}
+
+int parse_filter_category(const char *value_json, int *category) {
+  JVal v;
+  std::string err, tag;
+  if (!value_json || !parse_json(value_json, v, err) || !metadata_value(v, tag))
+    return fail(VG_ERR_INVALID_PARAMETER, "filter value must be {\"Int\"|\"Float\"|\"Str\"|\"Bool\": value}");
+  return int_category(v, tag, category, true);
+}
+
+}  // namespace vg
 
 extern "C" {
 

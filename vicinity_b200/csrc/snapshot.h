@@ -45,4 +45,16 @@ int snapshot_adopt(vg_index *ix, SnapshotState &st);
 
 void set_last_error(const char *msg);
 
+// Validate one document's metadata, a JSON object in the reference's serde
+// form ({"field": {"Int": 3}, "label": {"Str": "x"}}, DocumentMetadata of
+// src/filtering/mod.rs), and read the category of `field`: 0..63, or -1 when
+// the document has no value for it (search.rs:439-470).  On success
+// `canonical` holds the object re-serialised compactly.  Returns a vg_status
+// (VG_ERR_INVALID_PARAMETER with the reference's message on a bad value).
+int parse_metadata(const char *json, const std::string &field, int *category, std::string *canonical);
+
+// Validate a filter value in the same serde form ({"Int": 3}) as the
+// category search_with_filter accepts (search.rs:1428-1446): 0..63.
+int parse_filter_category(const char *value_json, int *category);
+
 }  // namespace vg

@@ -8,6 +8,7 @@ method is a thin call into the C ABI of ``libvicinity_gpu.so``.
 from __future__ import annotations
 
 import ctypes as C
+import json
 import os
 
 import numpy as np
@@ -46,6 +47,19 @@ def _ptr(a: np.ndarray) -> int:
     return a.ctypes.data
 
 
+def _metadata_value(v) -> dict:
+    """A Python value in the serde form of MetadataValue (filtering/mod.rs)."""
+    if isinstance(v, (bool, np.bool_)):
+        return {"Bool": bool(v)}
+    if isinstance(v, (int, np.integer)):
+        return {"Int": int(v)}
+    if isinstance(v, (float, np.floating)):
+        return {"Float": float(v)}
+    if isinstance(v, str):
+        return {"Str": v}
+    raise TypeError(f"metadata values are int, float, str or bool, got {type(v).__name__}")
+
+
 class IVFPQIndex:
     """IVF-PQ index on one GPU (or one shard of a multi-GPU group)."""
 
@@ -59,6 +73,7 @@ class IVFPQIndex:
         use_opq: bool = False,
         seed: int = 42,
         device: int = 0,
+        filter_field: str | None = None,
     ):
         num_codebooks = default_ivfpq_codebooks(dim) if num_codebooks is None else num_codebooks
         _validate_shape(dim, num_clusters, num_codebooks, codebook_size, nprobe)
@@ -77,6 +92,8 @@ class IVFPQIndex:
         self._h = handle
         self._used_ids: set[int] = set()
         self._dim = dim
+        if filter_field is not None:  # IVFPQIndex::with_filtering (search.rs:414-434)
+            _lib.check(self._lib.vg_ivfpq_set_filter_field(self._h, str(filter_field).encode()))
 
     # -- lifecycle ---------------------------------------------------------
     def close(self) -> None:
@@ -227,6 +244,43 @@ class IVFPQIndex:
             )
         _lib.check(st)
         return ids, dists, counts
+
+    # -- metadata filtering (search.rs:414-475, 1407-1549) ---------------------
+    def add_metadata(self, doc_id: int, metadata: dict) -> None:
+        """Attach metadata to a document: {field: int | float | str | bool};
+        the filter field's value must be an int in 0..63."""
+        body = json.dumps({str(k): _metadata_value(v) for k, v in metadata.items()})
+        _lib.check(self._lib.vg_ivfpq_add_metadata(self._h, int(doc_id), body.encode()))
+
+    def _filtered_rows(self, q: np.ndarray, k: int, field: str, value):
+        nq = q.shape[0]
+        ids = np.empty((nq, k), dtype=np.uint32)
+        dists = np.empty((nq, k), dtype=np.float32)
+        counts = np.empty(nq, dtype=np.uint32)
+        _lib.check(self._lib.vg_ivfpq_search_filtered_batch(
+            self._h, _ptr(q), nq, k, str(field).encode(), json.dumps(_metadata_value(value)).encode(),
+            _ptr(ids), _ptr(dists), _ptr(counts)))
+        return ids, dists, counts
+
+    def search_with_filter(self, query, k: int, field: str, value):
+        """Nearest documents with metadata `field == value` (an int category
+        in 0..63): (doc ids int64, distances float32), ascending."""
+        q = np.ascontiguousarray(query, dtype=np.float32)
+        if q.ndim != 1 or q.shape[0] != self._dim:
+            raise ValueError(f"query dimension mismatch: index expects {self._dim}")
+        ids, dists, counts = self._filtered_rows(q.reshape(1, -1), k, field, value)
+        c = int(counts[0])
+        return ids[0, :c].astype(np.int64), dists[0, :c].copy()
+
+    def batch_search_with_filter(self, queries, k: int, field: str, value):
+        """search_with_filter over rows, padded like batch_search."""
+        q = np.ascontiguousarray(queries, dtype=np.float32)
+        if q.ndim != 2 or q.shape[1] != self._dim:
+            raise ValueError(f"queries dimension mismatch: index expects {self._dim}")
+        ids, dists, counts = self._filtered_rows(q, k, field, value)
+        out = ids.astype(np.int64)
+        out[np.arange(k)[None, :] >= counts.astype(np.int64)[:, None]] = MISSING_LABEL
+        return out, dists
 
     def search(self, query, k: int, nprobe=None, rerank_pool=None):
         """src/python.rs:683-718: (ids int64, distances float32), ascending."""
