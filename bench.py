@@ -11,9 +11,14 @@ written back before the timed step starts rather than inside it.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl engine|reference]
 
-N > 1 runs under torchrun, one rank per GPU: the inverted lists are sharded
-by list across ranks, every rank searches the same batch and the per-rank
-top-k are merged with one NCCL all-gather (strong scaling: total work fixed).
+N > 1 runs under torchrun, one rank per GPU.  Queries are independent, so by
+default every rank holds a replica of the index (built identically: training
+is deterministic) and searches its own batch of the configuration's size --
+no collective on the data path, weak scaling (work per GPU fixed), value =
+all ranks' queries / the slowest rank's time.  --shard lists instead splits the
+inverted lists across ranks; every rank then searches the same batch and the
+per-rank top-k are merged with one NCCL all-gather (strong scaling), the layout
+for an index larger than one GPU.
 """
 from __future__ import annotations
 
@@ -49,6 +54,8 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--nq", type=int, default=None, help="query batch (default: the configuration's)")
+    p.add_argument("--shard", choices=["queries", "lists"], default="queries",
+                   help="multi-GPU layout: index replicas with per-rank query batches, or list sharding")
     return p.parse_args()
 
 
@@ -140,16 +147,22 @@ def run_engine(args):
     n, d, k = cfg["n"], cfg["d"], cfg["k"]
     nq = args.nq or cfg["nq"]
     t0 = time.time()
-    x, q = config_data(args.config, seed=0, nq=nq)
+    by_lists = world > 1 and args.shard == "lists"
+    # per-rank batches: rows [rank*nq, (rank+1)*nq) of the configuration's query
+    # stream (rank 0's batch is the single-GPU batch)
+    x, q = config_data(args.config, seed=0, nq=nq * (1 if by_lists else world))
+    if not by_lists:
+        q = np.ascontiguousarray(q[rank * nq:(rank + 1) * nq])
     ix = IVFPQIndex(d, num_clusters=cfg["nlist"], num_codebooks=cfg["M"], codebook_size=cfg["ks"],
                     nprobe=cfg["nprobe"], seed=42, device=local)
     ix.add_items(x)
     ix.build(training_sample_size=min(args.train_sample, n), kmeans_max_iter=args.train_iters)
     build_s = time.time() - t0
-    if world > 1:
+    if by_lists:
         obj = [nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         ix.shard(rank, world, obj[0], timeout_ms=120_000)
+    queries_total = nq * (1 if by_lists else world)  # queries all ranks answer per step
 
     # One explicit stream carries everything timed: the L2 flush, the CUDA
     # events and the engine's kernels (torch's default stream has handle 0,
@@ -207,7 +220,7 @@ def run_engine(args):
     prof = ix.profile()
     ix.set_profiling(False)
     dev_ms_max = max_over_ranks(dev_ms)
-    value = nq * args.steps / (dev_ms_max / 1e3)
+    value = queries_total * args.steps / (dev_ms_max / 1e3)
 
     # end to end through the same call with pinned host buffers
     q_h = torch.from_numpy(q).pin_memory()
@@ -221,7 +234,7 @@ def run_engine(args):
     for _ in range(max(1, args.warmup // 2)):
         step_e2e()
     e2e_ms = max_over_ranks(timed(step_e2e, args.steps))
-    e2e_value = nq * args.steps / (e2e_ms / 1e3)
+    e2e_value = queries_total * args.steps / (e2e_ms / 1e3)
 
     # recall@10 against the exact top-10 of the normalised data (flat engine search)
     recall = None
@@ -264,7 +277,7 @@ def run_engine(args):
             "warmup": args.warmup,
             "ms_per_step": round(dev_ms_max / args.steps, 4),
             "higher_is_better": True,
-            "scaling": "strong",
+            "scaling": "strong" if by_lists or world == 1 else "weak",
             "vs_baseline": None,
             "dtype": "f32",
             "data": "synthetic: seeded Gaussian mixture with the configuration's generator (no dataset)",
@@ -274,7 +287,8 @@ def run_engine(args):
                 "recall_at_10": None if recall is None else round(recall, 4),
                 "train_sample": min(args.train_sample, n), "train_iters": args.train_iters,
                 "l2": "flushed between timed steps (512 MiB write, then 512 MiB read of another buffer; index codes fit in L2)",
-                "parallelism": f"list-sharded x{world}" if world > 1 else "single GPU",
+                "parallelism": ("single GPU" if world == 1 else f"list-sharded x{world}" if by_lists
+                                else f"index replica per GPU, {nq} queries per rank x{world}"),
                 "build_s": round(build_s, 1),
             },
             "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
