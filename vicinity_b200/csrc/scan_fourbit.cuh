@@ -227,45 +227,63 @@ __global__ void __launch_bounds__(kScanThreads, 2) ivfpq_four_kernel(const ScanP
       const uint32_t qset_a = smem_u32(qset);
       for (uint32_t x0 = warp * 32; x0 < pre4; x0 += kScanThreads) {
         const uint32_t x = x0 + lane;
+        // threshold first: candidates whose partial sum already exceeds it stop
+        // early (the quantised distance is non-decreasing in the integer sum)
+        uint64_t thr = tk.worst();
+        const uint64_t bound = s_bound;
+        thr = bound < thr ? bound : thr;
+        const uint32_t tkey = static_cast<uint32_t>(thr >> 32);
         float dist = 0.0f;
         int g = 0;
         uint32_t c = 0;
-        if (x < pre4) {
+        bool alive = x < pre4, quant = false;
+        const uint8_t *vp = p.packed;
+        uint32_t list = 0;
+        if (alive) {
           g = (x >= pre1) + (x >= pre2) + (x >= pre3);
           const uint32_t lo = g == 0 ? 0u : g == 1 ? pre1 : g == 2 ? pre2 : pre3;
           const uint32_t hi = g == 0 ? pre1 : g == 1 ? pre2 : g == 2 ? pre3 : pre4;
           c = x - lo;
-          const uint32_t list = s_list[b0 + g];
-          if (hi - lo >= 16) {  // search.rs:1261 (SIMD_BATCH_THRESHOLD)
-            const uint8_t *vp = p.packed + p.pack_off[list] + static_cast<uint64_t>(c) * ((M + 1) >> 1);
-            const uint32_t qa = qset_a + static_cast<uint32_t>(g * qstride);
-            uint32_t acc = 0;
-            if ((M & 15) == 0) {
-              for (int m0 = 0; m0 < M; m0 += 64) {
-                uint2 w[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u)
-                  w[u] = m0 + 16 * u < M ? *reinterpret_cast<const uint2 *>(vp + (m0 >> 1) + 8 * u)
-                                         : make_uint2(0u, 0u);
-#pragma unroll
-                for (int u = 0; u < 4; ++u)
-                  if (m0 + 16 * u < M) acc += nibble_sum16(w[u], qa + static_cast<uint32_t>((m0 + 16 * u) * 16));
-              }
-            } else {
-              const uint8_t *ql = qset + static_cast<size_t>(g) * qstride;
-              for (int m = 0; m < M; ++m) acc += ql[m * 16 + ((vp[m >> 1] >> ((m & 1) * 4)) & 15u)];
-            }
-            dist = __fadd_rn(__fmul_rn(__uint2float_rn(acc), s_scale[set][g]), s_fbase[set][g]);
-          } else {
-            const uint8_t *cp = p.list_codes + p.code_off[list] + static_cast<uint64_t>(c) * M;
-            dist = adc_row_sum<16>(cp, fset + static_cast<size_t>(g) * fstride, M, 16);
-          }
+          list = s_list[b0 + g];
+          quant = hi - lo >= 16;  // search.rs:1261 (SIMD_BATCH_THRESHOLD)
+          if (quant) vp = p.packed + p.pack_off[list] + static_cast<uint64_t>(c) * ((M + 1) >> 1);
         }
-        uint64_t thr = tk.worst();
-        const uint64_t bound = s_bound;
-        thr = bound < thr ? bound : thr;
+        // quantised lists: integer sums of the u8 table, checked every 16 codes
+        const float sc = s_scale[set][g], fb = s_fbase[set][g];
+        bool qlive = alive && quant;
+        uint32_t acc = 0;
+        if ((M & 15) == 0) {
+          const uint32_t qa = qset_a + static_cast<uint32_t>(g * qstride);
+          for (int m0 = 0; m0 < M; m0 += 64) {
+            if (!__any_sync(VG_FULL_MASK, qlive)) break;
+            uint2 w[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              w[u] = (qlive && m0 + 16 * u < M) ? *reinterpret_cast<const uint2 *>(vp + (m0 >> 1) + 8 * u)
+                                                : make_uint2(0u, 0u);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              if (m0 + 16 * u >= M) break;
+              if (u > 0 && !__any_sync(VG_FULL_MASK, qlive)) break;
+              if (qlive) {
+                acc += nibble_sum16(w[u], qa + static_cast<uint32_t>((m0 + 16 * u) * 16));
+                qlive = order_key(__fadd_rn(__fmul_rn(__uint2float_rn(acc), sc), fb)) <= tkey;
+              }
+            }
+          }
+        } else if (qlive) {
+          const uint8_t *ql = qset + static_cast<size_t>(g) * qstride;
+          for (int m = 0; m < M; ++m) acc += ql[m * 16 + ((vp[m >> 1] >> ((m & 1) * 4)) & 15u)];
+        }
+        if (quant) {
+          alive = qlive;
+          dist = __fadd_rn(__fmul_rn(__uint2float_rn(acc), sc), fb);
+        } else if (alive) {  // lists under 16 vectors: float table, sequential sum
+          const uint8_t *cp = p.list_codes + p.code_off[list] + static_cast<uint64_t>(c) * M;
+          dist = adc_row_sum<16>(cp, fset + static_cast<size_t>(g) * fstride, M, 16);
+        }
         const uint32_t dk = order_key(dist);
-        const bool pass = x < pre4 && dk <= static_cast<uint32_t>(thr >> 32);
+        const bool pass = alive && dk <= tkey;
         unsigned mask = __ballot_sync(VG_FULL_MASK, pass);
         if (!mask) continue;
         const uint64_t key = pass ? ((static_cast<uint64_t>(dk) << 32) | p.list_ids[s_lbeg[b0 + g] + c]) : kEmptyKey;

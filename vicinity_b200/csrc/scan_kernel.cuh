@@ -111,6 +111,47 @@ __device__ __forceinline__ float adc_row_sum(const uint8_t *cp, const float *lg,
   return acc;
 }
 
+// adc_row_sum with early exit against a key threshold.  Table entries are
+// >= +0 (squares) and a rounded add of a non-negative term never decreases
+// the sum, so once the partial sum's order key exceeds tkey the full sum
+// cannot pass `key <= tkey` either: the lane stops (alive = false) and its
+// result is discarded by the caller.  The warp leaves the loop when no lane
+// is alive.  Every lane of the warp must call this (it votes).
+template <int KS>
+__device__ __forceinline__ float adc_row_sum_bounded(const uint8_t *cp, const float *lg, int M, int ks,
+                                                     uint32_t tkey, bool &alive) {
+  const int row_len = KS > 0 ? KS : ks;
+  float acc = 0.0f;
+  if ((M & 15) == 0) {
+    for (int m0 = 0; m0 < M; m0 += 16) {
+      if (!__any_sync(VG_FULL_MASK, alive)) break;
+      if (alive) {
+        const uint4 w = *reinterpret_cast<const uint4 *>(cp + m0);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        const float *row = lg + m0 * row_len;
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+          const uint32_t code = __byte_perm(ws[b >> 2], 0u, 0x4440u + (b & 3));
+          acc = __fadd_rn(acc, row[b * row_len + code]);
+        }
+        alive = order_key(acc) <= tkey;
+        if (alive) {
+#pragma unroll
+          for (int b = 8; b < 16; ++b) {
+            const uint32_t code = __byte_perm(ws[b >> 2], 0u, 0x4440u + (b & 3));
+            acc = __fadd_rn(acc, row[b * row_len + code]);
+          }
+          alive = order_key(acc) <= tkey;
+        }
+      }
+    }
+  } else if (alive) {
+    for (int m = 0; m < M; ++m) acc = __fadd_rn(acc, lg[m * row_len + cp[m]]);
+    alive = order_key(acc) <= tkey;
+  }
+  return acc;
+}
+
 // Squared distance of one residual subvector to one codeword, summed in the
 // reference's order.  The first term is taken as is: for s >= +0 the
 // reference's 0.0 + s equals s exactly, and a square is never -0.
@@ -279,10 +320,16 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
       const uint32_t ctotal = pre4;
       for (uint32_t x0 = warp * 32; x0 < ctotal; x0 += kScanThreads) {
         const uint32_t x = x0 + lane;
-        float dist = 0.0f;
+        // threshold first: candidates whose partial sum already exceeds it stop early
+        uint64_t thr = tk.worst();
+        const uint64_t bound = s_bound;
+        thr = bound < thr ? bound : thr;
+        const uint32_t tkey = static_cast<uint32_t>(thr >> 32);
         int g = 0;
         uint32_t c = 0, vid = 0;
         bool live = x < ctotal;
+        const uint8_t *cp = p.list_codes;
+        const float *lg = lut;
         if (live) {
           g = (x >= pre1) + (x >= pre2) + (x >= pre3);
           const uint32_t lo = g == 0 ? 0u : g == 1 ? pre1 : g == 2 ? pre2 : pre3;
@@ -291,17 +338,12 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
             vid = p.list_ids[s_lbeg[b0 + g] + c];
             live = p.category[vid] == static_cast<uint8_t>(p.want_cat);
           }
-          if (live) {
-            const uint32_t list = blist[g];
-            const uint8_t *cp = p.list_codes + p.code_off[list] + static_cast<uint64_t>(c) * M;
-            dist = adc_row_sum<KS>(cp, lut + static_cast<size_t>(g) * tstride, M, ks);
-          }
+          cp = p.list_codes + p.code_off[blist[g]] + static_cast<uint64_t>(c) * M;
+          lg = lut + static_cast<size_t>(g) * tstride;
         }
-        uint64_t thr = tk.worst();
-        const uint64_t bound = s_bound;
-        thr = bound < thr ? bound : thr;
+        const float dist = adc_row_sum_bounded<KS>(cp, lg, M, ks, tkey, live);
         const uint32_t dk = order_key(dist);
-        const bool pass = live && dk <= static_cast<uint32_t>(thr >> 32);
+        const bool pass = live && dk <= tkey;
         unsigned mask = __ballot_sync(VG_FULL_MASK, pass);
         if (!mask) continue;
         const uint64_t key =

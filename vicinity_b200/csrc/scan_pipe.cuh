@@ -143,20 +143,25 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_pipe_kernel(const ScanP
       const uint32_t pre4 = pre3 + (nb > 3 ? s_len[b0 + 3] : 0u);
       for (uint32_t x0 = warp * 32; x0 < pre4; x0 += kScanThreads) {
         const uint32_t x = x0 + lane;
-        float dist = 0.0f;
-        int g = 0;
-        uint32_t c = 0;
-        if (x < pre4) {
-          g = (x >= pre1) + (x >= pre2) + (x >= pre3);
-          c = x - (g == 0 ? 0u : g == 1 ? pre1 : g == 2 ? pre2 : pre3);
-          const uint8_t *cp = p.list_codes + s_coff[b0 + g] + static_cast<uint64_t>(c) * M;
-          dist = adc_row_sum<KS>(cp, tset + static_cast<size_t>(g) * tstride, M, ks);
-        }
+        // threshold first: candidates whose partial sum already exceeds it stop early
         uint64_t thr = tk.worst();
         const uint64_t bound = s_bound;
         thr = bound < thr ? bound : thr;
+        const uint32_t tkey = static_cast<uint32_t>(thr >> 32);
+        int g = 0;
+        uint32_t c = 0;
+        bool alive = x < pre4;
+        const uint8_t *cp = p.list_codes;
+        const float *lg = tset;
+        if (alive) {
+          g = (x >= pre1) + (x >= pre2) + (x >= pre3);
+          c = x - (g == 0 ? 0u : g == 1 ? pre1 : g == 2 ? pre2 : pre3);
+          cp = p.list_codes + s_coff[b0 + g] + static_cast<uint64_t>(c) * M;
+          lg = tset + static_cast<size_t>(g) * tstride;
+        }
+        const float dist = adc_row_sum_bounded<KS>(cp, lg, M, ks, tkey, alive);
         const uint32_t dk = order_key(dist);
-        const bool pass = x < pre4 && dk <= static_cast<uint32_t>(thr >> 32);
+        const bool pass = alive && dk <= tkey;
         unsigned mask = __ballot_sync(VG_FULL_MASK, pass);
         if (!mask) continue;
         const uint64_t key = pass ? ((static_cast<uint64_t>(dk) << 32) | p.list_ids[s_lbeg[b0 + g] + c]) : kEmptyKey;
