@@ -158,6 +158,35 @@ __global__ void pack_nibbles_kernel(const uint8_t *__restrict__ list_codes, cons
   }
 }
 
+// Largest reconstructed-residual norm of each list (double, rounded up).
+__global__ void list_radius_kernel(const uint8_t *__restrict__ list_codes, const uint64_t *__restrict__ code_off,
+                                   const uint64_t *__restrict__ list_off, int M, int ks, int dsub,
+                                   const float *__restrict__ codebooks, float *__restrict__ radius) {
+  __shared__ double red[32];
+  const size_t l = blockIdx.x;
+  const uint64_t len = list_off[l + 1] - list_off[l];
+  const uint8_t *codes = list_codes + code_off[l];
+  double best = 0.0;
+  for (uint64_t v = threadIdx.x; v < len; v += blockDim.x) {
+    double s = 0.0;
+    for (int m = 0; m < M; ++m) {
+      const float *cw = codebooks + (static_cast<size_t>(m) * ks + codes[v * M + m]) * dsub;
+      for (int j = 0; j < dsub; ++j) s += static_cast<double>(cw[j]) * static_cast<double>(cw[j]);
+    }
+    best = s > best ? s : best;
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    const double o = __shfl_xor_sync(0xffffffffu, best, off);
+    best = o > best ? o : best;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (unsigned w = 1; w < (blockDim.x + 31) / 32; ++w) best = red[w] > best ? red[w] : best;
+    radius[l] = __double2float_ru(sqrt(best) * (1.0 + 1e-12));
+  }
+}
+
 // Deterministic cluster mean: members are visited in ascending order and
 // each dimension is summed sequentially by one thread.
 __global__ void kmeans_update_kernel(const float *__restrict__ x, int d, const uint32_t *__restrict__ sorted_ids,
@@ -286,6 +315,15 @@ cudaError_t launch_pack_lists_4bit(const uint8_t *list_codes, const uint64_t *li
                                    cudaStream_t s) {
   if (L == 0) return cudaSuccess;
   pack_nibbles_kernel<<<static_cast<unsigned>(L), 256, 0, s>>>(list_codes, list_off, code_off, pack_off, M, packed);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_list_radius(const uint8_t *list_codes, const uint64_t *code_off, const uint64_t *list_off,
+                               size_t L, int M, int ks, int dsub, const float *codebooks, float *radius,
+                               cudaStream_t s) {
+  if (L == 0) return cudaSuccess;
+  list_radius_kernel<<<static_cast<unsigned>(L), 256, 0, s>>>(list_codes, code_off, list_off, M, ks, dsub,
+                                                              codebooks, radius);
   return cudaGetLastError();
 }
 

@@ -171,6 +171,7 @@ struct vg_index {
 
   DevBuf vectors, doc_ids, centroids, codebooks, assign, codes;
   DevBuf list_off, list_ids, code_off, list_codes, pack_off, packed;
+  DevBuf list_radius;  // f32 [Lc]: largest reconstructed-residual norm per list (list pruning)
   std::vector<uint64_t> h_list_off;
   std::vector<uint32_t> h_doc_ids;
 
@@ -198,7 +199,7 @@ struct vg_index {
 
   // search workspace
   DevBuf ws_q, ws_qn, ws_dist, ws_probes, ws_pdist, ws_scalars,
-      ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count;
+      ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_lb;
   DevBuf stats;  // u64 [pairs, vectors, code bytes] accumulated while profiling
 
   // error flag of bounded device waits, in mapped pinned host memory
@@ -213,7 +214,8 @@ struct vg_index {
   size_t device_bytes() const {
     return vectors.cap + doc_ids.cap + centroids.cap + codebooks.cap + assign.cap + codes.cap +
            list_off.cap + list_ids.cap + code_off.cap + list_codes.cap + pack_off.cap + packed.cap +
-           owner.cap + rotation.cap + rotation_t.cap + category_d.cap + bitmask_d.cap + cat_counts.cap;
+           owner.cap + rotation.cap + rotation_t.cap + category_d.cap + bitmask_d.cap + cat_counts.cap +
+           list_radius.cap;
   }
 };
 
@@ -603,6 +605,10 @@ int build_list_storage(vg_index *ix, const uint32_t *sorted_lists) {
                                  ix->code_off.as<uint64_t>(), ix->pack_off.as<uint64_t>(), Lc, static_cast<int>(M),
                                  ix->packed.as<uint8_t>(), s));
   }
+  VG_CU(ix->list_radius.reserve(std::max<size_t>(Lc, 1) * 4));
+  VG_CU(launch_list_radius(ix->list_codes.as<uint8_t>(), ix->code_off.as<uint64_t>(), ix->list_off.as<uint64_t>(), Lc,
+                           static_cast<int>(M), static_cast<int>(ks), static_cast<int>(ix->dsub),
+                           ix->codebooks.as<float>(), ix->list_radius.as<float>(), s));
   VG_CU(cudaStreamSynchronize(s));
   ix->built = true;
   return VG_OK;
@@ -692,6 +698,15 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
                              static_cast<int>(M), ix->params.codebook_size == 16,
                              ix->stats.as<unsigned long long>(), s));
   }
+  // list pruning bounds (8-bit tables without a rotation; see launch_probe_lb)
+  const bool prune = ix->params.codebook_size != 16 && ix->h_rotation.empty();
+  if (prune) {
+    VG_CU(ix->ws_lb.reserve(nq * P * 4));
+    VG_CU(launch_probe_lb(ix->ws_qn.as<float>(), nq, static_cast<int>(d), ix->ws_probes.as<uint32_t>(),
+                          static_cast<int>(P), ix->centroids.as<float>(), ix->list_radius.as<float>(),
+                          static_cast<int>(M), static_cast<int>(ix->dsub), ix->ws_lb.as<float>(), s));
+    ix->launches += 1;
+  }
   mark(ix, 5);
 
   // outputs: device pointers are written in place, host ones via staging
@@ -724,6 +739,7 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   sp.list_ids = ix->list_ids.as<uint32_t>();
   sp.doc_ids = doc_map;
   sp.rot_t = ix->h_rotation.empty() ? nullptr : ix->rotation_t.as<float>();
+  sp.probe_lb = prune ? ix->ws_lb.as<float>() : nullptr;
   sp.d = static_cast<int>(d);
   sp.M = static_cast<int>(M);
   sp.ks = static_cast<int>(ix->params.codebook_size);

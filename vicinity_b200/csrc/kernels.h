@@ -111,6 +111,21 @@ cudaError_t launch_filter_widen(const uint32_t *probes, size_t nq, int P, const 
                                 const uint32_t *counts, int want, size_t k, uint8_t *widen,
                                 cudaStream_t s);
 
+// List pruning.  radius[l] = max over the list's vectors of the norm of the
+// reconstructed residual (concatenated codewords), in double, rounded up to
+// float (list_codes [L] lists at code_off, codebooks [M][ks][dsub]).
+cudaError_t launch_list_radius(const uint8_t *list_codes, const uint64_t *code_off, const uint64_t *list_off,
+                               size_t L, int M, int ks, int dsub, const float *codebooks, float *radius,
+                               cudaStream_t s);
+
+// lb[q][p] = a lower bound on every computed ADC distance of probe p of query
+// q: (||r|| - radius)^2 with r the float residual qn[q] - centroid (computed
+// as the scan kernels compute it), times 1 - (M + dsub + 2) 2^-24 for the
+// rounding of the table sums, rounded down; 0 when ||r|| <= radius.
+cudaError_t launch_probe_lb(const float *qn, size_t nq, int d, const uint32_t *probes, int P,
+                            const float *centroids, const float *radius, int M, int dsub, float *lb,
+                            cudaStream_t s);
+
 // Number of positions where a[i] != b[i] added to *changed.
 cudaError_t launch_count_diff_u8(const uint8_t *a, const uint8_t *b, size_t n,
                                  unsigned int *changed, cudaStream_t s);
@@ -145,6 +160,7 @@ struct ScanParams {
   const uint8_t *category;       // [n] filter category per vector id, 255 = none (nullable: no filter)
   const uint64_t *bitmask;       // [L] categories present per list (at build)
   int want_cat;                  // category to keep, 0..63
+  const float *probe_lb;         // [nq][P] distance lower bound per probe (nullable: no list pruning)
 };
 
 // Fused per-query kernel: for each probed list the query residual, the ADC

@@ -185,6 +185,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
   __shared__ uint32_t s_list[kScanThreads], s_len[kScanThreads];
   __shared__ uint64_t s_lbeg[kScanThreads];
   __shared__ unsigned long long s_bound;
+  __shared__ float s_lb[kScanThreads];      // distance lower bound of each compacted probe
+  __shared__ uint8_t s_skip[kMaxBatch];     // list of the current batch skipped (pruned)
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
@@ -245,6 +247,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
         s_list[pos] = l;
         s_lbeg[pos] = b;
         s_len[pos] = static_cast<uint32_t>(p.list_off[l + 1] - b);
+        s_lb[pos] = p.probe_lb ? p.probe_lb[static_cast<size_t>(q) * P + pc + tid] : 0.0f;
       }
       if (tid == 0) s_nvalid = total;
       __syncthreads();
@@ -257,6 +260,13 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
       for (int i = tid; i < nb * d; i += kScanThreads) {
         int g = i / d, j = i - g * d;
         qres[g * dpad + j] = __fsub_rn(qv[j], p.centroids[static_cast<size_t>(blist[g]) * d + j]);
+      }
+      // list pruning (bound > block k-th distance: no candidate can enter);
+      // decided by one thread, read by all after the barrier
+      if (tid == 0) {
+        const uint64_t bnd = s_bound;
+        const float bdist = key_dist(bnd);
+        for (int g = 0; g < kMaxBatch; ++g) s_skip[g] = g < nb && bnd != kEmptyKey && s_lb[b0 + g] > bdist;
       }
       __syncthreads();
       // OPQ: tables are built from the rotated residual R r (opq.rs:115-121);
@@ -278,6 +288,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
       // ---- ADC tables: sequential sum over the subvector, no FMA --------
 #pragma unroll 1
       for (int g = 0; g < nb; ++g) {
+        if (s_skip[g]) continue;
         const float *qg = tq + g * dpad;
         float *lg = lut + static_cast<size_t>(g) * tstride;
         if (DSUB > 0) {
@@ -311,10 +322,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
       __syncthreads();
 
       // candidate prefix over the batch's lists (kMaxBatch == 4)
-      const uint32_t pre1 = s_len[b0];
-      const uint32_t pre2 = pre1 + (nb > 1 ? s_len[b0 + 1] : 0u);
-      const uint32_t pre3 = pre2 + (nb > 2 ? s_len[b0 + 2] : 0u);
-      const uint32_t pre4 = pre3 + (nb > 3 ? s_len[b0 + 3] : 0u);
+      const uint32_t pre1 = s_skip[0] ? 0u : s_len[b0];
+      const uint32_t pre2 = pre1 + (nb > 1 && !s_skip[1] ? s_len[b0 + 1] : 0u);
+      const uint32_t pre3 = pre2 + (nb > 2 && !s_skip[2] ? s_len[b0 + 2] : 0u);
+      const uint32_t pre4 = pre3 + (nb > 3 && !s_skip[3] ? s_len[b0 + 3] : 0u);
 
       // ---- score and select ---------------------------------------------
       const uint32_t ctotal = pre4;

@@ -42,6 +42,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_pipe_kernel(const ScanP
   __shared__ uint32_t s_list[kScanThreads], s_len[kScanThreads];
   __shared__ uint64_t s_lbeg[kScanThreads], s_coff[kScanThreads];
   __shared__ unsigned long long s_bound;
+  __shared__ float s_lb[kScanThreads];            // distance lower bound of each compacted probe
+  __shared__ uint8_t s_skip[3][kMaxBatch];        // list skipped, per batch (indexed batch % 3)
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool build_first = (warp & 1) == 0;
@@ -98,12 +100,28 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_pipe_kernel(const ScanP
         s_lbeg[pos] = b;
         s_len[pos] = static_cast<uint32_t>(p.list_off[l + 1] - b);
         s_coff[pos] = p.code_off[l];
+        s_lb[pos] = p.probe_lb ? p.probe_lb[static_cast<size_t>(q) * P + tid] : 0.0f;
       }
       if (tid == 0) s_nvalid = total;
       __syncthreads();
     }
     const int nvalid = s_nvalid;
     const int nbat = (nvalid + batch - 1) / batch;
+
+    // List pruning: a list whose distance lower bound exceeds the block's k-th
+    // distance cannot contribute (every computed distance is >= its bound), so
+    // its table is not built and its codes are not read.  One thread decides
+    // for batch bb just before a block barrier; the flags are read after it,
+    // by builders and scanners alike, and kept until batch bb + 3 reuses them.
+    auto decide = [&](int bb) {
+      if (tid != 0 || bb >= nbat) return;
+      const uint64_t bnd = s_bound;
+      const float bdist = key_dist(bnd);
+      for (int g = 0; g < batch; ++g) {
+        const int li = bb * batch + g;
+        s_skip[bb % 3][g] = li < nvalid && bnd != kEmptyKey && s_lb[li] > bdist;
+      }
+    };
 
     // table of every list of batch b into table set `set` (residuals of batch
     // b live in residual set b & 1)
@@ -113,6 +131,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_pipe_kernel(const ScanP
       float *tset = tables + static_cast<size_t>(set) * batch * tstride;
 #pragma unroll 1
       for (int g = 0; g < nb; ++g) {
+        if (s_skip[b % 3][g]) continue;
         const float *qg = qset + g * dpad;
         float *lg = tset + static_cast<size_t>(g) * tstride;
 #pragma unroll
@@ -137,10 +156,12 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_pipe_kernel(const ScanP
       const int b0 = b * batch;
       const int nb = min(batch, nvalid - b0);
       const float *tset = tables + static_cast<size_t>(set) * batch * tstride;
-      const uint32_t pre1 = s_len[b0];
-      const uint32_t pre2 = pre1 + (nb > 1 ? s_len[b0 + 1] : 0u);
-      const uint32_t pre3 = pre2 + (nb > 2 ? s_len[b0 + 2] : 0u);
-      const uint32_t pre4 = pre3 + (nb > 3 ? s_len[b0 + 3] : 0u);
+      // candidates of the batch's lists that are not skipped
+      const uint8_t *skip = s_skip[b % 3];
+      const uint32_t pre1 = skip[0] ? 0u : s_len[b0];
+      const uint32_t pre2 = pre1 + (nb > 1 && !skip[1] ? s_len[b0 + 1] : 0u);
+      const uint32_t pre3 = pre2 + (nb > 2 && !skip[2] ? s_len[b0 + 2] : 0u);
+      const uint32_t pre4 = pre3 + (nb > 3 && !skip[3] ? s_len[b0 + 3] : 0u);
       for (uint32_t x0 = warp * 32; x0 < pre4; x0 += kScanThreads) {
         const uint32_t x = x0 + lane;
         // threshold first: candidates whose partial sum already exceeds it stop early
@@ -187,8 +208,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_pipe_kernel(const ScanP
         qres[static_cast<size_t>(li / batch) * batch * dpad + (li % batch) * dpad + j] =
             __fsub_rn(qv[j], p.centroids[static_cast<size_t>(s_list[li]) * d + j]);
       }
+      decide(0);
       __syncthreads();
       build(0, 0);
+      decide(1);
       __syncthreads();
     }
     for (int b = 0; b < nbat; ++b) {
@@ -228,6 +251,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_pipe_kernel(const ScanP
         const int g = i / d, j = i - g * d;
         qdst[g * dpad + j] = __fsub_rn(qv[j], p.centroids[static_cast<size_t>(s_list[l2 + g]) * d + j]);
       }
+      decide(b + 2);  // built in phase b + 1, scanned in phase b + 2
       __syncthreads();
     }
 

@@ -548,6 +548,57 @@ cudaError_t launch_filter_widen(const uint32_t *probes, size_t nq, int P, const 
 }
 
 // ---------------------------------------------------------------------------
+// List pruning bounds.  For candidate i of list l the exact value of the sums
+// the scan computes is E_i = ||r - w_i||^2 (r: the float residual, w_i: the
+// concatenated codewords), which is >= (||r|| - ||w_i||)^2 >= (||r|| - R_l)^2
+// when ||r|| > R_l.  The computed sum of non-negative terms is >= E_i (1-u)^n
+// with n = M + dsub + 1 roundings on the longest chain (u = 2^-24).  Norms are
+// taken in double from the float values, so the bound is rigorous; it is
+// scaled by 1 - (n + 1) u and rounded down to float.
+// ---------------------------------------------------------------------------
+namespace {
+__global__ void probe_lb_kernel(const float *__restrict__ qn, size_t nq, int d, const uint32_t *__restrict__ probes,
+                                int P, const float *__restrict__ centroids, const float *__restrict__ radius,
+                                int M, int dsub, float *__restrict__ lb) {
+  const size_t pair = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (pair >= nq * P) return;
+  const int lane = lane_id();
+  const size_t q = pair / P;
+  const uint32_t l = probes[pair];
+  if (l == 0xffffffffu) {
+    if (lane == 0) lb[pair] = 0.0f;
+    return;
+  }
+  const float *qv = qn + q * d;
+  const float *c = centroids + static_cast<size_t>(l) * d;
+  double s = 0.0;
+  for (int j = lane; j < d; j += 32) {
+    const double r = static_cast<double>(__fsub_rn(qv[j], c[j]));  // the scan kernels' residual
+    s += r * r;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(VG_FULL_MASK, s, off);
+  if (lane == 0) {
+    // double rounding of d squares and sums: relative < 1e-13, covered below
+    const double gap = sqrt(s) - static_cast<double>(radius[l]);
+    double b = gap > 0.0 ? gap * gap : 0.0;
+    b *= 1.0 - (static_cast<double>(M + dsub + 2) * 5.9604644775390625e-8 + 1e-12);
+    lb[pair] = __double2float_rd(b);
+  }
+}
+}  // namespace
+
+cudaError_t launch_probe_lb(const float *qn, size_t nq, int d, const uint32_t *probes, int P,
+                            const float *centroids, const float *radius, int M, int dsub, float *lb,
+                            cudaStream_t s) {
+  const size_t pairs = nq * static_cast<size_t>(P);
+  if (pairs == 0) return cudaSuccess;
+  probe_lb_kernel<<<static_cast<unsigned>((pairs * 32 + 255) / 256), 256, 0, s>>>(qn, nq, d, probes, P, centroids,
+                                                                                 radius, M, dsub, lb);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
 // Exact rerank (search.rs:1117-1158): each approximate candidate is re-scored
 // with cosine_distance_normalized = 1 - dot(q, x) (distance.rs:104-109), the
 // dot summed in index order, then the k best are kept.  Warp per query; lane
