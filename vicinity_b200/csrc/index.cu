@@ -698,8 +698,8 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
                              static_cast<int>(M), ix->params.codebook_size == 16,
                              ix->stats.as<unsigned long long>(), s));
   }
-  // list pruning bounds (8-bit tables without a rotation; see launch_probe_lb)
-  const bool prune = ix->params.codebook_size != 16 && ix->h_rotation.empty();
+  // list pruning bounds (tables without a rotation; see launch_probe_lb)
+  const bool prune = ix->h_rotation.empty();
   if (prune) {
     VG_CU(ix->ws_lb.reserve(nq * P * 4));
     VG_CU(launch_probe_lb(ix->ws_qn.as<float>(), nq, static_cast<int>(d), ix->ws_probes.as<uint32_t>(),

@@ -96,6 +96,8 @@ __global__ void __launch_bounds__(kScanThreads, 2) ivfpq_four_kernel(const ScanP
   __shared__ unsigned long long s_bound;
   __shared__ float s_rmin[kMaxBatch][kFourGroup / 32], s_rmax[kMaxBatch][kFourGroup / 32];
   __shared__ float s_scale[2][kMaxBatch], s_fbase[2][kMaxBatch];
+  __shared__ float s_lb[kScanThreads];     // distance lower bound of each compacted probe (float tables)
+  __shared__ uint8_t s_skip[2][kMaxBatch];  // list not scanned (pruned), per table set
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int grp = tid / kFourGroup, gt = tid % kFourGroup;  // list slot of the batch, thread in group
@@ -137,6 +139,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) ivfpq_four_kernel(const ScanP
         s_list[pos] = l;
         s_lbeg[pos] = b;
         s_len[pos] = static_cast<uint32_t>(p.list_off[l + 1] - b);
+        s_lb[pos] = p.probe_lb ? p.probe_lb[static_cast<size_t>(q) * P + tid] : 0.0f;
       }
       if (tid == 0) s_nvalid = total;
       __syncthreads();
@@ -213,17 +216,31 @@ __global__ void __launch_bounds__(kScanThreads, 2) ivfpq_four_kernel(const ScanP
           ql[e] = static_cast<uint8_t>(t);
         }
         if (gt == 0) {
-          s_scale[set][grp] = flat ? 1.0f : __fdiv_rn(range, 255.0f);
+          const float scale = flat ? 1.0f : __fdiv_rn(range, 255.0f);
+          s_scale[set][grp] = scale;
           s_fbase[set][grp] = __fmul_rn(gmin, static_cast<float>(M));
+          // List pruning.  s_lb bounds every float-table sum from below; a
+          // quantised entry is its float value minus at most scale / 2 (round
+          // to nearest, pq_simd.rs:607-609), up to a few more roundings in
+          // (v - min) * (255 / range), the sum's scale and + min * M.  So every
+          // quantised distance is >= lb (1 - 16 u) - M scale / 2 (1 + 1e-5) for
+          // lists of >= 16 vectors, and >= lb for the smaller float-path lists.
+          const uint64_t bnd = s_bound;
+          double lbq = static_cast<double>(s_lb[b0 + grp]);
+          if (s_len[b0 + grp] >= 16)
+            lbq = lbq * (1.0 - 16 * 5.9604644775390625e-8) - 0.5 * M * static_cast<double>(scale) * (1.0 + 1e-5);
+          s_skip[set][grp] = bnd != kEmptyKey && lbq > static_cast<double>(key_dist(bnd));
         }
       }
       __syncthreads();
 
       // ---- score and select ---------------------------------------------
-      const uint32_t pre1 = s_len[b0];
-      const uint32_t pre2 = pre1 + (nb > 1 ? s_len[b0 + 1] : 0u);
-      const uint32_t pre3 = pre2 + (nb > 2 ? s_len[b0 + 2] : 0u);
-      const uint32_t pre4 = pre3 + (nb > 3 ? s_len[b0 + 3] : 0u);
+      // candidates of the batch's lists that are not skipped
+      const uint8_t *skip = s_skip[set];
+      const uint32_t pre1 = skip[0] ? 0u : s_len[b0];
+      const uint32_t pre2 = pre1 + (nb > 1 && !skip[1] ? s_len[b0 + 1] : 0u);
+      const uint32_t pre3 = pre2 + (nb > 2 && !skip[2] ? s_len[b0 + 2] : 0u);
+      const uint32_t pre4 = pre3 + (nb > 3 && !skip[3] ? s_len[b0 + 3] : 0u);
       const uint32_t qset_a = smem_u32(qset);
       for (uint32_t x0 = warp * 32; x0 < pre4; x0 += kScanThreads) {
         const uint32_t x = x0 + lane;
