@@ -214,30 +214,90 @@ cudaError_t launch_rotate_rows(const float *x, size_t n, int d, const float *rot
 // Row selection: one warp per row, WarpTopK over the row's columns.
 // ---------------------------------------------------------------------------
 namespace {
+constexpr int kSelectWarps = 8;
+constexpr int kSelectBuf = 256;  // keys per warp gathered under the bound
+
+// Exact per-row top-k of [rows][cols] values as (order key, column) keys,
+// one warp per row, in two passes over the row:
+//  1. every lane keeps its 2R smallest keys (sorted insertion); the k-th
+//     smallest of these 64R keys bounds the row's k-th key from above (they
+//     are keys of the row);
+//  2. the keys <= that bound -- the row's k smallest among them -- are
+//     gathered in shared memory (ballot / popc append, no sorting in the
+//     loop) and selected with one warp top-k.  If more than kSelectBuf keys
+//     fall under the bound the warp selects from the row directly.
 template <int R>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kSelectWarps * 32)
     select_rows_kernel(const float *__restrict__ dist, size_t rows, size_t cols, size_t ld, int k,
                        uint32_t *__restrict__ out_ids, float *__restrict__ out_dist,
                        unsigned long long *__restrict__ out_keys, size_t out_ld, uint32_t col_base) {
+  __shared__ unsigned long long s_buf[kSelectWarps][kSelectBuf];
+  constexpr int R2 = 2 * R;
   const size_t row = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   if (row >= rows) return;
-  const int lane = lane_id();
+  const int lane = lane_id(), warp = threadIdx.x >> 5;
   const float *drow = dist + row * ld;
+  auto key_at = [&](size_t c) { return pack_key(drow[c], col_base + static_cast<uint32_t>(c)); };
+
+  // pass 1: per-lane 2R smallest, four independent loads in flight
+  uint64_t a[R2];
+#pragma unroll
+  for (int r = 0; r < R2; ++r) a[r] = kEmptyKey;
+  auto insert = [&](uint64_t key) {
+#pragma unroll
+    for (int r = 0; r < R2; ++r) {
+      const uint64_t lo = key < a[r] ? key : a[r];
+      key = key < a[r] ? a[r] : key;
+      a[r] = lo;
+    }
+  };
+  size_t c = lane;
+  for (; c + 96 < cols; c += 128) {
+    const uint64_t k0 = key_at(c), k1 = key_at(c + 32), k2 = key_at(c + 64), k3 = key_at(c + 96);
+    insert(k0);
+    insert(k1);
+    insert(k2);
+    insert(k3);
+  }
+  for (; c < cols; c += 32) insert(key_at(c));
+  WarpTopK<R2> cand;
+  cand.init();
+#pragma unroll
+  for (int r = 0; r < R2; ++r) cand.add(a[r]);
+  const uint64_t bound = cand.get(k - 1);  // kEmptyKey when the row has fewer than k columns
+
+  // pass 2: gather the keys under the bound
+  unsigned long long *buf = s_buf[warp];
+  int n = 0;
+  bool overflow = false;
+  for (size_t c0 = 0; c0 < cols && !overflow; c0 += 32) {
+    const size_t cc = c0 + lane;
+    const uint64_t key = cc < cols ? key_at(cc) : kEmptyKey;
+    const bool take = cc < cols && key <= bound;
+    const unsigned m = __ballot_sync(VG_FULL_MASK, take);
+    if (n + __popc(m) > kSelectBuf) {
+      overflow = true;
+      break;
+    }
+    if (take) buf[n + __popc(m & ((1u << lane) - 1u))] = key;
+    n += __popc(m);
+  }
+  __syncwarp();
   WarpTopK<R> tk;
   tk.init();
-  for (size_t c0 = 0; c0 < cols; c0 += 32) {
-    size_t c = c0 + lane;
-    uint64_t key = c < cols ? pack_key(drow[c], col_base + static_cast<uint32_t>(c)) : kEmptyKey;
-    tk.add(key);
+  if (!overflow) {
+    for (int i0 = 0; i0 < n; i0 += 32) tk.add(i0 + lane < n ? buf[i0 + lane] : kEmptyKey);
+  } else {
+    for (size_t c0 = 0; c0 < cols; c0 += 32) tk.add(c0 + lane < cols ? key_at(c0 + lane) : kEmptyKey);
   }
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    int i = r * 32 + lane;
+    const int i = r * 32 + lane;
     if (i < k) {
-      uint64_t key = tk.v[r];
+      const uint64_t key = tk.v[r];
       if (out_keys) out_keys[row * out_ld + i] = key;
       if (out_ids) {
-        bool real = key != kEmptyKey;
+        const bool real = key != kEmptyKey;
         out_ids[row * out_ld + i] = real ? key_id(key) : 0xffffffffu;
         out_dist[row * out_ld + i] = real ? key_dist(key) : __int_as_float(0x7f800000);
       }
@@ -249,9 +309,8 @@ template <int R>
 cudaError_t launch_select_impl(const float *dist, size_t rows, size_t cols, size_t ld, int k,
                                uint32_t *ids, float *dst, unsigned long long *keys, size_t out_ld,
                                uint32_t col_base, cudaStream_t s) {
-  size_t threads = rows * 32;
-  dim3 grid(static_cast<unsigned>((threads + 255) / 256));
-  select_rows_kernel<R><<<grid, 256, 0, s>>>(dist, rows, cols, ld, k, ids, dst, keys, out_ld, col_base);
+  dim3 grid(static_cast<unsigned>((rows + kSelectWarps - 1) / kSelectWarps));
+  select_rows_kernel<R><<<grid, kSelectWarps * 32, 0, s>>>(dist, rows, cols, ld, k, ids, dst, keys, out_ld, col_base);
   return cudaGetLastError();
 }
 
