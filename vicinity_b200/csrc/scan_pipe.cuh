@@ -9,8 +9,12 @@
 // in the other, so at any time half the warps feed the FP32 pipe and half the
 // shared-memory pipe.  One block barrier per phase separates the sets.
 //
-// The residuals of batch b + 2 are loaded from the centroid rows during phase
-// b and written into the residual buffer that batch b has finished with.
+// Batches are formed as the search goes: the next batch takes the next lists
+// in probe order whose distance lower bound does not exceed the block's k-th
+// distance (list pruning), so pruned lists cost neither a table, a scan nor a
+// phase.  Table builders read their residual subvectors straight from the
+// query and centroid rows (L1-resident), so no residual buffer has to be
+// filled ahead of the batch.
 #pragma once
 
 #include "f32x2.cuh"
@@ -20,8 +24,27 @@ namespace vg {
 
 __host__ __device__ inline size_t pipe_smem_bytes(int d, int M, int ks, int batch, int R) {
   const size_t table = static_cast<size_t>((M * ks + 3) & ~3) * 4;
-  const size_t vec = static_cast<size_t>((d + 3) & ~3) * 4;
-  return static_cast<size_t>(kScanWarps) * 32 * R * 8 + 2 * static_cast<size_t>(batch) * (table + vec);
+  (void)d;
+  return static_cast<size_t>(kScanWarps) * 32 * R * 8 + 2 * static_cast<size_t>(batch) * table;
+}
+
+// D floats of row `a` minus row `b` at offset o, each an IEEE subtraction.
+template <int D>
+__device__ __forceinline__ void load_residual(const float *a, const float *b, int o, bool vec4, float (&r)[D]) {
+  if (D % 4 == 0 && vec4) {
+#pragma unroll
+    for (int j = 0; j < D; j += 4) {
+      const float4 x = *reinterpret_cast<const float4 *>(a + o + j);
+      const float4 y = *reinterpret_cast<const float4 *>(b + o + j);
+      r[j] = __fsub_rn(x.x, y.x);
+      r[j + 1] = __fsub_rn(x.y, y.y);
+      r[j + 2] = __fsub_rn(x.z, y.z);
+      r[j + 3] = __fsub_rn(x.w, y.w);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < D; ++j) r[j] = __fsub_rn(a[o + j], b[o + j]);
+  }
 }
 
 template <int DSUB, int GPT, int R, int KS>
@@ -31,10 +54,9 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_pipe_kernel(const ScanP
   constexpr int ks = KS;
   const int nent = M * ks;
   const int tstride = (nent + 3) & ~3;
-  const int dpad = (d + 3) & ~3;
+  const bool vec4 = (d & 3) == 0;  // rows 16-byte aligned: subvectors load as float4
   unsigned long long *wl = reinterpret_cast<unsigned long long *>(smem);     // [warps][32R]
   float *tables = reinterpret_cast<float *>(wl + kScanWarps * 32 * R);        // [2][batch][tstride]
-  float *qres = tables + 2 * static_cast<size_t>(batch) * tstride;            // [2][batch][dpad]
 
   __shared__ uint32_t s_query;
   __shared__ int s_nvalid;
@@ -42,8 +64,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_pipe_kernel(const ScanP
   __shared__ uint32_t s_list[kScanThreads], s_len[kScanThreads];
   __shared__ uint64_t s_lbeg[kScanThreads], s_coff[kScanThreads];
   __shared__ unsigned long long s_bound;
-  __shared__ float s_lb[kScanThreads];            // distance lower bound of each compacted probe
-  __shared__ uint8_t s_skip[3][kMaxBatch];        // list skipped, per batch (indexed batch % 3)
+  __shared__ float s_lb[kScanThreads];           // distance lower bound of each compacted probe
+  __shared__ uint16_t s_bat[3][kMaxBatch];       // probe positions of batch j (slot j % 3)
+  __shared__ int s_bn[3];                        // lists in batch j (slot j % 3)
+  __shared__ int s_cursor;                       // next probe position to consider
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool build_first = (warp & 1) == 0;
@@ -106,43 +130,39 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_pipe_kernel(const ScanP
       __syncthreads();
     }
     const int nvalid = s_nvalid;
-    const int nbat = (nvalid + batch - 1) / batch;
 
-    // List pruning: a list whose distance lower bound exceeds the block's k-th
-    // distance cannot contribute (every computed distance is >= its bound), so
-    // its table is not built and its codes are not read.  One thread decides
-    // for batch bb just before a block barrier; the flags are read after it,
-    // by builders and scanners alike, and kept until batch bb + 3 reuses them.
-    auto decide = [&](int bb) {
-      if (tid != 0 || bb >= nbat) return;
+    // Batch j: the next `batch` lists from the cursor whose lower bound does
+    // not exceed the block's k-th distance (a pruned list holds no candidate
+    // that could enter the top-k).  Formed by thread 0 just before a block
+    // barrier, read by every thread after it; slot j % 3 is rewritten only
+    // after batch j has been built and scanned.
+    auto form = [&](int j) {
       const uint64_t bnd = s_bound;
       const float bdist = key_dist(bnd);
-      for (int g = 0; g < batch; ++g) {
-        const int li = bb * batch + g;
-        s_skip[bb % 3][g] = li < nvalid && bnd != kEmptyKey && s_lb[li] > bdist;
-      }
+      int n = 0, cur = s_cursor;
+      for (; cur < nvalid && n < batch; ++cur)
+        if (bnd == kEmptyKey || !(s_lb[cur] > bdist)) s_bat[j % 3][n++] = static_cast<uint16_t>(cur);
+      s_bn[j % 3] = n;
+      s_cursor = cur;
     };
 
-    // table of every list of batch b into table set `set` (residuals of batch
-    // b live in residual set b & 1)
-    auto build = [&](int b, int set) {
-      const int nb = min(batch, nvalid - b * batch);
-      const float *qset = qres + static_cast<size_t>(b & 1) * batch * dpad;
+    // tables of batch j into table set `set`
+    auto build = [&](int j, int set) {
+      const int nb = s_bn[j % 3];
       float *tset = tables + static_cast<size_t>(set) * batch * tstride;
 #pragma unroll 1
       for (int g = 0; g < nb; ++g) {
-        if (s_skip[b % 3][g]) continue;
-        const float *qg = qset + g * dpad;
+        const float *cent = p.centroids + static_cast<size_t>(s_list[s_bat[j % 3][g]]) * d;
         float *lg = tset + static_cast<size_t>(g) * tstride;
 #pragma unroll
         for (int i = 0; i < GPT; ++i) {
           const int G = tid + i * kScanThreads;
           if (G < ngroups) {
             float qs[DSUB];
-            load_subvector<DSUB>(qg + ((4 * G) / ks) * DSUB, qs);
+            load_residual<DSUB>(qv, cent, ((4 * G) / ks) * DSUB, vec4, qs);
             f32x2 qq[DSUB];
 #pragma unroll
-            for (int j = 0; j < DSUB; ++j) qq[j] = f2_pack(qs[j], qs[j]);
+            for (int jj = 0; jj < DSUB; ++jj) qq[jj] = f2_pack(qs[jj], qs[jj]);
             const float2 e01 = f2_unpack(sq_dist_x2<DSUB>(qq, cb[i][0], nz));
             const float2 e23 = f2_unpack(sq_dist_x2<DSUB>(qq, cb[i][1], nz));
             *reinterpret_cast<float4 *>(lg + 4 * G) = make_float4(e01.x, e01.y, e23.x, e23.y);
@@ -151,17 +171,15 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_pipe_kernel(const ScanP
       }
     };
 
-    // score and select the candidates of batch b against table set `set`
-    auto scan = [&](int b, int set) {
-      const int b0 = b * batch;
-      const int nb = min(batch, nvalid - b0);
+    // score and select the candidates of batch j against table set `set`
+    auto scan = [&](int j, int set) {
+      const int nb = s_bn[j % 3];
+      const uint16_t *bat = s_bat[j % 3];
       const float *tset = tables + static_cast<size_t>(set) * batch * tstride;
-      // candidates of the batch's lists that are not skipped
-      const uint8_t *skip = s_skip[b % 3];
-      const uint32_t pre1 = skip[0] ? 0u : s_len[b0];
-      const uint32_t pre2 = pre1 + (nb > 1 && !skip[1] ? s_len[b0 + 1] : 0u);
-      const uint32_t pre3 = pre2 + (nb > 2 && !skip[2] ? s_len[b0 + 2] : 0u);
-      const uint32_t pre4 = pre3 + (nb > 3 && !skip[3] ? s_len[b0 + 3] : 0u);
+      const uint32_t pre1 = s_len[bat[0]];
+      const uint32_t pre2 = pre1 + (nb > 1 ? s_len[bat[1]] : 0u);
+      const uint32_t pre3 = pre2 + (nb > 2 ? s_len[bat[2]] : 0u);
+      const uint32_t pre4 = pre3 + (nb > 3 ? s_len[bat[3]] : 0u);
       for (uint32_t x0 = warp * 32; x0 < pre4; x0 += kScanThreads) {
         const uint32_t x = x0 + lane;
         // threshold first: candidates whose partial sum already exceeds it stop early
@@ -177,7 +195,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_pipe_kernel(const ScanP
         if (alive) {
           g = (x >= pre1) + (x >= pre2) + (x >= pre3);
           c = x - (g == 0 ? 0u : g == 1 ? pre1 : g == 2 ? pre2 : pre3);
-          cp = p.list_codes + s_coff[b0 + g] + static_cast<uint64_t>(c) * M;
+          cp = p.list_codes + s_coff[bat[g]] + static_cast<uint64_t>(c) * M;
           lg = tset + static_cast<size_t>(g) * tstride;
         }
         const float dist = adc_row_sum_bounded<KS>(cp, lg, M, ks, tkey, alive);
@@ -185,7 +203,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_pipe_kernel(const ScanP
         const bool pass = alive && dk <= tkey;
         unsigned mask = __ballot_sync(VG_FULL_MASK, pass);
         if (!mask) continue;
-        const uint64_t key = pass ? ((static_cast<uint64_t>(dk) << 32) | p.list_ids[s_lbeg[b0 + g] + c]) : kEmptyKey;
+        const uint64_t key = pass ? ((static_cast<uint64_t>(dk) << 32) | p.list_ids[s_lbeg[bat[g]] + c]) : kEmptyKey;
         if (__popc(mask) > 4) {
           tk.add(key < thr ? key : kEmptyKey);
         } else {
@@ -201,57 +219,25 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_pipe_kernel(const ScanP
       }
     };
 
-    if (nbat > 0) {
-      // prologue: residuals of batches 0 and 1, tables of batch 0
-      for (int i = tid; i < min(2 * batch, nvalid) * d; i += kScanThreads) {
-        const int li = i / d, j = i - li * d;
-        qres[static_cast<size_t>(li / batch) * batch * dpad + (li % batch) * dpad + j] =
-            __fsub_rn(qv[j], p.centroids[static_cast<size_t>(s_list[li]) * d + j]);
-      }
-      decide(0);
-      __syncthreads();
-      build(0, 0);
-      decide(1);
-      __syncthreads();
+    if (tid == 0) {
+      s_cursor = 0;
+      form(0);
+      form(1);
     }
-    for (int b = 0; b < nbat; ++b) {
-      const int set = b & 1;
-      const bool has_next = b + 1 < nbat;
-      // residuals of batch b + 2: centroid rows loaded now, written after the
-      // phase into residual set b & 1 (batch b's, no longer read)
-      const int l2 = (b + 2) * batch;
-      const int n2 = max(0, min(batch, nvalid - l2));
-      float cnext[2];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int i = tid + u * kScanThreads;
-        cnext[u] = 0.0f;
-        if (i < n2 * d) {
-          const int g = i / d, j = i - g * d;
-          cnext[u] = p.centroids[static_cast<size_t>(s_list[l2 + g]) * d + j];
-        }
-      }
+    __syncthreads();
+    if (s_bn[0] > 0) build(0, 0);
+    __syncthreads();
+    for (int j = 0; s_bn[j % 3] > 0; ++j) {
+      const int set = j & 1;
+      const bool has_next = s_bn[(j + 1) % 3] > 0;
       if (build_first) {
-        if (has_next) build(b + 1, set ^ 1);
-        scan(b, set);
+        if (has_next) build(j + 1, set ^ 1);
+        scan(j, set);
       } else {
-        scan(b, set);
-        if (has_next) build(b + 1, set ^ 1);
+        scan(j, set);
+        if (has_next) build(j + 1, set ^ 1);
       }
-      float *qdst = qres + static_cast<size_t>(set) * batch * dpad;
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int i = tid + u * kScanThreads;
-        if (i < n2 * d) {
-          const int g = i / d, j = i - g * d;
-          qdst[g * dpad + j] = __fsub_rn(qv[j], cnext[u]);
-        }
-      }
-      for (int i = tid + 2 * kScanThreads; i < n2 * d; i += kScanThreads) {  // batch * d > 1024 only
-        const int g = i / d, j = i - g * d;
-        qdst[g * dpad + j] = __fsub_rn(qv[j], p.centroids[static_cast<size_t>(s_list[l2 + g]) * d + j]);
-      }
-      decide(b + 2);  // built in phase b + 1, scanned in phase b + 2
+      if (tid == 0) form(j + 2);  // built in phase j + 1, scanned in phase j + 2
       __syncthreads();
     }
 
