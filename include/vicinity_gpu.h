@@ -141,6 +141,14 @@ int vg_ivfpq_search_batch(vg_index *ix, const float *queries, size_t nq,
                           size_t k, size_t nprobe, uint32_t *out_ids,
                           float *out_dist, uint32_t *out_count);
 
+/* src/ivf_pq/search.rs:1602-1617 (find_nearest_centroids) over nq query
+ * rows, normalised first as search does (search.rs:55-66, 1202-1208): out_lists /
+ * out_dist are [nq][p], p = min(nprobe (0: the index default), num
+ * centroids), each row the p nearest lists by 1 - q.c ascending (ties by
+ * list id), with those distances.  nprobe at most 256. */
+int vg_ivfpq_nearest_lists(vg_index *ix, const float *queries, size_t nq,
+                           size_t nprobe, uint32_t *out_lists, float *out_dist);
+
 /* src/ivf_pq/search.rs:1117-1158 (search_reranked) over nq rows: the
  * candidate_pool best approximate candidates re-scored by exact cosine
  * distance 1 - dot.  Unsupported after compact. */

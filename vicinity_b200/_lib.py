@@ -121,6 +121,7 @@ SIGNATURES = {
     "vg_ivfpq_get_info": (_i, [_vp, C.POINTER(VgInfo)]),
     "vg_ivfpq_search_batch": (_i, [_vp, _vp, _sz, _sz, _sz, _vp, _vp, _vp]),
     "vg_ivfpq_search_batch_reranked": (_i, [_vp, _vp, _sz, _sz, _sz, _sz, _vp, _vp, _vp]),
+    "vg_ivfpq_nearest_lists": (_i, [_vp, _vp, _sz, _sz, _vp, _vp]),
     "vg_ivfpq_set_filter_field": (_i, [_vp, C.c_char_p]),
     "vg_ivfpq_add_metadata": (_i, [_vp, C.c_uint32, C.c_char_p]),
     "vg_ivfpq_search_filtered_batch": (_i, [_vp, _vp, _sz, _sz, C.c_char_p, C.c_char_p, _vp, _vp, _vp]),
@@ -142,26 +143,30 @@ SIGNATURES = {
 _lib: C.CDLL | None = None
 
 
-def _preload_torch_nccl() -> None:
-    """Load the NCCL that PyTorch in this environment ships (the nvidia-nccl
-    wheel), when there is one, before the engine library.
+def _preload_torch_libs() -> None:
+    """Load the NCCL and cuBLAS that PyTorch in this environment ships (the
+    nvidia-nccl and nvidia-cublas wheels), when there are any, before the
+    engine library.
 
-    The engine links libnccl.so.2 by soname.  Were the older system copy
-    loaded first, a later `import torch` would bind to it as well and fail
-    on symbols only torch's newer NCCL exports; with torch's copy loaded
-    first both share it (NCCL keeps its C API backward compatible).
+    The engine links libnccl.so.2 and libcublas.so.12 by soname.  Were the
+    system copies loaded first, a later `import torch` would bind to them as
+    well (and fail on symbols only torch's newer NCCL exports) or load a
+    second cuBLAS; with torch's copies loaded first both share them (NCCL and
+    cuBLAS keep their C APIs backward compatible within a major version).
     """
     import importlib.util
 
-    try:
-        spec = importlib.util.find_spec("nvidia.nccl")
-    except (ImportError, ValueError):
-        return
-    for base in (spec.submodule_search_locations or []) if spec else []:
-        path = Path(base) / "lib" / "libnccl.so.2"
-        if path.exists():
-            C.CDLL(os.fspath(path), mode=C.RTLD_GLOBAL)
-            return
+    for pkg, names in (("nvidia.nccl", ("libnccl.so.2",)), ("nvidia.cublas", ("libcublasLt.so.12", "libcublas.so.12"))):
+        try:
+            spec = importlib.util.find_spec(pkg)
+        except (ImportError, ValueError):
+            continue
+        for base in (spec.submodule_search_locations or []) if spec else []:
+            paths = [Path(base) / "lib" / n for n in names]
+            if all(path.exists() for path in paths):
+                for path in paths:
+                    C.CDLL(os.fspath(path), mode=C.RTLD_GLOBAL)
+                break
 
 
 def load() -> C.CDLL:
@@ -174,7 +179,7 @@ def load() -> C.CDLL:
             f"{LIB_PATH} is missing; build it with `python -m vicinity_b200.build` "
             "(the engine has no CPU fallback)"
         )
-    _preload_torch_nccl()
+    _preload_torch_libs()
     lib = C.CDLL(os.fspath(LIB_PATH))
     for name, (res, args) in SIGNATURES.items():
         fn = getattr(lib, name)

@@ -187,6 +187,28 @@ __global__ void list_radius_kernel(const uint8_t *__restrict__ list_codes, const
   }
 }
 
+// Largest centroid norm, rounded up; NaN when any centroid holds a NaN (so
+// that a consumer's bound fails its finiteness test).  One block.
+__global__ void centroid_norm_max_kernel(const float *__restrict__ cent, size_t L, int d, float *__restrict__ out) {
+  __shared__ double red[32];
+  double best = 0.0;
+  for (size_t l = threadIdx.x; l < L; l += blockDim.x) {
+    double s = 0.0;
+    for (int j = 0; j < d; ++j) s += static_cast<double>(cent[l * d + j]) * static_cast<double>(cent[l * d + j]);
+    best = (s > best || s != s) ? s : best;
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    const double o = __shfl_xor_sync(0xffffffffu, best, off);
+    best = (o > best || o != o) ? o : best;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (unsigned w = 1; w < (blockDim.x + 31) / 32; ++w) best = (red[w] > best || red[w] != red[w]) ? red[w] : best;
+    *out = __double2float_ru(sqrt(best) * (1.0 + 1e-12));
+  }
+}
+
 // Deterministic cluster mean: members are visited in ascending order and
 // each dimension is summed sequentially by one thread.
 __global__ void kmeans_update_kernel(const float *__restrict__ x, int d, const uint32_t *__restrict__ sorted_ids,
@@ -324,6 +346,11 @@ cudaError_t launch_list_radius(const uint8_t *list_codes, const uint64_t *code_o
   if (L == 0) return cudaSuccess;
   list_radius_kernel<<<static_cast<unsigned>(L), 256, 0, s>>>(list_codes, code_off, list_off, M, ks, dsub,
                                                               codebooks, radius);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_centroid_norm_max(const float *cent, size_t L, int d, float *out, cudaStream_t s) {
+  centroid_norm_max_kernel<<<1, 1024, 0, s>>>(cent, L, d, out);
   return cudaGetLastError();
 }
 

@@ -16,6 +16,7 @@
 //   pack_off   u64 [Lc]            (ks == 16) 16-byte aligned byte offset of
 //   packed     u8                  each list's nibble-packed codes: vector-major,
 //                                  ceil(M/2) bytes per vector, lists >= 16 only
+#include <cublas_v2.h>
 #include <nccl.h>
 
 #include <algorithm>
@@ -172,6 +173,8 @@ struct vg_index {
   DevBuf vectors, doc_ids, centroids, codebooks, assign, codes;
   DevBuf list_off, list_ids, code_off, list_codes, pack_off, packed;
   DevBuf list_radius;  // f32 [Lc]: largest reconstructed-residual norm per list (list pruning)
+  DevBuf cent_norm;    // f32 [1]: largest centroid norm (probe shortlist error bound)
+  cublasHandle_t blas = nullptr;  // TF32 coarse products (probe shortlist)
   std::vector<uint64_t> h_list_off;
   std::vector<uint32_t> h_doc_ids;
 
@@ -215,7 +218,7 @@ struct vg_index {
     return vectors.cap + doc_ids.cap + centroids.cap + codebooks.cap + assign.cap + codes.cap +
            list_off.cap + list_ids.cap + code_off.cap + list_codes.cap + pack_off.cap + packed.cap +
            owner.cap + rotation.cap + rotation_t.cap + category_d.cap + bitmask_d.cap + cat_counts.cap +
-           list_radius.cap;
+           list_radius.cap + cent_norm.cap;
   }
 };
 
@@ -609,12 +612,57 @@ int build_list_storage(vg_index *ix, const uint32_t *sorted_lists) {
   VG_CU(launch_list_radius(ix->list_codes.as<uint8_t>(), ix->code_off.as<uint64_t>(), ix->list_off.as<uint64_t>(), Lc,
                            static_cast<int>(M), static_cast<int>(ks), static_cast<int>(ix->dsub),
                            ix->codebooks.as<float>(), ix->list_radius.as<float>(), s));
+  VG_CU(ix->cent_norm.reserve(4));
+  VG_CU(launch_centroid_norm_max(ix->centroids.as<float>(), Lc, static_cast<int>(ix->d), ix->cent_norm.as<float>(), s));
   VG_CU(cudaStreamSynchronize(s));
   ix->built = true;
   return VG_OK;
 }
 
 // ---- search -------------------------------------------------------------
+
+// The nprobe nearest lists of rows normalised queries qn (search.rs:1602-1617:
+// 1 - q.c in sequential f32, ascending, ties by list id) into probes / pdist
+// (row stride P).  Many lists: a TF32 tensor-core GEMM gives approximate
+// products and launch_probe_shortlist re-scores, with the reference's
+// arithmetic, every list the approximation cannot rule out -- the same probes
+// as the exact path.  Few lists, or nprobe beyond the shortlist's window: the
+// exact distance tile and a row selection.  Calls mark(3) between the two
+// phases; returns the number of this library's kernels launched in *launches.
+constexpr size_t kShortlistMinLists = 1024;
+
+int coarse_probes(vg_index *ix, const float *qn, size_t rows, size_t P, uint32_t *probes, float *pdist,
+                  uint64_t *launches) {
+  cudaStream_t s = ix->stream;
+  const size_t Lc = ix->num_centroids, d = ix->d;
+  const bool shortlist = Lc >= kShortlistMinLists && P <= 128 && d <= 2048;
+  if (shortlist) {
+    if (!ix->blas) {
+      if (cublasCreate(&ix->blas) != CUBLAS_STATUS_SUCCESS) return fail(VG_ERR_CUDA, "cublasCreate failed");
+    }
+    if (cublasSetStream(ix->blas, s) != CUBLAS_STATUS_SUCCESS) return fail(VG_ERR_CUDA, "cublasSetStream failed");
+    const float one = 1.0f, zero = 0.0f;
+    // column-major: S^T [Lc x rows] = C [Lc x d] * Qn^T [d x rows], i.e. row-major S[rows][Lc] = Qn C^T
+    const cublasStatus_t st =
+        cublasGemmEx(ix->blas, CUBLAS_OP_T, CUBLAS_OP_N, static_cast<int>(Lc), static_cast<int>(rows),
+                     static_cast<int>(d), &one, ix->centroids.p, CUDA_R_32F, static_cast<int>(d), qn, CUDA_R_32F,
+                     static_cast<int>(d), &zero, ix->ws_dist.p, CUDA_R_32F, static_cast<int>(Lc),
+                     CUBLAS_COMPUTE_32F_FAST_TF32, CUBLAS_GEMM_DEFAULT);
+    if (st != CUBLAS_STATUS_SUCCESS) return fail(VG_ERR_CUDA, "cublasGemmEx failed");
+    mark(ix, 3);
+    VG_CU(launch_probe_shortlist(ix->ws_dist.as<float>(), rows, Lc, Lc, qn, static_cast<int>(d),
+                                 ix->centroids.as<float>(), ix->cent_norm.as<float>(), static_cast<int>(P), probes,
+                                 pdist, P, s));
+    *launches += 1;
+    return VG_OK;
+  }
+  VG_CU(launch_coarse_dist(qn, rows, ix->centroids.as<float>(), Lc, static_cast<int>(d), ix->ws_dist.as<float>(), Lc,
+                           s));
+  mark(ix, 3);
+  VG_CU(launch_select_rows(ix->ws_dist.as<float>(), rows, Lc, Lc, static_cast<int>(P), probes, pdist, P, 0, s));
+  *launches += 2;
+  return VG_OK;
+}
 
 int write_padding(vg_index *ix, size_t nq, size_t k, uint32_t *out_ids, float *out_dist, uint32_t *out_count) {
   std::vector<uint32_t> ids(nq * k, 0xffffffffu), cnt(nq, 0);
@@ -670,13 +718,9 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   double coarse_ms = 0, select_ms = 0;
   for (size_t r0 = 0; r0 < nq; r0 += tile) {
     size_t rows = std::min(tile, nq - r0);
-    VG_CU(launch_coarse_dist(ix->ws_qn.as<float>() + r0 * d, rows, ix->centroids.as<float>(), Lc,
-                             static_cast<int>(d), ix->ws_dist.as<float>(), Lc, s));
-    mark(ix, 3);
-    VG_CU(launch_select_rows(ix->ws_dist.as<float>(), rows, Lc, Lc, static_cast<int>(P),
-                             ix->ws_probes.as<uint32_t>() + r0 * P, ix->ws_pdist.as<float>() + r0 * P, P, 0, s));
+    VG_TRY(coarse_probes(ix, ix->ws_qn.as<float>() + r0 * d, rows, P, ix->ws_probes.as<uint32_t>() + r0 * P,
+                         ix->ws_pdist.as<float>() + r0 * P, &ix->launches));
     mark(ix, 4);
-    ix->launches += 2;
     if (prof && r0 + tile < nq) {  // accumulate per tile when tiled
       float a = 0, b = 0;
       VG_CU(cudaEventSynchronize(ix->ev[4]));
@@ -905,10 +949,8 @@ int search_filtered_impl(vg_index *ix, const float *queries, size_t nq, size_t k
   VG_CU(ix->ws_pdist.reserve(nq * P * 4));
   for (size_t r0 = 0; r0 < nq; r0 += tile) {
     const size_t rows = std::min(tile, nq - r0);
-    VG_CU(launch_coarse_dist(ix->ws_qn.as<float>() + r0 * d, rows, ix->centroids.as<float>(), Lc,
-                             static_cast<int>(d), ix->ws_dist.as<float>(), Lc, s));
-    VG_CU(launch_select_rows(ix->ws_dist.as<float>(), rows, Lc, Lc, static_cast<int>(P),
-                             ix->ws_probes.as<uint32_t>() + r0 * P, ix->ws_pdist.as<float>() + r0 * P, P, 0, s));
+    VG_TRY(coarse_probes(ix, ix->ws_qn.as<float>() + r0 * d, rows, P, ix->ws_probes.as<uint32_t>() + r0 * P,
+                         ix->ws_pdist.as<float>() + r0 * P, &ix->launches));
   }
 
   // which queries find fewer than k matches in their probed lists
@@ -1203,9 +1245,10 @@ int vg_ivfpq_destroy(vg_index *ix) {
     for (int i = 0; i < kPhaseEvents; ++i)
       if (ix->ev[i]) cudaEventDestroy(ix->ev[i]);
     if (ix->h_err) cudaFreeHost(ix->h_err);
+    if (ix->blas) cublasDestroy(ix->blas);
     if (ix->own_stream) cudaStreamDestroy(ix->own_stream);
+    delete ix;
   }
-  delete ix;
   return VG_OK;
 }
 
@@ -1380,6 +1423,42 @@ int vg_ivfpq_search_batch(vg_index *ix, const float *queries, size_t nq, size_t 
   if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
   DeviceGuard g(ix->device);
   return search_impl(ix, queries, nq, k, 0, nprobe, out_ids, out_dist, out_count);
+}
+
+int vg_ivfpq_nearest_lists(vg_index *ix, const float *queries, size_t nq, size_t nprobe, uint32_t *out_lists,
+                           float *out_dist) {
+  if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
+  DeviceGuard g(ix->device);
+  if (!ix->built) return fail(VG_ERR_NOT_BUILT, "index not built");
+  const size_t Lc = ix->num_centroids, d = ix->d;
+  const size_t P = std::min(nprobe ? nprobe : static_cast<size_t>(ix->params.nprobe), Lc);
+  if (nq == 0 || P == 0) return VG_OK;
+  if (!queries || !out_lists || !out_dist) return fail(VG_ERR_INVALID_PARAMETER, "null query or output buffer");
+  if (P > 256) return fail(VG_ERR_INVALID_PARAMETER, "nprobe must be at most 256");
+  if (nq * P > 0xffffffffull) return fail(VG_ERR_INVALID_PARAMETER, "nq * nprobe must fit in 32 bits");
+  cudaStream_t s = ix->stream;
+  const float *dq = queries;
+  if (!is_device_ptr(queries)) {
+    VG_CU(ix->ws_q.reserve(nq * d * 4));
+    VG_CU(cudaMemcpyAsync(ix->ws_q.p, queries, nq * d * 4, cudaMemcpyHostToDevice, s));
+    dq = ix->ws_q.as<float>();
+  }
+  VG_CU(ix->ws_qn.reserve(nq * d * 4));
+  VG_CU(launch_normalize_rows(dq, nq, static_cast<int>(d), ix->ws_qn.as<float>(), s));
+  const size_t tile = std::max<size_t>(1, std::min(nq, kDistBudgetBytes / (Lc * 4)));
+  VG_CU(ix->ws_dist.reserve(tile * Lc * 4));
+  VG_CU(ix->ws_probes.reserve(nq * P * 4));
+  VG_CU(ix->ws_pdist.reserve(nq * P * 4));
+  uint64_t launches = 1;
+  for (size_t r0 = 0; r0 < nq; r0 += tile) {
+    const size_t rows = std::min(tile, nq - r0);
+    VG_TRY(coarse_probes(ix, ix->ws_qn.as<float>() + r0 * d, rows, P, ix->ws_probes.as<uint32_t>() + r0 * P,
+                         ix->ws_pdist.as<float>() + r0 * P, &launches));
+  }
+  VG_CU(cudaMemcpyAsync(out_lists, ix->ws_probes.p, nq * P * 4, cudaMemcpyDefault, s));
+  VG_CU(cudaMemcpyAsync(out_dist, ix->ws_pdist.p, nq * P * 4, cudaMemcpyDefault, s));
+  VG_CU(cudaStreamSynchronize(s));
+  return VG_OK;
 }
 
 int vg_ivfpq_search_batch_reranked(vg_index *ix, const float *queries, size_t nq, size_t k, size_t candidate_pool,

@@ -48,6 +48,15 @@ cudaError_t launch_select_rows(const float *dist, size_t rows, size_t cols,
                                float *out_dist, size_t out_ld,
                                uint32_t col_base, cudaStream_t s);
 
+// Exact top-k probes per row from approximate products s[row][l] ~ q . c_l
+// (TF32 tensor-core GEMM): candidates within the approximation's error bound
+// of the k-th are re-scored with the reference's sequential 1 - dot; rows
+// with too many candidates or non-finite inputs are scored exactly over all
+// L.  Same output as launch_select_rows on exact 1 - dot distances.
+cudaError_t launch_probe_shortlist(const float *s, size_t rows, size_t L, size_t ld, const float *qn, int d,
+                                   const float *cent, const float *cmax, int k, uint32_t *out_ids, float *out_dist,
+                                   size_t out_ld, cudaStream_t st);
+
 // Same selection, but writing packed keys (for later merging).
 cudaError_t launch_select_rows_keys(const float *dist, size_t rows,
                                     size_t cols, size_t ld, int k,
@@ -117,6 +126,10 @@ cudaError_t launch_filter_widen(const uint32_t *probes, size_t nq, int P, const 
 cudaError_t launch_list_radius(const uint8_t *list_codes, const uint64_t *code_off, const uint64_t *list_off,
                                size_t L, int M, int ks, int dsub, const float *codebooks, float *radius,
                                cudaStream_t s);
+
+// *out = the largest centroid norm (double, rounded up to float), NaN when a
+// centroid holds a NaN.
+cudaError_t launch_centroid_norm_max(const float *cent, size_t L, int d, float *out, cudaStream_t s);
 
 // lb[q][p] = a lower bound on every computed ADC distance of probe p of query
 // q: (||r|| - radius)^2 with r the float residual qn[q] - centroid (computed

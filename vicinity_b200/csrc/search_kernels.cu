@@ -339,6 +339,216 @@ cudaError_t launch_select_rows_keys(const float *dist, size_t rows, size_t cols,
 }
 
 // ---------------------------------------------------------------------------
+// Probe shortlist from approximate coarse products (search.rs:1602-1617).
+//
+// s[row][l] approximates q . c_l (a TF32 tensor-core product) within eps(row)
+// = (2^-9 + 2^-19 + 3 d 2^-24) |q| cmax (TF32 truncation of both operands,
+// accumulation, and the rounding of the exact sequential dot) plus 2^-20.  With
+// A = 1 - s, every probe of the exact top-P has A <= A_P + 2 eps, where A_P is
+// the P-th smallest A: those are gathered (under an upper bound on A_P taken
+// from the lanes' 2R smallest), re-scored with the reference's arithmetic --
+// 1 - (sum_j q_j c_j in j order, separately rounded products and adds) -- and
+// the exact top-P is kept.  A row whose window overflows the buffer, or whose
+// inputs are not finite, is scored exactly over every centroid.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int kShortBuf = 512;  // gathered candidates per warp
+
+// 1 - sum_j q_j c_j with the sum taken in j order from +0, every product and
+// add rounded separately (the exact coarse distance).  q in shared memory;
+// c a centroid row, read 32 floats ahead when rows are 16-byte aligned.
+__device__ __forceinline__ float exact_one_minus_dot(const float *q, const float *__restrict__ c, int d, bool vec) {
+  float acc = 0.0f;
+  int j = 0;
+  if (vec) {
+    const float4 *c4 = reinterpret_cast<const float4 *>(c);
+    const float4 *q4 = reinterpret_cast<const float4 *>(q);
+    for (; j + 32 <= d; j += 32) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __ldg(c4 + (j >> 2) + u);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float4 w = q4[(j >> 2) + u];
+        acc = __fadd_rn(acc, __fmul_rn(w.x, v[u].x));
+        acc = __fadd_rn(acc, __fmul_rn(w.y, v[u].y));
+        acc = __fadd_rn(acc, __fmul_rn(w.z, v[u].z));
+        acc = __fadd_rn(acc, __fmul_rn(w.w, v[u].w));
+      }
+    }
+  }
+  for (; j < d; ++j) acc = __fadd_rn(acc, __fmul_rn(q[j], __ldg(c + j)));
+  return __fsub_rn(1.0f, acc);
+}
+
+// Visit columns [0, L) of a row, four at a time: fn(col, v, valid[4]) with
+// v the four approximate products.  Trip counts are warp-uniform (fn may use
+// warp votes); rows must be 16-byte aligned with L % 4 == 0 when vec is set.
+// The last visit (kLast) streams the row past L2 with evict-first loads.
+template <bool kLast, typename F>
+__device__ __forceinline__ void for_each_quad(const float *__restrict__ srow, size_t L, bool vec, int lane, F &&fn) {
+  if (vec) {
+    const float4 *r4 = reinterpret_cast<const float4 *>(srow);
+    const size_t n4 = L >> 2;
+    size_t b = 0;
+    for (; b + 128 <= n4; b += 128) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = kLast ? __ldcs(r4 + b + u * 32 + lane) : __ldg(r4 + b + u * 32 + lane);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) fn((b + u * 32 + lane) * 4, v[u], true, true, true, true);
+    }
+    for (; b < n4; b += 32) {
+      const size_t i = b + lane;
+      const float4 v = i < n4 ? (kLast ? __ldcs(r4 + i) : __ldg(r4 + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      fn(i * 4, v, i < n4, i < n4, i < n4, i < n4);
+    }
+  } else {
+    for (size_t b = 0; b < L; b += 128) {
+      const size_t c = b + lane * 4;
+      float4 v;
+      v.x = c < L ? srow[c] : 0.f;
+      v.y = c + 1 < L ? srow[c + 1] : 0.f;
+      v.z = c + 2 < L ? srow[c + 2] : 0.f;
+      v.w = c + 3 < L ? srow[c + 3] : 0.f;
+      fn(c, v, c < L, c + 1 < L, c + 2 < L, c + 3 < L);
+    }
+  }
+}
+
+template <int R>
+__global__ void __launch_bounds__(kSelectWarps * 32)
+    shortlist_kernel(const float *__restrict__ s, size_t rows, size_t L, size_t ld, const float *__restrict__ qn,
+                     int d, const float *__restrict__ cent, const float *__restrict__ cmax_p, int k,
+                     uint32_t *__restrict__ out_ids, float *__restrict__ out_dist, size_t out_ld) {
+  extern __shared__ __align__(16) unsigned char sh[];
+  constexpr int R2 = 2 * R;
+  const int lane = lane_id(), warp = threadIdx.x >> 5;
+  const size_t row = static_cast<size_t>(blockIdx.x) * kSelectWarps + warp;
+  if (row >= rows) return;
+  uint32_t *buf = reinterpret_cast<uint32_t *>(sh) + static_cast<size_t>(warp) * kShortBuf;
+  const int dpad = (d + 3) & ~3;
+  float *qs = reinterpret_cast<float *>(reinterpret_cast<uint32_t *>(sh) + kSelectWarps * kShortBuf) +
+              static_cast<size_t>(warp) * dpad;
+  const float *srow = s + row * ld;
+  const float *qrow = qn + row * d;
+  for (int j = lane; j < d; j += 32) qs[j] = qrow[j];
+  __syncwarp();
+  double qq = 0.0;
+  for (int j = lane; j < d; j += 32) qq += static_cast<double>(qs[j]) * qs[j];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) qq += __shfl_xor_sync(VG_FULL_MASK, qq, off);
+  const double eps = (1.0 / 512 + 1.0 / 524288 + 4.0 * d / 16777216.0 + 1.0 / 4194304) * sqrt(qq) *
+                         static_cast<double>(*cmax_p) * 1.01 +
+                     1.0 / 1048576;
+  bool exact_all = !(eps < 1.0);  // non-finite or useless bound
+  const bool svec = (L & 3) == 0 && (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(s) & 15) == 0;
+  const bool cvec = (d & 3) == 0 && (reinterpret_cast<uintptr_t>(cent) & 15) == 0;
+
+  uint64_t a[R2];
+#pragma unroll
+  for (int r = 0; r < R2; ++r) a[r] = kEmptyKey;
+  auto insert = [&](uint64_t key) {
+#pragma unroll
+    for (int r = 0; r < R2; ++r) {
+      const uint64_t lo = key < a[r] ? key : a[r];
+      key = key < a[r] ? a[r] : key;
+      a[r] = lo;
+    }
+  };
+  if (!exact_all) {
+    for_each_quad<false>(srow, L, svec, lane, [&](size_t c, float4 v, bool ox, bool oy, bool oz, bool ow) {
+      if (ox) insert(pack_key(__fsub_rn(1.0f, v.x), static_cast<uint32_t>(c)));
+      if (oy) insert(pack_key(__fsub_rn(1.0f, v.y), static_cast<uint32_t>(c + 1)));
+      if (oz) insert(pack_key(__fsub_rn(1.0f, v.z), static_cast<uint32_t>(c + 2)));
+      if (ow) insert(pack_key(__fsub_rn(1.0f, v.w), static_cast<uint32_t>(c + 3)));
+    });
+  }
+  WarpTopK<R2> cand;
+  cand.init();
+#pragma unroll
+  for (int r = 0; r < R2; ++r) cand.add(a[r]);
+  const uint64_t ub = cand.get(k - 1);
+  // every exact top-k list has approximate distance <= limit (rounded up)
+  const float limit =
+      ub == kEmptyKey ? __int_as_float(0x7f800000) : __double2float_ru(static_cast<double>(key_dist(ub)) + 2.0 * eps);
+  if (!(limit < __int_as_float(0x7f800000)) && ub != kEmptyKey) exact_all = true;
+
+  int n = 0;
+  if (!exact_all) {
+    bool over = false;
+    for_each_quad<true>(srow, L, svec, lane, [&](size_t c, float4 v, bool ox, bool oy, bool oz, bool ow) {
+      const bool t[4] = {ox && !(__fsub_rn(1.0f, v.x) > limit), oy && !(__fsub_rn(1.0f, v.y) > limit),
+                         oz && !(__fsub_rn(1.0f, v.z) > limit), ow && !(__fsub_rn(1.0f, v.w) > limit)};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const unsigned m = __ballot_sync(VG_FULL_MASK, t[h]);
+        const int pos = n + __popc(m & ((1u << lane) - 1u));
+        if (t[h] && pos < kShortBuf) buf[pos] = static_cast<uint32_t>(c + h);
+        n += __popc(m);
+      }
+    });
+    over = n > kShortBuf;
+    exact_all = over;
+  }
+  __syncwarp();
+  WarpTopK<R> tk;
+  tk.init();
+  if (!exact_all) {
+    for (int i0 = 0; i0 < n; i0 += 32) {
+      uint64_t key = kEmptyKey;
+      if (i0 + lane < n) {
+        const uint32_t c = buf[i0 + lane];
+        key = pack_key(exact_one_minus_dot(qs, cent + static_cast<size_t>(c) * d, d, cvec), c);
+      }
+      tk.add(key);
+    }
+  } else {
+    for (size_t c0 = 0; c0 < L; c0 += 32) {
+      const size_t c = c0 + lane;
+      tk.add(c < L ? pack_key(exact_one_minus_dot(qs, cent + c * d, d, cvec), static_cast<uint32_t>(c)) : kEmptyKey);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = r * 32 + lane;
+    if (i < k) {
+      const uint64_t key = tk.v[r];
+      const bool real = key != kEmptyKey;
+      out_ids[row * out_ld + i] = real ? key_id(key) : 0xffffffffu;
+      out_dist[row * out_ld + i] = real ? key_dist(key) : __int_as_float(0x7f800000);
+    }
+  }
+}
+
+template <int R>
+cudaError_t launch_shortlist_impl(const float *s, size_t rows, size_t L, size_t ld, const float *qn, int d,
+                                  const float *cent, const float *cmax, int k, uint32_t *ids, float *dst, size_t out_ld,
+                                  cudaStream_t st) {
+  const size_t smem = static_cast<size_t>(kSelectWarps) * (kShortBuf * 4 + static_cast<size_t>((d + 3) & ~3) * 4);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(shortlist_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  dim3 grid(static_cast<unsigned>((rows + kSelectWarps - 1) / kSelectWarps));
+  shortlist_kernel<R><<<grid, kSelectWarps * 32, smem, st>>>(s, rows, L, ld, qn, d, cent, cmax, k, ids, dst, out_ld);
+  return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_probe_shortlist(const float *s, size_t rows, size_t L, size_t ld, const float *qn, int d,
+                                   const float *cent, const float *cmax, int k, uint32_t *out_ids, float *out_dist,
+                                   size_t out_ld, cudaStream_t st) {
+  if (rows == 0 || k <= 0) return cudaSuccess;
+  if (k <= 32) return launch_shortlist_impl<1>(s, rows, L, ld, qn, d, cent, cmax, k, out_ids, out_dist, out_ld, st);
+  if (k <= 64) return launch_shortlist_impl<2>(s, rows, L, ld, qn, d, cent, cmax, k, out_ids, out_dist, out_ld, st);
+  if (k <= 128) return launch_shortlist_impl<4>(s, rows, L, ld, qn, d, cent, cmax, k, out_ids, out_dist, out_ld, st);
+  if (k <= 256) return launch_shortlist_impl<8>(s, rows, L, ld, qn, d, cent, cmax, k, out_ids, out_dist, out_ld, st);
+  return cudaErrorInvalidValue;
+}
+
+// ---------------------------------------------------------------------------
 // List-major pair grouping (counting sort by list id).
 // ---------------------------------------------------------------------------
 namespace {

@@ -306,6 +306,25 @@ class IVFPQIndex:
         out[np.arange(k)[None, :] >= counts.astype(np.int64)[:, None]] = MISSING_LABEL
         return out, dists
 
+    def nearest_lists(self, queries, nprobe=None):
+        """search.rs:1602-1617 (find_nearest_centroids) for each normalised
+        query row: ([nq, p] list ids, [nq, p] distances 1 - q.c), nearest
+        first, p = min(nprobe or the index default, number of centroids)."""
+        q = np.ascontiguousarray(queries, dtype=np.float32)
+        if q.ndim != 2 or q.shape[1] != self._dim:
+            raise ValueError(
+                f"queries dimension mismatch: index expects {self._dim}, got {q.shape[-1] if q.ndim else 0}"
+            )
+        np_ = 0 if nprobe is None else int(nprobe)
+        if nprobe is not None and np_ == 0:
+            raise ValueError("nprobe must be greater than 0")
+        info = self.info()
+        p = min(np_ or info.nprobe, info.num_centroids)
+        lists = np.empty((q.shape[0], p), dtype=np.uint32)
+        dists = np.empty((q.shape[0], p), dtype=np.float32)
+        _lib.check(self._lib.vg_ivfpq_nearest_lists(self._h, _ptr(q), q.shape[0], np_, _ptr(lists), _ptr(dists)))
+        return lists.astype(np.int64), dists
+
     def search_raw(self, q_ptr: int, nq: int, k: int, nprobe: int, ids_ptr: int, dist_ptr: int,
                    count_ptr: int = 0, rerank_pool: int = 0) -> None:
         """Search with caller-provided buffers (host or device addresses)."""
