@@ -54,6 +54,8 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--nq", type=int, default=None, help="query batch (default: the configuration's)")
+    p.add_argument("--n", type=int, default=None,
+                   help="database vectors (default: the configuration's; smaller only for profiler captures)")
     p.add_argument("--shard", choices=["queries", "lists"], default="queries",
                    help="multi-GPU layout: index replicas with per-rank query batches, or list sharding")
     return p.parse_args()
@@ -196,13 +198,13 @@ def run_engine(args):
     cfg = CONFIGS[args.config]
     if cfg["centre"] == "flat":
         raise SystemExit("config 2 is the flat path; the IVF-PQ bench runs configs 0, 1, 3")
-    n, d, k = cfg["n"], cfg["d"], cfg["k"]
+    n, d, k = args.n or cfg["n"], cfg["d"], cfg["k"]
     nq = args.nq or cfg["nq"]
     t0 = time.time()
     by_lists = world > 1 and args.shard == "lists"
     # per-rank batches: rows [rank*nq, (rank+1)*nq) of the configuration's query
     # stream (rank 0's batch is the single-GPU batch)
-    x, q = config_data(args.config, seed=0, nq=nq * (1 if by_lists else world))
+    x, q = config_data(args.config, seed=0, n=n, nq=nq * (1 if by_lists else world))
     if not by_lists:
         q = np.ascontiguousarray(q[rank * nq:(rank + 1) * nq])
     ix = IVFPQIndex(d, num_clusters=cfg["nlist"], num_codebooks=cfg["M"], codebook_size=cfg["ks"],
