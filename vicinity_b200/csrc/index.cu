@@ -202,7 +202,7 @@ struct vg_index {
 
   // search workspace
   DevBuf ws_q, ws_qn, ws_dist, ws_probes, ws_pdist, ws_scalars,
-      ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_lb;
+      ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_lb, ws_rec;
   DevBuf stats;  // u64 [pairs, vectors, code bytes] accumulated while profiling
 
   // error flag of bounded device waits, in mapped pinned host memory
@@ -743,12 +743,18 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
                              ix->stats.as<unsigned long long>(), s));
   }
   // list pruning bounds (tables without a rotation; see launch_probe_lb)
+  // and, for 256-entry codebooks, the probe records the streaming kernel copies whole
   const bool prune = ix->h_rotation.empty();
+  const bool recs = prune && ix->params.codebook_size == 256;
   if (prune) {
     VG_CU(ix->ws_lb.reserve(nq * P * 4));
+    if (recs) VG_CU(ix->ws_rec.reserve(nq * P * sizeof(ProbeRec)));
     VG_CU(launch_probe_lb(ix->ws_qn.as<float>(), nq, static_cast<int>(d), ix->ws_probes.as<uint32_t>(),
                           static_cast<int>(P), ix->centroids.as<float>(), ix->list_radius.as<float>(),
-                          static_cast<int>(M), static_cast<int>(ix->dsub), ix->ws_lb.as<float>(), s));
+                          static_cast<int>(M), static_cast<int>(ix->dsub), ix->ws_lb.as<float>(),
+                          ix->list_off.as<uint64_t>(), ix->code_off.as<uint64_t>(),
+                          ix->world > 1 ? ix->owner.as<uint8_t>() : nullptr,
+                          recs ? ix->ws_rec.as<ProbeRec>() : nullptr, s));
     ix->launches += 1;
   }
   mark(ix, 5);
@@ -784,6 +790,7 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   sp.doc_ids = doc_map;
   sp.rot_t = ix->h_rotation.empty() ? nullptr : ix->rotation_t.as<float>();
   sp.probe_lb = prune ? ix->ws_lb.as<float>() : nullptr;
+  sp.probe_rec = recs ? ix->ws_rec.as<ProbeRec>() : nullptr;
   sp.d = static_cast<int>(d);
   sp.M = static_cast<int>(M);
   sp.ks = static_cast<int>(ix->params.codebook_size);
@@ -1221,7 +1228,10 @@ int vg_ivfpq_create(size_t dim, const vg_ivfpq_params *params, int device, vg_in
     e = cudaHostGetDevicePointer(reinterpret_cast<void **>(&ix->d_err), ix->h_err, 0);
   }
   if (const char *fam = std::getenv("VICINITY_SCAN_KERNEL"))
-    vg::set_scan_family(std::strcmp(fam, "pipeline") == 0 ? 0 : std::strcmp(fam, "query") == 0 ? 1 : 2);
+    vg::set_scan_family(std::strcmp(fam, "pipeline") == 0 ? 0
+                        : std::strcmp(fam, "query") == 0  ? 1
+                        : std::strcmp(fam, "double") == 0 ? 2
+                                                          : 3);
   if (e != cudaSuccess) {
     vg_ivfpq_destroy(ix);
     return cuda_fail(e, "stream/event creation");
@@ -1240,7 +1250,7 @@ int vg_ivfpq_destroy(vg_index *ix) {
                       &ix->list_off, &ix->list_ids, &ix->code_off, &ix->list_codes, &ix->pack_off, &ix->packed,
                       &ix->owner, &ix->ws_q, &ix->ws_qn, &ix->ws_dist, &ix->ws_probes, &ix->ws_pdist,
                       &ix->ws_scalars, &ix->ws_keys, &ix->ws_all_keys, &ix->ws_out_ids, &ix->ws_out_dist,
-                      &ix->ws_out_count, &ix->stats})
+                      &ix->ws_out_count, &ix->stats, &ix->ws_lb, &ix->ws_rec})
       b->release();
     for (int i = 0; i < kPhaseEvents; ++i)
       if (ix->ev[i]) cudaEventDestroy(ix->ev[i]);

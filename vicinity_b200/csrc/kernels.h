@@ -135,15 +135,30 @@ cudaError_t launch_centroid_norm_max(const float *cent, size_t L, int d, float *
 // q: (||r|| - radius)^2 with r the float residual qn[q] - centroid (computed
 // as the scan kernels compute it), times 1 - (M + dsub + 2) 2^-24 for the
 // rounding of the table sums, rounded down; 0 when ||r|| <= radius.
+// When rec is non-null, rec[q][p] also receives the probe's record (list id,
+// or 0xffffffff when the probe is empty or its list not owned; list length,
+// list_off and code_off of the list; the bound).
 cudaError_t launch_probe_lb(const float *qn, size_t nq, int d, const uint32_t *probes, int P,
                             const float *centroids, const float *radius, int M, int dsub, float *lb,
-                            cudaStream_t s);
+                            const uint64_t *list_off, const uint64_t *code_off, const uint8_t *owner,
+                            struct ProbeRec *rec, cudaStream_t s);
 
 // Number of positions where a[i] != b[i] added to *changed.
 cudaError_t launch_count_diff_u8(const uint8_t *a, const uint8_t *b, size_t n,
                                  unsigned int *changed, cudaStream_t s);
 
 // ---- scan_kernels.cu ------------------------------------------------------
+
+// One probe of one query as the streaming 8-bit kernel reads it: 32 bytes,
+// copied into shared memory a query at a time.
+struct ProbeRec {
+  uint32_t list;  // 0xffffffff: no list to scan (empty probe or list not owned)
+  uint32_t len;   // vectors in the list
+  uint64_t lbeg;  // list_off[list]
+  uint64_t coff;  // code_off[list]
+  float lb;       // distance lower bound (list pruning)
+  uint32_t pad;
+};
 
 struct ScanParams {
   const float *qn;          // [nq][d] normalised queries
@@ -174,6 +189,7 @@ struct ScanParams {
   const uint64_t *bitmask;       // [L] categories present per list (at build)
   int want_cat;                  // category to keep, 0..63
   const float *probe_lb;         // [nq][P] distance lower bound per probe (nullable: no list pruning)
+  const ProbeRec *probe_rec;     // [nq][P] probe records (streaming 8-bit kernel; nullable)
 };
 
 // Fused per-query kernel: for each probed list the query residual, the ADC

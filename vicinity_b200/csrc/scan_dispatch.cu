@@ -15,9 +15,11 @@ cudaError_t launch_scan_four(const ScanParams &p, int dsub, int ept, int num_sms
 cudaError_t launch_scan_eight(const ScanParams &p, int dsub, int ept, int num_sms, cudaStream_t s);
 cudaError_t launch_scan_ws(const ScanParams &p, int dsub, int ept, int num_sms, cudaStream_t s);
 cudaError_t launch_scan_pipe(const ScanParams &p, int dsub, int gpt, int num_sms, cudaStream_t s);
+cudaError_t launch_scan_stream(const ScanParams &p, int dsub, int gpt, int num_sms, cudaStream_t s);
 
 namespace {
-int g_family = 2;  // double-buffered kernel by default
+// 0 warp-specialised, 1 query-major, 2 double-buffered, 3 query-stream (default)
+int g_family = 3;
 
 // Entries per producer thread for the warp-specialised kernel (0 = n/a).
 int pick_ws_ept(const ScanParams &p) {
@@ -47,7 +49,10 @@ cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms, cudaStream_t s) 
   const int ws = p.rot_t ? 0 : pick_ws_ept(p);
   if (ws) return launch_scan_ws(p, p.dsub, ws, num_sms, s);
   const int gpt = pick_gpt(p);
-  if (g_family == 2 && gpt && p.ks == 256 && !p.rot_t) return launch_scan_pipe(p, p.dsub, gpt, num_sms, s);
+  if (g_family >= 2 && gpt && p.ks == 256 && !p.rot_t) {
+    if (g_family == 3 && p.probe_rec && p.P <= 256) return launch_scan_stream(p, p.dsub, gpt, num_sms, s);
+    return launch_scan_pipe(p, p.dsub, gpt, num_sms, s);
+  }
   if (p.ks == 16) return launch_scan_four(p, gpt ? p.dsub : 0, gpt, num_sms, s);
   return launch_scan_eight(p, gpt ? p.dsub : 0, gpt, num_sms, s);
 }
@@ -62,7 +67,11 @@ int ivfpq_scan_variant_name(const ScanParams &p, char *buf, size_t len) {
   const int ws = p.rot_t ? 0 : pick_ws_ept(p);
   if (ws) return snprintf(buf, len, "ivfpq_ws_kernel<%d,%d,1,256>", p.dsub, ws);
   const int gpt = pick_gpt(p);
-  if (g_family == 2 && gpt && p.ks == 256 && !p.rot_t) return snprintf(buf, len, "ivfpq_pipe_kernel<%d,%d,1,256>", p.dsub, gpt);
+  if (g_family >= 2 && gpt && p.ks == 256 && !p.rot_t) {
+    if (g_family == 3 && p.probe_rec && p.P <= 256)
+      return snprintf(buf, len, "ivfpq_stream_kernel<%d,%d,1,256>", p.dsub, gpt);
+    return snprintf(buf, len, "ivfpq_pipe_kernel<%d,%d,1,256>", p.dsub, gpt);
+  }
   if (p.ks == 16) return snprintf(buf, len, "ivfpq_four_kernel<%d>", p.k <= 32 ? 1 : p.k <= 64 ? 2 : p.k <= 128 ? 4 : 8);
   return snprintf(buf, len, "ivfpq_query_kernel<%d,%d,%d,%s>", gpt ? p.dsub : 0, gpt,
                   p.k <= 32 ? 1 : p.k <= 64 ? 2 : p.k <= 128 ? 4 : 8, p.ks == 16 ? "4bit" : "8bit");

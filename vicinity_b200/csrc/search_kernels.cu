@@ -828,14 +828,19 @@ cudaError_t launch_filter_widen(const uint32_t *probes, size_t nq, int P, const 
 namespace {
 __global__ void probe_lb_kernel(const float *__restrict__ qn, size_t nq, int d, const uint32_t *__restrict__ probes,
                                 int P, const float *__restrict__ centroids, const float *__restrict__ radius,
-                                int M, int dsub, float *__restrict__ lb) {
+                                int M, int dsub, float *__restrict__ lb, const uint64_t *__restrict__ list_off,
+                                const uint64_t *__restrict__ code_off, const uint8_t *__restrict__ owner,
+                                ProbeRec *__restrict__ rec) {
   const size_t pair = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   if (pair >= nq * P) return;
   const int lane = lane_id();
   const size_t q = pair / P;
   const uint32_t l = probes[pair];
-  if (l == 0xffffffffu) {
-    if (lane == 0) lb[pair] = 0.0f;
+  if (l == 0xffffffffu || (owner && !owner[l])) {
+    if (lane == 0) {
+      lb[pair] = 0.0f;
+      if (rec) rec[pair] = ProbeRec{0xffffffffu, 0u, 0ull, 0ull, 0.0f, 0u};
+    }
     return;
   }
   const float *qv = qn + q * d;
@@ -853,17 +858,22 @@ __global__ void probe_lb_kernel(const float *__restrict__ qn, size_t nq, int d, 
     double b = gap > 0.0 ? gap * gap : 0.0;
     b *= 1.0 - (static_cast<double>(M + dsub + 2) * 5.9604644775390625e-8 + 1e-12);
     lb[pair] = __double2float_rd(b);
+    if (rec) {
+      const uint64_t beg = list_off[l];
+      rec[pair] = ProbeRec{l, static_cast<uint32_t>(list_off[l + 1] - beg), beg, code_off[l], __double2float_rd(b), 0u};
+    }
   }
 }
 }  // namespace
 
 cudaError_t launch_probe_lb(const float *qn, size_t nq, int d, const uint32_t *probes, int P,
                             const float *centroids, const float *radius, int M, int dsub, float *lb,
+                            const uint64_t *list_off, const uint64_t *code_off, const uint8_t *owner, ProbeRec *rec,
                             cudaStream_t s) {
   const size_t pairs = nq * static_cast<size_t>(P);
   if (pairs == 0) return cudaSuccess;
-  probe_lb_kernel<<<static_cast<unsigned>((pairs * 32 + 255) / 256), 256, 0, s>>>(qn, nq, d, probes, P, centroids,
-                                                                                 radius, M, dsub, lb);
+  probe_lb_kernel<<<static_cast<unsigned>((pairs * 32 + 255) / 256), 256, 0, s>>>(
+      qn, nq, d, probes, P, centroids, radius, M, dsub, lb, list_off, code_off, owner, rec);
   return cudaGetLastError();
 }
 
