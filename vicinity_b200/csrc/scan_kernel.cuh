@@ -123,10 +123,13 @@ __device__ __forceinline__ float adc_row_sum_bounded(const uint8_t *cp, const fl
   const int row_len = KS > 0 ? KS : ks;
   float acc = 0.0f;
   if ((M & 15) == 0) {
+    // the next 16 codes are loaded while the current 16 are summed
+    uint4 wn = alive ? *reinterpret_cast<const uint4 *>(cp) : make_uint4(0u, 0u, 0u, 0u);
     for (int m0 = 0; m0 < M; m0 += 16) {
       if (!__any_sync(VG_FULL_MASK, alive)) break;
+      const uint4 w = wn;
+      if (alive && m0 + 16 < M) wn = *reinterpret_cast<const uint4 *>(cp + m0 + 16);
       if (alive) {
-        const uint4 w = *reinterpret_cast<const uint4 *>(cp + m0);
         const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
         const float *row = lg + m0 * row_len;
 #pragma unroll

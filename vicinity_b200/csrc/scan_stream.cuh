@@ -134,11 +134,15 @@ __global__ void __launch_bounds__(kScanThreads, 1)
       const float bdist = key_dist(bnd);
       const ProbeRec *r = recs + static_cast<size_t>(F) * P;
       int c0 = s_cursor[F];
-      while (c0 < P && cnt < batch) {
+      // a query's first batches are formed before its earlier ones have been
+      // scored (no bound yet, nothing pruned): batch j of a query holds at
+      // most j + 1 lists, so pruning starts after its nearest list
+      const int cap = min(batch, s_formed[F] + 1);
+      while (c0 < P && cnt < cap) {
         const int pos = c0 + lane;
         const bool ok = pos < P && r[pos].list != 0xffffffffu && !(bnd != kEmptyKey && r[pos].lb > bdist);
         const unsigned m = __ballot_sync(VG_FULL_MASK, ok);
-        const int avail = __popc(m), take = min(avail, batch - cnt);
+        const int avail = __popc(m), take = min(avail, cap - cnt);
         const int rank = __popc(m & ((1u << lane) - 1u));
         if (ok && rank < take) s_bat[j % 3][cnt + rank] = static_cast<uint16_t>(pos);
         if (take < avail) {  // batch full: resume after the last list taken
