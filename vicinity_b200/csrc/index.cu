@@ -632,7 +632,8 @@ int build_list_storage(vg_index *ix, const uint32_t *sorted_lists) {
 constexpr size_t kShortlistMinLists = 1024;
 
 int coarse_probes(vg_index *ix, const float *qn, size_t rows, size_t P, uint32_t *probes, float *pdist,
-                  uint64_t *launches) {
+                  uint64_t *launches, const ProbeBoundArgs *bounds = nullptr, bool *bounds_done = nullptr) {
+  if (bounds_done) *bounds_done = false;
   cudaStream_t s = ix->stream;
   const size_t Lc = ix->num_centroids, d = ix->d;
   const bool shortlist = Lc >= kShortlistMinLists && P <= 128 && d <= 2048;
@@ -652,8 +653,9 @@ int coarse_probes(vg_index *ix, const float *qn, size_t rows, size_t P, uint32_t
     mark(ix, 3);
     VG_CU(launch_probe_shortlist(ix->ws_dist.as<float>(), rows, Lc, Lc, qn, static_cast<int>(d),
                                  ix->centroids.as<float>(), ix->cent_norm.as<float>(), static_cast<int>(P), probes,
-                                 pdist, P, s));
+                                 pdist, P, bounds ? *bounds : ProbeBoundArgs{}, s));
     *launches += 1;
+    if (bounds_done) *bounds_done = bounds != nullptr;
     return VG_OK;
   }
   VG_CU(launch_coarse_dist(qn, rows, ix->centroids.as<float>(), Lc, static_cast<int>(d), ix->ws_dist.as<float>(), Lc,
@@ -715,11 +717,28 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   VG_CU(ix->ws_dist.reserve(tile * Lc * 4));
   VG_CU(ix->ws_probes.reserve(nq * P * 4));
   VG_CU(ix->ws_pdist.reserve(nq * P * 4));
+  // list pruning bounds (tables without a rotation; see launch_probe_lb)
+  // and, for 256-entry codebooks, the probe records the streaming kernel
+  // copies whole: written by the probe shortlist when it runs, else below
+  const bool prune = ix->h_rotation.empty();
+  const bool recs = prune && ix->params.codebook_size == 256;
+  if (prune) {
+    VG_CU(ix->ws_lb.reserve(nq * P * 4));
+    if (recs) VG_CU(ix->ws_rec.reserve(nq * P * sizeof(ProbeRec)));
+  }
+  bool bounds_done = prune;
   double coarse_ms = 0, select_ms = 0;
   for (size_t r0 = 0; r0 < nq; r0 += tile) {
     size_t rows = std::min(tile, nq - r0);
+    ProbeBoundArgs ba{ix->list_radius.as<float>(), static_cast<int>(M), static_cast<int>(ix->dsub),
+                      ix->list_off.as<uint64_t>(), ix->code_off.as<uint64_t>(),
+                      ix->world > 1 ? ix->owner.as<uint8_t>() : nullptr,
+                      prune ? ix->ws_lb.as<float>() + r0 * P : nullptr,
+                      recs ? ix->ws_rec.as<ProbeRec>() + r0 * P : nullptr};
+    bool tile_done = false;
     VG_TRY(coarse_probes(ix, ix->ws_qn.as<float>() + r0 * d, rows, P, ix->ws_probes.as<uint32_t>() + r0 * P,
-                         ix->ws_pdist.as<float>() + r0 * P, &ix->launches));
+                         ix->ws_pdist.as<float>() + r0 * P, &ix->launches, prune ? &ba : nullptr, &tile_done));
+    bounds_done = bounds_done && tile_done;
     mark(ix, 4);
     if (prof && r0 + tile < nq) {  // accumulate per tile when tiled
       float a = 0, b = 0;
@@ -742,13 +761,7 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
                              static_cast<int>(M), ix->params.codebook_size == 16,
                              ix->stats.as<unsigned long long>(), s));
   }
-  // list pruning bounds (tables without a rotation; see launch_probe_lb)
-  // and, for 256-entry codebooks, the probe records the streaming kernel copies whole
-  const bool prune = ix->h_rotation.empty();
-  const bool recs = prune && ix->params.codebook_size == 256;
-  if (prune) {
-    VG_CU(ix->ws_lb.reserve(nq * P * 4));
-    if (recs) VG_CU(ix->ws_rec.reserve(nq * P * sizeof(ProbeRec)));
+  if (prune && !bounds_done) {
     VG_CU(launch_probe_lb(ix->ws_qn.as<float>(), nq, static_cast<int>(d), ix->ws_probes.as<uint32_t>(),
                           static_cast<int>(P), ix->centroids.as<float>(), ix->list_radius.as<float>(),
                           static_cast<int>(M), static_cast<int>(ix->dsub), ix->ws_lb.as<float>(),

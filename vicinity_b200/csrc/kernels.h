@@ -53,9 +53,32 @@ cudaError_t launch_select_rows(const float *dist, size_t rows, size_t cols,
 // of the k-th are re-scored with the reference's sequential 1 - dot; rows
 // with too many candidates or non-finite inputs are scored exactly over all
 // L.  Same output as launch_select_rows on exact 1 - dot distances.
+// One probe of one query as the streaming 8-bit kernel reads it: 32 bytes,
+// copied into shared memory a query at a time.
+struct ProbeRec {
+  uint32_t list;  // 0xffffffff: no list to scan (empty probe or list not owned)
+  uint32_t len;   // vectors in the list
+  uint64_t lbeg;  // list_off[list]
+  uint64_t coff;  // code_off[list]
+  float lb;       // distance lower bound (list pruning)
+  uint32_t pad;
+};
+
+// List-pruning bounds and probe records of selected probes, written beside
+// them (same row stride); lb == nullptr: none.  Same values as
+// launch_probe_lb.
+struct ProbeBoundArgs {
+  const float *radius;
+  int M, dsub;
+  const uint64_t *list_off, *code_off;
+  const uint8_t *owner;  // nullable: every list owned
+  float *lb;
+  ProbeRec *rec;         // nullable
+};
+
 cudaError_t launch_probe_shortlist(const float *s, size_t rows, size_t L, size_t ld, const float *qn, int d,
                                    const float *cent, const float *cmax, int k, uint32_t *out_ids, float *out_dist,
-                                   size_t out_ld, cudaStream_t st);
+                                   size_t out_ld, const ProbeBoundArgs &bounds, cudaStream_t st);
 
 // Same selection, but writing packed keys (for later merging).
 cudaError_t launch_select_rows_keys(const float *dist, size_t rows,
@@ -148,17 +171,6 @@ cudaError_t launch_count_diff_u8(const uint8_t *a, const uint8_t *b, size_t n,
                                  unsigned int *changed, cudaStream_t s);
 
 // ---- scan_kernels.cu ------------------------------------------------------
-
-// One probe of one query as the streaming 8-bit kernel reads it: 32 bytes,
-// copied into shared memory a query at a time.
-struct ProbeRec {
-  uint32_t list;  // 0xffffffff: no list to scan (empty probe or list not owned)
-  uint32_t len;   // vectors in the list
-  uint64_t lbeg;  // list_off[list]
-  uint64_t coff;  // code_off[list]
-  float lb;       // distance lower bound (list pruning)
-  uint32_t pad;
-};
 
 struct ScanParams {
   const float *qn;          // [nq][d] normalised queries

@@ -420,7 +420,8 @@ template <int R>
 __global__ void __launch_bounds__(kSelectWarps * 32)
     shortlist_kernel(const float *__restrict__ s, size_t rows, size_t L, size_t ld, const float *__restrict__ qn,
                      int d, const float *__restrict__ cent, const float *__restrict__ cmax_p, int k,
-                     uint32_t *__restrict__ out_ids, float *__restrict__ out_dist, size_t out_ld) {
+                     uint32_t *__restrict__ out_ids, float *__restrict__ out_dist, size_t out_ld,
+                     const ProbeBoundArgs bnd) {
   extern __shared__ __align__(16) unsigned char sh[];
   constexpr int R2 = 2 * R;
   const int lane = lane_id(), warp = threadIdx.x >> 5;
@@ -491,6 +492,16 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
     over = n > kShortBuf;
     exact_all = over;
   }
+  // The row of products is not read again: drop its lines from L2 without
+  // writing them back (whole 128-byte lines inside the row only), so the
+  // search kernels that follow do not pay for its write-back.
+  __syncwarp();
+  {
+    const uintptr_t lo = (reinterpret_cast<uintptr_t>(srow) + 127) & ~uintptr_t(127);
+    const uintptr_t hi = (reinterpret_cast<uintptr_t>(srow + L)) & ~uintptr_t(127);
+    for (uintptr_t a = lo + 128 * static_cast<uintptr_t>(lane); a < hi; a += 128 * 32)
+      asm volatile("discard.global.L2 [%0], 128;" ::"l"(a) : "memory");
+  }
   __syncwarp();
   WarpTopK<R> tk;
   tk.init();
@@ -517,6 +528,47 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
       const bool real = key != kEmptyKey;
       out_ids[row * out_ld + i] = real ? key_id(key) : 0xffffffffu;
       out_dist[row * out_ld + i] = real ? key_dist(key) : __int_as_float(0x7f800000);
+      if (bnd.lb) {  // the probe's pruning bound, as probe_lb_kernel computes it
+        const uint32_t l = key_id(key);
+        const size_t o = row * out_ld + i;
+        if (!real || (bnd.owner && !bnd.owner[l])) {
+          bnd.lb[o] = 0.0f;
+          if (bnd.rec) bnd.rec[o] = ProbeRec{0xffffffffu, 0u, 0ull, 0ull, 0.0f, 0u};
+        } else {
+          const float *c = cent + static_cast<size_t>(l) * d;
+          double sq = 0.0;
+          int j = 0;
+          if (cvec) {  // 32 floats of the centroid row in flight at a time
+            const float4 *c4 = reinterpret_cast<const float4 *>(c);
+            const float4 *q4 = reinterpret_cast<const float4 *>(qs);
+            for (; j + 32 <= d; j += 32) {
+              float4 v[8];
+#pragma unroll
+              for (int u = 0; u < 8; ++u) v[u] = __ldg(c4 + (j >> 2) + u);
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                const float4 a = q4[(j >> 2) + u];
+                const double r0 = __fsub_rn(a.x, v[u].x), r1 = __fsub_rn(a.y, v[u].y);
+                const double r2 = __fsub_rn(a.z, v[u].z), r3 = __fsub_rn(a.w, v[u].w);
+                sq += r0 * r0 + r1 * r1 + r2 * r2 + r3 * r3;
+              }
+            }
+          }
+          for (; j < d; ++j) {
+            const double rj = __fsub_rn(qs[j], __ldg(c + j));
+            sq += rj * rj;
+          }
+          const double gap = sqrt(sq) - static_cast<double>(bnd.radius[l]);
+          double b = gap > 0.0 ? gap * gap : 0.0;
+          b *= 1.0 - (static_cast<double>(bnd.M + bnd.dsub + 2) * 5.9604644775390625e-8 + 1e-12);
+          const float lbf = __double2float_rd(b);
+          bnd.lb[o] = lbf;
+          if (bnd.rec) {
+            const uint64_t beg = bnd.list_off[l];
+            bnd.rec[o] = ProbeRec{l, static_cast<uint32_t>(bnd.list_off[l + 1] - beg), beg, bnd.code_off[l], lbf, 0u};
+          }
+        }
+      }
     }
   }
 }
@@ -524,7 +576,7 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
 template <int R>
 cudaError_t launch_shortlist_impl(const float *s, size_t rows, size_t L, size_t ld, const float *qn, int d,
                                   const float *cent, const float *cmax, int k, uint32_t *ids, float *dst, size_t out_ld,
-                                  cudaStream_t st) {
+                                  const ProbeBoundArgs &bnd, cudaStream_t st) {
   const size_t smem = static_cast<size_t>(kSelectWarps) * (kShortBuf * 4 + static_cast<size_t>((d + 3) & ~3) * 4);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(shortlist_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -532,19 +584,20 @@ cudaError_t launch_shortlist_impl(const float *s, size_t rows, size_t L, size_t 
     if (e != cudaSuccess) return e;
   }
   dim3 grid(static_cast<unsigned>((rows + kSelectWarps - 1) / kSelectWarps));
-  shortlist_kernel<R><<<grid, kSelectWarps * 32, smem, st>>>(s, rows, L, ld, qn, d, cent, cmax, k, ids, dst, out_ld);
+  shortlist_kernel<R><<<grid, kSelectWarps * 32, smem, st>>>(s, rows, L, ld, qn, d, cent, cmax, k, ids, dst, out_ld,
+                                                              bnd);
   return cudaGetLastError();
 }
 }  // namespace
 
 cudaError_t launch_probe_shortlist(const float *s, size_t rows, size_t L, size_t ld, const float *qn, int d,
                                    const float *cent, const float *cmax, int k, uint32_t *out_ids, float *out_dist,
-                                   size_t out_ld, cudaStream_t st) {
+                                   size_t out_ld, const ProbeBoundArgs &bnd, cudaStream_t st) {
   if (rows == 0 || k <= 0) return cudaSuccess;
-  if (k <= 32) return launch_shortlist_impl<1>(s, rows, L, ld, qn, d, cent, cmax, k, out_ids, out_dist, out_ld, st);
-  if (k <= 64) return launch_shortlist_impl<2>(s, rows, L, ld, qn, d, cent, cmax, k, out_ids, out_dist, out_ld, st);
-  if (k <= 128) return launch_shortlist_impl<4>(s, rows, L, ld, qn, d, cent, cmax, k, out_ids, out_dist, out_ld, st);
-  if (k <= 256) return launch_shortlist_impl<8>(s, rows, L, ld, qn, d, cent, cmax, k, out_ids, out_dist, out_ld, st);
+  if (k <= 32) return launch_shortlist_impl<1>(s, rows, L, ld, qn, d, cent, cmax, k, out_ids, out_dist, out_ld, bnd, st);
+  if (k <= 64) return launch_shortlist_impl<2>(s, rows, L, ld, qn, d, cent, cmax, k, out_ids, out_dist, out_ld, bnd, st);
+  if (k <= 128) return launch_shortlist_impl<4>(s, rows, L, ld, qn, d, cent, cmax, k, out_ids, out_dist, out_ld, bnd, st);
+  if (k <= 256) return launch_shortlist_impl<8>(s, rows, L, ld, qn, d, cent, cmax, k, out_ids, out_dist, out_ld, bnd, st);
   return cudaErrorInvalidValue;
 }
 
