@@ -187,6 +187,36 @@ __global__ void list_radius_kernel(const uint8_t *__restrict__ list_codes, const
   }
 }
 
+// Largest codeword norm of each subspace (double, rounded up): rad[m] =
+// max_c |codebooks[m][c]|, and rad[M] = max_m rad[m].  One block.
+__global__ void subspace_radius_kernel(const float *__restrict__ codebooks, int M, int ks, int dsub,
+                                       float *__restrict__ rad) {
+  __shared__ float red[32];
+  float top = 0.0f;
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    double best = 0.0;
+    for (int c = 0; c < ks; ++c) {
+      const float *cw = codebooks + (static_cast<size_t>(m) * ks + c) * dsub;
+      double s = 0.0;
+      for (int j = 0; j < dsub; ++j) s += static_cast<double>(cw[j]) * static_cast<double>(cw[j]);
+      best = (s > best || s != s) ? s : best;
+    }
+    const float r = __double2float_ru(sqrt(best) * (1.0 + 1e-12));
+    rad[m] = r;
+    top = (r > top || r != r) ? r : top;
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    const float o = __shfl_xor_sync(0xffffffffu, top, off);
+    top = (o > top || o != o) ? o : top;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = top;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (unsigned w = 1; w < (blockDim.x + 31) / 32; ++w) top = (red[w] > top || red[w] != red[w]) ? red[w] : top;
+    rad[M] = top;
+  }
+}
+
 // Largest centroid norm, rounded up; NaN when any centroid holds a NaN (so
 // that a consumer's bound fails its finiteness test).  One block.
 __global__ void centroid_norm_max_kernel(const float *__restrict__ cent, size_t L, int d, float *__restrict__ out) {
@@ -346,6 +376,12 @@ cudaError_t launch_list_radius(const uint8_t *list_codes, const uint64_t *code_o
   if (L == 0) return cudaSuccess;
   list_radius_kernel<<<static_cast<unsigned>(L), 256, 0, s>>>(list_codes, code_off, list_off, M, ks, dsub,
                                                               codebooks, radius);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_subspace_radius(const float *codebooks, int M, int ks, int dsub, float *rad, cudaStream_t s) {
+  if (M <= 0) return cudaSuccess;
+  subspace_radius_kernel<<<1, 256, 0, s>>>(codebooks, M, ks, dsub, rad);
   return cudaGetLastError();
 }
 

@@ -174,6 +174,7 @@ struct vg_index {
   DevBuf list_off, list_ids, code_off, list_codes, pack_off, packed;
   DevBuf list_radius;  // f32 [Lc]: largest reconstructed-residual norm per list (list pruning)
   DevBuf cent_norm;    // f32 [1]: largest centroid norm (probe shortlist error bound)
+  DevBuf sub_radius;   // f32 [M]: largest codeword norm per subspace (4-bit list pruning)
   cublasHandle_t blas = nullptr;  // TF32 coarse products (probe shortlist)
   std::vector<uint64_t> h_list_off;
   std::vector<uint32_t> h_doc_ids;
@@ -202,7 +203,7 @@ struct vg_index {
 
   // search workspace
   DevBuf ws_q, ws_qn, ws_dist, ws_probes, ws_pdist, ws_scalars,
-      ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_lb, ws_rec;
+      ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_lb, ws_rec, ws_lbq;
   DevBuf stats;  // u64 [pairs, vectors, code bytes] accumulated while profiling
 
   // error flag of bounded device waits, in mapped pinned host memory
@@ -218,7 +219,7 @@ struct vg_index {
     return vectors.cap + doc_ids.cap + centroids.cap + codebooks.cap + assign.cap + codes.cap +
            list_off.cap + list_ids.cap + code_off.cap + list_codes.cap + pack_off.cap + packed.cap +
            owner.cap + rotation.cap + rotation_t.cap + category_d.cap + bitmask_d.cap + cat_counts.cap +
-           list_radius.cap + cent_norm.cap;
+           list_radius.cap + cent_norm.cap + sub_radius.cap;
   }
 };
 
@@ -612,6 +613,9 @@ int build_list_storage(vg_index *ix, const uint32_t *sorted_lists) {
   VG_CU(launch_list_radius(ix->list_codes.as<uint8_t>(), ix->code_off.as<uint64_t>(), ix->list_off.as<uint64_t>(), Lc,
                            static_cast<int>(M), static_cast<int>(ks), static_cast<int>(ix->dsub),
                            ix->codebooks.as<float>(), ix->list_radius.as<float>(), s));
+  VG_CU(ix->sub_radius.reserve((M + 1) * 4));
+  VG_CU(launch_subspace_radius(ix->codebooks.as<float>(), static_cast<int>(M), static_cast<int>(ks),
+                               static_cast<int>(ix->dsub), ix->sub_radius.as<float>(), s));
   VG_CU(ix->cent_norm.reserve(4));
   VG_CU(launch_centroid_norm_max(ix->centroids.as<float>(), Lc, static_cast<int>(ix->d), ix->cent_norm.as<float>(), s));
   VG_CU(cudaStreamSynchronize(s));
@@ -722,19 +726,25 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   // copies whole: written by the probe shortlist when it runs, else below
   const bool prune = ix->h_rotation.empty();
   const bool recs = prune && ix->params.codebook_size == 256;
+  const bool quant = prune && ix->params.codebook_size == 16;  // bounds of quantised 4-bit distances
   if (prune) {
     VG_CU(ix->ws_lb.reserve(nq * P * 4));
     if (recs) VG_CU(ix->ws_rec.reserve(nq * P * sizeof(ProbeRec)));
+    if (quant) VG_CU(ix->ws_lbq.reserve(nq * P * 4));
   }
+  auto bound_args = [&](size_t r0) {
+    return ProbeBoundArgs{ix->list_radius.as<float>(), static_cast<int>(M), static_cast<int>(ix->dsub),
+                          ix->list_off.as<uint64_t>(), ix->code_off.as<uint64_t>(),
+                          ix->world > 1 ? ix->owner.as<uint8_t>() : nullptr,
+                          prune ? ix->ws_lb.as<float>() + r0 * P : nullptr,
+                          recs ? ix->ws_rec.as<ProbeRec>() + r0 * P : nullptr, ix->sub_radius.as<float>(),
+                          quant ? ix->ws_lbq.as<float>() + r0 * P : nullptr};
+  };
   bool bounds_done = prune;
   double coarse_ms = 0, select_ms = 0;
   for (size_t r0 = 0; r0 < nq; r0 += tile) {
     size_t rows = std::min(tile, nq - r0);
-    ProbeBoundArgs ba{ix->list_radius.as<float>(), static_cast<int>(M), static_cast<int>(ix->dsub),
-                      ix->list_off.as<uint64_t>(), ix->code_off.as<uint64_t>(),
-                      ix->world > 1 ? ix->owner.as<uint8_t>() : nullptr,
-                      prune ? ix->ws_lb.as<float>() + r0 * P : nullptr,
-                      recs ? ix->ws_rec.as<ProbeRec>() + r0 * P : nullptr};
+    const ProbeBoundArgs ba = bound_args(r0);
     bool tile_done = false;
     VG_TRY(coarse_probes(ix, ix->ws_qn.as<float>() + r0 * d, rows, P, ix->ws_probes.as<uint32_t>() + r0 * P,
                          ix->ws_pdist.as<float>() + r0 * P, &ix->launches, prune ? &ba : nullptr, &tile_done));
@@ -763,11 +773,7 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   }
   if (prune && !bounds_done) {
     VG_CU(launch_probe_lb(ix->ws_qn.as<float>(), nq, static_cast<int>(d), ix->ws_probes.as<uint32_t>(),
-                          static_cast<int>(P), ix->centroids.as<float>(), ix->list_radius.as<float>(),
-                          static_cast<int>(M), static_cast<int>(ix->dsub), ix->ws_lb.as<float>(),
-                          ix->list_off.as<uint64_t>(), ix->code_off.as<uint64_t>(),
-                          ix->world > 1 ? ix->owner.as<uint8_t>() : nullptr,
-                          recs ? ix->ws_rec.as<ProbeRec>() : nullptr, s));
+                          static_cast<int>(P), ix->centroids.as<float>(), bound_args(0), s));
     ix->launches += 1;
   }
   mark(ix, 5);
@@ -804,6 +810,7 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   sp.rot_t = ix->h_rotation.empty() ? nullptr : ix->rotation_t.as<float>();
   sp.probe_lb = prune ? ix->ws_lb.as<float>() : nullptr;
   sp.probe_rec = recs ? ix->ws_rec.as<ProbeRec>() : nullptr;
+  sp.probe_lbq = quant ? ix->ws_lbq.as<float>() : nullptr;
   sp.d = static_cast<int>(d);
   sp.M = static_cast<int>(M);
   sp.ks = static_cast<int>(ix->params.codebook_size);
@@ -1263,7 +1270,7 @@ int vg_ivfpq_destroy(vg_index *ix) {
                       &ix->list_off, &ix->list_ids, &ix->code_off, &ix->list_codes, &ix->pack_off, &ix->packed,
                       &ix->owner, &ix->ws_q, &ix->ws_qn, &ix->ws_dist, &ix->ws_probes, &ix->ws_pdist,
                       &ix->ws_scalars, &ix->ws_keys, &ix->ws_all_keys, &ix->ws_out_ids, &ix->ws_out_dist,
-                      &ix->ws_out_count, &ix->stats, &ix->ws_lb, &ix->ws_rec})
+                      &ix->ws_out_count, &ix->stats, &ix->ws_lb, &ix->ws_rec, &ix->ws_lbq})
       b->release();
     for (int i = 0; i < kPhaseEvents; ++i)
       if (ix->ev[i]) cudaEventDestroy(ix->ev[i]);

@@ -74,6 +74,11 @@ struct ProbeBoundArgs {
   const uint8_t *owner;  // nullable: every list owned
   float *lb;
   ProbeRec *rec;         // nullable
+  // 4-bit tables: a lower bound on every quantised distance of the probe,
+  // known before its table is built (sub_radius[M]: the largest codeword
+  // norm of any subspace); lbq == nullptr: none
+  const float *sub_radius;
+  float *lbq;
 };
 
 cudaError_t launch_probe_shortlist(const float *s, size_t rows, size_t L, size_t ld, const float *qn, int d,
@@ -150,6 +155,10 @@ cudaError_t launch_list_radius(const uint8_t *list_codes, const uint64_t *code_o
                                size_t L, int M, int ks, int dsub, const float *codebooks, float *radius,
                                cudaStream_t s);
 
+// rad[m] = the largest codeword norm of subspace m (double, rounded up);
+// rad[M] = the largest of them.  rad holds M + 1 floats.
+cudaError_t launch_subspace_radius(const float *codebooks, int M, int ks, int dsub, float *rad, cudaStream_t s);
+
 // *out = the largest centroid norm (double, rounded up to float), NaN when a
 // centroid holds a NaN.
 cudaError_t launch_centroid_norm_max(const float *cent, size_t L, int d, float *out, cudaStream_t s);
@@ -158,13 +167,11 @@ cudaError_t launch_centroid_norm_max(const float *cent, size_t L, int d, float *
 // q: (||r|| - radius)^2 with r the float residual qn[q] - centroid (computed
 // as the scan kernels compute it), times 1 - (M + dsub + 2) 2^-24 for the
 // rounding of the table sums, rounded down; 0 when ||r|| <= radius.
-// When rec is non-null, rec[q][p] also receives the probe's record (list id,
-// or 0xffffffff when the probe is empty or its list not owned; list length,
-// list_off and code_off of the list; the bound).
+// b.lb[q][p] (and, when non-null, b.lbq and b.rec) for every probe, with
+// the same values the probe shortlist writes beside the probes it selects;
+// b.rec[q][p].list is 0xffffffff when the probe is empty or its list not owned.
 cudaError_t launch_probe_lb(const float *qn, size_t nq, int d, const uint32_t *probes, int P,
-                            const float *centroids, const float *radius, int M, int dsub, float *lb,
-                            const uint64_t *list_off, const uint64_t *code_off, const uint8_t *owner,
-                            struct ProbeRec *rec, cudaStream_t s);
+                            const float *centroids, const struct ProbeBoundArgs &b, cudaStream_t s);
 
 // Number of positions where a[i] != b[i] added to *changed.
 cudaError_t launch_count_diff_u8(const uint8_t *a, const uint8_t *b, size_t n,
@@ -202,6 +209,7 @@ struct ScanParams {
   int want_cat;                  // category to keep, 0..63
   const float *probe_lb;         // [nq][P] distance lower bound per probe (nullable: no list pruning)
   const ProbeRec *probe_rec;     // [nq][P] probe records (streaming 8-bit kernel; nullable)
+  const float *probe_lbq;        // [nq][P] bound on quantised 4-bit distances before the table (nullable)
 };
 
 // Fused per-query kernel: for each probed list the query residual, the ADC

@@ -12,7 +12,7 @@ cudaError_t launch_four_variant(const ScanParams &p, int num_sms, cudaStream_t s
   if (e != cudaSuccess) return e;
   e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if (e != cudaSuccess) return e;
-  const size_t reserve = 12288;  // static shared memory of the kernel (~10.5 KB)
+  const size_t reserve = 14336;  // static shared memory of the kernel (~12.3 KB)
   const size_t smem = four_smem_bytes(p.M, p.dsub, R, p.rot_t != nullptr);
   if (smem + reserve > static_cast<size_t>(optin)) return cudaErrorInvalidConfiguration;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));

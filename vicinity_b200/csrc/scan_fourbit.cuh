@@ -16,7 +16,12 @@
 //     offset is an immediate.  All lanes read the same 16-byte row, so the
 //     lookups are free of bank conflicts;
 //   - lists under 16 vectors use the unquantised float table and the
-//     sequential float sum, as the reference does (search.rs:1261).
+//     sequential float sum, as the reference does (search.rs:1261);
+//   - batches are formed one ahead from the lists whose quantised distances
+//     may still come under the block's k-th distance (a bound computed before
+//     the table exists, from the residual's per-subspace norms), so pruned
+//     lists cost no table; after quantisation the exact scale decides again
+//     whether the list is scored.
 // The quantised distance is sum * scale + min * M (pq_simd.rs:721-769) with
 // the integer sum exact in any order.
 #pragma once
@@ -97,6 +102,9 @@ __global__ void __launch_bounds__(kScanThreads, 2) ivfpq_four_kernel(const ScanP
   __shared__ float s_rmin[kMaxBatch][kFourGroup / 32], s_rmax[kMaxBatch][kFourGroup / 32];
   __shared__ float s_scale[2][kMaxBatch], s_fbase[2][kMaxBatch];
   __shared__ float s_lb[kScanThreads];     // distance lower bound of each compacted probe (float tables)
+  __shared__ float s_lbq[kScanThreads];    // bound on its quantised distances, before its table is built
+  __shared__ uint16_t s_bat[3][kMaxBatch];  // probe positions of batch j (ring j % 3)
+  __shared__ int s_bn[3], s_cur;
   __shared__ uint8_t s_skip[2][kMaxBatch];  // list not scanned (pruned), per table set
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -140,20 +148,43 @@ __global__ void __launch_bounds__(kScanThreads, 2) ivfpq_four_kernel(const ScanP
         s_lbeg[pos] = b;
         s_len[pos] = static_cast<uint32_t>(p.list_off[l + 1] - b);
         s_lb[pos] = p.probe_lb ? p.probe_lb[static_cast<size_t>(q) * P + tid] : 0.0f;
+        s_lbq[pos] = p.probe_lbq ? p.probe_lbq[static_cast<size_t>(q) * P + tid] : -__int_as_float(0x7f800000);
       }
       if (tid == 0) s_nvalid = total;
       __syncthreads();
     }
     const int nvalid = s_nvalid;
 
-    for (int b0 = 0, set = 0; b0 < nvalid; b0 += kMaxBatch, set ^= 1) {
-      const int nb = min(kMaxBatch, nvalid - b0);
+    // Batch j (thread 0, before the barrier that precedes scoring batch j - 1):
+    // the next lists in probe order whose quantised distances may still come
+    // under the block's k-th distance -- the others get no table at all.
+    // Batch j holds at most j + 1 lists: the first are formed before anything
+    // has been scored.
+    auto form = [&](int j) {
+      const uint64_t bnd = s_bound;
+      const float bdist = key_dist(bnd);
+      const int cap = min(kMaxBatch, j + 1);
+      int n = 0, c = s_cur;
+      for (; c < nvalid && n < cap; ++c)
+        if (bnd == kEmptyKey || !(s_lbq[c] > bdist)) s_bat[j % 3][n++] = static_cast<uint16_t>(c);
+      s_bn[j % 3] = n;
+      s_cur = c;
+    };
+    if (tid == 0) {
+      s_cur = 0;
+      form(0);
+    }
+    __syncthreads();
+
+    for (int b = 0, set = 0; s_bn[b % 3] > 0; ++b, set ^= 1) {
+      const int nb = s_bn[b % 3];
+      const uint16_t *bat = s_bat[b % 3];
       float *fset = flut + static_cast<size_t>(set) * kMaxBatch * fstride;
       uint8_t *qset = qlut + static_cast<size_t>(set) * kMaxBatch * qstride;
 
       // ---- tables: list slot `grp` by its 128 threads --------------------
       if (grp < nb) {
-        const float *cent = p.centroids + static_cast<size_t>(s_list[b0 + grp]) * d;
+        const float *cent = p.centroids + static_cast<size_t>(s_list[bat[grp]]) * d;
         float *fl = fset + static_cast<size_t>(grp) * fstride;
         // OPQ: the table is built from the rotated residual R r (opq.rs:115-121),
         // kept in shared memory; output i is sum_j R[i][j] r_j from 0.0
@@ -226,21 +257,22 @@ __global__ void __launch_bounds__(kScanThreads, 2) ivfpq_four_kernel(const ScanP
           // quantised distance is >= lb (1 - 16 u) - M scale / 2 (1 + 1e-5) for
           // lists of >= 16 vectors, and >= lb for the smaller float-path lists.
           const uint64_t bnd = s_bound;
-          double lbq = static_cast<double>(s_lb[b0 + grp]);
-          if (s_len[b0 + grp] >= 16)
+          double lbq = static_cast<double>(s_lb[bat[grp]]);
+          if (s_len[bat[grp]] >= 16)
             lbq = lbq * (1.0 - 16 * 5.9604644775390625e-8) - 0.5 * M * static_cast<double>(scale) * (1.0 + 1e-5);
           s_skip[set][grp] = bnd != kEmptyKey && lbq > static_cast<double>(key_dist(bnd));
         }
       }
+      if (tid == 0) form(b + 1);  // built next, while slower warps still score this batch
       __syncthreads();
 
       // ---- score and select ---------------------------------------------
       // candidates of the batch's lists that are not skipped
       const uint8_t *skip = s_skip[set];
-      const uint32_t pre1 = skip[0] ? 0u : s_len[b0];
-      const uint32_t pre2 = pre1 + (nb > 1 && !skip[1] ? s_len[b0 + 1] : 0u);
-      const uint32_t pre3 = pre2 + (nb > 2 && !skip[2] ? s_len[b0 + 2] : 0u);
-      const uint32_t pre4 = pre3 + (nb > 3 && !skip[3] ? s_len[b0 + 3] : 0u);
+      const uint32_t pre1 = skip[0] ? 0u : s_len[bat[0]];
+      const uint32_t pre2 = pre1 + (nb > 1 && !skip[1] ? s_len[bat[1]] : 0u);
+      const uint32_t pre3 = pre2 + (nb > 2 && !skip[2] ? s_len[bat[2]] : 0u);
+      const uint32_t pre4 = pre3 + (nb > 3 && !skip[3] ? s_len[bat[3]] : 0u);
       const uint32_t qset_a = smem_u32(qset);
       for (uint32_t x0 = warp * 32; x0 < pre4; x0 += kScanThreads) {
         const uint32_t x = x0 + lane;
@@ -261,7 +293,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) ivfpq_four_kernel(const ScanP
           const uint32_t lo = g == 0 ? 0u : g == 1 ? pre1 : g == 2 ? pre2 : pre3;
           const uint32_t hi = g == 0 ? pre1 : g == 1 ? pre2 : g == 2 ? pre3 : pre4;
           c = x - lo;
-          list = s_list[b0 + g];
+          list = s_list[bat[g]];
           quant = hi - lo >= 16;  // search.rs:1261 (SIMD_BATCH_THRESHOLD)
           if (quant) vp = p.packed + p.pack_off[list] + static_cast<uint64_t>(c) * ((M + 1) >> 1);
         }
@@ -303,7 +335,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) ivfpq_four_kernel(const ScanP
         const bool pass = alive && dk <= tkey;
         unsigned mask = __ballot_sync(VG_FULL_MASK, pass);
         if (!mask) continue;
-        const uint64_t key = pass ? ((static_cast<uint64_t>(dk) << 32) | p.list_ids[s_lbeg[b0 + g] + c]) : kEmptyKey;
+        const uint64_t key = pass ? ((static_cast<uint64_t>(dk) << 32) | p.list_ids[s_lbeg[bat[g]] + c]) : kEmptyKey;
         if (__popc(mask) > 4) {
           tk.add(key < thr ? key : kEmptyKey);
         } else {

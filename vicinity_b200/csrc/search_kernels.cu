@@ -339,6 +339,40 @@ cudaError_t launch_select_rows_keys(const float *dist, size_t rows, size_t cols,
 }
 
 // ---------------------------------------------------------------------------
+// Pruning bounds of one probe.  lb bounds every float ADC distance of the
+// list from below: (|r| - R_l)^2 less the float sum's rounding.  For 4-bit
+// tables the quantised distance (pq_simd.rs:576-769) can lie below the float
+// one by up to half a quantisation step per subspace, M scale / 2 with scale
+// = range / 255 of the query's table; the table is not built yet, but every
+// entry is at most gmax = (max_m |r_m| + C)^2 (C the largest codeword norm of
+// any subspace, times the rounding of the entry's float sum), so scale <=
+// gmax / 255.  A flat table (range < 2^-23) is quantised with scale 1, all
+// entries 0; its distance M gmin is within M 2^-23 of the float sum, covered
+// by a scale of at least 2^-22.
+// ---------------------------------------------------------------------------
+namespace {
+__device__ __forceinline__ float lb_from_norm(double sq, float radius, int M, int dsub) {
+  const double gap = sqrt(sq) - static_cast<double>(radius);
+  double b = gap > 0.0 ? gap * gap : 0.0;
+  b *= 1.0 - (static_cast<double>(M + dsub + 2) * 5.9604644775390625e-8 + 1e-12);
+  return __double2float_rd(b);
+}
+
+__device__ __forceinline__ float lbq_from_lb(float lb, double gmax, int M, int dsub) {
+  gmax *= 1.0 + static_cast<double>(dsub + 3) * 5.9604644775390625e-8;
+  const double scale = fmax(gmax * (1.0 + 1e-5) / 255.0, 2.384185791015625e-7);
+  const double b = static_cast<double>(lb) * (1.0 - 16 * 5.9604644775390625e-8) - 0.5 * M * scale * (1.0 + 1e-5);
+  return __double2float_rd(b);
+}
+
+// gmax from smax >= max_m |r_m|^2 and C, every operation rounded up
+__device__ __forceinline__ double table_max_bound(float smax, float C) {
+  const float e = __fadd_ru(__fsqrt_ru(smax), C);
+  return static_cast<double>(__fmul_ru(e, e));
+}
+}  // namespace
+
+// ---------------------------------------------------------------------------
 // Probe shortlist from approximate coarse products (search.rs:1602-1617).
 //
 // s[row][l] approximates q . c_l (a TF32 tensor-core product) within eps(row)
@@ -533,10 +567,27 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
         const size_t o = row * out_ld + i;
         if (!real || (bnd.owner && !bnd.owner[l])) {
           bnd.lb[o] = 0.0f;
+          if (bnd.lbq) bnd.lbq[o] = 0.0f;
           if (bnd.rec) bnd.rec[o] = ProbeRec{0xffffffffu, 0u, 0ull, 0ull, 0.0f, 0u};
         } else {
           const float *c = cent + static_cast<size_t>(l) * d;
+          // |r|^2 in double; for 4-bit tables also the largest subvector norm
+          // squared (float, rounded up), subspace by subspace in j order
           double sq = 0.0;
+          float smax = 0.0f, sacc = 0.0f;
+          int cnt = 0;
+          const bool want_q = bnd.lbq != nullptr;
+          auto acc = [&](float r) {
+            sq += static_cast<double>(r) * r;
+            if (want_q) {
+              sacc = __fmaf_ru(r, r, sacc);
+              if (++cnt == bnd.dsub) {
+                smax = fmaxf(smax, sacc);
+                sacc = 0.0f;
+                cnt = 0;
+              }
+            }
+          };
           int j = 0;
           if (cvec) {  // 32 floats of the centroid row in flight at a time
             const float4 *c4 = reinterpret_cast<const float4 *>(c);
@@ -548,21 +599,17 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
 #pragma unroll
               for (int u = 0; u < 8; ++u) {
                 const float4 a = q4[(j >> 2) + u];
-                const double r0 = __fsub_rn(a.x, v[u].x), r1 = __fsub_rn(a.y, v[u].y);
-                const double r2 = __fsub_rn(a.z, v[u].z), r3 = __fsub_rn(a.w, v[u].w);
-                sq += r0 * r0 + r1 * r1 + r2 * r2 + r3 * r3;
+                acc(__fsub_rn(a.x, v[u].x));
+                acc(__fsub_rn(a.y, v[u].y));
+                acc(__fsub_rn(a.z, v[u].z));
+                acc(__fsub_rn(a.w, v[u].w));
               }
             }
           }
-          for (; j < d; ++j) {
-            const double rj = __fsub_rn(qs[j], __ldg(c + j));
-            sq += rj * rj;
-          }
-          const double gap = sqrt(sq) - static_cast<double>(bnd.radius[l]);
-          double b = gap > 0.0 ? gap * gap : 0.0;
-          b *= 1.0 - (static_cast<double>(bnd.M + bnd.dsub + 2) * 5.9604644775390625e-8 + 1e-12);
-          const float lbf = __double2float_rd(b);
+          for (; j < d; ++j) acc(__fsub_rn(qs[j], __ldg(c + j)));
+          const float lbf = lb_from_norm(sq, bnd.radius[l], bnd.M, bnd.dsub);
           bnd.lb[o] = lbf;
+          if (want_q) bnd.lbq[o] = lbq_from_lb(lbf, table_max_bound(smax, bnd.sub_radius[bnd.M]), bnd.M, bnd.dsub);
           if (bnd.rec) {
             const uint64_t beg = bnd.list_off[l];
             bnd.rec[o] = ProbeRec{l, static_cast<uint32_t>(bnd.list_off[l + 1] - beg), beg, bnd.code_off[l], lbf, 0u};
@@ -880,53 +927,58 @@ cudaError_t launch_filter_widen(const uint32_t *probes, size_t nq, int P, const 
 // ---------------------------------------------------------------------------
 namespace {
 __global__ void probe_lb_kernel(const float *__restrict__ qn, size_t nq, int d, const uint32_t *__restrict__ probes,
-                                int P, const float *__restrict__ centroids, const float *__restrict__ radius,
-                                int M, int dsub, float *__restrict__ lb, const uint64_t *__restrict__ list_off,
-                                const uint64_t *__restrict__ code_off, const uint8_t *__restrict__ owner,
-                                ProbeRec *__restrict__ rec) {
+                                int P, const float *__restrict__ centroids, const ProbeBoundArgs b) {
   const size_t pair = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   if (pair >= nq * P) return;
   const int lane = lane_id();
   const size_t q = pair / P;
   const uint32_t l = probes[pair];
-  if (l == 0xffffffffu || (owner && !owner[l])) {
+  if (l == 0xffffffffu || (b.owner && !b.owner[l])) {
     if (lane == 0) {
-      lb[pair] = 0.0f;
-      if (rec) rec[pair] = ProbeRec{0xffffffffu, 0u, 0ull, 0ull, 0.0f, 0u};
+      b.lb[pair] = 0.0f;
+      if (b.lbq) b.lbq[pair] = 0.0f;
+      if (b.rec) b.rec[pair] = ProbeRec{0xffffffffu, 0u, 0ull, 0ull, 0.0f, 0u};
     }
     return;
   }
   const float *qv = qn + q * d;
   const float *c = centroids + static_cast<size_t>(l) * d;
+  // lane m takes subspaces m, m + 32, ...: their squared residual norms give
+  // both |r|^2 and the 4-bit table bound
   double s = 0.0;
-  for (int j = lane; j < d; j += 32) {
-    const double r = static_cast<double>(__fsub_rn(qv[j], c[j]));  // the scan kernels' residual
-    s += r * r;
+  float smax = 0.0f;
+  for (int m = lane; m < b.M; m += 32) {
+    float sm = 0.0f;
+    for (int jj = 0; jj < b.dsub; ++jj) {
+      const float r = __fsub_rn(qv[m * b.dsub + jj], c[m * b.dsub + jj]);  // the scan kernels' residual
+      s += static_cast<double>(r) * r;
+      sm = __fmaf_ru(r, r, sm);
+    }
+    smax = fmaxf(smax, sm);
   }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(VG_FULL_MASK, s, off);
+  for (int off = 16; off > 0; off >>= 1) {
+    s += __shfl_xor_sync(VG_FULL_MASK, s, off);
+    smax = fmaxf(smax, __shfl_xor_sync(VG_FULL_MASK, smax, off));
+  }
   if (lane == 0) {
-    // double rounding of d squares and sums: relative < 1e-13, covered below
-    const double gap = sqrt(s) - static_cast<double>(radius[l]);
-    double b = gap > 0.0 ? gap * gap : 0.0;
-    b *= 1.0 - (static_cast<double>(M + dsub + 2) * 5.9604644775390625e-8 + 1e-12);
-    lb[pair] = __double2float_rd(b);
-    if (rec) {
-      const uint64_t beg = list_off[l];
-      rec[pair] = ProbeRec{l, static_cast<uint32_t>(list_off[l + 1] - beg), beg, code_off[l], __double2float_rd(b), 0u};
+    // double rounding of d squares and sums: relative < 1e-13, covered by lb_from_norm
+    const float lbf = lb_from_norm(s, b.radius[l], b.M, b.dsub);
+    b.lb[pair] = lbf;
+    if (b.lbq) b.lbq[pair] = lbq_from_lb(lbf, table_max_bound(smax, b.sub_radius[b.M]), b.M, b.dsub);
+    if (b.rec) {
+      const uint64_t beg = b.list_off[l];
+      b.rec[pair] = ProbeRec{l, static_cast<uint32_t>(b.list_off[l + 1] - beg), beg, b.code_off[l], lbf, 0u};
     }
   }
 }
 }  // namespace
 
 cudaError_t launch_probe_lb(const float *qn, size_t nq, int d, const uint32_t *probes, int P,
-                            const float *centroids, const float *radius, int M, int dsub, float *lb,
-                            const uint64_t *list_off, const uint64_t *code_off, const uint8_t *owner, ProbeRec *rec,
-                            cudaStream_t s) {
+                            const float *centroids, const ProbeBoundArgs &b, cudaStream_t s) {
   const size_t pairs = nq * static_cast<size_t>(P);
   if (pairs == 0) return cudaSuccess;
-  probe_lb_kernel<<<static_cast<unsigned>((pairs * 32 + 255) / 256), 256, 0, s>>>(
-      qn, nq, d, probes, P, centroids, radius, M, dsub, lb, list_off, code_off, owner, rec);
+  probe_lb_kernel<<<static_cast<unsigned>((pairs * 32 + 255) / 256), 256, 0, s>>>(qn, nq, d, probes, P, centroids, b);
   return cudaGetLastError();
 }
 
