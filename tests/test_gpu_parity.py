@@ -230,3 +230,20 @@ def test_flat_ip_matches_oracle():
         assert np.array_equal(gd.view(np.uint32), rd.view(np.uint32))
     gi, gd = flat_search_ip(db[:50], q, 100)
     assert (gi[:, 50:] == MISSING_LABEL).all()
+
+
+@pytest.mark.parametrize("L,M,ks", [(64, 8, 256), (1100, 8, 256), (1100, 16, 16)])
+def test_large_host_batch_matches_small_batches(L, M, ks):
+    # queries are searched independently: one large host batch, the same
+    # queries in smaller batches, and the oracle agree bit for bit
+    x, q = mixture(30_000, 32, 60, 0.3, seed=L + ks, nq=6000)
+    ix, ref = build_pair(x, 32, L, M, ks, nprobe=12, sample=20_000, iters=4)
+    big_ids, big_d = ix.batch_search(q, 10)
+    parts = [ix.batch_search(q[i:i + 2000], 10) for i in range(0, 6000, 2000)]
+    assert np.array_equal(big_ids, np.concatenate([p[0] for p in parts]))
+    assert np.array_equal(big_d.view(np.uint32), np.concatenate([p[1] for p in parts]).view(np.uint32))
+    ri, rd, rc = ref.search_batch(q[:300], 10, nprobe=12)
+    ri = ri.astype(np.int64)
+    ri[np.arange(10)[None, :] >= rc.astype(np.int64)[:, None]] = MISSING_LABEL
+    assert np.array_equal(big_ids[:300], ri)
+    assert np.array_equal(big_d[:300].view(np.uint32), rd.view(np.uint32))

@@ -682,6 +682,46 @@ int write_padding(vg_index *ix, size_t nq, size_t k, uint32_t *out_ids, float *o
   return VG_OK;
 }
 
+// Scan-kernel parameters common to every search launch: the device layout
+// and the probe workspaces.
+vg::ScanParams base_scan_params(vg_index *ix, size_t P, size_t kk, bool prune, bool recs, bool quant) {
+  vg::ScanParams sp{};
+  sp.qn = ix->ws_qn.as<float>();
+  sp.centroids = ix->centroids.as<float>();
+  sp.codebooks = ix->codebooks.as<float>();
+  sp.probes = ix->ws_probes.as<uint32_t>();
+  sp.owner = ix->world > 1 ? ix->owner.as<uint8_t>() : nullptr;
+  sp.list_off = ix->list_off.as<uint64_t>();
+  sp.code_off = ix->code_off.as<uint64_t>();
+  sp.list_codes = ix->list_codes.as<uint8_t>();
+  sp.pack_off = ix->pack_off.as<uint64_t>();
+  sp.packed = ix->packed.as<uint8_t>();
+  sp.list_ids = ix->list_ids.as<uint32_t>();
+  sp.doc_ids = ix->doc_ids.as<uint32_t>();
+  sp.rot_t = ix->h_rotation.empty() ? nullptr : ix->rotation_t.as<float>();
+  sp.probe_lb = prune ? ix->ws_lb.as<float>() : nullptr;
+  sp.probe_rec = recs ? ix->ws_rec.as<ProbeRec>() : nullptr;
+  sp.probe_lbq = quant ? ix->ws_lbq.as<float>() : nullptr;
+  sp.d = static_cast<int>(ix->d);
+  sp.M = static_cast<int>(ix->params.num_codebooks);
+  sp.ks = static_cast<int>(ix->params.codebook_size);
+  sp.dsub = static_cast<int>(ix->dsub);
+  sp.P = static_cast<int>(P);
+  sp.k = static_cast<int>(kk);
+  sp.error = ix->d_err;
+  return sp;
+}
+
+// Pruning bounds (and probe records) written for probe rows from r0 on.
+ProbeBoundArgs bound_args_at(vg_index *ix, size_t P, size_t r0, bool prune, bool recs, bool quant) {
+  return ProbeBoundArgs{ix->list_radius.as<float>(), static_cast<int>(ix->params.num_codebooks),
+                        static_cast<int>(ix->dsub), ix->list_off.as<uint64_t>(), ix->code_off.as<uint64_t>(),
+                        ix->world > 1 ? ix->owner.as<uint8_t>() : nullptr,
+                        prune ? ix->ws_lb.as<float>() + r0 * P : nullptr,
+                        recs ? ix->ws_rec.as<ProbeRec>() + r0 * P : nullptr, ix->sub_radius.as<float>(),
+                        quant ? ix->ws_lbq.as<float>() + r0 * P : nullptr};
+}
+
 int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t pool, size_t nprobe,
                 uint32_t *out_ids, float *out_dist, uint32_t *out_count) {
   if (!ix->built) return fail(VG_ERR_NOT_BUILT, "IVF-PQ index is not built: cannot search");
@@ -732,14 +772,7 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
     if (recs) VG_CU(ix->ws_rec.reserve(nq * P * sizeof(ProbeRec)));
     if (quant) VG_CU(ix->ws_lbq.reserve(nq * P * 4));
   }
-  auto bound_args = [&](size_t r0) {
-    return ProbeBoundArgs{ix->list_radius.as<float>(), static_cast<int>(M), static_cast<int>(ix->dsub),
-                          ix->list_off.as<uint64_t>(), ix->code_off.as<uint64_t>(),
-                          ix->world > 1 ? ix->owner.as<uint8_t>() : nullptr,
-                          prune ? ix->ws_lb.as<float>() + r0 * P : nullptr,
-                          recs ? ix->ws_rec.as<ProbeRec>() + r0 * P : nullptr, ix->sub_radius.as<float>(),
-                          quant ? ix->ws_lbq.as<float>() + r0 * P : nullptr};
-  };
+  auto bound_args = [&](size_t r0) { return bound_args_at(ix, P, r0, prune, recs, quant); };
   bool bounds_done = prune;
   double coarse_ms = 0, select_ms = 0;
   for (size_t r0 = 0; r0 < nq; r0 += tile) {
@@ -793,30 +826,9 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   const uint32_t *doc_map = ix->doc_ids.as<uint32_t>();
   const bool direct = ix->world == 1 && !rerank;  // the kernel writes final results
 
-  vg::ScanParams sp{};
-  sp.qn = ix->ws_qn.as<float>();
-  sp.centroids = ix->centroids.as<float>();
-  sp.codebooks = ix->codebooks.as<float>();
-  sp.probes = ix->ws_probes.as<uint32_t>();
-  sp.owner = ix->world > 1 ? ix->owner.as<uint8_t>() : nullptr;
+  vg::ScanParams sp = base_scan_params(ix, P, kk, prune, recs, quant);
   sp.counter = d_counter;
-  sp.list_off = ix->list_off.as<uint64_t>();
-  sp.code_off = ix->code_off.as<uint64_t>();
-  sp.list_codes = ix->list_codes.as<uint8_t>();
-  sp.pack_off = ix->pack_off.as<uint64_t>();
-  sp.packed = ix->packed.as<uint8_t>();
-  sp.list_ids = ix->list_ids.as<uint32_t>();
   sp.doc_ids = doc_map;
-  sp.rot_t = ix->h_rotation.empty() ? nullptr : ix->rotation_t.as<float>();
-  sp.probe_lb = prune ? ix->ws_lb.as<float>() : nullptr;
-  sp.probe_rec = recs ? ix->ws_rec.as<ProbeRec>() : nullptr;
-  sp.probe_lbq = quant ? ix->ws_lbq.as<float>() : nullptr;
-  sp.d = static_cast<int>(d);
-  sp.M = static_cast<int>(M);
-  sp.ks = static_cast<int>(ix->params.codebook_size);
-  sp.dsub = static_cast<int>(ix->dsub);
-  sp.P = static_cast<int>(P);
-  sp.k = static_cast<int>(kk);
   sp.nq = static_cast<int>(nq);
   if (direct) {
     sp.out_ids = o_ids;
@@ -827,7 +839,6 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
     sp.out_keys = ix->ws_keys.as<unsigned long long>();
   }
   *reinterpret_cast<volatile int *>(ix->h_err) = 0;
-  sp.error = ix->d_err;
   VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
   ix->launches += 1;
   mark(ix, 6);
