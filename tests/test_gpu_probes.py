@@ -1,13 +1,13 @@
 """Probe selection (find_nearest_centroids, src/ivf_pq/search.rs:1602-1617):
 the nprobe nearest lists of each normalised query by 1 - q.c, ties by list
-id.  From 1024 lists up the engine ranks lists with an approximate
+id.  From 1024 lists up the engine ranks lists with an approximate binary16
 tensor-core product and re-scores, with the reference's sequential f32
 arithmetic, every list the approximation's error bound cannot rule out; the
 lists and distances it returns must still equal the oracle's exactly.  The
 cases here crowd the bound: exact duplicates (ties broken by id), clusters
 of near-duplicates (many lists inside the error window), centroids of mixed
-norms, zero and unnormalised queries, and centroids large enough that the
-bound is useless (every list scored exactly).
+norms, zero and unnormalised queries, and centroids too long for a useful
+bound (the exact path).
 """
 from __future__ import annotations
 

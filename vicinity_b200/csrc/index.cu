@@ -174,7 +174,9 @@ struct vg_index {
   DevBuf list_off, list_ids, code_off, list_codes, pack_off, packed;
   DevBuf list_radius;  // f32 [Lc]: largest reconstructed-residual norm per list (list pruning)
   DevBuf cent_norm;    // f32 [1]: largest centroid norm (probe shortlist error bound)
-  DevBuf sub_radius;   // f32 [M]: largest codeword norm per subspace (4-bit list pruning)
+  DevBuf sub_radius;   // f32 [M + 1]: largest codeword norm per subspace, then of all (4-bit list pruning)
+  DevBuf cent_h;       // binary16 [Lc][d]: centroids for the approximate coarse products
+  float h_cmax = 0.0f; // largest centroid norm (host copy)
   cublasHandle_t blas = nullptr;  // TF32 coarse products (probe shortlist)
   std::vector<uint64_t> h_list_off;
   std::vector<uint32_t> h_doc_ids;
@@ -203,7 +205,7 @@ struct vg_index {
 
   // search workspace
   DevBuf ws_q, ws_qn, ws_dist, ws_probes, ws_pdist, ws_scalars,
-      ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_lb, ws_rec, ws_lbq;
+      ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_lb, ws_rec, ws_lbq, ws_qh;
   DevBuf stats;  // u64 [pairs, vectors, code bytes] accumulated while profiling
 
   // error flag of bounded device waits, in mapped pinned host memory
@@ -219,7 +221,7 @@ struct vg_index {
     return vectors.cap + doc_ids.cap + centroids.cap + codebooks.cap + assign.cap + codes.cap +
            list_off.cap + list_ids.cap + code_off.cap + list_codes.cap + pack_off.cap + packed.cap +
            owner.cap + rotation.cap + rotation_t.cap + category_d.cap + bitmask_d.cap + cat_counts.cap +
-           list_radius.cap + cent_norm.cap + sub_radius.cap;
+           list_radius.cap + cent_norm.cap + sub_radius.cap + cent_h.cap;
   }
 };
 
@@ -618,6 +620,9 @@ int build_list_storage(vg_index *ix, const uint32_t *sorted_lists) {
                                static_cast<int>(ix->dsub), ix->sub_radius.as<float>(), s));
   VG_CU(ix->cent_norm.reserve(4));
   VG_CU(launch_centroid_norm_max(ix->centroids.as<float>(), Lc, static_cast<int>(ix->d), ix->cent_norm.as<float>(), s));
+  VG_CU(cudaMemcpyAsync(&ix->h_cmax, ix->cent_norm.p, 4, cudaMemcpyDeviceToHost, s));
+  VG_CU(ix->cent_h.reserve(std::max<size_t>(Lc * ix->d, 1) * 2));
+  VG_CU(launch_to_half(ix->centroids.as<float>(), Lc * ix->d, ix->cent_h.p, s));
   VG_CU(cudaStreamSynchronize(s));
   ix->built = true;
   return VG_OK;
@@ -627,11 +632,12 @@ int build_list_storage(vg_index *ix, const uint32_t *sorted_lists) {
 
 // The nprobe nearest lists of rows normalised queries qn (search.rs:1602-1617:
 // 1 - q.c in sequential f32, ascending, ties by list id) into probes / pdist
-// (row stride P).  Many lists: a TF32 tensor-core GEMM gives approximate
+// (row stride P).  Many lists: a binary16 tensor-core GEMM gives approximate
 // products and launch_probe_shortlist re-scores, with the reference's
 // arithmetic, every list the approximation cannot rule out -- the same probes
-// as the exact path.  Few lists, or nprobe beyond the shortlist's window: the
-// exact distance tile and a row selection.  Calls mark(3) between the two
+// as the exact path.  Few lists, nprobe beyond the shortlist's window, or
+// centroids too long for a useful error bound: the exact distance tile and a
+// row selection.  Calls mark(3) between the two
 // phases; returns the number of this library's kernels launched in *launches.
 constexpr size_t kShortlistMinLists = 1024;
 
@@ -640,24 +646,39 @@ int coarse_probes(vg_index *ix, const float *qn, size_t rows, size_t P, uint32_t
   if (bounds_done) *bounds_done = false;
   cudaStream_t s = ix->stream;
   const size_t Lc = ix->num_centroids, d = ix->d;
-  const bool shortlist = Lc >= kShortlistMinLists && P <= 128 && d <= 2048;
+  // the shortlist's error bound grows with the centroid norms: beyond a few
+  // units it admits most lists, and past the binary16 range it is void
+  const bool shortlist =
+      Lc >= kShortlistMinLists && P <= 128 && d <= 2048 && std::isfinite(ix->h_cmax) && ix->h_cmax < 100.0f;
   if (shortlist) {
     if (!ix->blas) {
       if (cublasCreate(&ix->blas) != CUBLAS_STATUS_SUCCESS) return fail(VG_ERR_CUDA, "cublasCreate failed");
     }
     if (cublasSetStream(ix->blas, s) != CUBLAS_STATUS_SUCCESS) return fail(VG_ERR_CUDA, "cublasSetStream failed");
     const float one = 1.0f, zero = 0.0f;
+    // Products in binary16: operands rounded to nearest, f32 accumulation,
+    // binary16 results (half the bytes of an f32 product matrix; every
+    // product is far inside the range, |q.c| <= |c| < 100).  The error
+    // coefficients cover operand and result rounding (subnormal operands as
+    // an absolute term), accumulation in any order (2 d u), the exact dot's
+    // own rounding (d u) and the subtractions from 1.
+    const double u = 1.0 / 16777216.0, dd = static_cast<double>(d);
+    const double rel = 3.0 * 8192 * u + 4 * u + 2 * u + 4 * dd * u;  // 2^-10 + 2^-11 + 2^-22 + 2^-23 + 4 d u
+    const double abs_coef = std::sqrt(dd) * u;
+    VG_CU(ix->ws_qh.reserve(std::max<size_t>(rows * d, 1) * 2));
+    VG_CU(launch_to_half(qn, rows * d, ix->ws_qh.p, s));
+    *launches += 1;
     // column-major: S^T [Lc x rows] = C [Lc x d] * Qn^T [d x rows], i.e. row-major S[rows][Lc] = Qn C^T
     const cublasStatus_t st =
         cublasGemmEx(ix->blas, CUBLAS_OP_T, CUBLAS_OP_N, static_cast<int>(Lc), static_cast<int>(rows),
-                     static_cast<int>(d), &one, ix->centroids.p, CUDA_R_32F, static_cast<int>(d), qn, CUDA_R_32F,
-                     static_cast<int>(d), &zero, ix->ws_dist.p, CUDA_R_32F, static_cast<int>(Lc),
-                     CUBLAS_COMPUTE_32F_FAST_TF32, CUBLAS_GEMM_DEFAULT);
+                     static_cast<int>(d), &one, ix->cent_h.p, CUDA_R_16F, static_cast<int>(d), ix->ws_qh.p,
+                     CUDA_R_16F, static_cast<int>(d), &zero, ix->ws_dist.p, CUDA_R_16F, static_cast<int>(Lc),
+                     CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
     if (st != CUBLAS_STATUS_SUCCESS) return fail(VG_ERR_CUDA, "cublasGemmEx failed");
     mark(ix, 3);
-    VG_CU(launch_probe_shortlist(ix->ws_dist.as<float>(), rows, Lc, Lc, qn, static_cast<int>(d),
-                                 ix->centroids.as<float>(), ix->cent_norm.as<float>(), static_cast<int>(P), probes,
-                                 pdist, P, bounds ? *bounds : ProbeBoundArgs{}, s));
+    VG_CU(launch_probe_shortlist(ix->ws_dist.p, true, rows, Lc, Lc, qn, static_cast<int>(d),
+                                 ix->centroids.as<float>(), ix->cent_norm.as<float>(), rel, abs_coef,
+                                 static_cast<int>(P), probes, pdist, P, bounds ? *bounds : ProbeBoundArgs{}, s));
     *launches += 1;
     if (bounds_done) *bounds_done = bounds != nullptr;
     return VG_OK;
@@ -1281,7 +1302,7 @@ int vg_ivfpq_destroy(vg_index *ix) {
                       &ix->list_off, &ix->list_ids, &ix->code_off, &ix->list_codes, &ix->pack_off, &ix->packed,
                       &ix->owner, &ix->ws_q, &ix->ws_qn, &ix->ws_dist, &ix->ws_probes, &ix->ws_pdist,
                       &ix->ws_scalars, &ix->ws_keys, &ix->ws_all_keys, &ix->ws_out_ids, &ix->ws_out_dist,
-                      &ix->ws_out_count, &ix->stats, &ix->ws_lb, &ix->ws_rec, &ix->ws_lbq})
+                      &ix->ws_out_count, &ix->stats, &ix->ws_lb, &ix->ws_rec, &ix->ws_lbq, &ix->ws_qh})
       b->release();
     for (int i = 0; i < kPhaseEvents; ++i)
       if (ix->ev[i]) cudaEventDestroy(ix->ev[i]);

@@ -48,11 +48,6 @@ cudaError_t launch_select_rows(const float *dist, size_t rows, size_t cols,
                                float *out_dist, size_t out_ld,
                                uint32_t col_base, cudaStream_t s);
 
-// Exact top-k probes per row from approximate products s[row][l] ~ q . c_l
-// (TF32 tensor-core GEMM): candidates within the approximation's error bound
-// of the k-th are re-scored with the reference's sequential 1 - dot; rows
-// with too many candidates or non-finite inputs are scored exactly over all
-// L.  Same output as launch_select_rows on exact 1 - dot distances.
 // One probe of one query as the streaming 8-bit kernel reads it: 32 bytes,
 // copied into shared memory a query at a time.
 struct ProbeRec {
@@ -81,9 +76,20 @@ struct ProbeBoundArgs {
   float *lbq;
 };
 
-cudaError_t launch_probe_shortlist(const float *s, size_t rows, size_t L, size_t ld, const float *qn, int d,
-                                   const float *cent, const float *cmax, int k, uint32_t *out_ids, float *out_dist,
-                                   size_t out_ld, const ProbeBoundArgs &bounds, cudaStream_t st);
+// Exact top-k probes per row from approximate products s[row][l] ~ q . c_l
+// (a tensor-core GEMM, f32 or, with s_half, binary16 results): candidates
+// within eps = rel |q| cmax + abs_coef (1 + cmax) + 2^-20 of the k-th are
+// re-scored with the reference's sequential 1 - dot; rows with too many
+// candidates or non-finite inputs are scored exactly over all L.  Same
+// output as launch_select_rows on exact 1 - dot distances.  With bounds.lb
+// set, the probes' pruning bounds and records are written beside them.
+cudaError_t launch_probe_shortlist(const void *s, bool s_half, size_t rows, size_t L, size_t ld, const float *qn,
+                                   int d, const float *cent, const float *cmax, double rel, double abs_coef, int k,
+                                   uint32_t *out_ids, float *out_dist, size_t out_ld, const ProbeBoundArgs &bounds,
+                                   cudaStream_t st);
+
+// out[i] = x[i] rounded to the nearest half (IEEE binary16).
+cudaError_t launch_to_half(const float *x, size_t n, void *out, cudaStream_t s);
 
 // Same selection, but writing packed keys (for later merging).
 cudaError_t launch_select_rows_keys(const float *dist, size_t rows,

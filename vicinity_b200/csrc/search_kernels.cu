@@ -8,6 +8,8 @@
 //   finish_top_k_by_distance   src/ivf_pq/search.rs:64-75
 //   doc-id mapping             src/ivf_pq/search.rs:1087-1093
 //   batch padding              src/python.rs:745-795 (-1 / +inf)
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 #include "f32x2.cuh"
 #include "kernels.h"
@@ -375,9 +377,12 @@ __device__ __forceinline__ double table_max_bound(float smax, float C) {
 // ---------------------------------------------------------------------------
 // Probe shortlist from approximate coarse products (search.rs:1602-1617).
 //
-// s[row][l] approximates q . c_l (a TF32 tensor-core product) within eps(row)
-// = (2^-9 + 2^-19 + 3 d 2^-24) |q| cmax (TF32 truncation of both operands,
-// accumulation, and the rounding of the exact sequential dot) plus 2^-20.  With
+// s[row][l] approximates q . c_l (a tensor-core product) within eps(row) =
+// rel |q| cmax + abs_coef (1 + cmax) + 2^-20, the coefficients set by the
+// caller for the operand and result formats (rounding or truncation of both
+// operands, accumulation, the result's own rounding, the rounding of the exact
+// sequential dot and of the subtractions from 1; binary16 adds an absolute
+// term for subnormal operands).  With
 // A = 1 - s, every probe of the exact top-P has A <= A_P + 2 eps, where A_P is
 // the P-th smallest A: those are gathered (under an upper bound on A_P taken
 // from the lanes' 2R smallest), re-scored with the reference's arithmetic --
@@ -415,47 +420,62 @@ __device__ __forceinline__ float exact_one_minus_dot(const float *q, const float
   return __fsub_rn(1.0f, acc);
 }
 
-// Visit columns [0, L) of a row, four at a time: fn(col, v, valid[4]) with
-// v the four approximate products.  Trip counts are warp-uniform (fn may use
-// warp votes); rows must be 16-byte aligned with L % 4 == 0 when vec is set.
-// The last visit (kLast) streams the row past L2 with evict-first loads.
-template <bool kLast, typename F>
-__device__ __forceinline__ void for_each_quad(const float *__restrict__ srow, size_t L, bool vec, int lane, F &&fn) {
+// Four products of a row as floats: from a float4, or from four halves.
+__device__ __forceinline__ float4 quad_to_float(const float4 v) { return v; }
+__device__ __forceinline__ float4 quad_to_float(const uint2 v) {
+  const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&v.x));
+  const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&v.y));
+  return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+__device__ __forceinline__ float elem_to_float(float v) { return v; }
+__device__ __forceinline__ float elem_to_float(__half v) { return __half2float(v); }
+template <typename TS> struct QuadOf { using type = float4; };
+template <> struct QuadOf<__half> { using type = uint2; };
+
+// Visit columns [0, L) of a row of TS (float or half), four at a time:
+// fn(col, v, valid[4]) with v the four approximate products.  Trip counts are
+// warp-uniform (fn may use warp votes); rows must be aligned to four elements
+// with L % 4 == 0 when vec is set.  The last visit (kLast) streams the row
+// past L2 with evict-first loads.
+template <bool kLast, typename TS, typename F>
+__device__ __forceinline__ void for_each_quad(const TS *__restrict__ srow, size_t L, bool vec, int lane, F &&fn) {
+  using Q = typename QuadOf<TS>::type;
   if (vec) {
-    const float4 *r4 = reinterpret_cast<const float4 *>(srow);
+    const Q *r4 = reinterpret_cast<const Q *>(srow);
     const size_t n4 = L >> 2;
     size_t b = 0;
     for (; b + 128 <= n4; b += 128) {
-      float4 v[4];
+      Q v[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) v[u] = kLast ? __ldcs(r4 + b + u * 32 + lane) : __ldg(r4 + b + u * 32 + lane);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) fn((b + u * 32 + lane) * 4, v[u], true, true, true, true);
+      for (int u = 0; u < 4; ++u) fn((b + u * 32 + lane) * 4, quad_to_float(v[u]), true, true, true, true);
     }
     for (; b < n4; b += 32) {
       const size_t i = b + lane;
-      const float4 v = i < n4 ? (kLast ? __ldcs(r4 + i) : __ldg(r4 + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
-      fn(i * 4, v, i < n4, i < n4, i < n4, i < n4);
+      Q v{};
+      if (i < n4) v = kLast ? __ldcs(r4 + i) : __ldg(r4 + i);
+      fn(i * 4, quad_to_float(v), i < n4, i < n4, i < n4, i < n4);
     }
   } else {
     for (size_t b = 0; b < L; b += 128) {
       const size_t c = b + lane * 4;
       float4 v;
-      v.x = c < L ? srow[c] : 0.f;
-      v.y = c + 1 < L ? srow[c + 1] : 0.f;
-      v.z = c + 2 < L ? srow[c + 2] : 0.f;
-      v.w = c + 3 < L ? srow[c + 3] : 0.f;
+      v.x = c < L ? elem_to_float(srow[c]) : 0.f;
+      v.y = c + 1 < L ? elem_to_float(srow[c + 1]) : 0.f;
+      v.z = c + 2 < L ? elem_to_float(srow[c + 2]) : 0.f;
+      v.w = c + 3 < L ? elem_to_float(srow[c + 3]) : 0.f;
       fn(c, v, c < L, c + 1 < L, c + 2 < L, c + 3 < L);
     }
   }
 }
 
-template <int R>
+template <int R, typename TS>
 __global__ void __launch_bounds__(kSelectWarps * 32)
-    shortlist_kernel(const float *__restrict__ s, size_t rows, size_t L, size_t ld, const float *__restrict__ qn,
-                     int d, const float *__restrict__ cent, const float *__restrict__ cmax_p, int k,
-                     uint32_t *__restrict__ out_ids, float *__restrict__ out_dist, size_t out_ld,
-                     const ProbeBoundArgs bnd) {
+    shortlist_kernel(const TS *__restrict__ s, size_t rows, size_t L, size_t ld, const float *__restrict__ qn,
+                     int d, const float *__restrict__ cent, const float *__restrict__ cmax_p, double rel,
+                     double abs_coef, int k, uint32_t *__restrict__ out_ids, float *__restrict__ out_dist,
+                     size_t out_ld, const ProbeBoundArgs bnd) {
   extern __shared__ __align__(16) unsigned char sh[];
   constexpr int R2 = 2 * R;
   const int lane = lane_id(), warp = threadIdx.x >> 5;
@@ -465,7 +485,7 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
   const int dpad = (d + 3) & ~3;
   float *qs = reinterpret_cast<float *>(reinterpret_cast<uint32_t *>(sh) + kSelectWarps * kShortBuf) +
               static_cast<size_t>(warp) * dpad;
-  const float *srow = s + row * ld;
+  const TS *srow = s + row * ld;
   const float *qrow = qn + row * d;
   for (int j = lane; j < d; j += 32) qs[j] = qrow[j];
   __syncwarp();
@@ -473,36 +493,39 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
   for (int j = lane; j < d; j += 32) qq += static_cast<double>(qs[j]) * qs[j];
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) qq += __shfl_xor_sync(VG_FULL_MASK, qq, off);
-  const double eps = (1.0 / 512 + 1.0 / 524288 + 4.0 * d / 16777216.0 + 1.0 / 4194304) * sqrt(qq) *
-                         static_cast<double>(*cmax_p) * 1.01 +
-                     1.0 / 1048576;
+  const double cmax = static_cast<double>(*cmax_p);
+  const double eps = rel * sqrt(qq) * cmax * 1.01 + abs_coef * (1.0 + cmax) + 1.0 / 1048576;
   bool exact_all = !(eps < 1.0);  // non-finite or useless bound
-  const bool svec = (L & 3) == 0 && (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(s) & 15) == 0;
+  const bool svec = (L & 3) == 0 && (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(s) % (4 * sizeof(TS))) == 0;
   const bool cvec = (d & 3) == 0 && (reinterpret_cast<uintptr_t>(cent) & 15) == 0;
 
-  uint64_t a[R2];
+  // pass 1: each lane's 2R smallest approximate distances (values only: the
+  // bound needs no list ids; NaN never enters, +inf marks an empty slot)
+  const float kInf = __int_as_float(0x7f800000);
+  float a[R2];
 #pragma unroll
-  for (int r = 0; r < R2; ++r) a[r] = kEmptyKey;
-  auto insert = [&](uint64_t key) {
+  for (int r = 0; r < R2; ++r) a[r] = kInf;
+  auto insert = [&](float x) {
 #pragma unroll
     for (int r = 0; r < R2; ++r) {
-      const uint64_t lo = key < a[r] ? key : a[r];
-      key = key < a[r] ? a[r] : key;
+      const float lo = fminf(x, a[r]);
+      x = fmaxf(x, a[r]);
       a[r] = lo;
     }
   };
   if (!exact_all) {
-    for_each_quad<false>(srow, L, svec, lane, [&](size_t c, float4 v, bool ox, bool oy, bool oz, bool ow) {
-      if (ox) insert(pack_key(__fsub_rn(1.0f, v.x), static_cast<uint32_t>(c)));
-      if (oy) insert(pack_key(__fsub_rn(1.0f, v.y), static_cast<uint32_t>(c + 1)));
-      if (oz) insert(pack_key(__fsub_rn(1.0f, v.z), static_cast<uint32_t>(c + 2)));
-      if (ow) insert(pack_key(__fsub_rn(1.0f, v.w), static_cast<uint32_t>(c + 3)));
+    for_each_quad<false, TS>(srow, L, svec, lane, [&](size_t, float4 v, bool ox, bool oy, bool oz, bool ow) {
+      if (ox) insert(__fsub_rn(1.0f, v.x));
+      if (oy) insert(__fsub_rn(1.0f, v.y));
+      if (oz) insert(__fsub_rn(1.0f, v.z));
+      if (ow) insert(__fsub_rn(1.0f, v.w));
     });
   }
   WarpTopK<R2> cand;
   cand.init();
 #pragma unroll
-  for (int r = 0; r < R2; ++r) cand.add(a[r]);
+  for (int r = 0; r < R2; ++r)
+    cand.add(a[r] == kInf ? kEmptyKey : pack_key(a[r], static_cast<uint32_t>(lane * R2 + r)));
   const uint64_t ub = cand.get(k - 1);
   // every exact top-k list has approximate distance <= limit (rounded up)
   const float limit =
@@ -512,9 +535,10 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
   int n = 0;
   if (!exact_all) {
     bool over = false;
-    for_each_quad<true>(srow, L, svec, lane, [&](size_t c, float4 v, bool ox, bool oy, bool oz, bool ow) {
+    for_each_quad<true, TS>(srow, L, svec, lane, [&](size_t c, float4 v, bool ox, bool oy, bool oz, bool ow) {
       const bool t[4] = {ox && !(__fsub_rn(1.0f, v.x) > limit), oy && !(__fsub_rn(1.0f, v.y) > limit),
                          oz && !(__fsub_rn(1.0f, v.z) > limit), ow && !(__fsub_rn(1.0f, v.w) > limit)};
+      if (!__any_sync(VG_FULL_MASK, t[0] || t[1] || t[2] || t[3])) return;  // nearly every quad
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         const unsigned m = __ballot_sync(VG_FULL_MASK, t[h]);
@@ -620,32 +644,56 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
   }
 }
 
-template <int R>
-cudaError_t launch_shortlist_impl(const float *s, size_t rows, size_t L, size_t ld, const float *qn, int d,
-                                  const float *cent, const float *cmax, int k, uint32_t *ids, float *dst, size_t out_ld,
-                                  const ProbeBoundArgs &bnd, cudaStream_t st) {
+template <int R, typename TS>
+cudaError_t launch_shortlist_impl(const TS *s, size_t rows, size_t L, size_t ld, const float *qn, int d,
+                                  const float *cent, const float *cmax, double rel, double abs_coef, int k,
+                                  uint32_t *ids, float *dst, size_t out_ld, const ProbeBoundArgs &bnd,
+                                  cudaStream_t st) {
   const size_t smem = static_cast<size_t>(kSelectWarps) * (kShortBuf * 4 + static_cast<size_t>((d + 3) & ~3) * 4);
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(shortlist_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(shortlist_kernel<R, TS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
   dim3 grid(static_cast<unsigned>((rows + kSelectWarps - 1) / kSelectWarps));
-  shortlist_kernel<R><<<grid, kSelectWarps * 32, smem, st>>>(s, rows, L, ld, qn, d, cent, cmax, k, ids, dst, out_ld,
-                                                              bnd);
+  shortlist_kernel<R, TS><<<grid, kSelectWarps * 32, smem, st>>>(s, rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k,
+                                                                  ids, dst, out_ld, bnd);
   return cudaGetLastError();
+}
+
+template <typename TS>
+cudaError_t shortlist_dispatch(const TS *s, size_t rows, size_t L, size_t ld, const float *qn, int d,
+                               const float *cent, const float *cmax, double rel, double abs_coef, int k,
+                               uint32_t *ids, float *dst, size_t out_ld, const ProbeBoundArgs &bnd, cudaStream_t st) {
+  if (k <= 32) return launch_shortlist_impl<1>(s, rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k, ids, dst, out_ld, bnd, st);
+  if (k <= 64) return launch_shortlist_impl<2>(s, rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k, ids, dst, out_ld, bnd, st);
+  if (k <= 128) return launch_shortlist_impl<4>(s, rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k, ids, dst, out_ld, bnd, st);
+  if (k <= 256) return launch_shortlist_impl<8>(s, rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k, ids, dst, out_ld, bnd, st);
+  return cudaErrorInvalidValue;
+}
+
+__global__ void to_half_kernel(const float *__restrict__ x, size_t n, __half *__restrict__ out) {
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = __float2half_rn(x[i]);
 }
 }  // namespace
 
-cudaError_t launch_probe_shortlist(const float *s, size_t rows, size_t L, size_t ld, const float *qn, int d,
-                                   const float *cent, const float *cmax, int k, uint32_t *out_ids, float *out_dist,
-                                   size_t out_ld, const ProbeBoundArgs &bnd, cudaStream_t st) {
+cudaError_t launch_probe_shortlist(const void *s, bool s_half, size_t rows, size_t L, size_t ld, const float *qn,
+                                   int d, const float *cent, const float *cmax, double rel, double abs_coef, int k,
+                                   uint32_t *out_ids, float *out_dist, size_t out_ld, const ProbeBoundArgs &bnd,
+                                   cudaStream_t st) {
   if (rows == 0 || k <= 0) return cudaSuccess;
-  if (k <= 32) return launch_shortlist_impl<1>(s, rows, L, ld, qn, d, cent, cmax, k, out_ids, out_dist, out_ld, bnd, st);
-  if (k <= 64) return launch_shortlist_impl<2>(s, rows, L, ld, qn, d, cent, cmax, k, out_ids, out_dist, out_ld, bnd, st);
-  if (k <= 128) return launch_shortlist_impl<4>(s, rows, L, ld, qn, d, cent, cmax, k, out_ids, out_dist, out_ld, bnd, st);
-  if (k <= 256) return launch_shortlist_impl<8>(s, rows, L, ld, qn, d, cent, cmax, k, out_ids, out_dist, out_ld, bnd, st);
-  return cudaErrorInvalidValue;
+  if (s_half)
+    return shortlist_dispatch(static_cast<const __half *>(s), rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k,
+                              out_ids, out_dist, out_ld, bnd, st);
+  return shortlist_dispatch(static_cast<const float *>(s), rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k, out_ids,
+                            out_dist, out_ld, bnd, st);
+}
+
+cudaError_t launch_to_half(const float *x, size_t n, void *out, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  to_half_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(x, n, static_cast<__half *>(out));
+  return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------
