@@ -247,3 +247,24 @@ def test_large_host_batch_matches_small_batches(L, M, ks):
     ri[np.arange(10)[None, :] >= rc.astype(np.int64)[:, None]] = MISSING_LABEL
     assert np.array_equal(big_ids[:300], ri)
     assert np.array_equal(big_d[:300].view(np.uint32), rd.view(np.uint32))
+
+
+def test_direct_kernel_matches_oracle_on_every_shape():
+    # Large batches (16 queries per SM and up) are scored by the direct-ADC
+    # kernel, the small batches above by the query-stream kernel.  Re-run the
+    # shape tests in a child process that sends every batch to the direct
+    # kernel, so that both kernels are checked against the oracle on all
+    # subvector sizes.
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    env = dict(os.environ, VICINITY_SCAN_KERNEL="direct")
+    root = Path(__file__).resolve().parents[1]
+    res = subprocess.run(
+        [sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider", str(root / "tests" / "test_gpu_parity.py"),
+         "-k", "test_build_and_search_match_oracle or test_config0 or test_config1 or test_rerank or test_edge_cases",
+         "-m", "gpu"],
+        cwd=root, env=env, capture_output=True, text=True, timeout=900)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-2000:]

@@ -1283,7 +1283,9 @@ int vg_ivfpq_create(size_t dim, const vg_ivfpq_params *params, int device, vg_in
     vg::set_scan_family(std::strcmp(fam, "pipeline") == 0 ? 0
                         : std::strcmp(fam, "query") == 0  ? 1
                         : std::strcmp(fam, "double") == 0 ? 2
-                                                          : 3);
+                        : std::strcmp(fam, "stream") == 0 ? 3
+                        : std::strcmp(fam, "direct") == 0 ? 5
+                                                          : 4);
   if (e != cudaSuccess) {
     vg_ivfpq_destroy(ix);
     return cuda_fail(e, "stream/event creation");

@@ -229,7 +229,7 @@ cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms,
 cudaError_t launch_ivfpq_scan_generic(const ScanParams &p, int num_sms, cudaStream_t s);
 
 // Name of the kernel variant launch_ivfpq_scan would run for p.
-int ivfpq_scan_variant_name(const ScanParams &p, char *buf, size_t len);
+int ivfpq_scan_variant_name(const ScanParams &p, int num_sms, char *buf, size_t len);
 
 // Kernel family selection: 2 (default) = double-buffered kernel where it
 // applies, 1 = single-buffered query-major kernel, 0 = the warp-specialised

@@ -16,10 +16,13 @@ cudaError_t launch_scan_eight(const ScanParams &p, int dsub, int ept, int num_sm
 cudaError_t launch_scan_ws(const ScanParams &p, int dsub, int ept, int num_sms, cudaStream_t s);
 cudaError_t launch_scan_pipe(const ScanParams &p, int dsub, int gpt, int num_sms, cudaStream_t s);
 cudaError_t launch_scan_stream(const ScanParams &p, int dsub, int gpt, int num_sms, cudaStream_t s);
+cudaError_t launch_scan_direct(const ScanParams &p, int num_sms, cudaStream_t s);
+bool scan_direct_fits(const ScanParams &p);
 
 namespace {
-// 0 warp-specialised, 1 query-major, 2 double-buffered, 3 query-stream (default)
-int g_family = 3;
+// 0 warp-specialised, 1 query-major, 2 double-buffered, 3 query-stream, 4 direct ADC for large batches
+// else query-stream (default), 5 direct ADC wherever it applies
+int g_family = 4;
 
 // Entries per producer thread for the warp-specialised kernel (0 = n/a).
 int pick_ws_ept(const ScanParams &p) {
@@ -32,6 +35,15 @@ int pick_ws_ept(const ScanParams &p) {
 }  // namespace
 
 void set_scan_family(int family) { g_family = family; }
+
+namespace {
+// The direct kernel gives each query one warp for its whole search: it needs
+// a batch that keeps every warp busy (16 queries per SM here); smaller
+// batches go to the query-stream kernel, whose blocks share a query.
+bool use_direct(const ScanParams &p, int num_sms) {
+  return scan_direct_fits(p) && (g_family == 5 || p.nq >= 16 * num_sms);
+}
+}  // namespace
 
 namespace {
 int pick_gpt(const ScanParams &p) {
@@ -48,9 +60,10 @@ cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms, cudaStream_t s) 
   // an OPQ rotation is applied by the query-major and 4-bit kernels only
   const int ws = p.rot_t ? 0 : pick_ws_ept(p);
   if (ws) return launch_scan_ws(p, p.dsub, ws, num_sms, s);
+  if (g_family >= 4 && use_direct(p, num_sms)) return launch_scan_direct(p, num_sms, s);
   const int gpt = pick_gpt(p);
   if (g_family >= 2 && gpt && p.ks == 256 && !p.rot_t) {
-    if (g_family == 3 && p.probe_rec && p.P <= 256) return launch_scan_stream(p, p.dsub, gpt, num_sms, s);
+    if (g_family >= 3 && p.probe_rec && p.P <= 256) return launch_scan_stream(p, p.dsub, gpt, num_sms, s);
     return launch_scan_pipe(p, p.dsub, gpt, num_sms, s);
   }
   if (p.ks == 16) return launch_scan_four(p, gpt ? p.dsub : 0, gpt, num_sms, s);
@@ -63,12 +76,14 @@ cudaError_t launch_ivfpq_scan_generic(const ScanParams &p, int num_sms, cudaStre
   return launch_scan_eight(p, gpt ? p.dsub : 0, gpt, num_sms, s);
 }
 
-int ivfpq_scan_variant_name(const ScanParams &p, char *buf, size_t len) {
+int ivfpq_scan_variant_name(const ScanParams &p, int num_sms, char *buf, size_t len) {
   const int ws = p.rot_t ? 0 : pick_ws_ept(p);
   if (ws) return snprintf(buf, len, "ivfpq_ws_kernel<%d,%d,1,256>", p.dsub, ws);
+  if (g_family >= 4 && use_direct(p, num_sms))
+    return snprintf(buf, len, "ivfpq_direct_kernel<%d,%d>", p.dsub, p.k <= 32 ? 1 : 2);
   const int gpt = pick_gpt(p);
   if (g_family >= 2 && gpt && p.ks == 256 && !p.rot_t) {
-    if (g_family == 3 && p.probe_rec && p.P <= 256)
+    if (g_family >= 3 && p.probe_rec && p.P <= 256)
       return snprintf(buf, len, "ivfpq_stream_kernel<%d,%d,1,256>", p.dsub, gpt);
     return snprintf(buf, len, "ivfpq_pipe_kernel<%d,%d,1,256>", p.dsub, gpt);
   }
