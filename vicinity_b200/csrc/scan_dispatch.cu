@@ -17,11 +17,13 @@ cudaError_t launch_scan_ws(const ScanParams &p, int dsub, int ept, int num_sms, 
 cudaError_t launch_scan_pipe(const ScanParams &p, int dsub, int gpt, int num_sms, cudaStream_t s);
 cudaError_t launch_scan_stream(const ScanParams &p, int dsub, int gpt, int num_sms, cudaStream_t s);
 cudaError_t launch_scan_direct(const ScanParams &p, int num_sms, cudaStream_t s);
+cudaError_t launch_scan_four_warp(const ScanParams &p, int num_sms, cudaStream_t s);
+bool scan_four_warp_fits(const ScanParams &p);
 bool scan_direct_fits(const ScanParams &p);
 
 namespace {
-// 0 warp-specialised, 1 query-major, 2 double-buffered, 3 query-stream, 4 direct ADC for large batches
-// else query-stream (default), 5 direct ADC wherever it applies
+// 0 warp-specialised, 1 query-major, 2 double-buffered, 3 query-stream, 4 warp-per-query kernels (direct
+// ADC, 4-bit warp) for large batches else the block kernels (default), 5 warp-per-query wherever they apply
 int g_family = 4;
 
 // Entries per producer thread for the warp-specialised kernel (0 = n/a).
@@ -42,6 +44,9 @@ namespace {
 // batches go to the query-stream kernel, whose blocks share a query.
 bool use_direct(const ScanParams &p, int num_sms) {
   return scan_direct_fits(p) && (g_family == 5 || p.nq >= 16 * num_sms);
+}
+bool use_four_warp(const ScanParams &p, int num_sms) {
+  return g_family >= 4 && scan_four_warp_fits(p) && (g_family == 5 || p.nq >= 16 * num_sms);
 }
 }  // namespace
 
@@ -66,7 +71,10 @@ cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms, cudaStream_t s) 
     if (g_family >= 3 && p.probe_rec && p.P <= 256) return launch_scan_stream(p, p.dsub, gpt, num_sms, s);
     return launch_scan_pipe(p, p.dsub, gpt, num_sms, s);
   }
-  if (p.ks == 16) return launch_scan_four(p, gpt ? p.dsub : 0, gpt, num_sms, s);
+  if (p.ks == 16) {
+    if (use_four_warp(p, num_sms)) return launch_scan_four_warp(p, num_sms, s);
+    return launch_scan_four(p, gpt ? p.dsub : 0, gpt, num_sms, s);
+  }
   return launch_scan_eight(p, gpt ? p.dsub : 0, gpt, num_sms, s);
 }
 
@@ -87,6 +95,7 @@ int ivfpq_scan_variant_name(const ScanParams &p, int num_sms, char *buf, size_t 
       return snprintf(buf, len, "ivfpq_stream_kernel<%d,%d,1,256>", p.dsub, gpt);
     return snprintf(buf, len, "ivfpq_pipe_kernel<%d,%d,1,256>", p.dsub, gpt);
   }
+  if (use_four_warp(p, num_sms)) return snprintf(buf, len, "ivfpq_four_warp_kernel<%d>", p.k <= 32 ? 1 : 2);
   if (p.ks == 16) return snprintf(buf, len, "ivfpq_four_kernel<%d>", p.k <= 32 ? 1 : p.k <= 64 ? 2 : p.k <= 128 ? 4 : 8);
   return snprintf(buf, len, "ivfpq_query_kernel<%d,%d,%d,%s>", gpt ? p.dsub : 0, gpt,
                   p.k <= 32 ? 1 : p.k <= 64 ? 2 : p.k <= 128 ? 4 : 8, p.ks == 16 ? "4bit" : "8bit");

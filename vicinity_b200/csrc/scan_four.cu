@@ -1,5 +1,6 @@
-// Launcher of the 4-bit (16-entry codebook) search kernel, scan_fourbit.cuh.
-#include "scan_fourbit.cuh"
+// Launchers of the 4-bit (16-entry codebook) search kernels: block per query
+// (scan_fourbit.cuh) and warp per query (scan_four_warp.cuh).
+#include "scan_four_warp.cuh"
 
 namespace vg {
 
@@ -27,6 +28,25 @@ cudaError_t launch_four_variant(const ScanParams &p, int num_sms, cudaStream_t s
   return cudaGetLastError();
 }
 }  // namespace
+
+bool scan_four_warp_fits(const ScanParams &p) {
+  return p.ks == 16 && !p.rot_t && !p.qmap && !p.category && p.k <= 64 && p.dsub >= 1 &&
+         four_warp_smem_bytes(p.M, p.dsub, p.d) <= 200 * 1024;
+}
+
+cudaError_t launch_scan_four_warp(const ScanParams &p, int num_sms, cudaStream_t s) {
+  if (!scan_four_warp_fits(p)) return cudaErrorInvalidValue;
+  const size_t smem = four_warp_smem_bytes(p.M, p.dsub, p.d);
+  auto kern1 = ivfpq_four_warp_kernel<1>;
+  auto kern2 = ivfpq_four_warp_kernel<2>;
+  auto kern = p.k <= 32 ? kern1 : kern2;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  int grid = num_sms < p.nq ? num_sms : p.nq;  // one block per SM, a warp per query at a time
+  if (grid < 1) grid = 1;
+  kern<<<grid, kFourWarpThreads, smem, s>>>(p);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_scan_four(const ScanParams &p, int, int, int num_sms, cudaStream_t s) {
   if (p.ks != 16) return cudaErrorInvalidValue;

@@ -1,0 +1,196 @@
+// Warp-per-query search kernel for 16-entry (4-bit) codebooks.
+//
+// Same results as ivfpq_four_kernel (search.rs:1175-1391 with the FastScan
+// tables of pq_simd.rs:576-769).  Here one warp owns a query for its whole
+// search: for each probed list in order it
+//   - skips the list when the bound on its quantised distances (known
+//     before the table exists) exceeds the warp's current k-th distance;
+//   - builds the list's float table (entries e = lane + 32 i, warp-private),
+//     reduces its min/max with shuffles and quantises it into a warp-private
+//     768-byte u8 table;
+//   - checks the exact bound with the table's scale, then scores the
+//     candidates with integer sums of nibble lookups, exiting early per 16
+//     codes.
+// Lists under 16 vectors use the reference's float path: the float entries,
+// computed on the fly from the shared-memory codebook, summed in order.
+// No block barriers, no merge; the freshest k-th distance prunes every list.
+#pragma once
+
+#include <cfloat>
+
+#include "scan_fourbit.cuh"
+
+namespace vg {
+
+constexpr int kFourWarpThreads = 1024;
+constexpr int kFourWarpWarps = kFourWarpThreads / 32;
+
+// shared memory: codebook [M][16][dsub], then per warp the residual [d], the
+// float table [M * 16] and the u8 table [M][16]
+__host__ __device__ inline size_t four_warp_smem_bytes(int M, int dsub, int d) {
+  const size_t cb = (static_cast<size_t>(M) * 16 * dsub + 3) & ~size_t(3);
+  const size_t dpad = (static_cast<size_t>(d) + 3) & ~size_t(3);
+  return cb * 4 + kFourWarpWarps * ((dpad + four_float_stride(M)) * 4 + four_u8_stride(M));
+}
+
+// Float table entry (m, c): sum_j (r_j - w_j)^2 in j order (first square as is).
+__device__ __forceinline__ float four_entry(const float *rb, const float *cbs, int dsub, int m, int c) {
+  const float *r = rb + m * dsub, *w = cbs + (m * 16 + c) * dsub;
+  const float d0 = __fsub_rn(r[0], w[0]);
+  float t = __fmul_rn(d0, d0);
+  for (int j = 1; j < dsub; ++j) {
+    const float dj = __fsub_rn(r[j], w[j]);
+    t = __fadd_rn(t, __fmul_rn(dj, dj));
+  }
+  return t;
+}
+
+template <int R>
+__global__ void __launch_bounds__(kFourWarpThreads, 1) ivfpq_four_warp_kernel(const ScanParams p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int M = p.M, d = p.d, P = p.P, k = p.k, dsub = p.dsub;
+  const int nent = M * 16;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int dpad = (d + 3) & ~3;
+  const int fstride = static_cast<int>(four_float_stride(M));
+  float *cbs = reinterpret_cast<float *>(smem);                                     // [M][16][dsub]
+  float *rb = cbs + ((nent * dsub + 3) & ~3) + static_cast<size_t>(warp) * (dpad + fstride);  // residual [d]
+  float *ft = rb + dpad;                                                            // float table [M * 16]
+  uint8_t *qt = reinterpret_cast<uint8_t *>(cbs + ((nent * dsub + 3) & ~3) + kFourWarpWarps * (dpad + fstride)) +
+                static_cast<size_t>(warp) * four_u8_stride(M);                      // u8 table [M][16]
+  const uint32_t qt_a = smem_u32(qt);
+
+  for (int i = tid; i < nent * dsub; i += kFourWarpThreads) cbs[i] = p.codebooks[i];
+  __syncthreads();
+
+  for (;;) {
+    uint32_t q = 0;
+    if (lane == 0) q = atomicAdd(p.counter, 1u);
+    q = __shfl_sync(VG_FULL_MASK, q, 0);
+    if (q >= static_cast<uint32_t>(p.nq)) break;
+    const float *qv = p.qn + static_cast<size_t>(q) * d;
+    WarpTopK<R> tk;
+    tk.init();
+    uint64_t kth = kEmptyKey;
+    for (int pi = 0; pi < P; ++pi) {
+      const size_t pr = static_cast<size_t>(q) * P + pi;
+      const uint32_t l = p.probes[pr];
+      if (l == 0xffffffffu || (p.owner && !p.owner[l])) continue;
+      if (kth != kEmptyKey && p.probe_lbq && p.probe_lbq[pr] > key_dist(kth)) continue;  // before the table
+      const uint64_t lbeg = p.list_off[l];
+      const uint32_t len = static_cast<uint32_t>(p.list_off[l + 1] - lbeg);
+      if (len == 0) continue;
+      const float *cent = p.centroids + static_cast<size_t>(l) * d;
+      __syncwarp();
+      for (int j = lane; j < d; j += 32) rb[j] = __fsub_rn(qv[j], cent[j]);
+      __syncwarp();
+      const uint32_t *ids = p.list_ids + lbeg;
+      if (len < 16) {  // search.rs:1261: float table, sequential float sum
+        const uint8_t *codes = p.list_codes + p.code_off[l];
+        const bool alive = lane < static_cast<int>(len);
+        float dist = 0.0f;
+        if (alive)
+          for (int m = 0; m < M; ++m)
+            dist = __fadd_rn(dist, four_entry(rb, cbs, dsub, m, codes[static_cast<size_t>(lane) * M + m]));
+        const uint32_t dk = order_key(dist);
+        const bool pass = alive && (kth == kEmptyKey || dk <= static_cast<uint32_t>(kth >> 32));
+        const uint64_t key = pass ? ((static_cast<uint64_t>(dk) << 32) | ids[lane]) : kEmptyKey;
+        tk.add(key < kth ? key : kEmptyKey);
+        kth = tk.get(k - 1);
+        continue;
+      }
+      // float table (warp-private), its min / max (pq_simd.rs:587-598: NaNs
+      // skipped as the reference's comparisons do), u8 quantisation
+      float lmin = __int_as_float(0x7f800000), lmax = -__int_as_float(0x7f800000);
+      for (int e = lane; e < nent; e += 32) {
+        const float t = four_entry(rb, cbs, dsub, e >> 4, e & 15);
+        ft[e] = t;
+        lmin = fminf(lmin, t);
+        lmax = fmaxf(lmax, t);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        lmin = fminf(lmin, __shfl_xor_sync(VG_FULL_MASK, lmin, off));
+        lmax = fmaxf(lmax, __shfl_xor_sync(VG_FULL_MASK, lmax, off));
+      }
+      const float range = __fsub_rn(lmax, lmin);
+      const bool flat = range < FLT_EPSILON;
+      const float inv = flat ? 0.0f : __fdiv_rn(255.0f, range);
+      const float scale = flat ? 1.0f : __fdiv_rn(range, 255.0f);
+      const float fb = __fmul_rn(lmin, static_cast<float>(M));
+      // exact bound with this table's scale (see ivfpq_four_kernel)
+      if (kth != kEmptyKey && p.probe_lb) {
+        const double lbq = static_cast<double>(p.probe_lb[pr]) * (1.0 - 16 * 5.9604644775390625e-8) -
+                           0.5 * M * static_cast<double>(scale) * (1.0 + 1e-5);
+        if (lbq > static_cast<double>(key_dist(kth))) continue;
+      }
+      __syncwarp();
+      for (int e = lane; e < nent; e += 32) {  // each lane its own entries
+        // round half away from zero, clamp; NaN -> 0 (pq_simd.rs:607-609)
+        float t = roundf(__fmul_rn(__fsub_rn(ft[e], lmin), inv));
+        t = fminf(fmaxf(t, 0.0f), 255.0f);
+        qt[e] = static_cast<uint8_t>(t);
+      }
+      __syncwarp();
+      // candidates: integer sums of the u8 entries, checked every 16 codes
+      const uint8_t *packed = p.packed + p.pack_off[l];
+      const int vb = (M + 1) >> 1;  // bytes per vector in the nibble layout
+      for (uint32_t x0 = 0; x0 < len; x0 += 32) {
+        const uint32_t c = x0 + lane;
+        bool live = c < len;
+        const uint32_t tkey = static_cast<uint32_t>(kth >> 32);
+        const uint8_t *vp = packed + static_cast<uint64_t>(live ? c : 0u) * vb;
+        uint32_t acc = 0;
+        if ((M & 15) == 0) {
+          for (int m0 = 0; m0 < M; m0 += 16) {
+            if (!__any_sync(VG_FULL_MASK, live)) break;
+            if (live) {
+              const uint2 w = *reinterpret_cast<const uint2 *>(vp + (m0 >> 1));
+              acc += nibble_sum16(w, qt_a + static_cast<uint32_t>(m0 * 16));
+              live = order_key(__fadd_rn(__fmul_rn(__uint2float_rn(acc), scale), fb)) <= tkey;
+            }
+          }
+        } else if (live) {
+          for (int m = 0; m < M; ++m) acc += qt[m * 16 + ((vp[m >> 1] >> ((m & 1) * 4)) & 15u)];
+          live = order_key(__fadd_rn(__fmul_rn(__uint2float_rn(acc), scale), fb)) <= tkey;
+        }
+        const float dist = __fadd_rn(__fmul_rn(__uint2float_rn(acc), scale), fb);
+        const uint32_t dk = order_key(dist);
+        const bool pass = live && dk <= tkey;
+        unsigned mask = __ballot_sync(VG_FULL_MASK, pass);
+        if (!mask) continue;
+        const uint64_t key = pass ? ((static_cast<uint64_t>(dk) << 32) | ids[c]) : kEmptyKey;
+        if (__popc(mask) > 4) {
+          tk.add(key < kth ? key : kEmptyKey);
+        } else {
+          while (mask) {
+            const int src = __ffs(mask) - 1;
+            mask &= mask - 1;
+            const uint64_t kx = shfl64(key, src);
+            if (kx < kth) topk_insert_one(tk, kx);
+          }
+        }
+        kth = tk.get(k - 1);
+      }
+    }
+    uint32_t count = 0;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int i = r * 32 + lane;
+      const uint64_t key = tk.v[r];
+      const bool real = i < k && key != kEmptyKey;
+      count += __popc(__ballot_sync(VG_FULL_MASK, real));
+      if (i < k) {
+        const size_t o = static_cast<size_t>(q) * k + i;
+        if (p.out_keys) p.out_keys[o] = key;
+        if (p.out_ids) {
+          p.out_ids[o] = real ? p.doc_ids[key_id(key)] : 0xffffffffu;
+          p.out_dist[o] = real ? key_dist(key) : __int_as_float(0x7f800000);
+        }
+      }
+    }
+    if (p.out_count && lane == 0) p.out_count[q] = count;
+  }
+}
+
+}  // namespace vg
