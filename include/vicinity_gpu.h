@@ -75,6 +75,10 @@ typedef struct vg_search_profile {
       merge_ms, collective_ms, d2h_ms, total_ms;
   uint64_t calls, queries, probed_pairs, scanned_vectors, scanned_code_bytes;
   uint64_t kernel_launches, scan_launches;
+  /* lists and vectors actually scored after list pruning (filled by the
+   * warp-per-query kernels; 0 where another kernel ran); probed_pairs and
+   * scanned_vectors count every probed list */
+  uint64_t scored_lists, scored_vectors;
 } vg_search_profile;
 
 typedef struct vg_index vg_index;

@@ -97,6 +97,8 @@ class VgProfile(C.Structure):
             "scanned_code_bytes",
             "kernel_launches",
             "scan_launches",
+            "scored_lists",
+            "scored_vectors",
         )
     ]
 

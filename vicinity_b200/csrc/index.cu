@@ -206,7 +206,7 @@ struct vg_index {
   // search workspace
   DevBuf ws_q, ws_qn, ws_dist, ws_probes, ws_pdist, ws_scalars,
       ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_lb, ws_rec, ws_lbq, ws_qh;
-  DevBuf stats;  // u64 [pairs, vectors, code bytes] accumulated while profiling
+  DevBuf stats;  // u64 [pairs, vectors, code bytes, scored lists, scored vectors] while profiling
 
   // error flag of bounded device waits, in mapped pinned host memory
   int *h_err = nullptr, *d_err = nullptr;
@@ -849,6 +849,7 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
 
   vg::ScanParams sp = base_scan_params(ix, P, kk, prune, recs, quant);
   sp.counter = d_counter;
+  sp.scored = prof ? ix->stats.as<unsigned long long>() + 3 : nullptr;
   sp.doc_ids = doc_map;
   sp.nq = static_cast<int>(nq);
   if (direct) {
@@ -1606,8 +1607,8 @@ int vg_ivfpq_set_profiling(vg_index *ix, int on) {
   if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
   DeviceGuard g(ix->device);
   if (on && !ix->stats.p) {
-    VG_CU(ix->stats.reserve(3 * 8));
-    VG_CU(cudaMemset(ix->stats.p, 0, 3 * 8));
+    VG_CU(ix->stats.reserve(5 * 8));
+    VG_CU(cudaMemset(ix->stats.p, 0, 5 * 8));
   }
   ix->profiling = on != 0;
   return VG_OK;
@@ -1618,11 +1619,13 @@ int vg_ivfpq_get_profile(const vg_index *ix, vg_search_profile *out) {
   *out = ix->prof;
   if (ix->stats.p) {
     DeviceGuard g(ix->device);
-    unsigned long long st[3] = {0, 0, 0};
+    unsigned long long st[5] = {0, 0, 0, 0, 0};
     VG_CU(cudaMemcpy(st, ix->stats.p, sizeof(st), cudaMemcpyDeviceToHost));
     out->probed_pairs = st[0];
     out->scanned_vectors = st[1];
     out->scanned_code_bytes = st[2];
+    out->scored_lists = st[3];
+    out->scored_vectors = st[4];
   }
   return VG_OK;
 }
@@ -1632,7 +1635,7 @@ int vg_ivfpq_reset_profile(vg_index *ix) {
   ix->prof = vg_search_profile{};
   if (ix->stats.p) {
     DeviceGuard g(ix->device);
-    VG_CU(cudaMemset(ix->stats.p, 0, 3 * 8));
+    VG_CU(cudaMemset(ix->stats.p, 0, 5 * 8));
   }
   return VG_OK;
 }

@@ -216,6 +216,7 @@ struct ScanParams {
   const float *probe_lb;         // [nq][P] distance lower bound per probe (nullable: no list pruning)
   const ProbeRec *probe_rec;     // [nq][P] probe records (streaming 8-bit kernel; nullable)
   const float *probe_lbq;        // [nq][P] bound on quantised 4-bit distances before the table (nullable)
+  unsigned long long *scored;    // [2]: lists and vectors scored after pruning (nullable; warp-per-query kernels)
 };
 
 // Fused per-query kernel: for each probed list the query residual, the ADC

@@ -124,6 +124,7 @@ __global__ void __launch_bounds__(kDirectThreads, 1) ivfpq_direct_kernel(const S
     const float *qv = p.qn + static_cast<size_t>(q) * d;
     WarpTopK<R> tk;
     tk.init();
+    uint32_t n_lists = 0, n_vecs = 0;  // scored after pruning (profiling)
     for (int pi = 0; pi < P; ++pi) {
       const ProbeRec rec = p.probe_rec[static_cast<size_t>(q) * P + pi];
       if (rec.list == 0xffffffffu) continue;
@@ -133,6 +134,8 @@ __global__ void __launch_bounds__(kDirectThreads, 1) ivfpq_direct_kernel(const S
       __syncwarp();
       for (int j = lane; j < d; j += 32) rb[(j / DSUB) * DP + j % DSUB] = __fsub_rn(qv[j], cent[j]);
       __syncwarp();
+      ++n_lists;
+      n_vecs += rec.len;
       for (uint32_t x0 = 0; x0 < rec.len; x0 += 32) {
         const uint32_t c = x0 + lane;
         bool alive = c < rec.len;
@@ -174,6 +177,10 @@ __global__ void __launch_bounds__(kDirectThreads, 1) ivfpq_direct_kernel(const S
       }
     }
     if (p.out_count && lane == 0) p.out_count[q] = count;
+    if (p.scored && lane == 0) {
+      atomicAdd(p.scored, static_cast<unsigned long long>(n_lists));
+      atomicAdd(p.scored + 1, static_cast<unsigned long long>(n_vecs));
+    }
   }
 }
 

@@ -71,6 +71,7 @@ __global__ void __launch_bounds__(kFourWarpThreads, 1) ivfpq_four_warp_kernel(co
     const float *qv = p.qn + static_cast<size_t>(q) * d;
     WarpTopK<R> tk;
     tk.init();
+    uint32_t n_lists = 0, n_vecs = 0;  // scored after pruning (profiling)
     uint64_t kth = kEmptyKey;
     for (int pi = 0; pi < P; ++pi) {
       const size_t pr = static_cast<size_t>(q) * P + pi;
@@ -86,6 +87,8 @@ __global__ void __launch_bounds__(kFourWarpThreads, 1) ivfpq_four_warp_kernel(co
       __syncwarp();
       const uint32_t *ids = p.list_ids + lbeg;
       if (len < 16) {  // search.rs:1261: float table, sequential float sum
+        ++n_lists;
+        n_vecs += len;
         const uint8_t *codes = p.list_codes + p.code_off[l];
         const bool alive = lane < static_cast<int>(len);
         float dist = 0.0f;
@@ -133,6 +136,8 @@ __global__ void __launch_bounds__(kFourWarpThreads, 1) ivfpq_four_warp_kernel(co
       }
       __syncwarp();
       // candidates: integer sums of the u8 entries, checked every 16 codes
+      ++n_lists;
+      n_vecs += len;
       const uint8_t *packed = p.packed + p.pack_off[l];
       const int vb = (M + 1) >> 1;  // bytes per vector in the nibble layout
       for (uint32_t x0 = 0; x0 < len; x0 += 32) {
@@ -190,6 +195,10 @@ __global__ void __launch_bounds__(kFourWarpThreads, 1) ivfpq_four_warp_kernel(co
       }
     }
     if (p.out_count && lane == 0) p.out_count[q] = count;
+    if (p.scored && lane == 0) {
+      atomicAdd(p.scored, static_cast<unsigned long long>(n_lists));
+      atomicAdd(p.scored + 1, static_cast<unsigned long long>(n_vecs));
+    }
   }
 }
 
