@@ -45,7 +45,7 @@ FALLBACK_HBM_GBS = 6650.0
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--config", type=int, default=1)
     p.add_argument("--impl", choices=["engine", "reference"], default="engine")
@@ -72,13 +72,14 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """SM clocks and throttle reasons sampled every 50 ms during the timed steps.
+    """SM clocks and throttle reasons sampled every 10 ms during the timed steps.
 
     Sampled in-process through NVML (the library nvidia-smi reads): an
     nvidia-smi process polling every 50 ms stalled this GPU for ~90 ms now
     and then inside timed steps, the same queries made in-process did not.
     Falls back to nvidia-smi when NVML bindings are missing.  Only samples
-    taken between begin() and end() are reported.
+    taken between begin() and end() are reported; the 10 ms period leaves
+    several inside even a timed region of a few tens of milliseconds.
     """
 
     REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
@@ -114,7 +115,7 @@ class ClockSampler:
                                           int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))))
                     except Exception:
                         pass
-                    self._stop.wait(0.05)
+                    self._stop.wait(0.01)
 
             self.source = "nvml"
             self.thread = threading.Thread(target=loop, daemon=True)
@@ -153,7 +154,7 @@ class ClockSampler:
         self.window = (time.monotonic(), float("inf"))
 
     def end(self):
-        self.window = (self.window[0], time.monotonic() + 0.06)
+        self.window = (self.window[0], time.monotonic() + 0.012)
 
     def stop(self) -> dict:
         if not self.source:
