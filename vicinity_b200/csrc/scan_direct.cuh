@@ -9,8 +9,8 @@
 // the codebook -- so it returns the same ids and distances without building a
 // table.  What that buys:
 //   - a candidate whose partial sum passes the query's k-th distance stops
-//     (entries are >= +0 and a rounded add never decreases the sum), and the
-//     entries it never reaches are never computed;
+//     (entries are >= +0 and a rounded add never decreases the sum; checked
+//     every 4 subspaces), and the entries it never reaches are never computed;
 //   - each warp owns its query: it walks the probes in order, skips a list
 //     whose distance lower bound exceeds its current k-th distance (list
 //     pruning with the freshest bound), keeps the top-k in registers and
@@ -80,16 +80,15 @@ __device__ __forceinline__ float direct_row_sum(const uint8_t *cp, const float *
       if (alive && m0 + 16 < M) wn = *reinterpret_cast<const uint4 *>(cp + m0 + 16);
       if (alive) {
         const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        // four codes (one word) at a time, the bound checked after each word
 #pragma unroll
-        for (int b = 0; b < 8; ++b)
-          acc = __fadd_rn(acc, direct_entry<DSUB, DP>(rb, cbk, m0 + b, __byte_perm(ws[b >> 2], 0u, 0x4440u + (b & 3))));
-        alive = order_key(acc) <= tkey;
-        if (alive) {
+        for (int g = 0; g < 4; ++g) {
+          if (alive) {
 #pragma unroll
-          for (int b = 8; b < 16; ++b)
-            acc = __fadd_rn(acc,
-                            direct_entry<DSUB, DP>(rb, cbk, m0 + b, __byte_perm(ws[b >> 2], 0u, 0x4440u + (b & 3))));
-          alive = order_key(acc) <= tkey;
+            for (int b = 0; b < 4; ++b)
+              acc = __fadd_rn(acc, direct_entry<DSUB, DP>(rb, cbk, m0 + 4 * g + b, __byte_perm(ws[g], 0u, 0x4440u + b)));
+            alive = order_key(acc) <= tkey;
+          }
         }
       }
     }

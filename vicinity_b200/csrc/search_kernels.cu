@@ -10,6 +10,8 @@
 //   batch padding              src/python.rs:745-795 (-1 / +inf)
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "f32x2.cuh"
 #include "kernels.h"
@@ -470,6 +472,31 @@ __device__ __forceinline__ void for_each_quad(const TS *__restrict__ srow, size_
   }
 }
 
+// Visit a half row of L % 4 == 0 columns, 8-byte aligned, as raw quads: fn(col,
+// lo, hi, valid) with lo / hi the half2 pairs (col, col + 1) and (col + 2, col + 3).
+// Trip counts are warp-uniform.
+template <bool kLast, typename F>
+__device__ __forceinline__ void for_each_half_quad(const __half *__restrict__ srow, size_t L, int lane, F &&fn) {
+  const uint2 *r4 = reinterpret_cast<const uint2 *>(srow);
+  const size_t n4 = L >> 2;
+  size_t b = 0;
+  for (; b + 128 <= n4; b += 128) {
+    uint2 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = kLast ? __ldcs(r4 + b + u * 32 + lane) : __ldg(r4 + b + u * 32 + lane);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      fn((b + u * 32 + lane) * 4, *reinterpret_cast<const __half2 *>(&v[u].x),
+         *reinterpret_cast<const __half2 *>(&v[u].y), true);
+  }
+  for (; b < n4; b += 32) {
+    const size_t i = b + lane;
+    uint2 v = make_uint2(0u, 0u);
+    if (i < n4) v = kLast ? __ldcs(r4 + i) : __ldg(r4 + i);
+    fn(i * 4, *reinterpret_cast<const __half2 *>(&v.x), *reinterpret_cast<const __half2 *>(&v.y), i < n4);
+  }
+}
+
 template <int R, typename TS>
 __global__ void __launch_bounds__(kSelectWarps * 32)
     shortlist_kernel(const TS *__restrict__ s, size_t rows, size_t L, size_t ld, const float *__restrict__ qn,
@@ -513,7 +540,36 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
       a[r] = lo;
     }
   };
-  if (!exact_all) {
+  bool half_fast = false;
+  if constexpr (std::is_same<TS, __half>::value) half_fast = svec;
+  if (!exact_all && half_fast) {
+    if constexpr (std::is_same<TS, __half>::value) {
+      // the largest products are the smallest distances: keep the 2R largest
+      // of each half2 sublane with packed max / min (NaN never enters), then
+      // the 2R largest of the lane's two sorted sublanes (bitonic step)
+      const __half2 ninf = __halves2half2(__ushort_as_half(0xFC00u), __ushort_as_half(0xFC00u));
+      __half2 a2[R2];
+#pragma unroll
+      for (int r = 0; r < R2; ++r) a2[r] = ninf;
+      auto insert2 = [&](__half2 x) {
+#pragma unroll
+        for (int r = 0; r < R2; ++r) {
+          const __half2 hi = __hmax2(x, a2[r]);
+          x = __hmin2(x, a2[r]);
+          a2[r] = hi;
+        }
+      };
+      for_each_half_quad<false>(srow, L, lane, [&](size_t, __half2 lo, __half2 hi, bool ok) {
+        insert2(ok ? lo : ninf);
+        insert2(ok ? hi : ninf);
+      });
+#pragma unroll
+      for (int r = 0; r < R2; ++r) {
+        const float s = fmaxf(__low2float(a2[r]), __high2float(a2[R2 - 1 - r]));
+        a[r] = s == -kInf ? kInf : __fsub_rn(1.0f, s);
+      }
+    }
+  } else if (!exact_all) {
     for_each_quad<false, TS>(srow, L, svec, lane, [&](size_t, float4 v, bool ox, bool oy, bool oz, bool ow) {
       if (ox) insert(__fsub_rn(1.0f, v.x));
       if (oy) insert(__fsub_rn(1.0f, v.y));
@@ -533,23 +589,37 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
   if (!(limit < __int_as_float(0x7f800000)) && ub != kEmptyKey) exact_all = true;
 
   int n = 0;
-  if (!exact_all) {
-    bool over = false;
-    for_each_quad<true, TS>(srow, L, svec, lane, [&](size_t c, float4 v, bool ox, bool oy, bool oz, bool ow) {
-      const bool t[4] = {ox && !(__fsub_rn(1.0f, v.x) > limit), oy && !(__fsub_rn(1.0f, v.y) > limit),
-                         oz && !(__fsub_rn(1.0f, v.z) > limit), ow && !(__fsub_rn(1.0f, v.w) > limit)};
-      if (!__any_sync(VG_FULL_MASK, t[0] || t[1] || t[2] || t[3])) return;  // nearly every quad
+  auto gather = [&](size_t c, float4 v, bool ox, bool oy, bool oz, bool ow) {
+    const bool t[4] = {ox && !(__fsub_rn(1.0f, v.x) > limit), oy && !(__fsub_rn(1.0f, v.y) > limit),
+                       oz && !(__fsub_rn(1.0f, v.z) > limit), ow && !(__fsub_rn(1.0f, v.w) > limit)};
+    if (!__any_sync(VG_FULL_MASK, t[0] || t[1] || t[2] || t[3])) return;  // nearly every quad
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        const unsigned m = __ballot_sync(VG_FULL_MASK, t[h]);
-        const int pos = n + __popc(m & ((1u << lane) - 1u));
-        if (t[h] && pos < kShortBuf) buf[pos] = static_cast<uint32_t>(c + h);
-        n += __popc(m);
-      }
-    });
-    over = n > kShortBuf;
-    exact_all = over;
+    for (int h = 0; h < 4; ++h) {
+      const unsigned m = __ballot_sync(VG_FULL_MASK, t[h]);
+      const int pos = n + __popc(m & ((1u << lane) - 1u));
+      if (t[h] && pos < kShortBuf) buf[pos] = static_cast<uint32_t>(c + h);
+      n += __popc(m);
+    }
+  };
+  if (!exact_all && half_fast) {
+    if constexpr (std::is_same<TS, __half>::value) {
+      // a product below s_lo cannot give a distance <= limit (1 - s > limit
+      // by more than a rounding of 1 - s): one packed test per pair, the
+      // exact test only in quads where a lane may hold a candidate
+      const float s_lo = __double2float_rd(1.0 - static_cast<double>(limit) -
+                                           1e-6 * (1.0 + fabs(static_cast<double>(limit))));
+      const __half2 slo2 = __half2half2(__float2half_rd(s_lo));
+      for_each_half_quad<true>(srow, L, lane, [&](size_t c, __half2 lo, __half2 hi, bool ok) {
+        const bool maybe = ok && (!__hblt2(lo, slo2) || !__hblt2(hi, slo2));
+        if (!__any_sync(VG_FULL_MASK, maybe)) return;
+        const float2 fl = __half22float2(lo), fh = __half22float2(hi);
+        gather(c, make_float4(fl.x, fl.y, fh.x, fh.y), ok, ok, ok, ok);
+      });
+    }
+  } else if (!exact_all) {
+    for_each_quad<true, TS>(srow, L, svec, lane, gather);
   }
+  if (!exact_all) exact_all = n > kShortBuf;
   // The row of products is not read again: drop its lines from L2 without
   // writing them back (whole 128-byte lines inside the row only), so the
   // search kernels that follow do not pay for its write-back.
