@@ -33,6 +33,8 @@ __host__ __device__ inline size_t four_warp_smem_bytes(int M, int dsub, int d) {
   return cb * 4 + kFourWarpWarps * ((dpad + four_float_stride(M)) * 4 + four_u8_stride(M));
 }
 
+__device__ __forceinline__ void prefetch_l1_4(const void *a) { asm volatile("prefetch.global.L1 [%0];" ::"l"(a)); }
+
 // Float table entry (m, c): sum_j (r_j - w_j)^2 in j order (first square as is).
 __device__ __forceinline__ float four_entry(const float *rb, const float *cbs, int dsub, int m, int c) {
   const float *r = rb + m * dsub, *w = cbs + (m * 16 + c) * dsub;
@@ -102,6 +104,10 @@ __global__ void __launch_bounds__(kFourWarpThreads, 1) ivfpq_four_warp_kernel(co
         kth = tk.get(k - 1);
         continue;
       }
+      // the first codes of the list come in while the table is built
+      const uint8_t *packed = p.packed + p.pack_off[l];
+      const int vb = (M + 1) >> 1;  // bytes per vector in the nibble layout
+      if (static_cast<uint32_t>(lane) < len) prefetch_l1_4(packed + static_cast<uint64_t>(lane) * vb);
       // float table (warp-private), its min / max (pq_simd.rs:587-598: NaNs
       // skipped as the reference's comparisons do), u8 quantisation
       float lmin = __int_as_float(0x7f800000), lmax = -__int_as_float(0x7f800000);
@@ -138,11 +144,10 @@ __global__ void __launch_bounds__(kFourWarpThreads, 1) ivfpq_four_warp_kernel(co
       // candidates: integer sums of the u8 entries, checked every 16 codes
       ++n_lists;
       n_vecs += len;
-      const uint8_t *packed = p.packed + p.pack_off[l];
-      const int vb = (M + 1) >> 1;  // bytes per vector in the nibble layout
       for (uint32_t x0 = 0; x0 < len; x0 += 32) {
         const uint32_t c = x0 + lane;
         bool live = c < len;
+        if (c + 32 < len) prefetch_l1_4(packed + static_cast<uint64_t>(c + 32) * vb);  // next chunk
         const uint32_t tkey = static_cast<uint32_t>(kth >> 32);
         const uint8_t *vp = packed + static_cast<uint64_t>(live ? c : 0u) * vb;
         uint32_t acc = 0;
