@@ -33,6 +33,8 @@ __host__ __device__ inline size_t direct_smem_bytes(int M, int dsub) {
   return static_cast<size_t>(M) * 256 * dp * 4 + static_cast<size_t>(kDirectWarps) * M * dp * 4;
 }
 
+__device__ __forceinline__ void prefetch_codes(const void *a) { asm volatile("prefetch.global.L1 [%0];" ::"l"(a)); }
+
 template <int DP>
 __device__ __forceinline__ void lds_vec(const float *a, float (&v)[DP]) {
   if constexpr (DP == 8) {
@@ -130,6 +132,8 @@ __global__ void __launch_bounds__(kDirectThreads, 1) ivfpq_direct_kernel(const S
       uint64_t kth = tk.get(k - 1);
       if (kth != kEmptyKey && rec.lb > key_dist(kth)) continue;  // list pruning
       const float *cent = p.centroids + static_cast<size_t>(rec.list) * d;
+      const uint8_t *lcodes = p.list_codes + rec.coff;
+      if (static_cast<uint32_t>(lane) < rec.len) prefetch_codes(lcodes + static_cast<uint64_t>(lane) * M);
       __syncwarp();
       for (int j = lane; j < d; j += 32) rb[(j / DSUB) * DP + j % DSUB] = __fsub_rn(qv[j], cent[j]);
       __syncwarp();
@@ -138,8 +142,9 @@ __global__ void __launch_bounds__(kDirectThreads, 1) ivfpq_direct_kernel(const S
       for (uint32_t x0 = 0; x0 < rec.len; x0 += 32) {
         const uint32_t c = x0 + lane;
         bool alive = c < rec.len;
+        if (c + 32 < rec.len) prefetch_codes(lcodes + static_cast<uint64_t>(c + 32) * M);  // next chunk
         const uint32_t tkey = static_cast<uint32_t>(kth >> 32);
-        const uint8_t *cp = p.list_codes + rec.coff + static_cast<uint64_t>(alive ? c : 0u) * M;
+        const uint8_t *cp = lcodes + static_cast<uint64_t>(alive ? c : 0u) * M;
         const float dist = direct_row_sum<DSUB, DP>(cp, cbk, rb, M, tkey, alive);
         const uint32_t dk = order_key(dist);
         const bool pass = alive && dk <= tkey;
