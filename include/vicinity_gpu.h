@@ -200,6 +200,30 @@ int vg_ivfpq_save(const vg_index *ix, const char *dir);
  * malformed ones VG_ERR_FORMAT. */
 int vg_ivfpq_load(const char *dir, int device, vg_index **out);
 
+/* src/ivf_pq/search.rs:916-935 (save_to_generation) with
+ * persistence/generation.rs:30-140 (GenerationWriter): the snapshot is
+ * staged in root/generations/.staging-<id> with its component list in the
+ * manifest, read back, inventoried in GENERATION.json (length and CRC-32 of
+ * every file) and published under root/.PUBLISH.lock: renamed to
+ * root/generations/<id>, then root/CURRENT replaced atomically.  Earlier
+ * generations stay.  A concurrent publisher, or CURRENT changing meanwhile,
+ * gives VG_ERR_IO. */
+int vg_ivfpq_save_generation(const vg_index *ix, const char *root);
+
+/* src/ivf_pq/search.rs:939-943 (load_from_generation): vg_ivfpq_load of the
+ * directory root/CURRENT names (persistence/generation.rs:191-205). */
+int vg_ivfpq_load_generation(const char *root, int device, vg_index **out);
+
+/* persistence/generation.rs:191-205 (open_current): the path of the
+ * generation root/CURRENT names, NUL-terminated into out[len]. */
+int vg_generation_current(const char *root, char *out, size_t len);
+
+/* persistence/generation.rs:285-365 (verify_generation): every file of a
+ * generation directory against its GENERATION.json inventory; a missing or
+ * malformed inventory, an unlisted or missing file, or a length or CRC-32
+ * mismatch gives VG_ERR_FORMAT.  Host only. */
+int vg_verify_generation(const char *dir);
+
 /* Copies of index state for parity checks and persistence (host or device
  * destination, `bytes` must match):
  *   VG_EXPORT_CENTROIDS    f32 [num_centroids][dim]

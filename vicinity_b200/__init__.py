@@ -8,15 +8,20 @@ from ._lib import VicinityError, device_count
 from .ivf_pq import (
     MISSING_DISTANCE,
     MISSING_LABEL,
+    IVFPQFileSearcher,
     IVFPQIndex,
+    current_generation,
     default_ivfpq_codebooks,
     flat_search_ip,
     nccl_unique_id,
     shard_assign_lists,
+    verify_generation,
 )
 
 __all__ = [
+    "IVFPQFileSearcher",
     "IVFPQIndex",
+    "current_generation",
     "MISSING_DISTANCE",
     "MISSING_LABEL",
     "VicinityError",
@@ -25,4 +30,5 @@ __all__ = [
     "flat_search_ip",
     "nccl_unique_id",
     "shard_assign_lists",
+    "verify_generation",
 ]

@@ -139,6 +139,10 @@ SIGNATURES = {
     "vg_flat_search_ip": (_i, [_vp, _sz, _vp, _sz, _sz, _sz, _i, _vp, _vp, _vp]),
     "vg_ivfpq_save": (_i, [_vp, C.c_char_p]),
     "vg_ivfpq_load": (_i, [C.c_char_p, _i, C.POINTER(_vp)]),
+    "vg_ivfpq_save_generation": (_i, [_vp, C.c_char_p]),
+    "vg_ivfpq_load_generation": (_i, [C.c_char_p, C.c_int, C.POINTER(_vp)]),
+    "vg_generation_current": (_i, [C.c_char_p, C.c_char_p, _sz]),
+    "vg_verify_generation": (_i, [C.c_char_p]),
     "vg_flat_search_ip_noalloc": (_i, [_vp, _sz, _vp, _sz, _sz, _sz, _i, _vp, _vp, _vp, _vp]),
 }
 

@@ -24,6 +24,12 @@
 #include <cstdlib>
 #include <cstring>
 #include <fcntl.h>
+#include <algorithm>
+#include <cctype>
+#include <chrono>
+#include <atomic>
+#include <sys/file.h>
+#include <dirent.h>
 #include <string>
 #include <sys/stat.h>
 #include <unistd.h>
@@ -494,7 +500,7 @@ bool json_f32_array(std::string &o, const std::vector<float> &v) {
   return true;
 }
 
-bool manifest_text(const SnapshotState &st, std::string &o) {
+bool manifest_text(const SnapshotState &st, std::string &o, bool generation_components = false) {
   const auto &p = st.params;
   auto u = [](uint64_t v) { return std::to_string(v); };
   o = "{\n";
@@ -537,8 +543,14 @@ bool manifest_text(const SnapshotState &st, std::string &o) {
     o += i ? ",\n    " : "\n    ";
     o += "{\"doc_id\": " + u(st.metadata[i].first) + ", \"metadata\": " + st.metadata[i].second + "}";
   }
-  o += st.metadata.empty() ? "]\n" : "\n  ]\n";
-  o += "}\n";
+  o += st.metadata.empty() ? "]" : "\n  ]";
+  if (generation_components) {  // manifest.rs:64-77: the payload files of a generation
+    o += ",\n  \"generation_components\": [\"centroids.bin\", \"clusters.bin\", \"codes.bin\", \"doc_ids.bin\", "
+         "\"list_codes.bin\", \"list_offsets.bin\"";
+    if (!st.vectors.empty()) o += ", \"raw_vectors.bin\"";
+    o += "]";
+  }
+  o += "\n}\n";
   return true;
 }
 
@@ -692,6 +704,376 @@ int int_category(const JVal &v, const std::string &tag, int *category, bool at_s
   return VG_OK;
 }
 
+// Snapshot of ix into directory d (search.rs:945-1016); with generation
+// components the manifest lists the payload files (a generation's layout).
+int save_dir(const vg_index *ix, const std::string &d, bool components) {
+  SnapshotState st;
+  if (int s = vg::snapshot_export(ix, st)) return s;
+  std::string manifest;
+  if (!manifest_text(st, manifest, components)) return fail(VG_ERR_INVALID_PARAMETER, "non-finite value in the quantizer");
+  if (int s = make_dirs(d)) return s;
+  // list-contiguous codes for the file searcher (file_storage.rs:39-72)
+  const size_t M = st.params.num_codebooks;
+  std::vector<uint64_t> list_offsets(st.list_offsets.size());
+  std::vector<uint8_t> list_codes(st.list_ids.size() * M);
+  for (size_t i = 0; i < st.list_offsets.size(); ++i) list_offsets[i] = st.list_offsets[i] * M;
+  for (size_t p = 0; p < st.list_ids.size(); ++p)
+    std::memcpy(list_codes.data() + p * M, st.codes.data() + static_cast<size_t>(st.list_ids[p]) * M, M);
+  std::string clusters(kClusterMagic, 8);
+  const uint64_t L = st.bitmasks.size();
+  clusters.append(reinterpret_cast<const char *>(&L), 8);
+  for (size_t l = 0; l < L; ++l) {
+    const uint64_t len = st.list_offsets[l + 1] - st.list_offsets[l];
+    clusters.append(reinterpret_cast<const char *>(&st.bitmasks[l]), 8);
+    clusters.append(reinterpret_cast<const char *>(&len), 8);
+    clusters.append(reinterpret_cast<const char *>(st.list_ids.data() + st.list_offsets[l]), len * 4);
+  }
+  Writer w{d};
+  int s = w.put("manifest.json", manifest.data(), manifest.size());
+  if (!s) s = w.put("centroids.bin", st.centroids.data(), st.centroids.size() * 4);
+  if (!s) s = w.put("doc_ids.bin", st.doc_ids.data(), st.doc_ids.size() * 4);
+  if (!s) s = w.put("codes.bin", st.codes.data(), st.codes.size());
+  if (!s) s = w.put("list_offsets.bin", list_offsets.data(), list_offsets.size() * 8);
+  if (!s) s = w.put("list_codes.bin", list_codes.data(), list_codes.size());
+  if (!s) s = w.put("clusters.bin", clusters.data(), clusters.size());
+  if (!s && !st.vectors.empty()) s = w.put("raw_vectors.bin", st.vectors.data(), st.vectors.size() * 4);
+  if (s) return s;
+  const int fd = ::open(d.c_str(), O_RDONLY | O_DIRECTORY);
+  if (fd < 0) return io_fail(errno, d);
+  const int r = ::fsync(fd);
+  const int e = errno;
+  ::close(fd);
+  if (r != 0) return io_fail(e, d);
+  return VG_OK;
+}
+
+// Every file of a directory snapshot read and checked against its manifest
+// (persistence.rs:178-203, search.rs:1034-1084), host side only.
+int read_snapshot(const std::string &d, SnapshotState &st) {
+  std::string text;
+  if (int s = read_file(d + "/manifest.json", text)) return s;
+  if (int s = parse_manifest(text, st)) return s;
+  const bool raw = !st.vectors.empty();
+  const size_t n = st.num_vectors, dim = st.dim, M = st.params.num_codebooks;
+  if (int s = read_exact(d + "/doc_ids.bin", n, st.doc_ids)) return s;
+  if (int s = read_exact(d + "/centroids.bin", st.num_centroids * dim, st.centroids)) return s;
+  if (int s = read_exact(d + "/codes.bin", n * M, st.codes)) return s;
+  if (int s = read_clusters(d + "/clusters.bin", st.params.num_clusters, n, st)) return s;
+  if (raw) {
+    if (int s = read_exact(d + "/raw_vectors.bin", n * dim, st.vectors)) return s;
+  } else {
+    st.vectors.clear();
+  }
+  return VG_OK;
+}
+
+// ---- generations (persistence/generation.rs) ---------------------------------
+// A generation root holds generations/<id>/ snapshot directories and a CURRENT
+// file naming the published one; each generation carries GENERATION.json, an
+// inventory of its files with length and CRC-32.
+
+// CRC-32 (IEEE 802.3: reflected polynomial 0xEDB88320, initial value and
+// final xor 0xFFFFFFFF), table-driven.
+uint32_t crc32_update(uint32_t crc, const unsigned char *p, size_t n) {
+  static uint32_t table[256];
+  static bool ready = false;
+  if (!ready) {
+    for (uint32_t i = 0; i < 256; ++i) {
+      uint32_t c = i;
+      for (int b = 0; b < 8; ++b) c = (c & 1u) ? (c >> 1) ^ 0xEDB88320u : c >> 1;
+      table[i] = c;
+    }
+    ready = true;
+  }
+  for (size_t i = 0; i < n; ++i) crc = table[(crc ^ p[i]) & 0xFFu] ^ (crc >> 8);
+  return crc;
+}
+
+struct GenFile {
+  std::string path;  // relative, '/' separated
+  uint64_t length = 0;
+  uint32_t crc32 = 0;
+};
+
+int checksum_file(const std::string &path, uint64_t &length, uint32_t &crc) {
+  const int fd = ::open(path.c_str(), O_RDONLY);
+  if (fd < 0) return io_fail(errno, path);
+  std::vector<unsigned char> buf(1 << 16);
+  uint32_t c = 0xFFFFFFFFu;
+  uint64_t len = 0;
+  for (;;) {
+    const ssize_t r = ::read(fd, buf.data(), buf.size());
+    if (r < 0) {
+      const int e = errno;
+      if (e == EINTR) continue;
+      ::close(fd);
+      return io_fail(e, path);
+    }
+    if (r == 0) break;
+    c = crc32_update(c, buf.data(), static_cast<size_t>(r));
+    len += static_cast<uint64_t>(r);
+  }
+  ::close(fd);
+  length = len;
+  crc = ~c;
+  return VG_OK;
+}
+
+// Regular files below `dir` (recursively) except the inventory itself;
+// symlinks and other entries are errors (generation.rs:409-455).
+int collect_files(const std::string &root, const std::string &rel, std::vector<GenFile> &files) {
+  const std::string dir = rel.empty() ? root : root + "/" + rel;
+  DIR *dp = ::opendir(dir.c_str());
+  if (!dp) return io_fail(errno, dir);
+  std::vector<std::string> names;
+  while (struct dirent *e = ::readdir(dp)) {
+    const std::string name = e->d_name;
+    if (name != "." && name != "..") names.push_back(name);
+  }
+  ::closedir(dp);
+  for (const std::string &name : names) {
+    const std::string r = rel.empty() ? name : rel + "/" + name;
+    struct stat sb;
+    if (::lstat((root + "/" + r).c_str(), &sb) != 0) return io_fail(errno, root + "/" + r);
+    if (S_ISLNK(sb.st_mode)) return format_fail("generation contains symlink " + root + "/" + r);
+    if (S_ISDIR(sb.st_mode)) {
+      if (int s = collect_files(root, r, files)) return s;
+    } else if (S_ISREG(sb.st_mode)) {
+      if (r == "GENERATION.json") continue;
+      GenFile f;
+      f.path = r;
+      if (int s = checksum_file(root + "/" + r, f.length, f.crc32)) return s;
+      files.push_back(std::move(f));
+    } else {
+      return format_fail("generation contains unsupported entry " + root + "/" + r);
+    }
+  }
+  return VG_OK;
+}
+
+int fsync_path(const std::string &path, bool directory) {
+  const int fd = ::open(path.c_str(), directory ? (O_RDONLY | O_DIRECTORY) : O_RDONLY);
+  if (fd < 0) return io_fail(errno, path);
+  const int r = ::fsync(fd);
+  const int e = errno;
+  ::close(fd);
+  return r == 0 ? VG_OK : io_fail(e, path);
+}
+
+// CURRENT's generation id, or "" when there is no CURRENT (not_found set).
+int read_current(const std::string &root, std::string &id, bool &not_found) {
+  not_found = false;
+  id.clear();
+  std::string text;
+  const std::string path = root + "/CURRENT";
+  const int fd = ::open(path.c_str(), O_RDONLY);
+  if (fd < 0) {
+    if (errno == ENOENT) {
+      not_found = true;
+      return VG_OK;
+    }
+    return io_fail(errno, path);
+  }
+  ::close(fd);
+  if (int s = read_file(path, text)) return s;
+  size_t a = 0, b = text.size();
+  while (a < b && std::isspace(static_cast<unsigned char>(text[a]))) ++a;
+  while (b > a && std::isspace(static_cast<unsigned char>(text[b - 1]))) --b;
+  id = text.substr(a, b - a);
+  return VG_OK;
+}
+
+// generation.rs:481-488
+bool safe_generation_id(const std::string &id) {
+  return !id.empty() && id != "." && id != ".." && id.find('/') == std::string::npos &&
+         id.find('\\') == std::string::npos;
+}
+
+// generation.rs:191-205: the directory CURRENT names, which must be a real
+// directory below generations/.
+int open_current(const std::string &root, std::string &dir) {
+  std::string id;
+  bool none = false;
+  if (int s = read_current(root, id, none)) return s;
+  if (none) return fail(VG_ERR_NOT_FOUND, "no CURRENT generation pointer in " + root);
+  if (!safe_generation_id(id)) return format_fail("CURRENT must contain one safe generation basename");
+  dir = root + "/generations/" + id;
+  struct stat sb;
+  if (::lstat(dir.c_str(), &sb) != 0) return io_fail(errno, dir);
+  if (S_ISLNK(sb.st_mode) || !S_ISDIR(sb.st_mode))
+    return format_fail("current generation " + dir + " is not a directory");
+  return VG_OK;
+}
+
+std::string inventory_text(const std::vector<GenFile> &files) {  // serde_json pretty form
+  std::string o = "{\n  \"version\": 1,\n  \"files\": [";
+  for (size_t i = 0; i < files.size(); ++i) {
+    o += i ? ",\n    {\n" : "\n    {\n";
+    o += "      \"path\": ";
+    json_string(o, files[i].path);
+    o += ",\n      \"length\": " + std::to_string(files[i].length) + ",\n";
+    o += "      \"crc32\": " + std::to_string(files[i].crc32) + "\n    }";
+  }
+  o += files.empty() ? "]\n}" : "\n  ]\n}";
+  return o;
+}
+
+int write_whole(const std::string &path, const std::string &data) {
+  const int fd = ::open(path.c_str(), O_WRONLY | O_CREAT | O_TRUNC, 0644);
+  if (fd < 0) return io_fail(errno, path);
+  size_t off = 0;
+  while (off < data.size()) {
+    const ssize_t w = ::write(fd, data.data() + off, data.size() - off);
+    if (w < 0) {
+      if (errno == EINTR) continue;
+      const int e = errno;
+      ::close(fd);
+      return io_fail(e, path);
+    }
+    off += static_cast<size_t>(w);
+  }
+  const int r = ::fsync(fd);
+  const int e = errno;
+  ::close(fd);
+  return r == 0 ? VG_OK : io_fail(e, path);
+}
+
+std::atomic<uint64_t> g_generation_sequence{0};
+
+// generation.rs:472-479
+std::string unique_generation_id() {
+  const auto nanos = std::chrono::duration_cast<std::chrono::nanoseconds>(
+                         std::chrono::system_clock::now().time_since_epoch())
+                         .count();
+  return std::to_string(nanos) + "-" + std::to_string(::getpid()) + "-" +
+         std::to_string(g_generation_sequence.fetch_add(1));
+}
+
+// generation.rs:285-365: every file of dir against its GENERATION.json.
+int verify_generation_dir(const std::string &dir) {
+  std::string text;
+  {
+    const std::string path = dir + "/GENERATION.json";
+    const int fd = ::open(path.c_str(), O_RDONLY);
+    if (fd < 0) {
+      if (errno == ENOENT) return format_fail("generation inventory " + path + " is missing");
+      return io_fail(errno, path);
+    }
+    ::close(fd);
+    if (int s = read_file(path, text)) return s;
+  }
+  JVal root;
+  std::string err;
+  if (!parse_json(text, root, err) || root.kind != JVal::Obj)
+    return format_fail("invalid generation inventory: " + (err.empty() ? std::string("not an object") : err));
+  Fields f{root, "inventory"};
+  uint64_t version = 0;
+  if (!f.u64("version", version)) return format_fail("invalid generation inventory: " + f.err);
+  if (version != 1) return format_fail("unsupported generation inventory version " + std::to_string(version));
+  const JVal *arr = f.need("files", JVal::Arr);
+  if (!arr) return format_fail("invalid generation inventory: " + f.err);
+  std::vector<GenFile> listed;
+  for (const JVal &e : arr->arr) {
+    Fields ef{e, "inventory file"};
+    const JVal *path = ef.need("path", JVal::Str);
+    GenFile g;
+    uint64_t crc = 0;
+    if (!path || !ef.u64("length", g.length) || !ef.u64("crc32", crc) || crc > 0xffffffffull)
+      return format_fail("invalid generation inventory: " + ef.err);
+    g.path = path->text;
+    g.crc32 = static_cast<uint32_t>(crc);
+    if (g.path.empty() || g.path[0] == '/' || g.path.find('\\') != std::string::npos ||
+        g.path.find("..") != std::string::npos)
+      return format_fail("invalid generation file path " + g.path);
+    if (g.path == "GENERATION.json") return format_fail("GENERATION.json cannot inventory itself");
+    listed.push_back(std::move(g));
+  }
+  for (size_t i = 1; i < listed.size(); ++i)
+    if (!(listed[i - 1].path < listed[i].path))
+      return format_fail("generation inventory paths must be strictly sorted and unique");
+  std::vector<GenFile> actual;
+  if (int s = collect_files(dir, "", actual)) return s;
+  for (const GenFile &a : actual) {
+    auto it = std::lower_bound(listed.begin(), listed.end(), a,
+                               [](const GenFile &x, const GenFile &y) { return x.path < y.path; });
+    if (it == listed.end() || it->path != a.path)
+      return format_fail("generation file " + a.path + " is absent from GENERATION.json inventory");
+    if (it->length != a.length)
+      return format_fail("generation file " + a.path + " length mismatch: expected " + std::to_string(it->length) +
+                         ", got " + std::to_string(a.length));
+    if (it->crc32 != a.crc32)
+      return format_fail("generation file " + a.path + " checksum mismatch: expected " + std::to_string(it->crc32) +
+                         ", got " + std::to_string(a.crc32));
+  }
+  if (listed.size() != actual.size())
+    return format_fail("GENERATION.json lists a file that is missing from the generation");
+  return VG_OK;
+}
+
+// search.rs:916-935 with GenerationWriter (generation.rs:30-140): stage the
+// snapshot, check it, inventory it, then publish it under the advisory lock
+// by renaming it into generations/ and replacing CURRENT atomically.
+int save_generation(const vg_index *ix, const std::string &root) {
+  const std::string gens = root + "/generations";
+  if (int s = make_dirs(gens)) return s;
+  std::string expected;
+  bool none = false;
+  if (int s = read_current(root, expected, none)) return s;
+  const std::string id = unique_generation_id();
+  const std::string staging = gens + "/.staging-" + id;
+  if (::mkdir(staging.c_str(), 0755) != 0) return io_fail(errno, staging);
+  if (int s = save_dir(ix, staging, true)) return s;
+  {  // search.rs:1018-1031: the staged snapshot must read back
+    SnapshotState st;
+    std::string text;
+    if (int s = read_file(staging + "/manifest.json", text)) return s;
+    if (text.find("\"generation_components\"") == std::string::npos)
+      return format_fail("IVF-PQ generation manifest is missing its component inventory");
+    if (int s = read_snapshot(staging, st)) return s;
+  }
+  const std::string lock_path = root + "/.PUBLISH.lock";
+  const int lock = ::open(lock_path.c_str(), O_WRONLY | O_CREAT, 0644);
+  if (lock < 0) return io_fail(errno, lock_path);
+  struct LockGuard {
+    int fd;
+    ~LockGuard() {
+      ::flock(fd, LOCK_UN);
+      ::close(fd);
+    }
+  };
+  if (::flock(lock, LOCK_EX | LOCK_NB) != 0) {
+    const int e = errno;
+    ::close(lock);
+    if (e == EWOULDBLOCK) return fail(VG_ERR_IO, "lock failed on " + lock_path + ": another generation publisher holds the advisory lock");
+    return io_fail(e, lock_path);
+  }
+  LockGuard guard{lock};
+  std::string now;
+  if (int s = read_current(root, now, none)) return s;
+  if (now != expected)
+    return fail(VG_ERR_IO, "lock failed on " + root + "/CURRENT: CURRENT changed while this generation was being built");
+  std::vector<GenFile> files;
+  if (int s = collect_files(staging, "", files)) return s;
+  std::sort(files.begin(), files.end(), [](const GenFile &a, const GenFile &b) { return a.path < b.path; });
+  if (int s = write_whole(staging + "/GENERATION.json", inventory_text(files))) return s;
+  if (int s = fsync_path(staging, true)) return s;
+  const std::string published = gens + "/" + id;
+  if (::rename(staging.c_str(), published.c_str()) != 0) return io_fail(errno, published);
+  if (int s = fsync_path(gens, true)) return s;
+  const std::string tmp = root + "/.CURRENT.tmp." + std::to_string(::getpid()) + "." +
+                          std::to_string(g_generation_sequence.fetch_add(1));
+  if (int s = write_whole(tmp, id + "\n")) {
+    ::unlink(tmp.c_str());
+    return s;
+  }
+  if (::rename(tmp.c_str(), (root + "/CURRENT").c_str()) != 0) {
+    const int e = errno;
+    ::unlink(tmp.c_str());
+    return io_fail(e, root + "/CURRENT");
+  }
+  return fsync_path(root, true);
+}
+
 }  // namespace
 
 namespace vg {
@@ -729,66 +1111,42 @@ extern "C" {
 
 int vg_ivfpq_save(const vg_index *ix, const char *dir) {
   if (!ix || !dir || !*dir) return fail(VG_ERR_INVALID_PARAMETER, "null index or directory");
-  SnapshotState st;
-  if (int s = vg::snapshot_export(ix, st)) return s;
-  std::string manifest;
-  if (!manifest_text(st, manifest)) return fail(VG_ERR_INVALID_PARAMETER, "non-finite value in the quantizer");
-  const std::string d(dir);
-  if (int s = make_dirs(d)) return s;
-  // list-contiguous codes for the file searcher (file_storage.rs:39-72)
-  const size_t M = st.params.num_codebooks;
-  std::vector<uint64_t> list_offsets(st.list_offsets.size());
-  std::vector<uint8_t> list_codes(st.list_ids.size() * M);
-  for (size_t i = 0; i < st.list_offsets.size(); ++i) list_offsets[i] = st.list_offsets[i] * M;
-  for (size_t p = 0; p < st.list_ids.size(); ++p)
-    std::memcpy(list_codes.data() + p * M, st.codes.data() + static_cast<size_t>(st.list_ids[p]) * M, M);
-  std::string clusters(kClusterMagic, 8);
-  const uint64_t L = st.bitmasks.size();
-  clusters.append(reinterpret_cast<const char *>(&L), 8);
-  for (size_t l = 0; l < L; ++l) {
-    const uint64_t len = st.list_offsets[l + 1] - st.list_offsets[l];
-    clusters.append(reinterpret_cast<const char *>(&st.bitmasks[l]), 8);
-    clusters.append(reinterpret_cast<const char *>(&len), 8);
-    clusters.append(reinterpret_cast<const char *>(st.list_ids.data() + st.list_offsets[l]), len * 4);
-  }
-  Writer w{d};
-  int s = w.put("manifest.json", manifest.data(), manifest.size());
-  if (!s) s = w.put("centroids.bin", st.centroids.data(), st.centroids.size() * 4);
-  if (!s) s = w.put("doc_ids.bin", st.doc_ids.data(), st.doc_ids.size() * 4);
-  if (!s) s = w.put("codes.bin", st.codes.data(), st.codes.size());
-  if (!s) s = w.put("list_offsets.bin", list_offsets.data(), list_offsets.size() * 8);
-  if (!s) s = w.put("list_codes.bin", list_codes.data(), list_codes.size());
-  if (!s) s = w.put("clusters.bin", clusters.data(), clusters.size());
-  if (!s && !st.vectors.empty()) s = w.put("raw_vectors.bin", st.vectors.data(), st.vectors.size() * 4);
-  if (s) return s;
-  const int fd = ::open(d.c_str(), O_RDONLY | O_DIRECTORY);
-  if (fd < 0) return io_fail(errno, d);
-  const int r = ::fsync(fd);
-  const int e = errno;
-  ::close(fd);
-  if (r != 0) return io_fail(e, d);
+  return save_dir(ix, std::string(dir), false);
+}
+
+int vg_ivfpq_save_generation(const vg_index *ix, const char *root) {
+  if (!ix || !root || !*root) return fail(VG_ERR_INVALID_PARAMETER, "null index or directory");
+  return save_generation(ix, std::string(root));
+}
+
+int vg_ivfpq_load_generation(const char *root, int device, vg_index **out) {
+  if (!root || !*root || !out) return fail(VG_ERR_INVALID_PARAMETER, "null directory or output");
+  *out = nullptr;
+  std::string dir;
+  if (int s = open_current(std::string(root), dir)) return s;
+  return vg_ivfpq_load(dir.c_str(), device, out);
+}
+
+int vg_generation_current(const char *root, char *out, size_t len) {
+  if (!root || !*root || !out || len == 0) return fail(VG_ERR_INVALID_PARAMETER, "null directory or output");
+  std::string dir;
+  if (int s = open_current(std::string(root), dir)) return s;
+  if (dir.size() + 1 > len) return fail(VG_ERR_INVALID_PARAMETER, "output buffer too small for the generation path");
+  std::memcpy(out, dir.c_str(), dir.size() + 1);
   return VG_OK;
+}
+
+int vg_verify_generation(const char *dir) {
+  if (!dir || !*dir) return fail(VG_ERR_INVALID_PARAMETER, "null directory");
+  return verify_generation_dir(std::string(dir));
 }
 
 int vg_ivfpq_load(const char *dir, int device, vg_index **out) {
   if (!dir || !*dir || !out) return fail(VG_ERR_INVALID_PARAMETER, "null directory or output");
   *out = nullptr;
-  const std::string d(dir);
   SnapshotState st;
-  std::string text;
-  if (int s = read_file(d + "/manifest.json", text)) return s;
-  if (int s = parse_manifest(text, st)) return s;
-  const bool raw = !st.vectors.empty();
-  const size_t n = st.num_vectors, dim = st.dim, M = st.params.num_codebooks;
-  if (int s = read_exact(d + "/doc_ids.bin", n, st.doc_ids)) return s;
-  if (int s = read_exact(d + "/centroids.bin", st.num_centroids * dim, st.centroids)) return s;
-  if (int s = read_exact(d + "/codes.bin", n * M, st.codes)) return s;
-  if (int s = read_clusters(d + "/clusters.bin", st.params.num_clusters, n, st)) return s;
-  if (raw) {
-    if (int s = read_exact(d + "/raw_vectors.bin", n * dim, st.vectors)) return s;
-  } else {
-    st.vectors.clear();
-  }
+  if (int s = read_snapshot(std::string(dir), st)) return s;
+  const size_t dim = st.dim;
   vg_index *ix = nullptr;
   if (int s = vg_ivfpq_create(dim, &st.params, device, &ix)) {
     if (s == VG_ERR_CUDA || s == VG_ERR_OUT_OF_MEMORY) return s;

@@ -131,6 +131,25 @@ class IVFPQIndex:
         lib = _lib.load()
         handle = C.c_void_p()
         _lib.check(lib.vg_ivfpq_load(os.fsencode(os.fspath(path)), device, C.byref(handle)))
+        return IVFPQIndex._adopt(lib, handle)
+
+    def save_generation(self, path) -> None:
+        """Save this index as one published generation below ``path``
+        (IVFPQIndex::save_to_generation): ``path/generations/<id>`` plus an
+        atomically replaced ``path/CURRENT``; earlier generations stay."""
+        _lib.check(self._lib.vg_ivfpq_save_generation(self._h, os.fsencode(os.fspath(path))))
+
+    @staticmethod
+    def load_generation(path, device: int = 0) -> "IVFPQIndex":
+        """Load the generation named by ``path/CURRENT``
+        (IVFPQIndex::load_from_generation)."""
+        lib = _lib.load()
+        handle = C.c_void_p()
+        _lib.check(lib.vg_ivfpq_load_generation(os.fsencode(os.fspath(path)), device, C.byref(handle)))
+        return IVFPQIndex._adopt(lib, handle)
+
+    @staticmethod
+    def _adopt(lib, handle) -> "IVFPQIndex":
         ix = IVFPQIndex.__new__(IVFPQIndex)
         ix._lib = lib
         ix._h = handle
@@ -484,3 +503,82 @@ def flat_search_ip(db, queries, k: int, device: int = 0):
     out = ids.astype(np.int64)
     out[np.arange(k)[None, :] >= counts.astype(np.int64)[:, None]] = MISSING_LABEL
     return out, dists
+
+
+def current_generation(root) -> str:
+    """The directory ``root/CURRENT`` names (persistence/generation.rs:191-205)."""
+    lib = _lib.load()
+    buf = C.create_string_buffer(4096)
+    _lib.check(lib.vg_generation_current(os.fsencode(os.fspath(root)), buf, len(buf)))
+    return os.fsdecode(buf.value)
+
+
+def verify_generation(path) -> None:
+    """Check every file of a generation against its GENERATION.json inventory
+    (persistence/generation.rs:285-365): RuntimeError on any mismatch."""
+    lib = _lib.load()
+    _lib.check(lib.vg_verify_generation(os.fsencode(os.fspath(path))))
+
+
+class IVFPQFileSearcher:
+    """Search-only handle over a snapshot (IVFPQFileSearcher, search.rs:1620-1860;
+    Python binding python.rs:857-1110).  The reference reads codes and raw
+    vectors from the snapshot files through a block cache; here the snapshot
+    is loaded into device memory once and searched there, with the same
+    results."""
+
+    def __init__(self, index: IVFPQIndex):
+        self._ix = index
+
+    @staticmethod
+    def load(path, mmap=None, device: int = 0) -> "IVFPQFileSearcher":
+        if mmap is not None:
+            import warnings
+
+            warnings.warn("IVFPQFileSearcher.load(mmap=...) is deprecated and ignored", DeprecationWarning,
+                          stacklevel=2)
+        return IVFPQFileSearcher(IVFPQIndex.load(path, device=device))
+
+    @staticmethod
+    def load_generation(path, device: int = 0) -> "IVFPQFileSearcher":
+        return IVFPQFileSearcher(IVFPQIndex.load_generation(path, device=device))
+
+    def set_nprobe(self, nprobe: int) -> None:
+        self._ix.set_nprobe(nprobe)
+
+    def search(self, query, k: int, nprobe=None, rerank_pool=None):
+        return self._ix.search(query, k, nprobe=nprobe, rerank_pool=rerank_pool)
+
+    def batch_search(self, queries, k: int, nprobe=None, rerank_pool=None):
+        return self._ix.batch_search(queries, k, nprobe=nprobe, rerank_pool=rerank_pool)
+
+    @property
+    def num_vectors(self) -> int:
+        return len(self._ix)
+
+    @property
+    def dimension(self) -> int:
+        return int(self._ix.info().dimension)
+
+    @property
+    def num_clusters(self) -> int:
+        return int(self._ix.info().num_centroids)
+
+    @property
+    def num_codebooks(self) -> int:
+        return self._ix.num_codebooks
+
+    @property
+    def codebook_size(self) -> int:
+        return self._ix.codebook_size
+
+    @property
+    def nprobe(self) -> int:
+        return self._ix.nprobe
+
+    def __len__(self) -> int:
+        return self.num_vectors
+
+    def __repr__(self) -> str:
+        return (f"IVFPQFileSearcher(dim={self.dimension}, n={self.num_vectors}, num_clusters={self.num_clusters}, "
+                f"num_codebooks={self.num_codebooks}, codebook_size={self.codebook_size}, nprobe={self.nprobe})")
