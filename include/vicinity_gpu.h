@@ -155,7 +155,9 @@ int vg_ivfpq_nearest_lists(vg_index *ix, const float *queries, size_t nq,
 
 /* src/ivf_pq/search.rs:1117-1158 (search_reranked) over nq rows: the
  * candidate_pool best approximate candidates re-scored by exact cosine
- * distance 1 - dot.  Unsupported after compact. */
+ * distance 1 - dot.  k at most 256; candidate_pool at most 2^20 (above 256
+ * it is selected in passes of 256 and needs an unsharded index).
+ * Unsupported after compact. */
 int vg_ivfpq_search_batch_reranked(vg_index *ix, const float *queries,
                                    size_t nq, size_t k, size_t candidate_pool,
                                    size_t nprobe, uint32_t *out_ids,

@@ -101,6 +101,16 @@ def test_rerank_matches_oracle():
         assert_same_results(ix, ref, q, 10, 8, rerank=pool)
 
 
+@pytest.mark.parametrize("ks", [256, 16])
+def test_rerank_pool_above_256_matches_oracle(ks):
+    # pools above 256 are selected in passes of 256 keys; the last pass is
+    # partial, and pools larger than the probed candidates exhaust them
+    x, q = mixture(8000, 32, 30, 0.3, seed=19, nq=40)
+    ix, ref = build_pair(x, 32, 32, 8, ks)
+    for k, nprobe, pool in [(10, 8, 257), (10, 8, 300), (10, 8, 700), (200, 8, 1000), (20, 32, 5000)]:
+        assert_same_results(ix, ref, q, k, nprobe, rerank=pool)
+
+
 def test_adc_odd_sizes_exact(kats):
     # pq_simd.rs:1108-1132 on the device: list sizes 0..257 must give the
     # reference's sequential sums exactly, including the tail of each list.

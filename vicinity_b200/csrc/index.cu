@@ -205,7 +205,7 @@ struct vg_index {
 
   // search workspace
   DevBuf ws_q, ws_qn, ws_dist, ws_probes, ws_pdist, ws_scalars,
-      ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_lb, ws_rec, ws_lbq, ws_qh;
+      ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_lb, ws_rec, ws_lbq, ws_qh, ws_floor;
   DevBuf stats;  // u64 [pairs, vectors, code bytes, scored lists, scored vectors] while profiling
 
   // error flag of bounded device waits, in mapped pinned host memory
@@ -752,7 +752,10 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
     return fail(VG_ERR_UNSUPPORTED,
                 "unsupported: search_reranked after compact(); use search() instead, or keep raw vectors");
   const size_t kk = rerank ? std::max(pool, k) : k;
-  if (kk > 256) return fail(VG_ERR_INVALID_PARAMETER, "candidate_pool must be at most 256");
+  // pools above 256 are selected in passes of 256 on one device
+  if (kk > 256 && ix->world > 1)
+    return fail(VG_ERR_UNSUPPORTED, "unsupported: candidate_pool above 256 on a sharded index");
+  if (kk > (size_t{1} << 20)) return fail(VG_ERR_INVALID_PARAMETER, "candidate_pool must be at most 1048576");
   if (nq == 0 || k == 0) return write_padding(ix, nq, k, out_ids, out_dist, out_count);
   if ((nq && !queries) || !out_ids || !out_dist)
     return fail(VG_ERR_INVALID_PARAMETER, "null query or output buffer");
@@ -861,8 +864,31 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
     sp.out_keys = ix->ws_keys.as<unsigned long long>();
   }
   *reinterpret_cast<volatile int *>(ix->h_err) = 0;
-  VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
-  ix->launches += 1;
+  if (kk <= 256) {
+    VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
+    ix->launches += 1;
+  } else {
+    // the approximate top-pool in passes of 256: pass i keeps the keys above
+    // pass i-1's last one, so the passes concatenate into the sorted top-pool
+    constexpr size_t kPass = 256;
+    VG_CU(ix->ws_all_keys.reserve(nq * kPass * 8));
+    VG_CU(ix->ws_floor.reserve(nq * 8));
+    unsigned long long *pass_keys = ix->ws_all_keys.as<unsigned long long>();
+    unsigned long long *floor = ix->ws_floor.as<unsigned long long>();
+    sp.k = static_cast<int>(kPass);
+    sp.out_keys = pass_keys;
+    for (size_t c0 = 0; c0 < kk; c0 += kPass) {
+      const size_t w = std::min(kPass, kk - c0);
+      if (c0) VG_CU(cudaMemsetAsync(d_counter, 0, 4, s));
+      sp.key_floor = c0 ? floor : nullptr;
+      VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
+      ix->launches += 1;
+      VG_CU(cudaMemcpy2DAsync(ix->ws_keys.as<unsigned long long>() + c0, kk * 8, pass_keys, kPass * 8, w * 8, nq,
+                              cudaMemcpyDeviceToDevice, s));
+      if (c0 + kPass < kk)
+        VG_CU(cudaMemcpy2DAsync(floor, 8, pass_keys + kPass - 1, kPass * 8, 8, nq, cudaMemcpyDeviceToDevice, s));
+    }
+  }
   mark(ix, 6);
 
   if (!direct && ix->world == 1) {  // rerank on one device

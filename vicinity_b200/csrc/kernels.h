@@ -217,6 +217,10 @@ struct ScanParams {
   const ProbeRec *probe_rec;     // [nq][P] probe records (streaming 8-bit kernel; nullable)
   const float *probe_lbq;        // [nq][P] bound on quantised 4-bit distances before the table (nullable)
   unsigned long long *scored;    // [2]: lists and vectors scored after pruning (nullable; warp-per-query kernels)
+  // [nq] keys already selected by an earlier pass: only keys above a query's
+  // floor compete (nullable; query-major and 4-bit block kernels, which serve
+  // k up to 256: top-k beyond 256 in passes)
+  const unsigned long long *key_floor;
 };
 
 // Fused per-query kernel: for each probed list the query residual, the ADC

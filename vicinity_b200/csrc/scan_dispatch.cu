@@ -62,6 +62,11 @@ int pick_gpt(const ScanParams &p) {
 
 cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms, cudaStream_t s) {
   if (p.k < 1 || p.k > 256) return cudaErrorInvalidValue;
+  if (p.key_floor) {  // a key floor is applied by the query-major and 4-bit block kernels only
+    const int gpt = pick_gpt(p);
+    if (p.ks == 16) return launch_scan_four(p, gpt ? p.dsub : 0, gpt, num_sms, s);
+    return launch_scan_eight(p, gpt ? p.dsub : 0, gpt, num_sms, s);
+  }
   // an OPQ rotation is applied by the query-major and 4-bit kernels only
   const int ws = p.rot_t ? 0 : pick_ws_ept(p);
   if (ws) return launch_scan_ws(p, p.dsub, ws, num_sms, s);
@@ -85,17 +90,17 @@ cudaError_t launch_ivfpq_scan_generic(const ScanParams &p, int num_sms, cudaStre
 }
 
 int ivfpq_scan_variant_name(const ScanParams &p, int num_sms, char *buf, size_t len) {
-  const int ws = p.rot_t ? 0 : pick_ws_ept(p);
+  const int ws = p.rot_t || p.key_floor ? 0 : pick_ws_ept(p);
   if (ws) return snprintf(buf, len, "ivfpq_ws_kernel<%d,%d,1,256>", p.dsub, ws);
-  if (g_family >= 4 && use_direct(p, num_sms))
+  if (g_family >= 4 && !p.key_floor && use_direct(p, num_sms))
     return snprintf(buf, len, "ivfpq_direct_kernel<%d,%d>", p.dsub, p.k <= 32 ? 1 : 2);
   const int gpt = pick_gpt(p);
-  if (g_family >= 2 && gpt && p.ks == 256 && !p.rot_t) {
+  if (g_family >= 2 && gpt && p.ks == 256 && !p.rot_t && !p.key_floor) {
     if (g_family >= 3 && p.probe_rec && p.P <= 256)
       return snprintf(buf, len, "ivfpq_stream_kernel<%d,%d,1,256>", p.dsub, gpt);
     return snprintf(buf, len, "ivfpq_pipe_kernel<%d,%d,1,256>", p.dsub, gpt);
   }
-  if (use_four_warp(p, num_sms)) return snprintf(buf, len, "ivfpq_four_warp_kernel<%d>", p.k <= 32 ? 1 : 2);
+  if (!p.key_floor && use_four_warp(p, num_sms)) return snprintf(buf, len, "ivfpq_four_warp_kernel<%d>", p.k <= 32 ? 1 : 2);
   if (p.ks == 16) return snprintf(buf, len, "ivfpq_four_kernel<%d>", p.k <= 32 ? 1 : p.k <= 64 ? 2 : p.k <= 128 ? 4 : 8);
   return snprintf(buf, len, "ivfpq_query_kernel<%d,%d,%d,%s>", gpt ? p.dsub : 0, gpt,
                   p.k <= 32 ? 1 : p.k <= 64 ? 2 : p.k <= 128 ? 4 : 8, p.ks == 16 ? "4bit" : "8bit");

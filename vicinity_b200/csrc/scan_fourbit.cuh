@@ -335,7 +335,8 @@ __global__ void __launch_bounds__(kScanThreads, 2) ivfpq_four_kernel(const ScanP
         const bool pass = alive && dk <= tkey;
         unsigned mask = __ballot_sync(VG_FULL_MASK, pass);
         if (!mask) continue;
-        const uint64_t key = pass ? ((static_cast<uint64_t>(dk) << 32) | p.list_ids[s_lbeg[bat[g]] + c]) : kEmptyKey;
+        uint64_t key = pass ? ((static_cast<uint64_t>(dk) << 32) | p.list_ids[s_lbeg[bat[g]] + c]) : kEmptyKey;
+        if (p.key_floor && key <= p.key_floor[q]) key = kEmptyKey;  // selected by an earlier pass
         if (__popc(mask) > 4) {
           tk.add(key < thr ? key : kEmptyKey);
         } else {

@@ -360,8 +360,9 @@ __global__ void __launch_bounds__(kScanThreads, 1) ivfpq_query_kernel(const Scan
         const bool pass = live && dk <= tkey;
         unsigned mask = __ballot_sync(VG_FULL_MASK, pass);
         if (!mask) continue;
-        const uint64_t key =
+        uint64_t key =
             pass ? ((static_cast<uint64_t>(dk) << 32) | (p.category ? vid : p.list_ids[s_lbeg[b0 + g] + c])) : kEmptyKey;
+        if (p.key_floor && key <= p.key_floor[q]) key = kEmptyKey;  // selected by an earlier pass
         if (__popc(mask) > 4) {
           tk.add(key < thr ? key : kEmptyKey);
         } else {
