@@ -49,7 +49,8 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--config", type=int, default=1)
     p.add_argument("--impl", choices=["engine", "reference"], default="engine")
-    p.add_argument("--train-sample", type=int, default=131_072)
+    p.add_argument("--train-sample", type=int, default=None,
+                   help="k-means training rows (default: max(131072, 8 x nlist), at most n)")
     p.add_argument("--train-iters", type=int, default=20)
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -198,20 +199,33 @@ def run_engine(args):
 
     cfg = CONFIGS[args.config]
     if cfg["centre"] == "flat":
-        raise SystemExit("config 2 is the flat path; the IVF-PQ bench runs configs 0, 1, 3")
+        raise SystemExit("config 2 is the flat path; the IVF-PQ bench runs configs 0, 1, 3, 4")
     n, d, k = args.n or cfg["n"], cfg["d"], cfg["k"]
     nq = args.nq or cfg["nq"]
+    train_sample = min(args.train_sample or max(131_072, 8 * cfg["nlist"]), n)
+    on_device = cfg.get("generated") == "device"
     t0 = time.time()
     by_lists = world > 1 and args.shard == "lists"
-    # per-rank batches: rows [rank*nq, (rank+1)*nq) of the configuration's query
-    # stream (rank 0's batch is the single-GPU batch)
-    x, q = config_data(args.config, seed=0, n=n, nq=nq * (1 if by_lists else world))
-    if not by_lists:
-        q = np.ascontiguousarray(q[rank * nq:(rank + 1) * nq])
     ix = IVFPQIndex(d, num_clusters=cfg["nlist"], num_codebooks=cfg["M"], codebook_size=cfg["ks"],
                     nprobe=cfg["nprobe"], seed=42, device=local)
-    ix.add_items(x)
-    ix.build(training_sample_size=min(args.train_sample, n), kmeans_max_iter=args.train_iters)
+    # per-rank batches: rows [rank*nq, (rank+1)*nq) of the configuration's query
+    # stream (rank 0's batch is the single-GPU batch)
+    if on_device:  # the database is drawn on the GPU chunk by chunk and never held on the host
+        from vicinity_b200.synthetic import device_mixture
+
+        x = None
+        _, chunks, q = device_mixture(args.config, seed=0, device=local, n=n, nq=nq * (1 if by_lists else world))
+        for xc in chunks:
+            torch.cuda.synchronize()  # the chunk is complete before the engine's stream reads it
+            ix.add_device(xc.data_ptr(), xc.shape[0])
+            del xc
+        torch.cuda.empty_cache()
+    else:
+        x, q = config_data(args.config, seed=0, n=n, nq=nq * (1 if by_lists else world))
+        ix.add_items(x)
+    if not by_lists:
+        q = np.ascontiguousarray(q[rank * nq:(rank + 1) * nq])
+    ix.build(training_sample_size=train_sample, kmeans_max_iter=args.train_iters)
     build_s = time.time() - t0
     if by_lists:
         obj = [nccl_unique_id() if rank == 0 else None]
@@ -294,19 +308,22 @@ def run_engine(args):
     e2e_value = queries_total * args.steps / (e2e_ms / 1e3)
 
     # recall@10 against the exact top-10 of the normalised data (flat engine search)
+    # (a 1,000-query subset for a device-generated database)
     recall = None
+    rq = nq if not on_device else min(nq, 1000)
     if rank == 0:
         import ctypes as C
 
         vec_d = torch.empty((n, d), dtype=torch.float32, device="cuda")
         _lib.check(ix._lib.vg_ivfpq_export(ix.handle, _lib.EXPORT_VECTORS, vec_d.data_ptr(), vec_d.numel() * 4))
-        qn = q / np.maximum(np.linalg.norm(q, axis=1, keepdims=True), 1e-30)
+        qr = q[:rq]
+        qn = qr / np.maximum(np.linalg.norm(qr, axis=1, keepdims=True), 1e-30)
         qn_d = torch.from_numpy(qn.astype(np.float32)).cuda()
-        gt = torch.empty((nq, k), dtype=torch.int32, device="cuda")
-        gd = torch.empty((nq, k), dtype=torch.float32, device="cuda")
-        _lib.check(ix._lib.vg_flat_search_ip(vec_d.data_ptr(), n, qn_d.data_ptr(), nq, d, k, local,
+        gt = torch.empty((rq, k), dtype=torch.int32, device="cuda")
+        gd = torch.empty((rq, k), dtype=torch.float32, device="cuda")
+        _lib.check(ix._lib.vg_flat_search_ip(vec_d.data_ptr(), n, qn_d.data_ptr(), rq, d, k, local,
                                              gt.data_ptr(), gd.data_ptr(), C.c_void_p(0)))
-        got = ids_h.numpy().astype(np.int64)
+        got = ids_h.numpy()[:rq].astype(np.int64)
         truth = gt.cpu().numpy().astype(np.int64)
         recall = float(np.mean([len(set(a) & set(b)) / k for a, b in zip(got.tolist(), truth.tolist())]))
         del vec_d
@@ -327,7 +344,7 @@ def run_engine(args):
     traffic = scan_traffic_from_profiles(args.config)
 
     cpu_baseline = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and x is not None:
         cpu_baseline = cpu_baseline_port(ix, x, q, cfg, args.cpu_seconds)
 
     if rank == 0:
@@ -343,12 +360,14 @@ def run_engine(args):
             "scaling": "strong" if by_lists or world == 1 else "weak",
             "vs_baseline": None,
             "dtype": "f32",
-            "data": "synthetic: seeded Gaussian mixture with the configuration's generator (no dataset)",
+            "data": ("synthetic: seeded Gaussian mixture drawn on the GPU chunk by chunk (torch generator), "
+                     "never held on the host" if on_device else
+                     "synthetic: seeded Gaussian mixture with the configuration's generator (no dataset)"),
             "config": {
                 "workload": cfg["name"], "n": n, "d": d, "nlist": cfg["nlist"], "M": cfg["M"],
                 "codebook_size": cfg["ks"], "nprobe": cfg["nprobe"], "k": k, "batch": nq,
-                "recall_at_10": None if recall is None else round(recall, 4),
-                "train_sample": min(args.train_sample, n), "train_iters": args.train_iters,
+                "recall_at_10": None if recall is None else round(recall, 4), "recall_queries": rq,
+                "train_sample": train_sample, "train_iters": args.train_iters,
                 "l2": "flushed between timed steps (512 MiB write, then 512 MiB read of another buffer; index codes fit in L2)",
                 "parallelism": ("single GPU" if world == 1 else f"list-sharded x{world}" if by_lists
                                 else f"index replica per GPU, {nq} queries per rank x{world}"),
@@ -376,6 +395,9 @@ def run_engine(args):
             "clocks": clock_info,
             "cpu_baseline": cpu_baseline,
         }
+        if on_device and cpu_baseline is None:
+            line["cpu_baseline_note"] = ("not run: the CPU port would need the whole database on the host "
+                                         f"({n * d * 4 / 1e9:.0f} GB f32) and a CPU encode of it")
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -500,11 +522,16 @@ def run_reference(args):
     from vicinity_b200.synthetic import CONFIGS, config_data
 
     cfg = dict(CONFIGS[args.config])
+    if cfg.get("generated") == "device":
+        print(json.dumps({"impl": "reference", "unavailable": (
+            f"configuration {args.config} is generated on the GPU and never held on the host; the CPU "
+            f"reference would need a {cfg['n'] * cfg['d'] * 4 / 1e9:.0f} GB f32 host corpus")}), flush=True)
+        return
     if args.nq:
         cfg["nq"] = args.nq
     threads = host_threads()
     x, q = config_data(args.config, seed=0, nq=cfg["nq"])
-    cent, cb, assign, codes = numpy_train_and_encode(x, cfg, min(args.train_sample, 65_536), 8)
+    cent, cb, assign, codes = numpy_train_and_encode(x, cfg, min(args.train_sample or 65_536, 65_536), 8)
     ref = orc.OracleIndex(cfg["d"], cfg["nlist"], cfg["M"], cfg["ks"], cfg["nprobe"])
     ref.set_trained(cent, cb)
     ref.add(np.arange(x.shape[0], dtype=np.uint32), x)

@@ -278,3 +278,28 @@ def test_direct_kernel_matches_oracle_on_every_shape():
          "-m", "gpu"],
         cwd=root, env=env, capture_output=True, text=True, timeout=900)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-2000:]
+
+
+def test_add_device_builds_the_same_index_as_add_items():
+    # rows already in device memory (a CUDA tensor) added in two calls give
+    # the index add_items builds from the same rows on the host
+    import torch
+
+    x, q = mixture(6000, 32, 30, 0.3, seed=5, nq=64)
+    a = IVFPQIndex(32, num_clusters=32, num_codebooks=8, nprobe=8, seed=7)
+    a.add_items(x)
+    a.build(kmeans_max_iter=6)
+    b = IVFPQIndex(32, num_clusters=32, num_codebooks=8, nprobe=8, seed=7)
+    xd = torch.from_numpy(x).cuda()
+    torch.cuda.synchronize()
+    b.add_device(xd[:2500].data_ptr(), 2500)
+    b.add_device(xd[2500:].data_ptr(), 3500)
+    assert len(b) == 6000
+    with pytest.raises(ValueError, match="duplicate"):
+        b.add_items(x[:1], [17])
+    b.build(kmeans_max_iter=6)
+    assert np.array_equal(a.doc_ids(), b.doc_ids())
+    assert np.array_equal(a.codes(), b.codes())
+    ia, da = a.batch_search(q, 10)
+    ib, db = b.batch_search(q, 10)
+    assert np.array_equal(ia, ib) and np.array_equal(da.view(np.uint32), db.view(np.uint32))

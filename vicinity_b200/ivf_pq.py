@@ -91,6 +91,7 @@ class IVFPQIndex:
         _lib.check(self._lib.vg_ivfpq_create(dim, C.byref(params), device, C.byref(handle)))
         self._h = handle
         self._used_ids: set[int] = set()
+        self._id_ranges: list[tuple[int, int]] = []  # ids given by add_device, [lo, hi)
         self._dim = dim
         if filter_field is not None:  # IVFPQIndex::with_filtering (search.rs:414-434)
             _lib.check(self._lib.vg_ivfpq_set_filter_field(self._h, str(filter_field).encode()))
@@ -154,6 +155,7 @@ class IVFPQIndex:
         ix._lib = lib
         ix._h = handle
         ix._used_ids = set()
+        ix._id_ranges = []
         ix._dim = int(ix.info().dimension)
         return ix
 
@@ -192,7 +194,7 @@ class IVFPQIndex:
                     raise ValueError(
                         f"ids[{i}] = {v} out of range [0, 2**32); pyvicinity stores IDs as u32 internally"
                     )
-                if v in self._used_ids or v in batch:
+                if v in self._used_ids or v in batch or any(lo <= v < hi for lo, hi in self._id_ranges):
                     raise ValueError(f"duplicate doc_id {v} (IDs must be unique within an index)")
                 batch.add(v)
             id_u32 = ids.astype(np.uint32)
@@ -200,6 +202,22 @@ class IVFPQIndex:
             return
         _lib.check(self._lib.vg_ivfpq_add(self._h, _ptr(id_u32), _ptr(x), n))
         self._used_ids.update(id_u32.tolist())
+
+    def add_device(self, x_ptr: int, n: int) -> None:
+        """Add n rows [n][dim] f32 at address x_ptr (device or host memory)
+        with the implicit sequential ids len(self) .. len(self) + n - 1, as
+        add_items assigns them.  Rows generated on the GPU stay there: nothing
+        passes through host memory but the ids."""
+        base = len(self)
+        if n <= 0:
+            return
+        if base + n - 1 > 0xFFFFFFFF:
+            raise ValueError("implicit IDs exceed the u32 ID limit")
+        if any(base <= u < base + n for u in self._used_ids):
+            raise ValueError("implicit IDs collide with explicit ones; use add_items")
+        ids = np.arange(base, base + n, dtype=np.uint32)
+        _lib.check(self._lib.vg_ivfpq_add(self._h, _ptr(ids), x_ptr, n))
+        self._id_ranges.append((base, base + n))
 
     def set_trained(self, centroids, codebooks, rotation=None) -> None:
         """Adopt coarse centroids [nc][dim] and PQ codebooks [M][ks][dsub]

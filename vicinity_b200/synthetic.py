@@ -18,7 +18,7 @@ CONFIGS = {
     3: dict(name="c3_ivfpq4_n1e7_d96", n=10_000_000, d=96, nlist=16_384, M=48, ks=16, nprobe=64, k=10, nq=10_000,
             centres=10_000, centre="normal", sigma=0.15, integer=False),
     4: dict(name="c4_ivfpq_n1e8_d96", n=100_000_000, d=96, nlist=65_536, M=16, ks=256, nprobe=128, k=10,
-            nq=100_000, centres=100_000, centre="normal", sigma=0.15, integer=False),
+            nq=100_000, centres=100_000, centre="normal", sigma=0.15, integer=False, generated="device"),
 }
 
 
@@ -91,3 +91,43 @@ def recall_at_k(found: np.ndarray, truth: np.ndarray) -> float:
     for f, t in zip(found, truth):
         hits += len(set(f[:k].tolist()) & set(t.tolist()))
     return hits / float(truth.size)
+
+
+def device_mixture(cfg: int, seed: int, device: int, n: int | None = None, nq: int | None = None,
+                   chunk: int = 1 << 22):
+    """The configuration's Gaussian mixture drawn on the GPU (configuration 4:
+    1e8 rows are generated on the device and never held on the host).
+
+    Returns (centres, chunks, queries): ``chunks`` yields [rows, d] float32
+    CUDA tensors of the database in order; ``queries`` is a host array from
+    an independent stream of the same mixture.  Every chunk is a pure function
+    of (seed, chunk index), so each rank of a multi-GPU job regenerates the
+    identical database.
+    """
+    import torch
+
+    c = CONFIGS[cfg]
+    d, centres, sigma = c["d"], c["centres"], c["sigma"]
+    n = c["n"] if n is None else n
+    nq = c["nq"] if nq is None else nq
+    dev = torch.device("cuda", device)
+
+    def gen(stream: int) -> "torch.Generator":
+        g = torch.Generator(device=dev)
+        g.manual_seed((seed * 1_000_003 + stream) & 0x7FFF_FFFF_FFFF_FFFF)
+        return g
+
+    cen = torch.randn((centres, d), generator=gen(0), device=dev, dtype=torch.float32)
+
+    def draw(count: int, g: "torch.Generator") -> "torch.Tensor":
+        lab = torch.randint(0, centres, (count,), generator=g, device=dev)
+        out = torch.randn((count, d), generator=g, device=dev, dtype=torch.float32)
+        out.mul_(sigma).add_(cen.index_select(0, lab))
+        return out
+
+    def chunks():
+        for i, s in enumerate(range(0, n, chunk)):
+            yield draw(min(chunk, n - s), gen(1000 + i))
+
+    queries = draw(nq, gen(1)).cpu().numpy()
+    return cen, chunks(), queries
