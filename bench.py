@@ -50,7 +50,7 @@ def parse_args():
     p.add_argument("--config", type=int, default=1)
     p.add_argument("--impl", choices=["engine", "reference"], default="engine")
     p.add_argument("--train-sample", type=int, default=None,
-                   help="k-means training rows (default: max(131072, 8 x nlist), at most n)")
+                   help="k-means training rows (default: the configuration's, else 131072; at most n)")
     p.add_argument("--train-iters", type=int, default=20)
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -202,7 +202,7 @@ def run_engine(args):
         raise SystemExit("config 2 is the flat path; the IVF-PQ bench runs configs 0, 1, 3, 4")
     n, d, k = args.n or cfg["n"], cfg["d"], cfg["k"]
     nq = args.nq or cfg["nq"]
-    train_sample = min(args.train_sample or max(131_072, 8 * cfg["nlist"]), n)
+    train_sample = min(args.train_sample or cfg.get("train_sample", 131_072), n)
     on_device = cfg.get("generated") == "device"
     t0 = time.time()
     by_lists = world > 1 and args.shard == "lists"

@@ -214,6 +214,10 @@ struct vg_index {
   // profiling
   bool profiling = false;
   cudaEvent_t ev[kPhaseEvents] = {};
+  // per-tile (start, coarse done, select done) events of a tiled coarse stage,
+  // read after the call's final synchronisation; tile_marks redirects marks 2-4
+  std::vector<cudaEvent_t> tile_ev;
+  cudaEvent_t *tile_marks = nullptr;
   vg_search_profile prof{};
   uint64_t launches = 0;
 
@@ -286,7 +290,18 @@ int nccl_wait_ready(ncclComm_t comm, int timeout_ms) {
 }
 
 void mark(vg_index *ix, int i) {
-  if (ix->profiling) cudaEventRecord(ix->ev[i], ix->stream);
+  if (!ix->profiling) return;
+  cudaEventRecord(ix->tile_marks && i >= 2 && i <= 4 ? ix->tile_marks[i - 2] : ix->ev[i], ix->stream);
+}
+
+cudaError_t reserve_tile_events(vg_index *ix, size_t count) {
+  while (ix->tile_ev.size() < count) {
+    cudaEvent_t e = nullptr;
+    cudaError_t err = cudaEventCreate(&e);
+    if (err != cudaSuccess) return err;
+    ix->tile_ev.push_back(e);
+  }
+  return cudaSuccess;
 }
 
 // ---- training (device Lloyd iterations; not bit-pinned to the reference's
@@ -747,6 +762,7 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
                 uint32_t *out_ids, float *out_dist, uint32_t *out_count) {
   if (!ix->built) return fail(VG_ERR_NOT_BUILT, "IVF-PQ index is not built: cannot search");
   if (k > 256) return fail(VG_ERR_INVALID_PARAMETER, "k must be at most 256");
+  ix->tile_marks = nullptr;  // a call that failed mid-stage may have left it set
   const bool rerank = pool > 0;
   if (rerank && ix->compacted)
     return fail(VG_ERR_UNSUPPORTED,
@@ -798,25 +814,25 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   }
   auto bound_args = [&](size_t r0) { return bound_args_at(ix, P, r0, prune, recs, quant); };
   bool bounds_done = prune;
-  double coarse_ms = 0, select_ms = 0;
-  for (size_t r0 = 0; r0 < nq; r0 += tile) {
+  // a profiled tiled stage times each tile on its own events (no host wait between tiles)
+  const size_t ntiles = (nq + tile - 1) / tile;
+  const bool tiled_prof = prof && ntiles > 1;
+  if (tiled_prof) VG_CU(reserve_tile_events(ix, 3 * ntiles));
+  for (size_t r0 = 0, t = 0; r0 < nq; r0 += tile, ++t) {
     size_t rows = std::min(tile, nq - r0);
     const ProbeBoundArgs ba = bound_args(r0);
     bool tile_done = false;
+    if (tiled_prof) {
+      ix->tile_marks = ix->tile_ev.data() + 3 * t;
+      mark(ix, 2);
+    }
     VG_TRY(coarse_probes(ix, ix->ws_qn.as<float>() + r0 * d, rows, P, ix->ws_probes.as<uint32_t>() + r0 * P,
                          ix->ws_pdist.as<float>() + r0 * P, &ix->launches, prune ? &ba : nullptr, &tile_done));
     bounds_done = bounds_done && tile_done;
     mark(ix, 4);
-    if (prof && r0 + tile < nq) {  // accumulate per tile when tiled
-      float a = 0, b = 0;
-      VG_CU(cudaEventSynchronize(ix->ev[4]));
-      cudaEventElapsedTime(&a, ix->ev[2], ix->ev[3]);
-      cudaEventElapsedTime(&b, ix->ev[3], ix->ev[4]);
-      coarse_ms += a;
-      select_ms += b;
-      mark(ix, 2);
-    }
   }
+  ix->tile_marks = nullptr;
+  if (tiled_prof) mark(ix, 4);
 
   // per-query fused scan: probes -> (residual, table, scan, top-k) on chip
   VG_CU(ix->ws_scalars.reserve(64));
@@ -939,8 +955,18 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
     vg_search_profile &p = ix->prof;
     p.h2d_ms += el(0, 1);
     p.normalize_ms += el(1, 2);
-    p.coarse_ms += coarse_ms + el(2, 3);
-    p.select_ms += select_ms + el(3, 4);
+    if (tiled_prof) {
+      for (size_t t = 0; t < ntiles; ++t) {
+        float a = 0, b = 0;
+        cudaEventElapsedTime(&a, ix->tile_ev[3 * t], ix->tile_ev[3 * t + 1]);
+        cudaEventElapsedTime(&b, ix->tile_ev[3 * t + 1], ix->tile_ev[3 * t + 2]);
+        p.coarse_ms += a;
+        p.select_ms += b;
+      }
+    } else {
+      p.coarse_ms += el(2, 3);
+      p.select_ms += el(3, 4);
+    }
     p.pairs_ms += el(4, 5);
     p.scan_ms += el(5, 6);
     if (ix->world > 1) {
@@ -1331,10 +1357,11 @@ int vg_ivfpq_destroy(vg_index *ix) {
                       &ix->list_off, &ix->list_ids, &ix->code_off, &ix->list_codes, &ix->pack_off, &ix->packed,
                       &ix->owner, &ix->ws_q, &ix->ws_qn, &ix->ws_dist, &ix->ws_probes, &ix->ws_pdist,
                       &ix->ws_scalars, &ix->ws_keys, &ix->ws_all_keys, &ix->ws_out_ids, &ix->ws_out_dist,
-                      &ix->ws_out_count, &ix->stats, &ix->ws_lb, &ix->ws_rec, &ix->ws_lbq, &ix->ws_qh})
+                      &ix->ws_out_count, &ix->stats, &ix->ws_lb, &ix->ws_rec, &ix->ws_lbq, &ix->ws_qh, &ix->ws_floor})
       b->release();
     for (int i = 0; i < kPhaseEvents; ++i)
       if (ix->ev[i]) cudaEventDestroy(ix->ev[i]);
+    for (cudaEvent_t e : ix->tile_ev) cudaEventDestroy(e);
     if (ix->h_err) cudaFreeHost(ix->h_err);
     if (ix->blas) cublasDestroy(ix->blas);
     if (ix->own_stream) cudaStreamDestroy(ix->own_stream);

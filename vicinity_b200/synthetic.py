@@ -18,7 +18,8 @@ CONFIGS = {
     3: dict(name="c3_ivfpq4_n1e7_d96", n=10_000_000, d=96, nlist=16_384, M=48, ks=16, nprobe=64, k=10, nq=10_000,
             centres=10_000, centre="normal", sigma=0.15, integer=False),
     4: dict(name="c4_ivfpq_n1e8_d96", n=100_000_000, d=96, nlist=65_536, M=16, ks=256, nprobe=128, k=10,
-            nq=100_000, centres=100_000, centre="normal", sigma=0.15, integer=False, generated="device"),
+            nq=100_000, centres=100_000, centre="normal", sigma=0.15, integer=False, generated="device",
+            train_sample=2_097_152),
 }
 
 
