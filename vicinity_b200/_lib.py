@@ -120,6 +120,7 @@ SIGNATURES = {
     "vg_ivfpq_build": (_i, [_vp, _sz, _sz]),
     "vg_ivfpq_set_nprobe": (_i, [_vp, _sz]),
     "vg_ivfpq_set_stream": (_i, [_vp, _vp]),
+    "vg_ivfpq_set_coarse_tile_rows": (_i, [_vp, _sz]),
     "vg_ivfpq_get_info": (_i, [_vp, C.POINTER(VgInfo)]),
     "vg_ivfpq_search_batch": (_i, [_vp, _vp, _sz, _sz, _sz, _vp, _vp, _vp]),
     "vg_ivfpq_search_batch_reranked": (_i, [_vp, _vp, _sz, _sz, _sz, _sz, _vp, _vp, _vp]),

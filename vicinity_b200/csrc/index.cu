@@ -214,6 +214,7 @@ struct vg_index {
   // profiling
   bool profiling = false;
   cudaEvent_t ev[kPhaseEvents] = {};
+  size_t coarse_tile_rows = 0;  // query rows per coarse-product tile (0: from kDistBudgetBytes)
   // per-tile (start, coarse done, select done) events of a tiled coarse stage,
   // read after the call's final synchronisation; tile_marks redirects marks 2-4
   std::vector<cudaEvent_t> tile_ev;
@@ -797,7 +798,8 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   mark(ix, 2);
 
   // coarse distances + top-nprobe, tiled over queries
-  const size_t tile = std::max<size_t>(1, std::min(nq, kDistBudgetBytes / (Lc * 4)));
+  size_t tile = std::max<size_t>(1, std::min(nq, kDistBudgetBytes / (Lc * 4)));
+  if (ix->coarse_tile_rows) tile = std::min(tile, ix->coarse_tile_rows);
   VG_CU(ix->ws_dist.reserve(tile * Lc * 4));
   VG_CU(ix->ws_probes.reserve(nq * P * 4));
   VG_CU(ix->ws_pdist.reserve(nq * P * 4));
@@ -1511,6 +1513,12 @@ int vg_ivfpq_set_stream(vg_index *ix, void *stream) {
   DeviceGuard g(ix->device);
   VG_CU(cudaStreamSynchronize(ix->stream));
   ix->stream = stream ? static_cast<cudaStream_t>(stream) : ix->own_stream;
+  return VG_OK;
+}
+
+int vg_ivfpq_set_coarse_tile_rows(vg_index *ix, size_t rows) {
+  if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
+  ix->coarse_tile_rows = rows;
   return VG_OK;
 }
 

@@ -474,20 +474,34 @@ __device__ __forceinline__ void for_each_quad(const TS *__restrict__ srow, size_
 
 // Visit a half row of L % 4 == 0 columns, 8-byte aligned, as raw quads: fn(col,
 // lo, hi, valid) with lo / hi the half2 pairs (col, col + 1) and (col + 2, col + 3).
-// Trip counts are warp-uniform.
+// Trip counts are warp-uniform.  Blocks of 128 quads are software-pipelined:
+// the next block's loads are in flight while fn runs over the current one.
 template <bool kLast, typename F>
 __device__ __forceinline__ void for_each_half_quad(const __half *__restrict__ srow, size_t L, int lane, F &&fn) {
   const uint2 *r4 = reinterpret_cast<const uint2 *>(srow);
   const size_t n4 = L >> 2;
+  auto load = [&](size_t i) { return kLast ? __ldcs(r4 + i) : __ldg(r4 + i); };
   size_t b = 0;
-  for (; b + 128 <= n4; b += 128) {
+  if (n4 >= 128) {
     uint2 v[4];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) v[u] = kLast ? __ldcs(r4 + b + u * 32 + lane) : __ldg(r4 + b + u * 32 + lane);
+    for (int u = 0; u < 4; ++u) v[u] = load(u * 32 + lane);
+    for (;; b += 128) {  // v holds block b, which is whole
+      const bool more = b + 256 <= n4;
+      uint2 w[4];
+      if (more) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
-      fn((b + u * 32 + lane) * 4, *reinterpret_cast<const __half2 *>(&v[u].x),
-         *reinterpret_cast<const __half2 *>(&v[u].y), true);
+        for (int u = 0; u < 4; ++u) w[u] = load(b + 128 + u * 32 + lane);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        fn((b + u * 32 + lane) * 4, *reinterpret_cast<const __half2 *>(&v[u].x),
+           *reinterpret_cast<const __half2 *>(&v[u].y), true);
+      if (!more) break;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = w[u];
+    }
+    b += 128;
   }
   for (; b < n4; b += 32) {
     const size_t i = b + lane;

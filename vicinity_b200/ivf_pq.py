@@ -257,6 +257,11 @@ class IVFPQIndex:
         """Run device work on a caller's cudaStream_t (None: the index's own)."""
         _lib.check(self._lib.vg_ivfpq_set_stream(self._h, stream or None))
 
+    def set_coarse_tile_rows(self, rows: int) -> None:
+        """Query rows per tile of the coarse stage (0: automatic); a tuning
+        knob that leaves results unchanged."""
+        _lib.check(self._lib.vg_ivfpq_set_coarse_tile_rows(self._h, int(rows)))
+
     def compact(self) -> None:
         if not self.info().built:
             raise ValueError("index must be built before compact")
