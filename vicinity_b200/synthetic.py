@@ -99,8 +99,9 @@ def device_mixture(cfg: int, seed: int, device: int, n: int | None = None, nq: i
     """The configuration's Gaussian mixture drawn on the GPU (configuration 4:
     1e8 rows are generated on the device and never held on the host).
 
-    Returns (centres, chunks, queries): ``chunks`` yields [rows, d] float32
-    CUDA tensors of the database in order; ``queries`` is a host array from
+    ``device`` is a CUDA ordinal (or a torch device string).  Returns
+    (centres, chunks, queries): ``chunks`` yields [rows, d] float32 tensors of
+    the database in order, on that device; ``queries`` is a host array from
     an independent stream of the same mixture.  Every chunk is a pure function
     of (seed, chunk index), so each rank of a multi-GPU job regenerates the
     identical database.
@@ -111,7 +112,7 @@ def device_mixture(cfg: int, seed: int, device: int, n: int | None = None, nq: i
     d, centres, sigma = c["d"], c["centres"], c["sigma"]
     n = c["n"] if n is None else n
     nq = c["nq"] if nq is None else nq
-    dev = torch.device("cuda", device)
+    dev = torch.device(device) if isinstance(device, str) else torch.device("cuda", device)
 
     def gen(stream: int) -> "torch.Generator":
         g = torch.Generator(device=dev)
