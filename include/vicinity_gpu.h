@@ -134,9 +134,9 @@ int vg_ivfpq_set_nprobe(vg_index *ix, size_t nprobe);
 int vg_ivfpq_set_stream(vg_index *ix, void *stream);
 
 /* Query rows per tile of the coarse stage of a search (the query x centroid
- * products and the probe selection run tile by tile); 0 restores the
- * automatic size.  A tuning knob with no reference counterpart: results do
- * not depend on it. */
+ * products and the probe selection run tile by tile), at most the automatic
+ * size (1 GiB of f32 products); 0 restores the automatic size.  A tuning knob
+ * with no reference counterpart: results do not depend on it. */
 int vg_ivfpq_set_coarse_tile_rows(vg_index *ix, size_t rows);
 
 /* src/ivf_pq/search.rs:352-379 getters, plus engine state. */
