@@ -290,6 +290,23 @@ int vg_flat_search_ip(const float *db, size_t n, const float *queries,
                       size_t nq, size_t dim, size_t k, int device,
                       uint32_t *out_ids, float *out_dist, uint32_t *out_count);
 
+/* An exhaustive inner-product index over n rows of `dim` floats: the same
+ * search as vg_flat_search_ip, with the rows' device state (the caller's
+ * device rows in place -- they must outlive the index -- or a device copy of
+ * host rows, plus a binary16 image for the tensor-core products) built once.
+ * The reference computes this ground truth with a loop over the rows
+ * (src/benchmark/evaluation.rs:250-268, src/distance.rs:125-130). */
+typedef struct vg_flat vg_flat;
+int vg_flat_create(const float *db, size_t n, size_t dim, int device, vg_flat **out);
+int vg_flat_destroy(vg_flat *f);
+
+/* vg_flat_search_ip over the rows of f: queries and outputs host or device
+ * memory; the work runs on `stream` (a cudaStream_t of f's device, NULL = f's
+ * own stream) and the call returns when the outputs are written.  k at most
+ * 256. */
+int vg_flat_search(vg_flat *f, const float *queries, size_t nq, size_t k, void *stream, uint32_t *out_ids,
+                   float *out_dist, uint32_t *out_count);
+
 /* No counterpart in the reference.  vg_flat_search_ip for callers that
  * cannot allocate device memory at search time (memory handed out up front
  * to another allocator or budget, loops that cannot take cudaMalloc's

@@ -8,6 +8,7 @@ from ._lib import VicinityError, device_count
 from .ivf_pq import (
     MISSING_DISTANCE,
     MISSING_LABEL,
+    FlatIndex,
     IVFPQFileSearcher,
     IVFPQIndex,
     current_generation,
@@ -19,6 +20,7 @@ from .ivf_pq import (
 )
 
 __all__ = [
+    "FlatIndex",
     "IVFPQFileSearcher",
     "IVFPQIndex",
     "current_generation",

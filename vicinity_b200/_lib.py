@@ -138,6 +138,9 @@ SIGNATURES = {
     "vg_ivfpq_shard": (_i, [_vp, _i, _i, _vp, _i]),
     "vg_shard_assign_lists": (_i, [_vp, _sz, _i, _vp]),
     "vg_flat_search_ip": (_i, [_vp, _sz, _vp, _sz, _sz, _sz, _i, _vp, _vp, _vp]),
+    "vg_flat_create": (_i, [_vp, _sz, _sz, _i, C.POINTER(_vp)]),
+    "vg_flat_destroy": (_i, [_vp]),
+    "vg_flat_search": (_i, [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _vp]),
     "vg_ivfpq_save": (_i, [_vp, C.c_char_p]),
     "vg_ivfpq_load": (_i, [C.c_char_p, _i, C.POINTER(_vp)]),
     "vg_ivfpq_save_generation": (_i, [_vp, C.c_char_p]),

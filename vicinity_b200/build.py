@@ -78,7 +78,7 @@ def build_engine(force: bool = False, jobs: int | None = None) -> Path:
         with cf.ThreadPoolExecutor(max_workers=jobs or min(len(todo), os.cpu_count() or 4)) as ex:
             list(ex.map(compile_one, todo))
     if force or todo or _stale(LIB, objs):
-        cmd = [nvcc, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lnccl", "-lcublas", "-Xlinker", "--no-undefined"]
+        cmd = [nvcc, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lnccl", "-Xlinker", "--no-undefined"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")

@@ -433,7 +433,8 @@ cudaError_t launch_segments(const uint32_t *sorted_keys, size_t n, size_t nseg, 
 }
 
 namespace {
-__global__ void count_diff_kernel(const uint8_t *__restrict__ a, const uint8_t *__restrict__ b, size_t n,
+template <typename T>
+__global__ void count_diff_kernel(const T *__restrict__ a, const T *__restrict__ b, size_t n,
                                   unsigned int *changed) {
   size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   bool diff = i < n && a[i] != b[i];
@@ -445,7 +446,14 @@ __global__ void count_diff_kernel(const uint8_t *__restrict__ a, const uint8_t *
 cudaError_t launch_count_diff_u8(const uint8_t *a, const uint8_t *b, size_t n, unsigned int *changed,
                                  cudaStream_t s) {
   if (n == 0) return cudaSuccess;
-  count_diff_kernel<<<grid_for(n), 256, 0, s>>>(a, b, n, changed);
+  count_diff_kernel<uint8_t><<<grid_for(n), 256, 0, s>>>(a, b, n, changed);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_count_diff_u32(const uint32_t *a, const uint32_t *b, size_t n, unsigned int *changed,
+                                  cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  count_diff_kernel<uint32_t><<<grid_for(n), 256, 0, s>>>(a, b, n, changed);
   return cudaGetLastError();
 }
 

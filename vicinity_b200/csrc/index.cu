@@ -16,7 +16,6 @@
 //   pack_off   u64 [Lc]            (ks == 16) 16-byte aligned byte offset of
 //   packed     u8                  each list's nibble-packed codes: vector-major,
 //                                  ceil(M/2) bytes per vector, lists >= 16 only
-#include <cublas_v2.h>
 #include <nccl.h>
 
 #include <algorithm>
@@ -26,6 +25,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <memory>
 #include <mutex>
 #include <unordered_map>
 #include <numeric>
@@ -175,9 +175,9 @@ struct vg_index {
   DevBuf list_radius;  // f32 [Lc]: largest reconstructed-residual norm per list (list pruning)
   DevBuf cent_norm;    // f32 [1]: largest centroid norm (probe shortlist error bound)
   DevBuf sub_radius;   // f32 [M + 1]: largest codeword norm per subspace, then of all (4-bit list pruning)
-  DevBuf cent_h;       // binary16 [Lc][d]: centroids for the approximate coarse products
+  DevBuf cent_img;     // binary16 operand image of the centroids (tensor-core coarse products)
+  int cent_kp = 0;     // K padding of cent_img (0: no tensor-core path)
   float h_cmax = 0.0f; // largest centroid norm (host copy)
-  cublasHandle_t blas = nullptr;  // TF32 coarse products (probe shortlist)
   std::vector<uint64_t> h_list_off;
   std::vector<uint32_t> h_doc_ids;
 
@@ -205,7 +205,8 @@ struct vg_index {
 
   // search workspace
   DevBuf ws_q, ws_qn, ws_dist, ws_probes, ws_pdist, ws_scalars,
-      ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_lb, ws_rec, ws_lbq, ws_qh, ws_floor;
+      ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_lb, ws_rec, ws_lbq, ws_qimg, ws_eps, ws_tc,
+      ws_floor;
   DevBuf stats;  // u64 [pairs, vectors, code bytes, scored lists, scored vectors] while profiling
 
   // error flag of bounded device waits, in mapped pinned host memory
@@ -226,7 +227,7 @@ struct vg_index {
     return vectors.cap + doc_ids.cap + centroids.cap + codebooks.cap + assign.cap + codes.cap +
            list_off.cap + list_ids.cap + code_off.cap + list_codes.cap + pack_off.cap + packed.cap +
            owner.cap + rotation.cap + rotation_t.cap + category_d.cap + bitmask_d.cap + cat_counts.cap +
-           list_radius.cap + cent_norm.cap + sub_radius.cap + cent_h.cap;
+           list_radius.cap + cent_norm.cap + sub_radius.cap + cent_img.cap;
   }
 };
 
@@ -310,6 +311,124 @@ cudaError_t reserve_tile_events(vg_index *ix, size_t count) {
 
 int upload_rotation(vg_index *ix);
 
+// The tensor-core path (tc_select.cu) ranks columns by binary16 products and
+// re-scores, with the reference's arithmetic, every column its error bound
+// cannot rule out.  It applies to rows of up to 128 floats and centroids
+// shorter than 100 (beyond that the bound admits most lists); everything else
+// takes the exact SIMT tiles.  VICINITY_COARSE=exact forces the exact path.
+constexpr size_t kTcMinLists = 512;
+
+bool tc_disabled() {
+  static const bool off = [] {
+    const char *e = std::getenv("VICINITY_COARSE");
+    return e && std::strcmp(e, "exact") == 0;
+  }();
+  return off;
+}
+
+bool coarse_on_tensor_cores(const vg_index *ix, size_t P) {
+  return !tc_disabled() && ix->cent_kp && ix->num_centroids >= kTcMinLists && P >= 1 && P <= 256 &&
+         std::isfinite(ix->h_cmax) && ix->h_cmax < 100.0f;
+}
+
+// Largest centroid norm (device and host copies) and the binary16 operand
+// image of the centroids, after the centroids are final.
+int prepare_centroids(vg_index *ix) {
+  cudaStream_t s = ix->stream;
+  const size_t Lc = ix->num_centroids;
+  const int d = static_cast<int>(ix->d);
+  VG_CU(ix->cent_norm.reserve(4));
+  VG_CU(launch_centroid_norm_max(ix->centroids.as<float>(), Lc, d, ix->cent_norm.as<float>(), s));
+  VG_CU(cudaMemcpyAsync(&ix->h_cmax, ix->cent_norm.p, 4, cudaMemcpyDeviceToHost, s));
+  ix->cent_kp = umma_kp(d);
+  if (ix->cent_kp) {
+    VG_CU(ix->cent_img.reserve(umma_image_bytes(std::max<size_t>(Lc, 1), ix->cent_kp)));
+    VG_CU(launch_umma_image(ix->centroids.as<float>(), Lc, d, ix->cent_kp, ix->cent_img.p, nullptr, 0.0, 0.0,
+                            nullptr, s));
+  }
+  VG_CU(cudaStreamSynchronize(s));
+  return VG_OK;
+}
+
+int check_device_error(vg_index *ix, const char *what) {
+  if (const int code = *reinterpret_cast<volatile int *>(ix->h_err)) {
+    *reinterpret_cast<volatile int *>(ix->h_err) = 0;
+    return fail(VG_ERR_CUDA, std::string(what) + " gave up on a bounded device wait (code " + std::to_string(code) + ")");
+  }
+  return VG_OK;
+}
+
+// List of each of the n rows of X (kmeans.rs:97-107, used at search.rs:621):
+// argmin over the L centroids of 1 - x.c, ties to the lower list, into out.
+// With prev set, the rows whose list differs from prev are added to *changed.
+// Rows go through the tensor-core window with P = 1 (re-scored exactly), or
+// the exact argmin tiles when that path does not apply.
+constexpr size_t kTcAssignChunk = size_t(1) << 20;
+
+int assign_rows_to_lists(vg_index *ix, const float *X, size_t n, const float *cent, size_t L, uint32_t *out,
+                         const uint32_t *prev, unsigned int *changed) {
+  if (n == 0) return VG_OK;
+  cudaStream_t s = ix->stream;
+  const int d = static_cast<int>(ix->d), kp = umma_kp(d);
+  if (kp && L >= kTcMinLists && !tc_disabled()) {
+    DevBuf cn;
+    float cmax = 0.0f;
+    VG_CU(cn.reserve(4));
+    VG_CU(launch_centroid_norm_max(cent, L, d, cn.as<float>(), s));
+    VG_CU(cudaMemcpyAsync(&cmax, cn.p, 4, cudaMemcpyDeviceToHost, s));
+    VG_CU(cudaStreamSynchronize(s));
+    if (std::isfinite(cmax) && cmax < 100.0f) {
+      const size_t chunk = std::min(n, kTcAssignChunk);
+      DevBuf cimg, aimg, eps, ws, dist;
+      VG_CU(cimg.reserve(umma_image_bytes(L, kp)));
+      VG_CU(aimg.reserve(umma_image_bytes(chunk, kp)));
+      VG_CU(eps.reserve(chunk * 4));
+      VG_CU(ws.reserve(tc_select_workspace_bytes(chunk, L, 1, ix->num_sms)));
+      VG_CU(dist.reserve(chunk * 4));
+      VG_CU(launch_umma_image(cent, L, d, kp, cimg.p, nullptr, 0.0, 0.0, nullptr, s));
+      double rel = 0, abs_coef = 0;
+      tc_error_coefs(d, &rel, &abs_coef);
+      *reinterpret_cast<volatile int *>(ix->h_err) = 0;
+      for (size_t r0 = 0; r0 < n; r0 += chunk) {
+        const size_t rows = std::min(chunk, n - r0);
+        VG_CU(launch_umma_image(X + r0 * d, rows, d, kp, aimg.p, cn.as<float>(), rel, abs_coef, eps.as<float>(), s));
+        TcSelect t{};
+        t.a_img = aimg.p;
+        t.q = X + r0 * d;
+        t.rows = rows;
+        t.b_img = cimg.p;
+        t.x = cent;
+        t.cols = L;
+        t.d = d;
+        t.kp = kp;
+        t.P = 1;
+        t.mode = 0;
+        t.eps = eps.as<float>();
+        t.workspace = ws.p;
+        t.out_ids = out + r0;
+        t.out_dist = dist.as<float>();
+        t.out_ld = 1;
+        t.error = ix->d_err;
+        VG_CU(launch_tc_select(t, ix->num_sms, s));
+      }
+      if (prev) VG_CU(launch_count_diff_u32(out, prev, n, changed, s));
+      VG_CU(cudaStreamSynchronize(s));
+      return check_device_error(ix, "list assignment");
+    }
+  }
+  DevBuf best;
+  const size_t chunk = std::min(n, kAssignChunk);
+  VG_CU(best.reserve(chunk * 8));
+  for (size_t r0 = 0; r0 < n; r0 += chunk) {
+    const size_t rows = std::min(chunk, n - r0);
+    VG_CU(cudaMemsetAsync(best.p, 0xff, rows * 8, s));
+    VG_CU(launch_coarse_argmin(X + r0 * d, rows, cent, L, d, best.as<unsigned long long>(), s));
+    VG_CU(launch_keys_to_assign(best.as<unsigned long long>(), rows, out + r0, prev ? prev + r0 : nullptr, changed, s));
+  }
+  VG_CU(cudaStreamSynchronize(s));
+  return VG_OK;
+}
+
 int train(vg_index *ix, size_t n_train, size_t max_iter) {
   cudaStream_t s = ix->stream;
   const size_t d = ix->d, M = ix->params.num_codebooks, ks = ix->params.codebook_size;
@@ -321,7 +440,7 @@ int train(vg_index *ix, size_t n_train, size_t max_iter) {
     rows = seeded_prefix(ix->n, n_train, ix->params.seed);
     std::sort(rows.begin(), rows.end());
   }
-  DevBuf train_x, rows_d, best, assign_t, assign_prev, keys_sorted, ids_sorted, iota, seg, temp, scal, newc;
+  DevBuf train_x, rows_d, assign_t, assign_prev, keys_sorted, ids_sorted, iota, seg, temp, scal, newc;
   const float *X = ix->vectors.as<float>();
   if (!rows.empty()) {
     VG_CU(rows_d.reserve(n_train * 4));
@@ -341,7 +460,6 @@ int train(vg_index *ix, size_t n_train, size_t max_iter) {
     VG_CU(launch_gather_rows(X, static_cast<int>(d), init_d.as<uint32_t>(), Lc, ix->centroids.as<float>(), s));
     VG_CU(cudaStreamSynchronize(s));
   }
-  VG_CU(best.reserve(n_train * 8));
   VG_CU(assign_t.reserve(n_train * 4));
   VG_CU(assign_prev.reserve(n_train * 4));
   VG_CU(keys_sorted.reserve(n_train * 4));
@@ -357,22 +475,11 @@ int train(vg_index *ix, size_t n_train, size_t max_iter) {
   VG_CU(temp.reserve(temp_bytes));
   VG_CU(launch_iota(iota.as<uint32_t>(), n_train, s));
 
-  auto assign_rows = [&](const float *cent, size_t L) -> int {
-    for (size_t r0 = 0; r0 < n_train; r0 += kAssignChunk) {
-      size_t rows_n = std::min(kAssignChunk, n_train - r0);
-      VG_CU(cudaMemsetAsync(best.as<unsigned long long>() + r0, 0xff, rows_n * 8, s));
-      VG_CU(launch_coarse_argmin(X + r0 * d, rows_n, cent, L, static_cast<int>(d),
-                                 best.as<unsigned long long>() + r0, s));
-    }
-    return VG_OK;
-  };
-
   unsigned int changed = 1;
   for (size_t it = 0; it < max_iter && changed; ++it) {
-    VG_TRY(assign_rows(ix->centroids.as<float>(), Lc));
     VG_CU(cudaMemsetAsync(scal.p, 0, 4, s));
-    VG_CU(launch_keys_to_assign(best.as<unsigned long long>(), n_train, assign_t.as<uint32_t>(),
-                                it ? assign_prev.as<uint32_t>() : nullptr, scal.as<unsigned int>(), s));
+    VG_TRY(assign_rows_to_lists(ix, X, n_train, ix->centroids.as<float>(), Lc, assign_t.as<uint32_t>(),
+                                it ? assign_prev.as<uint32_t>() : nullptr, scal.as<unsigned int>()));
     size_t tb = temp_bytes;
     VG_CU(sort_pairs_u32(temp.p, tb, assign_t.as<uint32_t>(), keys_sorted.as<uint32_t>(), iota.as<uint32_t>(),
                          ids_sorted.as<uint32_t>(), n_train, 32, s));
@@ -387,8 +494,8 @@ int train(vg_index *ix, size_t n_train, size_t max_iter) {
   }
 
   // PQ: Euclidean Lloyd per subspace on training residuals (pq.rs:452-501)
-  VG_TRY(assign_rows(ix->centroids.as<float>(), Lc));
-  VG_CU(launch_keys_to_assign(best.as<unsigned long long>(), n_train, assign_t.as<uint32_t>(), nullptr, nullptr, s));
+  VG_TRY(assign_rows_to_lists(ix, X, n_train, ix->centroids.as<float>(), Lc, assign_t.as<uint32_t>(), nullptr,
+                              nullptr));
   DevBuf resid, codes_t, codes_prev, pkeys;
   VG_CU(resid.reserve(n_train * d * 4));
   VG_CU(launch_residuals(X, n_train, static_cast<int>(d), assign_t.as<uint32_t>(), ix->centroids.as<float>(),
@@ -537,18 +644,9 @@ int encode_and_layout(vg_index *ix) {
   cudaStream_t s = ix->stream;
   const size_t n = ix->n, d = ix->d, M = ix->params.num_codebooks, ks = ix->params.codebook_size;
   const size_t Lc = ix->num_centroids;
-  DevBuf best;
-  VG_CU(best.reserve(std::min(n, kAssignChunk) * 8));
   VG_CU(ix->assign.reserve(n * 4));
-  for (size_t r0 = 0; r0 < n; r0 += kAssignChunk) {
-    size_t rows = std::min(kAssignChunk, n - r0);
-    VG_CU(cudaMemsetAsync(best.p, 0xff, rows * 8, s));
-    VG_CU(launch_coarse_argmin(ix->vectors.as<float>() + r0 * d, rows, ix->centroids.as<float>(), Lc,
-                               static_cast<int>(d), best.as<unsigned long long>(), s));
-    VG_CU(launch_keys_to_assign(best.as<unsigned long long>(), rows, ix->assign.as<uint32_t>() + r0, nullptr,
-                                nullptr, s));
-  }
-  best.release();
+  VG_TRY(assign_rows_to_lists(ix, ix->vectors.as<float>(), n, ix->centroids.as<float>(), Lc,
+                              ix->assign.as<uint32_t>(), nullptr, nullptr));
   VG_CU(ix->codes.reserve(n * M));
   if (ix->h_rotation.empty()) {
     VG_CU(launch_encode(ix->vectors.as<float>(), n, static_cast<int>(d), ix->assign.as<uint32_t>(),
@@ -634,11 +732,7 @@ int build_list_storage(vg_index *ix, const uint32_t *sorted_lists) {
   VG_CU(ix->sub_radius.reserve((M + 1) * 4));
   VG_CU(launch_subspace_radius(ix->codebooks.as<float>(), static_cast<int>(M), static_cast<int>(ks),
                                static_cast<int>(ix->dsub), ix->sub_radius.as<float>(), s));
-  VG_CU(ix->cent_norm.reserve(4));
-  VG_CU(launch_centroid_norm_max(ix->centroids.as<float>(), Lc, static_cast<int>(ix->d), ix->cent_norm.as<float>(), s));
-  VG_CU(cudaMemcpyAsync(&ix->h_cmax, ix->cent_norm.p, 4, cudaMemcpyDeviceToHost, s));
-  VG_CU(ix->cent_h.reserve(std::max<size_t>(Lc * ix->d, 1) * 2));
-  VG_CU(launch_to_half(ix->centroids.as<float>(), Lc * ix->d, ix->cent_h.p, s));
+  VG_TRY(prepare_centroids(ix));
   VG_CU(cudaStreamSynchronize(s));
   ix->built = true;
   return VG_OK;
@@ -648,63 +742,74 @@ int build_list_storage(vg_index *ix, const uint32_t *sorted_lists) {
 
 // The nprobe nearest lists of rows normalised queries qn (search.rs:1602-1617:
 // 1 - q.c in sequential f32, ascending, ties by list id) into probes / pdist
-// (row stride P).  Many lists: a binary16 tensor-core GEMM gives approximate
-// products and launch_probe_shortlist re-scores, with the reference's
-// arithmetic, every list the approximation cannot rule out -- the same probes
-// as the exact path.  Few lists, nprobe beyond the shortlist's window, or
-// centroids too long for a useful error bound: the exact distance tile and a
-// row selection.  Calls mark(3) between the two
-// phases; returns the number of this library's kernels launched in *launches.
-constexpr size_t kShortlistMinLists = 1024;
-
+// (row stride P).  Many lists: tensor-core products with the fused candidate
+// window (tc_select.cu) -- the same probes as the exact path, no product
+// matrix in memory.  Few lists, rows beyond 128 floats or centroids too long
+// for a useful error bound: the exact distance tile (ws_dist, rows x Lc) and
+// a row selection.  Calls mark(3) between the two phases; adds the number of
+// this library's kernels launched to *launches.
 int coarse_probes(vg_index *ix, const float *qn, size_t rows, size_t P, uint32_t *probes, float *pdist,
                   uint64_t *launches, const ProbeBoundArgs *bounds = nullptr, bool *bounds_done = nullptr) {
   if (bounds_done) *bounds_done = false;
   cudaStream_t s = ix->stream;
   const size_t Lc = ix->num_centroids, d = ix->d;
-  // the shortlist's error bound grows with the centroid norms: beyond a few
-  // units it admits most lists, and past the binary16 range it is void
-  const bool shortlist =
-      Lc >= kShortlistMinLists && P <= 128 && d <= 2048 && std::isfinite(ix->h_cmax) && ix->h_cmax < 100.0f;
-  if (shortlist) {
-    if (!ix->blas) {
-      if (cublasCreate(&ix->blas) != CUBLAS_STATUS_SUCCESS) return fail(VG_ERR_CUDA, "cublasCreate failed");
-    }
-    if (cublasSetStream(ix->blas, s) != CUBLAS_STATUS_SUCCESS) return fail(VG_ERR_CUDA, "cublasSetStream failed");
-    const float one = 1.0f, zero = 0.0f;
-    // Products in binary16: operands rounded to nearest, f32 accumulation,
-    // binary16 results (half the bytes of an f32 product matrix; every
-    // product is far inside the range, |q.c| <= |c| < 100).  The error
-    // coefficients cover operand and result rounding (subnormal operands as
-    // an absolute term), accumulation in any order (2 d u), the exact dot's
-    // own rounding (d u) and the subtractions from 1.
-    const double u = 1.0 / 16777216.0, dd = static_cast<double>(d);
-    const double rel = 3.0 * 8192 * u + 4 * u + 2 * u + 4 * dd * u;  // 2^-10 + 2^-11 + 2^-22 + 2^-23 + 4 d u
-    const double abs_coef = std::sqrt(dd) * u;
-    VG_CU(ix->ws_qh.reserve(std::max<size_t>(rows * d, 1) * 2));
-    VG_CU(launch_to_half(qn, rows * d, ix->ws_qh.p, s));
-    *launches += 1;
-    // column-major: S^T [Lc x rows] = C [Lc x d] * Qn^T [d x rows], i.e. row-major S[rows][Lc] = Qn C^T
-    const cublasStatus_t st =
-        cublasGemmEx(ix->blas, CUBLAS_OP_T, CUBLAS_OP_N, static_cast<int>(Lc), static_cast<int>(rows),
-                     static_cast<int>(d), &one, ix->cent_h.p, CUDA_R_16F, static_cast<int>(d), ix->ws_qh.p,
-                     CUDA_R_16F, static_cast<int>(d), &zero, ix->ws_dist.p, CUDA_R_16F, static_cast<int>(Lc),
-                     CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-    if (st != CUBLAS_STATUS_SUCCESS) return fail(VG_ERR_CUDA, "cublasGemmEx failed");
+  if (coarse_on_tensor_cores(ix, P)) {
+    const int kp = ix->cent_kp;
+    double rel = 0, abs_coef = 0;
+    tc_error_coefs(static_cast<int>(d), &rel, &abs_coef);
+    VG_CU(ix->ws_qimg.reserve(umma_image_bytes(rows, kp)));
+    VG_CU(ix->ws_eps.reserve(rows * 4));
+    VG_CU(ix->ws_tc.reserve(tc_select_workspace_bytes(rows, Lc, static_cast<int>(P), ix->num_sms)));
+    VG_CU(launch_umma_image(qn, rows, static_cast<int>(d), kp, ix->ws_qimg.p, ix->cent_norm.as<float>(), rel,
+                            abs_coef, ix->ws_eps.as<float>(), s));
     mark(ix, 3);
-    VG_CU(launch_probe_shortlist(ix->ws_dist.p, true, rows, Lc, Lc, qn, static_cast<int>(d),
-                                 ix->centroids.as<float>(), ix->cent_norm.as<float>(), rel, abs_coef,
-                                 static_cast<int>(P), probes, pdist, P, bounds ? *bounds : ProbeBoundArgs{}, s));
-    *launches += 1;
+    TcSelect t{};
+    t.a_img = ix->ws_qimg.p;
+    t.q = qn;
+    t.rows = rows;
+    t.b_img = ix->cent_img.p;
+    t.x = ix->centroids.as<float>();
+    t.cols = Lc;
+    t.d = static_cast<int>(d);
+    t.kp = kp;
+    t.P = static_cast<int>(P);
+    t.mode = 0;
+    t.eps = ix->ws_eps.as<float>();
+    t.workspace = ix->ws_tc.p;
+    t.out_ids = probes;
+    t.out_dist = pdist;
+    t.out_ld = P;
+    if (bounds) t.bnd = *bounds;
+    t.error = ix->d_err;
+    VG_CU(launch_tc_select(t, ix->num_sms, s));
+    *launches += 3;
     if (bounds_done) *bounds_done = bounds != nullptr;
     return VG_OK;
   }
+  VG_CU(ix->ws_dist.reserve(rows * Lc * 4));
   VG_CU(launch_coarse_dist(qn, rows, ix->centroids.as<float>(), Lc, static_cast<int>(d), ix->ws_dist.as<float>(), Lc,
                            s));
   mark(ix, 3);
   VG_CU(launch_select_rows(ix->ws_dist.as<float>(), rows, Lc, Lc, static_cast<int>(P), probes, pdist, P, 0, s));
   *launches += 2;
   return VG_OK;
+}
+
+// Query rows per tile of the coarse stage: the exact path holds a tile of f32
+// distances (kDistBudgetBytes), the tensor-core path its candidate lists.
+size_t coarse_tile(const vg_index *ix, size_t nq, size_t P) {
+  const size_t Lc = std::max<size_t>(ix->num_centroids, 1);
+  size_t tile;
+  if (coarse_on_tensor_cores(ix, P)) {
+    const size_t est = std::min<size_t>(std::max<size_t>(nq, 1), size_t(1) << 20);
+    const size_t per_row = tc_select_workspace_bytes(est, Lc, static_cast<int>(P), ix->num_sms) / est + 1;
+    tile = std::max<size_t>(1024, kDistBudgetBytes / per_row);
+  } else {
+    tile = std::max<size_t>(1, kDistBudgetBytes / (Lc * 4));
+  }
+  tile = std::min(nq, tile);
+  if (ix->coarse_tile_rows) tile = std::min(tile, ix->coarse_tile_rows);
+  return std::max<size_t>(tile, 1);
 }
 
 int write_padding(vg_index *ix, size_t nq, size_t k, uint32_t *out_ids, float *out_dist, uint32_t *out_count) {
@@ -784,6 +889,7 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   const bool prof = ix->profiling;
   uint64_t launches0 = ix->launches;
 
+  *reinterpret_cast<volatile int *>(ix->h_err) = 0;
   mark(ix, 0);
   const float *dq = queries;
   if (!is_device_ptr(queries)) {
@@ -798,9 +904,7 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   mark(ix, 2);
 
   // coarse distances + top-nprobe, tiled over queries
-  size_t tile = std::max<size_t>(1, std::min(nq, kDistBudgetBytes / (Lc * 4)));
-  if (ix->coarse_tile_rows) tile = std::min(tile, ix->coarse_tile_rows);
-  VG_CU(ix->ws_dist.reserve(tile * Lc * 4));
+  const size_t tile = coarse_tile(ix, nq, P);
   VG_CU(ix->ws_probes.reserve(nq * P * 4));
   VG_CU(ix->ws_pdist.reserve(nq * P * 4));
   // list pruning bounds (tables without a rotation; see launch_probe_lb)
@@ -881,7 +985,6 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
     VG_CU(ix->ws_keys.reserve(nq * kk * 8));
     sp.out_keys = ix->ws_keys.as<unsigned long long>();
   }
-  *reinterpret_cast<volatile int *>(ix->h_err) = 0;
   if (kk <= 256) {
     VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
     ix->launches += 1;
@@ -945,8 +1048,7 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   }
   mark(ix, 10);
   VG_TRY(sync_stream(ix));
-  if (const int code = *reinterpret_cast<volatile int *>(ix->h_err))
-    return fail(VG_ERR_CUDA, "search kernel gave up on a bounded pipeline wait (code " + std::to_string(code) + ")");
+  VG_TRY(check_device_error(ix, "search"));
 
   if (prof) {
     auto el = [&](int a, int b) {
@@ -1057,10 +1159,10 @@ int search_filtered_impl(vg_index *ix, const float *queries, size_t nq, size_t k
   }
   VG_CU(ix->ws_qn.reserve(nq * d * 4));
   VG_CU(launch_normalize_rows(dq, nq, static_cast<int>(d), ix->ws_qn.as<float>(), s));
-  const size_t tile = std::max<size_t>(1, std::min(nq, kDistBudgetBytes / (Lc * 4)));
-  VG_CU(ix->ws_dist.reserve(tile * Lc * 4));
+  const size_t tile = coarse_tile(ix, nq, P);
   VG_CU(ix->ws_probes.reserve(nq * P * 4));
   VG_CU(ix->ws_pdist.reserve(nq * P * 4));
+  *reinterpret_cast<volatile int *>(ix->h_err) = 0;
   for (size_t r0 = 0; r0 < nq; r0 += tile) {
     const size_t rows = std::min(tile, nq - r0);
     VG_TRY(coarse_probes(ix, ix->ws_qn.as<float>() + r0 * d, rows, P, ix->ws_probes.as<uint32_t>() + r0 * P,
@@ -1150,7 +1252,7 @@ int search_filtered_impl(vg_index *ix, const float *queries, size_t nq, size_t k
     if (out_count) VG_CU(cudaMemcpyAsync(out_count, o_cnt, nq * 4, cudaMemcpyDeviceToHost, s));
   }
   VG_TRY(sync_stream(ix));
-  return VG_OK;
+  return check_device_error(ix, "filtered search");
 }
 
 }  // namespace
@@ -1359,13 +1461,13 @@ int vg_ivfpq_destroy(vg_index *ix) {
                       &ix->list_off, &ix->list_ids, &ix->code_off, &ix->list_codes, &ix->pack_off, &ix->packed,
                       &ix->owner, &ix->ws_q, &ix->ws_qn, &ix->ws_dist, &ix->ws_probes, &ix->ws_pdist,
                       &ix->ws_scalars, &ix->ws_keys, &ix->ws_all_keys, &ix->ws_out_ids, &ix->ws_out_dist,
-                      &ix->ws_out_count, &ix->stats, &ix->ws_lb, &ix->ws_rec, &ix->ws_lbq, &ix->ws_qh, &ix->ws_floor})
+                      &ix->ws_out_count, &ix->stats, &ix->ws_lb, &ix->ws_rec, &ix->ws_lbq, &ix->ws_qimg,
+                      &ix->ws_eps, &ix->ws_tc, &ix->ws_floor, &ix->cent_img})
       b->release();
     for (int i = 0; i < kPhaseEvents; ++i)
       if (ix->ev[i]) cudaEventDestroy(ix->ev[i]);
     for (cudaEvent_t e : ix->tile_ev) cudaEventDestroy(e);
     if (ix->h_err) cudaFreeHost(ix->h_err);
-    if (ix->blas) cublasDestroy(ix->blas);
     if (ix->own_stream) cudaStreamDestroy(ix->own_stream);
     delete ix;
   }
@@ -1571,10 +1673,10 @@ int vg_ivfpq_nearest_lists(vg_index *ix, const float *queries, size_t nq, size_t
   }
   VG_CU(ix->ws_qn.reserve(nq * d * 4));
   VG_CU(launch_normalize_rows(dq, nq, static_cast<int>(d), ix->ws_qn.as<float>(), s));
-  const size_t tile = std::max<size_t>(1, std::min(nq, kDistBudgetBytes / (Lc * 4)));
-  VG_CU(ix->ws_dist.reserve(tile * Lc * 4));
+  const size_t tile = coarse_tile(ix, nq, P);
   VG_CU(ix->ws_probes.reserve(nq * P * 4));
   VG_CU(ix->ws_pdist.reserve(nq * P * 4));
+  *reinterpret_cast<volatile int *>(ix->h_err) = 0;
   uint64_t launches = 1;
   for (size_t r0 = 0; r0 < nq; r0 += tile) {
     const size_t rows = std::min(tile, nq - r0);
@@ -1584,7 +1686,7 @@ int vg_ivfpq_nearest_lists(vg_index *ix, const float *queries, size_t nq, size_t
   VG_CU(cudaMemcpyAsync(out_lists, ix->ws_probes.p, nq * P * 4, cudaMemcpyDefault, s));
   VG_CU(cudaMemcpyAsync(out_dist, ix->ws_pdist.p, nq * P * 4, cudaMemcpyDefault, s));
   VG_CU(cudaStreamSynchronize(s));
-  return VG_OK;
+  return check_device_error(ix, "nearest_lists");
 }
 
 int vg_ivfpq_search_batch_reranked(vg_index *ix, const float *queries, size_t nq, size_t k, size_t candidate_pool,
@@ -1768,6 +1870,192 @@ int vg_ivfpq_shard(vg_index *ix, int rank, int world_size, const uint8_t nccl_id
 
 // ---- flat exact search ----------------------------------------------------
 
+}  // extern "C"
+
+// An exhaustive inner-product index over f32 rows (distance.rs:125-130; the
+// ground truth of evaluation.rs:250-268): the rows (the caller's device rows
+// in place, or a device copy of host rows), their largest norm, and the
+// binary16 operand image the tensor-core window reads.
+struct vg_flat {
+  int device = 0, num_sms = 148;
+  size_t n = 0, d = 0;
+  DevBuf own_rows;
+  const float *rows = nullptr;
+  DevBuf img, norm_d;
+  int kp = 0;
+  float xmax = 0.0f;
+  bool tc = false;  // tensor-core path usable (rows of <= 128 floats, norms below 2^14)
+  cudaStream_t own_stream = nullptr;
+  int *h_err = nullptr, *d_err = nullptr;
+  std::mutex mu;
+  DevBuf q, qimg, eps, ws, dist, chunk, ids, dst, cnt;
+};
+
+namespace {
+
+// Exact path: SIMT tiles of -dot in the reference's order, a top-k per tile
+// and a merge (rows beyond 128 floats, or norms too large for binary16).
+int flat_exact(vg_flat *f, const float *dq, size_t nq, size_t k, uint32_t *o_ids, float *o_dist, uint32_t *o_cnt,
+               cudaStream_t s) {
+  const size_t n = f->n, dim = f->d;
+  size_t tile = kDistBudgetBytes * 2 / (nq * 4);
+  tile = std::max<size_t>(128, tile / 128 * 128);
+  tile = std::min(tile, std::max<size_t>(n, 1));
+  const size_t chunks = (n + tile - 1) / tile;
+  VG_CU(f->dist.reserve(nq * tile * 4));
+  VG_CU(f->chunk.reserve(nq * chunks * k * 8));
+  for (size_t ci = 0; ci < chunks; ++ci) {
+    const size_t c0 = ci * tile, cols = std::min(tile, n - c0);
+    VG_CU(launch_neg_dot(dq, nq, f->rows + c0 * dim, cols, static_cast<int>(dim), f->dist.as<float>(), tile, s));
+    VG_CU(launch_select_rows_keys(f->dist.as<float>(), nq, cols, tile, static_cast<int>(k),
+                                  f->chunk.as<unsigned long long>() + ci * k, chunks * k, static_cast<uint32_t>(c0),
+                                  s));
+  }
+  VG_CU(launch_merge_keys(f->chunk.as<unsigned long long>(), nq, chunks * k, chunks * k, static_cast<int>(k), nullptr,
+                          o_ids, o_dist, o_cnt, nullptr, s));
+  return VG_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int vg_flat_create(const float *db, size_t n, size_t dim, int device, vg_flat **out) {
+  if (!out) return fail(VG_ERR_INVALID_PARAMETER, "null output");
+  *out = nullptr;
+  if (dim == 0) return fail(VG_ERR_INVALID_CONFIG, "invalid config `dimension`: must be greater than 0");
+  if (n > 0xfffffffeull) return fail(VG_ERR_INVALID_PARAMETER, "at most 2^32 - 2 database rows");
+  if (n && !db) return fail(VG_ERR_INVALID_PARAMETER, "null database rows");
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count) {
+    cudaGetLastError();
+    return fail(VG_ERR_CUDA, "no CUDA device " + std::to_string(device) + " (the engine has no CPU path)");
+  }
+  DeviceGuard g(device);
+  auto f = std::make_unique<vg_flat>();
+  f->device = device;
+  f->n = n;
+  f->d = dim;
+  cudaDeviceGetAttribute(&f->num_sms, cudaDevAttrMultiProcessorCount, device);
+  VG_CU(cudaStreamCreateWithFlags(&f->own_stream, cudaStreamNonBlocking));
+  VG_CU(cudaHostAlloc(reinterpret_cast<void **>(&f->h_err), sizeof(int), cudaHostAllocMapped));
+  *f->h_err = 0;
+  VG_CU(cudaHostGetDevicePointer(reinterpret_cast<void **>(&f->d_err), f->h_err, 0));
+  cudaStream_t s = f->own_stream;
+  if (n && !is_device_ptr(db)) {
+    VG_CU(f->own_rows.reserve(n * dim * 4));
+    VG_CU(cudaMemcpyAsync(f->own_rows.p, db, n * dim * 4, cudaMemcpyHostToDevice, s));
+    f->rows = f->own_rows.as<float>();
+  } else {
+    f->rows = db;
+  }
+  f->kp = umma_kp(static_cast<int>(dim));
+  if (n && f->kp && !tc_disabled()) {
+    VG_CU(f->norm_d.reserve(4));
+    VG_CU(launch_centroid_norm_max(f->rows, n, static_cast<int>(dim), f->norm_d.as<float>(), s));
+    VG_CU(cudaMemcpyAsync(&f->xmax, f->norm_d.p, 4, cudaMemcpyDeviceToHost, s));
+    VG_CU(cudaStreamSynchronize(s));
+    f->tc = std::isfinite(f->xmax) && f->xmax < 16384.0f;
+    if (f->tc) {
+      VG_CU(f->img.reserve(umma_image_bytes(n, f->kp)));
+      VG_CU(launch_umma_image(f->rows, n, static_cast<int>(dim), f->kp, f->img.p, nullptr, 0.0, 0.0, nullptr, s));
+    }
+  }
+  VG_CU(cudaStreamSynchronize(s));
+  *out = f.release();
+  return VG_OK;
+}
+
+int vg_flat_destroy(vg_flat *f) {
+  if (!f) return VG_OK;
+  {
+    DeviceGuard g(f->device);
+    if (f->own_stream) cudaStreamSynchronize(f->own_stream);
+    for (DevBuf *b : {&f->own_rows, &f->img, &f->norm_d, &f->q, &f->qimg, &f->eps, &f->ws, &f->dist, &f->chunk,
+                      &f->ids, &f->dst, &f->cnt})
+      b->release();
+    if (f->h_err) cudaFreeHost(f->h_err);
+    if (f->own_stream) cudaStreamDestroy(f->own_stream);
+  }
+  delete f;
+  return VG_OK;
+}
+
+int vg_flat_search(vg_flat *f, const float *queries, size_t nq, size_t k, void *stream, uint32_t *out_ids,
+                   float *out_dist, uint32_t *out_count) {
+  if (!f) return fail(VG_ERR_INVALID_PARAMETER, "null flat index");
+  if (k > 256) return fail(VG_ERR_INVALID_PARAMETER, "k must be at most 256");
+  if (nq == 0 || k == 0) return VG_OK;
+  if (!queries || !out_ids || !out_dist) return fail(VG_ERR_INVALID_PARAMETER, "null query or output buffer");
+  DeviceGuard g(f->device);
+  std::lock_guard<std::mutex> lock(f->mu);
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : f->own_stream;
+  const size_t n = f->n, dim = f->d;
+  const float *dq = queries;
+  if (!is_device_ptr(queries)) {
+    VG_CU(f->q.reserve(nq * dim * 4));
+    VG_CU(cudaMemcpyAsync(f->q.p, queries, nq * dim * 4, cudaMemcpyHostToDevice, s));
+    dq = f->q.as<float>();
+  }
+  const bool dev_out = is_device_ptr(out_ids) && is_device_ptr(out_dist) && (!out_count || is_device_ptr(out_count));
+  uint32_t *o_ids = out_ids, *o_cnt = out_count;
+  float *o_dist = out_dist;
+  if (!dev_out) {
+    VG_CU(f->ids.reserve(nq * k * 4));
+    VG_CU(f->dst.reserve(nq * k * 4));
+    VG_CU(f->cnt.reserve(nq * 4));
+    o_ids = f->ids.as<uint32_t>();
+    o_dist = f->dst.as<float>();
+    o_cnt = f->cnt.as<uint32_t>();
+  }
+  *reinterpret_cast<volatile int *>(f->h_err) = 0;
+  if (n == 0) {
+    VG_CU(cudaMemsetAsync(o_ids, 0xff, nq * k * 4, s));
+    std::vector<float> inf(nq * k, __builtin_inff());
+    VG_CU(cudaMemcpyAsync(o_dist, inf.data(), nq * k * 4, cudaMemcpyHostToDevice, s));
+    if (o_cnt) VG_CU(cudaMemsetAsync(o_cnt, 0, nq * 4, s));
+    VG_CU(cudaStreamSynchronize(s));
+  } else if (f->tc) {
+    double rel = 0, abs_coef = 0;
+    tc_error_coefs(static_cast<int>(dim), &rel, &abs_coef);
+    VG_CU(f->qimg.reserve(umma_image_bytes(nq, f->kp)));
+    VG_CU(f->eps.reserve(nq * 4));
+    VG_CU(f->ws.reserve(tc_select_workspace_bytes(nq, n, static_cast<int>(k), f->num_sms)));
+    VG_CU(launch_umma_image(dq, nq, static_cast<int>(dim), f->kp, f->qimg.p, f->norm_d.as<float>(), rel, abs_coef,
+                            f->eps.as<float>(), s));
+    TcSelect t{};
+    t.a_img = f->qimg.p;
+    t.q = dq;
+    t.rows = nq;
+    t.b_img = f->img.p;
+    t.x = f->rows;
+    t.cols = n;
+    t.d = static_cast<int>(dim);
+    t.kp = f->kp;
+    t.P = static_cast<int>(k);
+    t.mode = 1;
+    t.eps = f->eps.as<float>();
+    t.workspace = f->ws.p;
+    t.out_ids = o_ids;
+    t.out_dist = o_dist;
+    t.out_ld = k;
+    t.out_count = o_cnt;
+    t.error = f->d_err;
+    VG_CU(launch_tc_select(t, f->num_sms, s));
+  } else {
+    VG_TRY(flat_exact(f, dq, nq, k, o_ids, o_dist, o_cnt, s));
+  }
+  if (!dev_out) {
+    VG_CU(cudaMemcpyAsync(out_ids, o_ids, nq * k * 4, cudaMemcpyDeviceToHost, s));
+    VG_CU(cudaMemcpyAsync(out_dist, o_dist, nq * k * 4, cudaMemcpyDeviceToHost, s));
+    if (out_count) VG_CU(cudaMemcpyAsync(out_count, o_cnt, nq * 4, cudaMemcpyDeviceToHost, s));
+  }
+  VG_CU(cudaStreamSynchronize(s));
+  if (const int code = *reinterpret_cast<volatile int *>(f->h_err))
+    return fail(VG_ERR_CUDA, "flat search gave up on a bounded device wait (code " + std::to_string(code) + ")");
+  return VG_OK;
+}
+
 int vg_flat_search_ip(const float *db, size_t n, const float *queries, size_t nq, size_t dim, size_t k, int device,
                       uint32_t *out_ids, float *out_dist, uint32_t *out_count) {
   if (dim == 0) return fail(VG_ERR_INVALID_CONFIG, "invalid config `dimension`: must be greater than 0");
@@ -1780,71 +2068,11 @@ int vg_flat_search_ip(const float *db, size_t n, const float *queries, size_t nq
   }
   if (nq == 0 || k == 0) return VG_OK;
   if (!db || !queries || !out_ids || !out_dist) return fail(VG_ERR_INVALID_PARAMETER, "null argument");
-  DeviceGuard g(device);
-  // One cached stream and workspace per device, serialised by a mutex.
-  struct FlatCtx {
-    std::mutex mu;
-    cudaStream_t s = nullptr;
-    DevBuf db, q, dist, chunk, ids, dst, cnt;
-  };
-  static FlatCtx *ctx = new FlatCtx[64];  // intentionally never freed (process lifetime)
-  if (device >= 64) return fail(VG_ERR_INVALID_PARAMETER, "device index out of range");
-  FlatCtx &c = ctx[device];
-  std::lock_guard<std::mutex> lock(c.mu);
-  if (!c.s) VG_CU(cudaStreamCreateWithFlags(&c.s, cudaStreamNonBlocking));
-  cudaStream_t s = c.s;
-  const float *ddb = db, *dq = queries;
-  if (!is_device_ptr(db)) {
-    VG_CU(c.db.reserve(n * dim * 4));
-    VG_CU(cudaMemcpyAsync(c.db.p, db, n * dim * 4, cudaMemcpyHostToDevice, s));
-    ddb = c.db.as<float>();
-  }
-  if (!is_device_ptr(queries)) {
-    VG_CU(c.q.reserve(nq * dim * 4));
-    VG_CU(cudaMemcpyAsync(c.q.p, queries, nq * dim * 4, cudaMemcpyHostToDevice, s));
-    dq = c.q.as<float>();
-  }
-  size_t tile = kDistBudgetBytes * 2 / (nq * 4);
-  tile = std::max<size_t>(128, tile / 128 * 128);
-  tile = std::min(tile, std::max<size_t>(n, 1));
-  const size_t chunks = n ? (n + tile - 1) / tile : 0;
-  const bool dev_out = is_device_ptr(out_ids) && is_device_ptr(out_dist) && (!out_count || is_device_ptr(out_count));
-  uint32_t *o_ids = out_ids, *o_cnt = out_count;
-  float *o_dist = out_dist;
-  if (!dev_out) {
-    VG_CU(c.ids.reserve(nq * k * 4));
-    VG_CU(c.dst.reserve(nq * k * 4));
-    VG_CU(c.cnt.reserve(nq * 4));
-    o_ids = c.ids.as<uint32_t>();
-    o_dist = c.dst.as<float>();
-    o_cnt = c.cnt.as<uint32_t>();
-  }
-  if (chunks) {
-    VG_CU(c.dist.reserve(nq * tile * 4));
-    VG_CU(c.chunk.reserve(nq * chunks * k * 8));
-    for (size_t ci = 0; ci < chunks; ++ci) {
-      size_t c0 = ci * tile, cols = std::min(tile, n - c0);
-      VG_CU(launch_neg_dot(dq, nq, ddb + c0 * dim, cols, static_cast<int>(dim), c.dist.as<float>(), tile, s));
-      VG_CU(launch_select_rows_keys(c.dist.as<float>(), nq, cols, tile, static_cast<int>(k),
-                                    c.chunk.as<unsigned long long>() + ci * k, chunks * k,
-                                    static_cast<uint32_t>(c0), s));
-    }
-    VG_CU(launch_merge_keys(c.chunk.as<unsigned long long>(), nq, chunks * k, chunks * k, static_cast<int>(k),
-                            nullptr, o_ids, o_dist, o_cnt, nullptr, s));
-  } else {
-    VG_CU(cudaMemsetAsync(o_ids, 0xff, nq * k * 4, s));
-    std::vector<float> inf(nq * k, __builtin_inff());
-    VG_CU(cudaMemcpyAsync(o_dist, inf.data(), nq * k * 4, cudaMemcpyHostToDevice, s));
-    if (o_cnt) VG_CU(cudaMemsetAsync(o_cnt, 0, nq * 4, s));
-    VG_CU(cudaStreamSynchronize(s));
-  }
-  if (!dev_out) {
-    VG_CU(cudaMemcpyAsync(out_ids, o_ids, nq * k * 4, cudaMemcpyDeviceToHost, s));
-    VG_CU(cudaMemcpyAsync(out_dist, o_dist, nq * k * 4, cudaMemcpyDeviceToHost, s));
-    if (out_count) VG_CU(cudaMemcpyAsync(out_count, o_cnt, nq * 4, cudaMemcpyDeviceToHost, s));
-  }
-  VG_CU(cudaStreamSynchronize(s));
-  return VG_OK;
+  vg_flat *f = nullptr;
+  VG_TRY(vg_flat_create(db, n, dim, device, &f));
+  const int st = vg_flat_search(f, queries, nq, k, nullptr, out_ids, out_dist, out_count);
+  vg_flat_destroy(f);
+  return st;
 }
 
 }  // extern "C"

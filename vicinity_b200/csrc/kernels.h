@@ -76,20 +76,58 @@ struct ProbeBoundArgs {
   float *lbq;
 };
 
-// Exact top-k probes per row from approximate products s[row][l] ~ q . c_l
-// (a tensor-core GEMM, f32 or, with s_half, binary16 results): candidates
-// within eps = rel |q| cmax + abs_coef (1 + cmax) + 2^-20 of the k-th are
-// re-scored with the reference's sequential 1 - dot; rows with too many
-// candidates or non-finite inputs are scored exactly over all L.  Same
-// output as launch_select_rows on exact 1 - dot distances.  With bounds.lb
-// set, the probes' pruning bounds and records are written beside them.
-cudaError_t launch_probe_shortlist(const void *s, bool s_half, size_t rows, size_t L, size_t ld, const float *qn,
-                                   int d, const float *cent, const float *cmax, double rel, double abs_coef, int k,
-                                   uint32_t *out_ids, float *out_dist, size_t out_ld, const ProbeBoundArgs &bounds,
-                                   cudaStream_t st);
+// ---- tc_select.cu: tensor-core products with a fused candidate window ----
 
-// out[i] = x[i] rounded to the nearest half (IEEE binary16).
-cudaError_t launch_to_half(const float *x, size_t n, void *out, cudaStream_t s);
+// K padding of a binary16 operand image for row length d: 64 or 128 (0: d
+// beyond 128, no tensor-core path).
+int umma_kp(int d);
+
+// Bytes of the operand image of `rows` rows: rows rounded up to 128, kp
+// binary16 elements each.
+size_t umma_image_bytes(size_t rows, int kp);
+
+// Operand image of x [rows][d] (f32, rounded to nearest binary16, zero
+// padded to kp columns and to whole 128-row tiles): 128-row tiles of kp/64
+// blocks of 128 rows x 128 bytes in the 128-byte-swizzled K-major layout the
+// tensor core reads.  With eps set, also eps[r] = rel |x_r| cmax + abs_coef
+// (1 + |x_r| + cmax) + 2^-20 (rounded up; +inf for rows too long for binary16),
+// the bound on |s - x_r . c| of the approximate products.
+cudaError_t launch_umma_image(const float *x, size_t rows, int d, int kp, void *img, const float *cmax,
+                              double rel, double abs_coef, float *eps, cudaStream_t s);
+
+// Error coefficients of the approximate products for row length d: operand
+// rounding of both sides, tensor-core accumulation (16 ulp per add), the
+// exact sequential dot's own rounding and the subtractions from 1 (rel);
+// subnormal binary16 operands (abs_coef).
+void tc_error_coefs(int d, double *rel, double *abs_coef);
+
+// The P best columns of every query row by exact distance (mode 0: 1 - q.x,
+// the probe order of find_nearest_centroids; mode 1: -q.x, exact inner-
+// product search), ascending, ties to the lower column, padded with
+// 0xffffffff / +inf: out_ids / out_dist [rows][out_ld].  Products come from
+// the tensor cores on the two images; columns within twice the error bound
+// of the P-th approximate product are re-scored with the reference's
+// sequential f32 dot from q [rows][d] and x [cols][d].  With bnd.lb set
+// (mode 0), the probes' pruning bounds and records are written beside them.
+struct TcSelect {
+  const void *a_img;      // query image (umma_image_bytes(rows, kp))
+  const float *q;         // [rows][d] f32 query rows
+  size_t rows;
+  const void *b_img;      // column image
+  const float *x;         // [cols][d] f32 column rows
+  size_t cols;
+  int d, kp, P, mode;     // P in 1..256
+  const float *eps;       // [rows] from launch_umma_image
+  void *workspace;        // tc_select_workspace_bytes(rows, cols, P, num_sms)
+  uint32_t *out_ids;
+  float *out_dist;
+  size_t out_ld;
+  uint32_t *out_count;    // [rows] real result counts (nullable)
+  ProbeBoundArgs bnd;     // bnd.lb == nullptr: no bounds
+  int *error;             // set nonzero when a bounded wait of the kernel gives up
+};
+size_t tc_select_workspace_bytes(size_t rows, size_t cols, int P, int num_sms);
+cudaError_t launch_tc_select(const TcSelect &t, int num_sms, cudaStream_t s);
 
 // Same selection, but writing packed keys (for later merging).
 cudaError_t launch_select_rows_keys(const float *dist, size_t rows,
@@ -182,6 +220,8 @@ cudaError_t launch_probe_lb(const float *qn, size_t nq, int d, const uint32_t *p
 // Number of positions where a[i] != b[i] added to *changed.
 cudaError_t launch_count_diff_u8(const uint8_t *a, const uint8_t *b, size_t n,
                                  unsigned int *changed, cudaStream_t s);
+cudaError_t launch_count_diff_u32(const uint32_t *a, const uint32_t *b, size_t n,
+                                  unsigned int *changed, cudaStream_t s);
 
 // ---- scan_kernels.cu ------------------------------------------------------
 

@@ -528,6 +528,66 @@ def flat_search_ip(db, queries, k: int, device: int = 0):
     return out, dists
 
 
+class FlatIndex:
+    """Exhaustive inner-product index over f32 rows (vg_flat_create): the
+    exact top-k by distance -dot (src/distance.rs:125-130), ascending, ties to
+    the lower row -- the ground truth of src/benchmark/evaluation.rs:250-268.
+    Host rows are copied to the device once; a device pointer (``from_device``)
+    is used in place and must outlive the index."""
+
+    def __init__(self, db=None, device: int = 0, *, _ptr_rows=None):
+        self._lib = _lib.load()
+        self._h = C.c_void_p()
+        self.device = device
+        if _ptr_rows is not None:
+            ptr, n, d = _ptr_rows
+            self._keep = None
+        else:
+            x = np.ascontiguousarray(db, dtype=np.float32)
+            if x.ndim != 2:
+                raise ValueError("db must be 2-D")
+            ptr, (n, d) = _ptr(x), x.shape
+            self._keep = x
+        self.n, self.dim = int(n), int(d)
+        _lib.check(self._lib.vg_flat_create(ptr, self.n, self.dim, device, C.byref(self._h)))
+        self._keep = None  # host rows were copied
+
+    @classmethod
+    def from_device(cls, ptr: int, n: int, dim: int, device: int = 0) -> "FlatIndex":
+        return cls(device=device, _ptr_rows=(ptr, n, dim))
+
+    def close(self) -> None:
+        if self._h:
+            self._lib.vg_flat_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):  # pragma: no cover - interpreter shutdown order
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def search(self, queries, k: int):
+        """(ids int64 padded with MISSING_LABEL, distances float32) of every query row."""
+        q = np.ascontiguousarray(queries, dtype=np.float32)
+        if q.ndim != 2 or q.shape[1] != self.dim:
+            raise ValueError(f"queries must be 2-D with dimension {self.dim}")
+        nq = q.shape[0]
+        ids = np.empty((nq, k), dtype=np.uint32)
+        dists = np.empty((nq, k), dtype=np.float32)
+        counts = np.empty(nq, dtype=np.uint32)
+        _lib.check(self._lib.vg_flat_search(self._h, _ptr(q), nq, k, None, _ptr(ids), _ptr(dists), _ptr(counts)))
+        out = ids.astype(np.int64)
+        out[np.arange(k)[None, :] >= counts.astype(np.int64)[:, None]] = MISSING_LABEL
+        return out, dists
+
+    def search_raw(self, q_ptr: int, nq: int, k: int, stream: int | None, ids_ptr: int, dist_ptr: int,
+                   count_ptr: int | None) -> None:
+        """vg_flat_search on raw host or device pointers, on a cudaStream_t handle."""
+        _lib.check(self._lib.vg_flat_search(self._h, q_ptr, nq, k, stream or None, ids_ptr, dist_ptr,
+                                            count_ptr or None))
+
+
 def current_generation(root) -> str:
     """The directory ``root/CURRENT`` names (persistence/generation.rs:191-205)."""
     lib = _lib.load()
