@@ -307,6 +307,12 @@ int vg_flat_destroy(vg_flat *f);
 int vg_flat_search(vg_flat *f, const float *queries, size_t nq, size_t k, void *stream, uint32_t *out_ids,
                    float *out_dist, uint32_t *out_count);
 
+/* Profiling of vg_flat_search calls (on: 1; clears the totals): device time
+ * of the query image (normalize_ms), the tensor-core window kernel (scan_ms)
+ * and the exact re-score (merge_ms), from CUDA events on the search stream. */
+int vg_flat_set_profiling(vg_flat *f, int on);
+int vg_flat_get_profile(const vg_flat *f, vg_search_profile *out);
+
 /* No counterpart in the reference.  vg_flat_search_ip for callers that
  * cannot allocate device memory at search time (memory handed out up front
  * to another allocator or budget, loops that cannot take cudaMalloc's

@@ -141,6 +141,8 @@ SIGNATURES = {
     "vg_flat_create": (_i, [_vp, _sz, _sz, _i, C.POINTER(_vp)]),
     "vg_flat_destroy": (_i, [_vp]),
     "vg_flat_search": (_i, [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _vp]),
+    "vg_flat_set_profiling": (_i, [_vp, _i]),
+    "vg_flat_get_profile": (_i, [_vp, C.POINTER(VgProfile)]),
     "vg_ivfpq_save": (_i, [_vp, C.c_char_p]),
     "vg_ivfpq_load": (_i, [C.c_char_p, _i, C.POINTER(_vp)]),
     "vg_ivfpq_save_generation": (_i, [_vp, C.c_char_p]),

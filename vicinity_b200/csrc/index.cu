@@ -1889,6 +1889,10 @@ struct vg_flat {
   int *h_err = nullptr, *d_err = nullptr;
   std::mutex mu;
   DevBuf q, qimg, eps, ws, dist, chunk, ids, dst, cnt;
+  // profiling: events around the query image, the window kernel and the finisher
+  bool profiling = false;
+  cudaEvent_t ev[4] = {};
+  vg_search_profile prof{};
 };
 
 namespace {
@@ -1975,6 +1979,8 @@ int vg_flat_destroy(vg_flat *f) {
                       &f->ids, &f->dst, &f->cnt})
       b->release();
     if (f->h_err) cudaFreeHost(f->h_err);
+    for (cudaEvent_t e : f->ev)
+      if (e) cudaEventDestroy(e);
     if (f->own_stream) cudaStreamDestroy(f->own_stream);
   }
   delete f;
@@ -2021,9 +2027,15 @@ int vg_flat_search(vg_flat *f, const float *queries, size_t nq, size_t k, void *
     VG_CU(f->qimg.reserve(umma_image_bytes(nq, f->kp)));
     VG_CU(f->eps.reserve(nq * 4));
     VG_CU(f->ws.reserve(tc_select_workspace_bytes(nq, n, static_cast<int>(k), f->num_sms)));
+    if (f->profiling) VG_CU(cudaEventRecord(f->ev[0], s));
     VG_CU(launch_umma_image(dq, nq, static_cast<int>(dim), f->kp, f->qimg.p, f->norm_d.as<float>(), rel, abs_coef,
                             f->eps.as<float>(), s));
     TcSelect t{};
+    if (f->profiling) {
+      t.marks[0] = f->ev[1];
+      t.marks[1] = f->ev[2];
+      t.marks[2] = f->ev[3];
+    }
     t.a_img = f->qimg.p;
     t.q = dq;
     t.rows = nq;
@@ -2053,6 +2065,36 @@ int vg_flat_search(vg_flat *f, const float *queries, size_t nq, size_t k, void *
   VG_CU(cudaStreamSynchronize(s));
   if (const int code = *reinterpret_cast<volatile int *>(f->h_err))
     return fail(VG_ERR_CUDA, "flat search gave up on a bounded device wait (code " + std::to_string(code) + ")");
+  if (f->profiling && f->tc && n) {
+    float a = 0, b = 0, c = 0;
+    cudaEventElapsedTime(&a, f->ev[0], f->ev[1]);
+    cudaEventElapsedTime(&b, f->ev[1], f->ev[2]);
+    cudaEventElapsedTime(&c, f->ev[2], f->ev[3]);
+    f->prof.normalize_ms += a;  // query image
+    f->prof.scan_ms += b;       // tensor-core window kernel
+    f->prof.merge_ms += c;      // exact re-score of the windows
+    f->prof.total_ms += a + b + c;
+    f->prof.calls += 1;
+    f->prof.queries += nq;
+    f->prof.kernel_launches += 3;
+    f->prof.scan_launches += 1;
+  }
+  return VG_OK;
+}
+
+int vg_flat_set_profiling(vg_flat *f, int on) {
+  if (!f) return fail(VG_ERR_INVALID_PARAMETER, "null flat index");
+  DeviceGuard g(f->device);
+  for (cudaEvent_t &e : f->ev)
+    if (!e) VG_CU(cudaEventCreate(&e));
+  f->profiling = on != 0;
+  f->prof = vg_search_profile{};
+  return VG_OK;
+}
+
+int vg_flat_get_profile(const vg_flat *f, vg_search_profile *out) {
+  if (!f || !out) return fail(VG_ERR_INVALID_PARAMETER, "null argument");
+  *out = f->prof;
   return VG_OK;
 }
 

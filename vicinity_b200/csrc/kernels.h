@@ -125,6 +125,7 @@ struct TcSelect {
   uint32_t *out_count;    // [rows] real result counts (nullable)
   ProbeBoundArgs bnd;     // bnd.lb == nullptr: no bounds
   int *error;             // set nonzero when a bounded wait of the kernel gives up
+  cudaEvent_t marks[3];   // recorded (when non-null) before the window kernel, between it and the finisher, after
 };
 size_t tc_select_workspace_bytes(size_t rows, size_t cols, int P, int num_sms);
 cudaError_t launch_tc_select(const TcSelect &t, int num_sms, cudaStream_t s);

@@ -665,9 +665,11 @@ cudaError_t launch_tc_select(const TcSelect &t, int num_sms, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   const size_t units = (t.rows + kTile - 1) / kTile * static_cast<size_t>(sp);
   const unsigned grid = static_cast<unsigned>(std::min<size_t>(units, static_cast<size_t>(num_sms)));
+  if (t.marks[0]) cudaEventRecord(t.marks[0], s);
   tc_window_kernel<<<grid, kWinThreads, smem, s>>>(wp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  if (t.marks[1]) cudaEventRecord(t.marks[1], s);
   FinParams fp{};
   fp.cand = cand;
   fp.count = count;
@@ -686,10 +688,10 @@ cudaError_t launch_tc_select(const TcSelect &t, int num_sms, cudaStream_t s) {
   fp.out_ld = t.out_ld;
   fp.out_count = t.out_count;
   fp.bnd = t.bnd;
-  if (t.P <= 32) return launch_finish<1>(fp, s);
-  if (t.P <= 64) return launch_finish<2>(fp, s);
-  if (t.P <= 128) return launch_finish<4>(fp, s);
-  return launch_finish<8>(fp, s);
+  e = t.P <= 32 ? launch_finish<1>(fp, s) : t.P <= 64 ? launch_finish<2>(fp, s)
+      : t.P <= 128 ? launch_finish<4>(fp, s) : launch_finish<8>(fp, s);
+  if (e == cudaSuccess && t.marks[2]) cudaEventRecord(t.marks[2], s);
+  return e;
 }
 
 }  // namespace vg

@@ -587,6 +587,14 @@ class FlatIndex:
         _lib.check(self._lib.vg_flat_search(self._h, q_ptr, nq, k, stream or None, ids_ptr, dist_ptr,
                                             count_ptr or None))
 
+    def set_profiling(self, on: bool) -> None:
+        _lib.check(self._lib.vg_flat_set_profiling(self._h, 1 if on else 0))
+
+    def profile(self) -> dict:
+        p = _lib.VgProfile()
+        _lib.check(self._lib.vg_flat_get_profile(self._h, C.byref(p)))
+        return {name: getattr(p, name) for name, _ in p._fields_}
+
 
 def current_generation(root) -> str:
     """The directory ``root/CURRENT`` names (persistence/generation.rs:191-205)."""
