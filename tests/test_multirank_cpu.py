@@ -1,21 +1,29 @@
-"""Sharded search logic with world_size 2 on CPU (gloo): each rank scans
-only the lists the engine's packer gives it, the per-rank top-k are
-all-gathered and merged by (distance, id), and the result must equal the
-unsharded search.  Ranks run the CPU oracle; the partition comes from the
-engine library's host-only vg_shard_assign_lists."""
+"""The list-sharded search protocol with world_size 2 on CPU (gloo ranks
+running the oracle).
+
+Each rank owns the lists the engine's packer gives it and searches a batch of
+its own.  The ranks exchange their queries, seed every query's bound with the
+k-th key of its nearest list (found by the rank that owns that list; all-
+reduce min), keep only keys at or below that seed in their own lists, and
+route every query's per-rank top-k back to its rank, which merges them by
+(distance, id).  The merged rows must equal the unsharded search of the same
+queries -- the property the engine's NCCL path
+(vg_ivfpq_shard / vg_ivfpq_search_batch) relies on.  The partition comes from
+the engine library's host-only vg_shard_assign_lists.
+"""
 from __future__ import annotations
 
 import os
 import socket
 
 import numpy as np
-import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
 WORLD = 2
-N, D, L, M, KS, NPROBE, K, NQ = 3000, 16, 24, 4, 16, 6, 10, 40
+N, D, L, M, KS, NPROBE, K, NQ = 3000, 16, 24, 4, 16, 6, 10, 40  # NQ queries per rank
+EMPTY = np.uint64(0xFFFFFFFFFFFFFFFF)
 
 
 def _free_port() -> int:
@@ -27,7 +35,7 @@ def _free_port() -> int:
 def _data():
     rng = np.random.default_rng(5)
     x = rng.standard_normal((N, D)).astype(np.float32)
-    q = rng.standard_normal((NQ, D)).astype(np.float32)
+    q = rng.standard_normal((NQ * WORLD, D)).astype(np.float32)
     import oracle as orc
 
     xn = orc.normalize(x)
@@ -36,53 +44,70 @@ def _data():
     return x, q, cent, cb
 
 
+def _keys(orc, ids, dists, cnt):
+    """(distance order, id) keys of result rows, EMPTY past the count."""
+    out = np.full(ids.shape, EMPTY, dtype=np.uint64)
+    for r in range(ids.shape[0]):
+        for i in range(int(cnt[r])):
+            out[r, i] = (np.uint64(orc.total_order_key(float(dists[r, i]))) << np.uint64(32)) | np.uint64(ids[r, i])
+    return out
+
+
 def _rank_main(rank, port, out_path):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=WORLD)
     import oracle as orc
     from vicinity_b200.ivf_pq import shard_assign_lists
 
-    x, q, cent, cb = _data()
-    ix = orc.OracleIndex(D, L, M, KS, NPROBE)
-    ix.set_trained(cent, cb)
-    ix.add(np.arange(N, dtype=np.uint32), x)  # doc id == internal id
-    ix.finalize()
-    sizes = np.diff(ix.list_offsets())
-    owner = shard_assign_lists(sizes, WORLD)
-    # this rank's shard: rebuild with foreign lists emptied (same codes, same
-    # probes: centroids stay replicated, only the scanned lists differ)
-    assign = ix.assignments()
+    x, q_all, cent, cb = _data()
+    full = orc.OracleIndex(D, L, M, KS, NPROBE)
+    full.set_trained(cent, cb)
+    full.add(np.arange(N, dtype=np.uint32), x)  # doc id == internal id
+    full.finalize()
+    owner = shard_assign_lists(np.diff(full.list_offsets()), WORLD)
+    assign = full.assignments()
     mine = owner[assign] == rank
+    # this rank's shard: foreign lists emptied (same codes; centroids stay
+    # whole, so every rank selects the same probes)
     shard = orc.OracleIndex(D, L, M, KS, NPROBE)
     shard.set_trained(cent, cb)
     shard.add(np.nonzero(mine)[0].astype(np.uint32), x[mine])
-    shard.adopt_codes(assign[mine], ix.codes()[mine])
+    shard.adopt_codes(assign[mine], full.codes()[mine])
+
+    # 1-2. every rank holds the global batch (its own rows at rank * NQ)
+    own = torch.from_numpy(np.ascontiguousarray(q_all[rank * NQ:(rank + 1) * NQ]))
+    parts = [torch.empty_like(own) for _ in range(WORLD)]
+    dist.all_gather(parts, own)
+    q = torch.cat(parts).numpy()
+    # 3. seed: the k-th key of each query's nearest list, from its owner
+    sid, sd, sc = shard.search_batch(q, K, nprobe=1)
+    seed = _keys(orc, sid, sd, sc)[:, K - 1]
+    seed_t = torch.from_numpy(seed.view(np.int64).copy())
+    # keys compare unsigned: all-reduce the order-preserving signed image
+    seed_t ^= torch.tensor(np.int64(-0x8000000000000000))
+    dist.all_reduce(seed_t, op=dist.ReduceOp.MIN)
+    seed_t ^= torch.tensor(np.int64(-0x8000000000000000))
+    ceiling = seed_t.numpy().view(np.uint64)
+    # 4. own lists for the global batch, keys at or below the ceiling only
     ids, dists, cnt = shard.search_batch(q, K)
-    packed = torch.from_numpy(np.stack([ids.astype(np.int64), dists.view(np.int32).astype(np.int64)], -1))
-    gathered = [torch.empty_like(packed) for _ in range(WORLD)]
-    dist.all_gather(gathered, packed)
-    if rank == 0:
-        keys = []
-        for g in gathered:
-            a = g.numpy()
-            keys.append((a[..., 0], a[..., 1].astype(np.int32).view(np.float32)))
-        merged = np.empty((NQ, K), np.int64)
-        for r in range(NQ):
-            cands = []
-            for ids_g, d_g in keys:
-                for i, dd in zip(ids_g[r], d_g[r]):
-                    if i != 0xFFFFFFFF:
-                        cands.append((orc.total_order_key(float(dd)), int(i)))
-            cands.sort()
-            merged[r] = [c[1] for c in cands[:K]]
-        full_ids, _, _ = ix.search_batch(q, K)
-        np.save(out_path, np.stack([merged, full_ids.astype(np.int64)]))
+    keys = _keys(orc, ids, dists, cnt)
+    keys[keys > ceiling[:, None]] = EMPTY
+    # 5. route every query's keys to its rank and merge
+    parts = [torch.empty((NQ * WORLD, K), dtype=torch.int64) for _ in range(WORLD)]
+    dist.all_gather(parts, torch.from_numpy(keys.view(np.int64)))
+    got = np.concatenate([p.numpy().view(np.uint64)[rank * NQ:(rank + 1) * NQ] for p in parts], axis=1)
+    merged = np.sort(got, axis=1)[:, :K]
+    fid, fd, fc = full.search_batch(q[rank * NQ:(rank + 1) * NQ], K)
+    np.save(f"{out_path}.{rank}.npy", np.stack([merged.view(np.int64), _keys(orc, fid, fd, fc).view(np.int64)]))
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_two_rank_sharded_merge_equals_unsharded(tmp_path):
-    out = tmp_path / "merged.npy"
+def test_two_rank_sharded_search_equals_unsharded(tmp_path):
+    out = tmp_path / "merged"
     mp.start_processes(_rank_main, args=(_free_port(), str(out)), nprocs=WORLD, start_method="spawn", join=True)
-    merged, full = np.load(out)
-    assert np.array_equal(merged, full)
+    for rank in range(WORLD):
+        merged, full = np.load(f"{out}.{rank}.npy")
+        assert np.array_equal(merged, full), f"rank {rank}"
+        # the seed bounded every query: at least one key survived per row
+        assert (merged[:, 0] != -1).all()

@@ -197,16 +197,21 @@ struct vg_index {
   DevBuf category_d, bitmask_d, cat_counts;        // [n] u8, [num_clusters] u64, [Lc][64] u32
   bool cat_dirty = true;                           // categories changed since the last upload
 
-  // sharding
+  // sharding: lists owned by this rank (owner[l] != 0); once sharded, the
+  // device list layout (list_off, code_off, pack_off, list_ids, list_codes,
+  // packed) holds this rank's lists only (other lists empty) and the
+  // insertion-order codes and assignments are dropped
   int rank = 0, world = 1;
   ncclComm_t comm = nullptr;
   int comm_timeout_ms = 60000;
   DevBuf owner;
+  bool partitioned = false;
+  DevBuf ws_seed;  // [world * nq] u64 seed keys of a sharded search
 
   // search workspace
   DevBuf ws_q, ws_qn, ws_dist, ws_probes, ws_pdist, ws_scalars,
       ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_lb, ws_rec, ws_lbq, ws_qimg, ws_eps, ws_tc,
-      ws_floor;
+      ws_floor, ws_qall;
   DevBuf stats;  // u64 [pairs, vectors, code bytes, scored lists, scored vectors] while profiling
 
   // error flag of bounded device waits, in mapped pinned host memory
@@ -329,6 +334,14 @@ bool tc_disabled() {
 bool coarse_on_tensor_cores(const vg_index *ix, size_t P) {
   return !tc_disabled() && ix->cent_kp && ix->num_centroids >= kTcMinLists && P >= 1 && P <= 256 &&
          std::isfinite(ix->h_cmax) && ix->h_cmax < 100.0f;
+}
+
+// Probe selection on the tensor cores: up to 128 probes the binary16 product
+// matrix (tile by tile, at most 1 GiB) and the probe shortlist; beyond, the
+// fused candidate window.
+constexpr size_t kShortlistMaxProbes = 128;
+bool coarse_via_products(const vg_index *ix, size_t P) {
+  return coarse_on_tensor_cores(ix, P) && P <= kShortlistMaxProbes;
 }
 
 // Largest centroid norm (device and host copies) and the binary16 operand
@@ -696,19 +709,30 @@ int encode_and_layout(vg_index *ix) {
 // CSR offsets), ix->list_ids (device, vector ids in list order) and
 // sorted_lists (device, the list of every position).  Gathers list_codes and,
 // for 16-entry codebooks, the nibble-packed scan copy.
+// 16-byte aligned byte offsets of every list's codes (M bytes per vector)
+// and, for 16-entry codebooks, of its nibble-packed scan copy (lists of at
+// least 16 vectors, ceil(M/2) bytes per vector), from CSR offsets `off`.
+void list_layout(const std::vector<uint64_t> &off, size_t Lc, size_t M, size_t ks, std::vector<uint64_t> &code_off,
+                 std::vector<uint64_t> &pack_off, uint64_t &code_bytes, uint64_t &pack_bytes) {
+  code_off.assign(Lc, 0);
+  pack_off.assign(Lc, 0);
+  code_bytes = pack_bytes = 0;
+  for (size_t l = 0; l < Lc; ++l) {
+    const uint64_t len = off[l + 1] - off[l];
+    code_off[l] = code_bytes;
+    code_bytes += (len * M + 15) & ~uint64_t(15);
+    pack_off[l] = pack_bytes;
+    if (ks == 16 && len >= 16) pack_bytes += (len * ((M + 1) / 2) + 15) & ~uint64_t(15);
+  }
+}
+
 int build_list_storage(vg_index *ix, const uint32_t *sorted_lists) {
   cudaStream_t s = ix->stream;
   const size_t n = ix->n, M = ix->params.num_codebooks, ks = ix->params.codebook_size;
   const size_t Lc = ix->num_centroids;
-  std::vector<uint64_t> h_code_off(Lc), h_pack_off(Lc);
+  std::vector<uint64_t> h_code_off, h_pack_off;
   uint64_t code_bytes = 0, pack_bytes = 0;
-  for (size_t l = 0; l < Lc; ++l) {
-    uint64_t len = ix->h_list_off[l + 1] - ix->h_list_off[l];
-    h_code_off[l] = code_bytes;
-    code_bytes += (len * M + 15) & ~uint64_t(15);
-    h_pack_off[l] = pack_bytes;
-    if (ks == 16 && len >= 16) pack_bytes += (len * ((M + 1) / 2) + 15) & ~uint64_t(15);
-  }
+  list_layout(ix->h_list_off, Lc, M, ks, h_code_off, h_pack_off, code_bytes, pack_bytes);
   VG_CU(ix->list_off.reserve((Lc + 1) * 8));
   VG_CU(ix->code_off.reserve(Lc * 8));
   VG_CU(ix->pack_off.reserve(Lc * 8));
@@ -738,6 +762,75 @@ int build_list_storage(vg_index *ix, const uint32_t *sorted_lists) {
   return VG_OK;
 }
 
+// Keep only the lists this rank owns (mine[l] != 0): the device layout is
+// rebuilt with every other list empty (list_off, code_off, pack_off) and the
+// owned lists' ids, codes and packed codes gathered; the insertion-order codes
+// and assignments are released.  Centroids, codebooks, pruning radii and the
+// doc-id map stay whole (every rank selects probes and maps ids).
+int partition_lists(vg_index *ix, const std::vector<uint8_t> &mine) {
+  cudaStream_t s = ix->stream;
+  const size_t Lc = ix->num_centroids, M = ix->params.num_codebooks, ks = ix->params.codebook_size;
+  const std::vector<uint64_t> &goff = ix->h_list_off;
+  std::vector<uint64_t> gcode, gpack, lcode, lpack, loff(Lc + 1, 0);
+  uint64_t gcb = 0, gpb = 0, lcb = 0, lpb = 0;
+  list_layout(goff, Lc, M, ks, gcode, gpack, gcb, gpb);
+  for (size_t l = 0; l < Lc; ++l) loff[l + 1] = loff[l] + (mine[l] ? goff[l + 1] - goff[l] : 0);
+  list_layout(loff, Lc, M, ks, lcode, lpack, lcb, lpb);
+  // segments to gather: ids, codes and (4-bit) packed codes of owned lists
+  std::vector<uint64_t> seg;  // [3][count] src, dst, bytes per table
+  auto build = [&](int table, std::vector<uint64_t> &src, std::vector<uint64_t> &dst, std::vector<uint64_t> &bytes) {
+    for (size_t l = 0; l < Lc; ++l) {
+      const uint64_t len = goff[l + 1] - goff[l];
+      if (!mine[l] || len == 0) continue;
+      if (table == 0) {
+        src.push_back(goff[l] * 4);
+        dst.push_back(loff[l] * 4);
+        bytes.push_back(len * 4);
+      } else if (table == 1) {
+        src.push_back(gcode[l]);
+        dst.push_back(lcode[l]);
+        bytes.push_back(len * M);
+      } else if (len >= 16) {
+        src.push_back(gpack[l]);
+        dst.push_back(lpack[l]);
+        bytes.push_back(len * ((M + 1) / 2));
+      }
+    }
+  };
+  DevBuf n_ids, n_codes, n_packed, offs;
+  VG_CU(n_ids.reserve(std::max<uint64_t>(loff[Lc] * 4, 16)));
+  VG_CU(n_codes.reserve(std::max<uint64_t>(lcb, 16)));
+  if (ks == 16) VG_CU(n_packed.reserve(std::max<uint64_t>(lpb, 16)));
+  for (int table = 0; table < (ks == 16 ? 3 : 2); ++table) {
+    std::vector<uint64_t> src, dst, bytes;
+    build(table, src, dst, bytes);
+    const size_t cnt = src.size();
+    if (!cnt) continue;
+    std::vector<uint64_t> h(3 * cnt);
+    std::copy(src.begin(), src.end(), h.begin());
+    std::copy(dst.begin(), dst.end(), h.begin() + cnt);
+    std::copy(bytes.begin(), bytes.end(), h.begin() + 2 * cnt);
+    VG_CU(offs.reserve(h.size() * 8));
+    VG_CU(cudaMemcpyAsync(offs.p, h.data(), h.size() * 8, cudaMemcpyHostToDevice, s));
+    const void *from = table == 0 ? ix->list_ids.p : table == 1 ? ix->list_codes.p : ix->packed.p;
+    void *to = table == 0 ? n_ids.p : table == 1 ? n_codes.p : n_packed.p;
+    VG_CU(launch_copy_segments(from, to, offs.as<uint64_t>(), offs.as<uint64_t>() + cnt, offs.as<uint64_t>() + 2 * cnt,
+                               cnt, s));
+    VG_CU(cudaStreamSynchronize(s));  // offs is reused by the next table
+  }
+  VG_CU(cudaMemcpyAsync(ix->list_off.p, loff.data(), (Lc + 1) * 8, cudaMemcpyHostToDevice, s));
+  VG_CU(cudaMemcpyAsync(ix->code_off.p, lcode.data(), Lc * 8, cudaMemcpyHostToDevice, s));
+  VG_CU(cudaMemcpyAsync(ix->pack_off.p, lpack.data(), Lc * 8, cudaMemcpyHostToDevice, s));
+  VG_CU(cudaStreamSynchronize(s));
+  ix->list_ids = std::move(n_ids);
+  ix->list_codes = std::move(n_codes);
+  if (ks == 16) ix->packed = std::move(n_packed);
+  ix->codes.release();
+  ix->assign.release();
+  ix->partitioned = true;
+  return VG_OK;
+}
+
 // ---- search -------------------------------------------------------------
 
 // The nprobe nearest lists of rows normalised queries qn (search.rs:1602-1617:
@@ -753,6 +846,27 @@ int coarse_probes(vg_index *ix, const float *qn, size_t rows, size_t P, uint32_t
   if (bounds_done) *bounds_done = false;
   cudaStream_t s = ix->stream;
   const size_t Lc = ix->num_centroids, d = ix->d;
+  if (coarse_via_products(ix, P)) {
+    // binary16 products of the tile (f32 accumulation, rounded once more to
+    // binary16: 2^-11 of |q| |c| on top of the window's coefficients), then the
+    // shortlist re-scores every list the bound cannot rule out
+    const int kp = ix->cent_kp;
+    double rel = 0, abs_coef = 0;
+    tc_error_coefs(static_cast<int>(d), &rel, &abs_coef);
+    rel += 1.0 / 2048;
+    VG_CU(ix->ws_qimg.reserve(umma_image_bytes(rows, kp)));
+    VG_CU(ix->ws_dist.reserve(std::max<size_t>(rows * Lc, 1) * 2));
+    VG_CU(launch_umma_image(qn, rows, static_cast<int>(d), kp, ix->ws_qimg.p, nullptr, 0.0, 0.0, nullptr, s));
+    VG_CU(launch_tc_gemm_f16(ix->ws_qimg.p, rows, ix->cent_img.p, Lc, static_cast<int>(d), kp, ix->ws_dist.p, Lc,
+                             ix->d_err, ix->num_sms, s));
+    mark(ix, 3);
+    VG_CU(launch_probe_shortlist(ix->ws_dist.p, true, rows, Lc, Lc, qn, static_cast<int>(d),
+                                 ix->centroids.as<float>(), ix->cent_norm.as<float>(), rel, abs_coef,
+                                 static_cast<int>(P), probes, pdist, P, bounds ? *bounds : ProbeBoundArgs{}, s));
+    *launches += 3;
+    if (bounds_done) *bounds_done = bounds != nullptr;
+    return VG_OK;
+  }
   if (coarse_on_tensor_cores(ix, P)) {
     const int kp = ix->cent_kp;
     double rel = 0, abs_coef = 0;
@@ -800,7 +914,9 @@ int coarse_probes(vg_index *ix, const float *qn, size_t rows, size_t P, uint32_t
 size_t coarse_tile(const vg_index *ix, size_t nq, size_t P) {
   const size_t Lc = std::max<size_t>(ix->num_centroids, 1);
   size_t tile;
-  if (coarse_on_tensor_cores(ix, P)) {
+  if (coarse_via_products(ix, P)) {
+    tile = std::max<size_t>(128, kDistBudgetBytes / (Lc * 2));
+  } else if (coarse_on_tensor_cores(ix, P)) {
     const size_t est = std::min<size_t>(std::max<size_t>(nq, 1), size_t(1) << 20);
     const size_t per_row = tc_select_workspace_bytes(est, Lc, static_cast<int>(P), ix->num_sms) / est + 1;
     tile = std::max<size_t>(1024, kDistBudgetBytes / per_row);
@@ -832,7 +948,7 @@ vg::ScanParams base_scan_params(vg_index *ix, size_t P, size_t kk, bool prune, b
   sp.centroids = ix->centroids.as<float>();
   sp.codebooks = ix->codebooks.as<float>();
   sp.probes = ix->ws_probes.as<uint32_t>();
-  sp.owner = ix->world > 1 ? ix->owner.as<uint8_t>() : nullptr;
+  sp.owner = ix->world > 1 ? ix->owner.as<uint8_t>() : nullptr;  // (the sharded search sets it)
   sp.list_off = ix->list_off.as<uint64_t>();
   sp.code_off = ix->code_off.as<uint64_t>();
   sp.list_codes = ix->list_codes.as<uint8_t>();
@@ -864,19 +980,224 @@ ProbeBoundArgs bound_args_at(vg_index *ix, size_t P, size_t r0, bool prune, bool
                         quant ? ix->ws_lbq.as<float>() + r0 * P : nullptr};
 }
 
+int nccl_ok(vg_index *ix, ncclResult_t r, const char *what) {
+  if (r == ncclSuccess) return VG_OK;
+  if (r == ncclInProgress) return nccl_wait_ready(ix->comm, ix->comm_timeout_ms);
+  return fail(VG_ERR_NCCL, std::string(what) + ": " + ncclGetErrorString(r));
+}
+
+// Search on a list-sharded index (every rank holds the lists it owns).  Each
+// rank passes a batch of its own, the same size on every rank, and receives
+// the results of its own queries:
+//   1. normalise and select the probes of its own queries (with their
+//      pruning bounds, valid on every rank);
+//   2. all-gather queries, probes and bounds: every rank holds the global
+//      batch (world * nq rows, rank r's rows at r * nq);
+//   3. seed: every rank scans, for every query, the query's nearest list when
+//      it owns it, and keeps that list's k-th key; an all-reduce (min) gives
+//      every query the k-th key of its nearest list -- a bound on its k-th key
+//      over every list, so each rank prunes from the start as one GPU would;
+//   4. every rank scans its lists for the global batch, keeping only keys at
+//      or below the ceiling;
+//   5. an all-to-all returns every query's per-rank top-k to the query's rank,
+//      which merges them (the reference's per-shard top-k merge,
+//      examples/large_scale.rs:1969-2025).
+// Without pruning bounds (an OPQ rotation) the seed is skipped.
+int search_sharded(vg_index *ix, const float *queries, size_t nq, size_t k, size_t pool, size_t nprobe,
+                   uint32_t *out_ids, float *out_dist, uint32_t *out_count) {
+  const bool rerank = pool > 0;
+  if (rerank && ix->compacted)
+    return fail(VG_ERR_UNSUPPORTED,
+                "unsupported: search_reranked after compact(); use search() instead, or keep raw vectors");
+  const size_t kk = rerank ? std::max(pool, k) : k;
+  if (kk > 256) return fail(VG_ERR_UNSUPPORTED, "unsupported: candidate_pool above 256 on a sharded index");
+  const size_t Lc = ix->num_centroids, d = ix->d, M = ix->params.num_codebooks;
+  const size_t P = std::min(nprobe ? nprobe : static_cast<size_t>(ix->params.nprobe), Lc);
+  if (nq == 0 || k == 0 || P == 0) return write_padding(ix, nq, k, out_ids, out_dist, out_count);
+  if (!queries || !out_ids || !out_dist) return fail(VG_ERR_INVALID_PARAMETER, "null query or output buffer");
+  const size_t W = static_cast<size_t>(ix->world), R = static_cast<size_t>(ix->rank), B = W * nq;
+  if (B * P > 0xffffffffull || B > 0x7fffffffull)
+    return fail(VG_ERR_INVALID_PARAMETER, "world_size * nq * nprobe must fit in 32 bits");
+  cudaStream_t s = ix->stream;
+  const bool prof = ix->profiling;
+  const uint64_t launches0 = ix->launches;
+  ix->tile_marks = nullptr;
+  *reinterpret_cast<volatile int *>(ix->h_err) = 0;
+  mark(ix, 0);
+  const float *dq = queries;
+  if (!is_device_ptr(queries)) {
+    VG_CU(ix->ws_q.reserve(nq * d * 4));
+    VG_CU(cudaMemcpyAsync(ix->ws_q.p, queries, nq * d * 4, cudaMemcpyHostToDevice, s));
+    dq = ix->ws_q.as<float>();
+  }
+  mark(ix, 1);
+  const bool prune = ix->h_rotation.empty();
+  const bool recs = prune && ix->params.codebook_size == 256;
+  const bool quant = prune && ix->params.codebook_size == 16;
+  VG_CU(ix->ws_qall.reserve(B * d * 4));
+  VG_CU(ix->ws_probes.reserve(B * P * 4));
+  VG_CU(ix->ws_pdist.reserve(B * P * 4));
+  VG_CU(ix->ws_lb.reserve(B * P * 4));
+  if (quant) VG_CU(ix->ws_lbq.reserve(B * P * 4));
+  if (recs) VG_CU(ix->ws_rec.reserve(B * P * sizeof(ProbeRec)));
+  VG_CU(ix->ws_seed.reserve(B * 8));
+  VG_CU(ix->ws_keys.reserve(B * kk * 8));
+  VG_CU(ix->ws_all_keys.reserve(B * kk * 8));
+  float *qall = ix->ws_qall.as<float>(), *qown = qall + R * nq * d;
+  uint32_t *pown = ix->ws_probes.as<uint32_t>() + R * nq * P;
+  VG_CU(launch_normalize_rows(dq, nq, static_cast<int>(d), qown, s));
+  ix->launches += 1;
+  mark(ix, 2);
+
+  // 1. probes of this rank's queries, with bounds for every probe
+  const size_t tile = coarse_tile(ix, nq, P);
+  for (size_t r0 = 0; r0 < nq; r0 += tile) {
+    const size_t rows = std::min(tile, nq - r0);
+    ProbeBoundArgs ba = bound_args_at(ix, P, R * nq + r0, prune, false, quant);
+    ba.owner = nullptr;  // bounds of every probe: other ranks scan with them
+    bool done = false;
+    VG_TRY(coarse_probes(ix, qown + r0 * d, rows, P, pown + r0 * P, ix->ws_pdist.as<float>() + (R * nq + r0) * P,
+                         &ix->launches, prune ? &ba : nullptr, &done));
+    if (prune && !done) {
+      VG_CU(launch_probe_lb(qown + r0 * d, rows, static_cast<int>(d), pown + r0 * P, static_cast<int>(P),
+                            ix->centroids.as<float>(), ba, s));
+      ix->launches += 1;
+    }
+  }
+  mark(ix, 4);
+
+  // 2. the global batch on every rank (in place: rank r's block is its own)
+  VG_TRY(nccl_ok(ix, ncclGroupStart(), "ncclGroupStart"));
+  ncclAllGather(qown, qall, nq * d, ncclFloat32, ix->comm, s);
+  ncclAllGather(pown, ix->ws_probes.p, nq * P, ncclUint32, ix->comm, s);
+  if (prune) ncclAllGather(ix->ws_lb.as<float>() + R * nq * P, ix->ws_lb.p, nq * P, ncclFloat32, ix->comm, s);
+  if (quant) ncclAllGather(ix->ws_lbq.as<float>() + R * nq * P, ix->ws_lbq.p, nq * P, ncclFloat32, ix->comm, s);
+  VG_TRY(nccl_ok(ix, ncclGroupEnd(), "ncclAllGather (queries, probes, bounds)"));
+  mark(ix, 5);
+  if (recs) {
+    VG_CU(launch_probe_records(ix->ws_probes.as<uint32_t>(), ix->ws_lb.as<float>(), B * P, ix->owner.as<uint8_t>(),
+                               ix->list_off.as<uint64_t>(), ix->code_off.as<uint64_t>(), ix->ws_rec.as<ProbeRec>(),
+                               s));
+    ix->launches += 1;
+  }
+  VG_CU(ix->ws_scalars.reserve(64));
+  uint32_t *d_counter = ix->ws_scalars.as<uint32_t>();
+  vg::ScanParams sp = base_scan_params(ix, P, kk, prune, recs, quant);
+  sp.qn = qall;
+  sp.owner = ix->owner.as<uint8_t>();
+  sp.counter = d_counter;
+  sp.scored = prof ? ix->stats.as<unsigned long long>() + 3 : nullptr;
+  sp.nq = static_cast<int>(B);
+  sp.force_warp = 1;
+  if (prof) {
+    VG_CU(launch_probe_stats(ix->ws_probes.as<uint32_t>(), B, static_cast<int>(P), ix->owner.as<uint8_t>(), Lc,
+                             ix->list_off.as<uint64_t>(), static_cast<int>(M), ix->params.codebook_size == 16,
+                             ix->stats.as<unsigned long long>(), s));
+  }
+
+  // 3. seed: the k-th key of every query's nearest list
+  const bool seeded = prune && ivfpq_scan_warp_applies(sp);
+  if (seeded) {
+    sp.pscan = 1;
+    sp.out_kth = ix->ws_seed.as<unsigned long long>();
+    VG_CU(cudaMemsetAsync(d_counter, 0, 4, s));
+    VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
+    ix->launches += 1;
+    mark(ix, 6);
+    VG_TRY(nccl_ok(ix, ncclAllReduce(ix->ws_seed.p, ix->ws_seed.p, B, ncclUint64, ncclMin, ix->comm, s),
+                   "ncclAllReduce (seed keys)"));
+    sp.pscan = 0;
+    sp.out_kth = nullptr;
+    sp.key_ceiling = ix->ws_seed.as<unsigned long long>();
+  } else {
+    mark(ix, 6);
+  }
+  mark(ix, 7);
+
+  // 4. this rank's lists for the global batch
+  sp.out_keys = ix->ws_keys.as<unsigned long long>();
+  VG_CU(cudaMemsetAsync(d_counter, 0, 4, s));
+  VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
+  ix->launches += 1;
+  mark(ix, 8);
+
+  // 5. every query's per-rank keys to its rank: [W][nq][kk]
+  VG_TRY(nccl_ok(ix, ncclGroupStart(), "ncclGroupStart"));
+  for (size_t r = 0; r < W; ++r) {
+    ncclSend(ix->ws_keys.as<unsigned long long>() + r * nq * kk, nq * kk, ncclUint64, static_cast<int>(r), ix->comm, s);
+    ncclRecv(ix->ws_all_keys.as<unsigned long long>() + r * nq * kk, nq * kk, ncclUint64, static_cast<int>(r), ix->comm,
+             s);
+  }
+  VG_TRY(nccl_ok(ix, ncclGroupEnd(), "ncclSend/ncclRecv (per-rank keys)"));
+  mark(ix, 9);
+  const bool dev_out = is_device_ptr(out_ids) && is_device_ptr(out_dist) && (!out_count || is_device_ptr(out_count));
+  uint32_t *o_ids = out_ids, *o_cnt = out_count;
+  float *o_dist = out_dist;
+  if (!dev_out) {
+    VG_CU(ix->ws_out_ids.reserve(nq * k * 4));
+    VG_CU(ix->ws_out_dist.reserve(nq * k * 4));
+    VG_CU(ix->ws_out_count.reserve(nq * 4));
+    o_ids = ix->ws_out_ids.as<uint32_t>();
+    o_dist = ix->ws_out_dist.as<float>();
+    o_cnt = ix->ws_out_count.as<uint32_t>();
+  }
+  const uint32_t *doc_map = ix->doc_ids.as<uint32_t>();
+  if (rerank) {
+    VG_CU(launch_merge_shards(ix->ws_all_keys.as<unsigned long long>(), static_cast<int>(W), nq, static_cast<int>(kk),
+                              nullptr, nullptr, nullptr, nullptr, ix->ws_keys.as<unsigned long long>(), s));
+    VG_CU(launch_rerank(qown, ix->vectors.as<float>(), static_cast<int>(d), ix->ws_keys.as<unsigned long long>(), nq,
+                        static_cast<int>(kk), static_cast<int>(k), doc_map, o_ids, o_dist, o_cnt, s));
+    ix->launches += 2;
+  } else {
+    VG_CU(launch_merge_shards(ix->ws_all_keys.as<unsigned long long>(), static_cast<int>(W), nq, static_cast<int>(k),
+                              doc_map, o_ids, o_dist, o_cnt, nullptr, s));
+    ix->launches += 1;
+  }
+  mark(ix, 10);
+  if (!dev_out) {
+    VG_CU(cudaMemcpyAsync(out_ids, o_ids, nq * k * 4, cudaMemcpyDeviceToHost, s));
+    VG_CU(cudaMemcpyAsync(out_dist, o_dist, nq * k * 4, cudaMemcpyDeviceToHost, s));
+    if (out_count) VG_CU(cudaMemcpyAsync(out_count, o_cnt, nq * 4, cudaMemcpyDeviceToHost, s));
+  }
+  mark(ix, 11);
+  VG_TRY(sync_stream(ix));
+  VG_TRY(check_device_error(ix, "sharded search"));
+  if (prof) {
+    auto el = [&](int a, int b) {
+      float ms = 0;
+      cudaEventElapsedTime(&ms, ix->ev[a], ix->ev[b]);
+      return static_cast<double>(ms);
+    };
+    vg_search_profile &pf = ix->prof;
+    pf.h2d_ms += el(0, 1);
+    pf.normalize_ms += el(1, 2);
+    pf.coarse_ms += el(2, 3);
+    pf.select_ms += el(3, 4);
+    pf.collective_ms += el(4, 5) + (seeded ? el(6, 7) : 0.0) + el(8, 9);
+    pf.pairs_ms += el(5, 6);  // probe records and the seed scan
+    pf.scan_ms += el(7, 8);
+    pf.merge_ms += el(9, 10);
+    pf.d2h_ms += el(10, 11);
+    pf.total_ms += el(0, 11);
+    pf.calls += 1;
+    pf.queries += nq;
+    pf.kernel_launches += ix->launches - launches0;
+    pf.scan_launches += seeded ? 2 : 1;
+  }
+  return VG_OK;
+}
+
 int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t pool, size_t nprobe,
                 uint32_t *out_ids, float *out_dist, uint32_t *out_count) {
   if (!ix->built) return fail(VG_ERR_NOT_BUILT, "IVF-PQ index is not built: cannot search");
   if (k > 256) return fail(VG_ERR_INVALID_PARAMETER, "k must be at most 256");
+  if (ix->world > 1) return search_sharded(ix, queries, nq, k, pool, nprobe, out_ids, out_dist, out_count);
   ix->tile_marks = nullptr;  // a call that failed mid-stage may have left it set
   const bool rerank = pool > 0;
   if (rerank && ix->compacted)
     return fail(VG_ERR_UNSUPPORTED,
                 "unsupported: search_reranked after compact(); use search() instead, or keep raw vectors");
   const size_t kk = rerank ? std::max(pool, k) : k;
-  // pools above 256 are selected in passes of 256 on one device
-  if (kk > 256 && ix->world > 1)
-    return fail(VG_ERR_UNSUPPORTED, "unsupported: candidate_pool above 256 on a sharded index");
   if (kk > (size_t{1} << 20)) return fail(VG_ERR_INVALID_PARAMETER, "candidate_pool must be at most 1048576");
   if (nq == 0 || k == 0) return write_padding(ix, nq, k, out_ids, out_dist, out_count);
   if ((nq && !queries) || !out_ids || !out_dist)
@@ -970,7 +1291,7 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
     o_cnt = ix->ws_out_count.as<uint32_t>();
   }
   const uint32_t *doc_map = ix->doc_ids.as<uint32_t>();
-  const bool direct = ix->world == 1 && !rerank;  // the kernel writes final results
+  const bool direct = !rerank;  // the kernel writes final results
 
   vg::ScanParams sp = base_scan_params(ix, P, kk, prune, recs, quant);
   sp.counter = d_counter;
@@ -1012,33 +1333,12 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   }
   mark(ix, 6);
 
-  if (!direct && ix->world == 1) {  // rerank on one device
-    mark(ix, 7);
+  mark(ix, 7);
+  if (rerank) {
     VG_CU(launch_rerank(ix->ws_qn.as<float>(), ix->vectors.as<float>(), static_cast<int>(d),
                         ix->ws_keys.as<unsigned long long>(), nq, static_cast<int>(kk), static_cast<int>(k),
                         doc_map, o_ids, o_dist, o_cnt, s));
     ix->launches += 1;
-  } else if (ix->world > 1) {
-    VG_CU(ix->ws_all_keys.reserve(static_cast<size_t>(ix->world) * nq * kk * 8));
-    mark(ix, 7);
-    ncclResult_t r = ncclAllGather(ix->ws_keys.p, ix->ws_all_keys.p, nq * kk, ncclUint64, ix->comm, s);
-    if (r == ncclInProgress) VG_TRY(nccl_wait_ready(ix->comm, ix->comm_timeout_ms));
-    else if (r != ncclSuccess) return fail(VG_ERR_NCCL, std::string("ncclAllGather: ") + ncclGetErrorString(r));
-    mark(ix, 8);
-    if (rerank) {
-      VG_CU(launch_merge_shards(ix->ws_all_keys.as<unsigned long long>(), ix->world, nq, static_cast<int>(kk),
-                                nullptr, nullptr, nullptr, nullptr, ix->ws_keys.as<unsigned long long>(), s));
-      VG_CU(launch_rerank(ix->ws_qn.as<float>(), ix->vectors.as<float>(), static_cast<int>(d),
-                          ix->ws_keys.as<unsigned long long>(), nq, static_cast<int>(kk), static_cast<int>(k),
-                          doc_map, o_ids, o_dist, o_cnt, s));
-      ix->launches += 2;
-    } else {
-      VG_CU(launch_merge_shards(ix->ws_all_keys.as<unsigned long long>(), ix->world, nq, static_cast<int>(k),
-                                doc_map, o_ids, o_dist, o_cnt, nullptr, s));
-      ix->launches += 1;
-    }
-  } else {
-    mark(ix, 7);
   }
   mark(ix, 9);
   if (!dev_out) {
@@ -1073,12 +1373,7 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
     }
     p.pairs_ms += el(4, 5);
     p.scan_ms += el(5, 6);
-    if (ix->world > 1) {
-      p.merge_ms += el(6, 7) + el(8, 9);
-      p.collective_ms += el(7, 8);
-    } else {
-      p.merge_ms += el(6, 7) + el(7, 9);
-    }
+    p.merge_ms += el(6, 9);
     p.d2h_ms += el(9, 10);
     p.total_ms += el(0, 10);
     p.calls += 1;
@@ -1266,6 +1561,8 @@ void set_last_error(const char *msg) { g_last_error = msg; }
 
 int snapshot_export(const vg_index *ix, SnapshotState &st) {
   if (!ix->built) return fail(VG_ERR_NOT_BUILT, "IVF-PQ index is not built: cannot save");
+  if (ix->partitioned)
+    return fail(VG_ERR_UNSUPPORTED, "unsupported: saving a list-sharded index (each rank holds its lists only)");
   DeviceGuard g(ix->device);
   const size_t n = ix->n, d = ix->d, M = ix->params.num_codebooks, ks = ix->params.codebook_size;
   const size_t Lc = ix->num_centroids, L = ix->params.num_clusters;
@@ -1437,9 +1734,7 @@ int vg_ivfpq_create(size_t dim, const vg_ivfpq_params *params, int device, vg_in
     e = cudaHostGetDevicePointer(reinterpret_cast<void **>(&ix->d_err), ix->h_err, 0);
   }
   if (const char *fam = std::getenv("VICINITY_SCAN_KERNEL"))
-    vg::set_scan_family(std::strcmp(fam, "pipeline") == 0 ? 0
-                        : std::strcmp(fam, "query") == 0  ? 1
-                        : std::strcmp(fam, "double") == 0 ? 2
+    vg::set_scan_family(std::strcmp(fam, "query") == 0    ? 1
                         : std::strcmp(fam, "stream") == 0 ? 3
                         : std::strcmp(fam, "direct") == 0 ? 5
                                                           : 4);
@@ -1462,7 +1757,7 @@ int vg_ivfpq_destroy(vg_index *ix) {
                       &ix->owner, &ix->ws_q, &ix->ws_qn, &ix->ws_dist, &ix->ws_probes, &ix->ws_pdist,
                       &ix->ws_scalars, &ix->ws_keys, &ix->ws_all_keys, &ix->ws_out_ids, &ix->ws_out_dist,
                       &ix->ws_out_count, &ix->stats, &ix->ws_lb, &ix->ws_rec, &ix->ws_lbq, &ix->ws_qimg,
-                      &ix->ws_eps, &ix->ws_tc, &ix->ws_floor, &ix->cent_img})
+                      &ix->ws_eps, &ix->ws_tc, &ix->ws_floor, &ix->cent_img, &ix->ws_seed, &ix->ws_qall})
       b->release();
     for (int i = 0; i < kPhaseEvents; ++i)
       if (ix->ev[i]) cudaEventDestroy(ix->ev[i]);
@@ -1702,6 +1997,8 @@ int vg_ivfpq_reconstruct(const vg_index *ix, size_t idx, float *out) {
   if (idx >= ix->n)
     return fail(VG_ERR_INVALID_PARAMETER, "invalid parameter: vector index " + std::to_string(idx) +
                                               " out of range (num_vectors = " + std::to_string(ix->n) + ")");
+  if (ix->partitioned)
+    return fail(VG_ERR_UNSUPPORTED, "unsupported: reconstruct on a list-sharded index (codes are partitioned)");
   DeviceGuard g(ix->device);
   const size_t d = ix->d, M = ix->params.num_codebooks, ks = ix->params.codebook_size, dsub = ix->dsub;
   uint32_t a = 0;
@@ -1760,6 +2057,9 @@ int vg_ivfpq_export(const vg_index *ix, int what, void *dst, size_t bytes) {
     default: return fail(VG_ERR_INVALID_PARAMETER, "unknown export selector");
   }
   if (needs_build && !ix->built) return fail(VG_ERR_NOT_BUILT, "IVF-PQ index is not built: nothing to export");
+  if (ix->partitioned && (what == VG_EXPORT_ASSIGNMENTS || what == VG_EXPORT_CODES ||
+                          what == VG_EXPORT_LIST_OFFSETS || what == VG_EXPORT_LIST_IDS))
+    return fail(VG_ERR_UNSUPPORTED, "unsupported: exporting codes or lists of a list-sharded index");
   if (bytes != need)
     return fail(VG_ERR_INVALID_PARAMETER, "export size mismatch: expected " + std::to_string(need) + " bytes");
   if (need) VG_CU(cudaMemcpy(dst, src, need, cudaMemcpyDefault));
@@ -1865,6 +2165,7 @@ int vg_ivfpq_shard(vg_index *ix, int rank, int world_size, const uint8_t nccl_id
   }
   ix->rank = rank;
   ix->world = world_size;
+  if (world_size > 1) VG_TRY(partition_lists(ix, mine));
   return VG_OK;
 }
 

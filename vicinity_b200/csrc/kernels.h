@@ -128,6 +128,24 @@ struct TcSelect {
   cudaEvent_t marks[3];   // recorded (when non-null) before the window kernel, between it and the finisher, after
 };
 size_t tc_select_workspace_bytes(size_t rows, size_t cols, int P, int num_sms);
+
+// out[r][c] (binary16, row stride ld) = q_r . x_c from the tensor cores
+// (binary16 operand images, f32 accumulation, rounded to nearest): the
+// approximate coarse products the probe shortlist ranks.
+cudaError_t launch_tc_gemm_f16(const void *a_img, size_t rows, const void *b_img, size_t cols, int d, int kp,
+                               void *out, size_t ld, int *error, int num_sms, cudaStream_t s);
+
+// Exact top-k probes per row from approximate products s[row][l] ~ q . c_l
+// (binary16 with s_half, else f32): candidates within eps = rel |q| cmax +
+// abs_coef (1 + cmax) + 2^-20 of the k-th are re-scored with the reference's
+// sequential 1 - dot; rows with too many candidates or non-finite inputs are
+// scored exactly over all L.  Same output as launch_select_rows on exact
+// 1 - dot distances; with bounds.lb set, the probes' pruning bounds and
+// records are written beside them (shortlist.cu).
+cudaError_t launch_probe_shortlist(const void *s, bool s_half, size_t rows, size_t L, size_t ld, const float *qn,
+                                   int d, const float *cent, const float *cmax, double rel, double abs_coef, int k,
+                                   uint32_t *out_ids, float *out_dist, size_t out_ld, const ProbeBoundArgs &bounds,
+                                   cudaStream_t st);
 cudaError_t launch_tc_select(const TcSelect &t, int num_sms, cudaStream_t s);
 
 // Same selection, but writing packed keys (for later merging).
@@ -218,6 +236,17 @@ cudaError_t launch_centroid_norm_max(const float *cent, size_t L, int d, float *
 cudaError_t launch_probe_lb(const float *qn, size_t nq, int d, const uint32_t *probes, int P,
                             const float *centroids, const struct ProbeBoundArgs &b, cudaStream_t s);
 
+// rec[i] for probes[i] (i < n): the list's record with the local layout
+// (list_off, code_off) and bound lb[i] when owner marks the list, else an
+// empty record (list 0xffffffff).
+cudaError_t launch_probe_records(const uint32_t *probes, const float *lb, size_t n, const uint8_t *owner,
+                                 const uint64_t *list_off, const uint64_t *code_off, ProbeRec *rec, cudaStream_t s);
+
+// dst + dst_off[i] <- bytes[i] bytes of src + src_off[i], i < count (a block
+// per segment; offsets and sizes in device memory).
+cudaError_t launch_copy_segments(const void *src, void *dst, const uint64_t *src_off, const uint64_t *dst_off,
+                                 const uint64_t *bytes, size_t count, cudaStream_t s);
+
 // Number of positions where a[i] != b[i] added to *changed.
 cudaError_t launch_count_diff_u8(const uint8_t *a, const uint8_t *b, size_t n,
                                  unsigned int *changed, cudaStream_t s);
@@ -262,6 +291,11 @@ struct ScanParams {
   // floor compete (nullable; query-major and 4-bit block kernels, which serve
   // k up to 256: top-k beyond 256 in passes)
   const unsigned long long *key_floor;
+  // list-sharded search (warp-per-query kernels only; zero-initialised = off):
+  int pscan;                             // probes visited per query (0: all P); the row stride stays P
+  unsigned long long *out_kth;           // [nq] the query's k-th kept key (kEmptyKey: fewer than k) (nullable)
+  const unsigned long long *key_ceiling; // [nq] keys above the query's ceiling are never kept (nullable)
+  int force_warp;                        // use the warp-per-query kernels at any batch size
 };
 
 // Fused per-query kernel: for each probed list the query residual, the ADC
@@ -274,12 +308,18 @@ cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms,
 // probe lists, query map and filter only that kernel reads.
 cudaError_t launch_ivfpq_scan_generic(const ScanParams &p, int num_sms, cudaStream_t s);
 
+// Whether launch_ivfpq_scan with force_warp runs a warp-per-query kernel for
+// p (the kernels that honour pscan, out_kth and key_ceiling).
+bool ivfpq_scan_warp_applies(const ScanParams &p);
+
 // Name of the kernel variant launch_ivfpq_scan would run for p.
 int ivfpq_scan_variant_name(const ScanParams &p, int num_sms, char *buf, size_t len);
 
-// Kernel family selection: 2 (default) = double-buffered kernel where it
-// applies, 1 = single-buffered query-major kernel, 0 = the warp-specialised
-// pipeline where it applies.
+// Kernel family selection (VICINITY_SCAN_KERNEL): 4 (default) = the
+// warp-per-query kernels for batches of at least 16 queries per SM, else the
+// query-stream (8-bit) and 4-bit block kernels; 5 = the warp-per-query
+// kernels wherever they apply; 3 = never the warp-per-query kernels; 1 = the
+// query-major kernel.
 void set_scan_family(int family);
 
 // ---- build_kernels.cu -----------------------------------------------------

@@ -45,6 +45,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
   return true;
 }
 
+// mbar_wait for waits that may last: each try_wait may suspend the thread
+// until the phase completes or about `hint_ns` pass, instead of spinning.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity) {
+  if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait_hint(bar, parity, 20000u)) {
+    if (clock64() - start > kWaitCycles) return false;
+  }
+  return true;
+}
+
 // Add `bytes` of expected transaction count to the current phase of *bar.
 __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");

@@ -126,10 +126,18 @@ __global__ void __launch_bounds__(kDirectThreads, 1) ivfpq_direct_kernel(const S
     WarpTopK<R> tk;
     tk.init();
     uint32_t n_lists = 0, n_vecs = 0;  // scored after pruning (profiling)
-    for (int pi = 0; pi < P; ++pi) {
+    // a ceiling key (a bound on the query's k-th key over every shard) keeps
+    // only keys at or below it
+    uint64_t kth0 = kEmptyKey;
+    if (p.key_ceiling) {
+      const uint64_t c = p.key_ceiling[q];
+      kth0 = c == kEmptyKey ? kEmptyKey : c + 1;
+    }
+    const int pn = p.pscan ? p.pscan : P;
+    for (int pi = 0; pi < pn; ++pi) {
       const ProbeRec rec = p.probe_rec[static_cast<size_t>(q) * P + pi];
       if (rec.list == 0xffffffffu) continue;
-      uint64_t kth = tk.get(k - 1);
+      uint64_t kth = min(tk.get(k - 1), kth0);
       if (kth != kEmptyKey && rec.lb > key_dist(kth)) continue;  // list pruning
       const float *cent = p.centroids + static_cast<size_t>(rec.list) * d;
       const uint8_t *lcodes = p.list_codes + rec.coff;
@@ -161,8 +169,12 @@ __global__ void __launch_bounds__(kDirectThreads, 1) ivfpq_direct_kernel(const S
             if (kx < kth) topk_insert_one(tk, kx);
           }
         }
-        kth = tk.get(k - 1);
+        kth = min(tk.get(k - 1), kth0);
       }
+    }
+    if (p.out_kth) {
+      const uint64_t kk = tk.get(k - 1);
+      if (lane == 0) p.out_kth[q] = kk;
     }
     uint32_t count = 0;
 #pragma unroll

@@ -13,8 +13,6 @@ namespace vg {
 
 cudaError_t launch_scan_four(const ScanParams &p, int dsub, int ept, int num_sms, cudaStream_t s);
 cudaError_t launch_scan_eight(const ScanParams &p, int dsub, int ept, int num_sms, cudaStream_t s);
-cudaError_t launch_scan_ws(const ScanParams &p, int dsub, int ept, int num_sms, cudaStream_t s);
-cudaError_t launch_scan_pipe(const ScanParams &p, int dsub, int gpt, int num_sms, cudaStream_t s);
 cudaError_t launch_scan_stream(const ScanParams &p, int dsub, int gpt, int num_sms, cudaStream_t s);
 cudaError_t launch_scan_direct(const ScanParams &p, int num_sms, cudaStream_t s);
 cudaError_t launch_scan_four_warp(const ScanParams &p, int num_sms, cudaStream_t s);
@@ -22,18 +20,10 @@ bool scan_four_warp_fits(const ScanParams &p);
 bool scan_direct_fits(const ScanParams &p);
 
 namespace {
-// 0 warp-specialised, 1 query-major, 2 double-buffered, 3 query-stream, 4 warp-per-query kernels (direct
-// ADC, 4-bit warp) for large batches else the block kernels (default), 5 warp-per-query wherever they apply
+// 1 query-major, 3 query-stream, 4 warp-per-query kernels (direct ADC, 4-bit
+// warp) for large batches else the block kernels (default), 5 warp-per-query
+// wherever they apply
 int g_family = 4;
-
-// Entries per producer thread for the warp-specialised kernel (0 = n/a).
-int pick_ws_ept(const ScanParams &p) {
-  if (g_family != 0 || p.ks != 256 || p.dsub < 1 || p.dsub > 8 || p.k > 32 || p.P > 384) return 0;
-  const int nent = p.M * p.ks;
-  for (int ept : {3, 6, 11, 22})
-    if (ept * 384 >= nent && ept * p.dsub <= 88) return ept;
-  return 0;
-}
 }  // namespace
 
 void set_scan_family(int family) { g_family = family; }
@@ -43,10 +33,11 @@ namespace {
 // a batch that keeps every warp busy (16 queries per SM here); smaller
 // batches go to the query-stream kernel, whose blocks share a query.
 bool use_direct(const ScanParams &p, int num_sms) {
-  return scan_direct_fits(p) && (g_family == 5 || p.nq >= 16 * num_sms);
+  return scan_direct_fits(p) && (g_family == 5 || p.force_warp || p.nq >= 16 * num_sms);
 }
 bool use_four_warp(const ScanParams &p, int num_sms) {
-  return g_family >= 4 && scan_four_warp_fits(p) && (g_family == 5 || p.nq >= 16 * num_sms);
+  return (g_family >= 4 || p.force_warp) && scan_four_warp_fits(p) &&
+         (g_family == 5 || p.force_warp || p.nq >= 16 * num_sms);
 }
 }  // namespace
 
@@ -68,19 +59,19 @@ cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms, cudaStream_t s) 
     return launch_scan_eight(p, gpt ? p.dsub : 0, gpt, num_sms, s);
   }
   // an OPQ rotation is applied by the query-major and 4-bit kernels only
-  const int ws = p.rot_t ? 0 : pick_ws_ept(p);
-  if (ws) return launch_scan_ws(p, p.dsub, ws, num_sms, s);
-  if (g_family >= 4 && use_direct(p, num_sms)) return launch_scan_direct(p, num_sms, s);
+  if ((g_family >= 4 || p.force_warp) && use_direct(p, num_sms)) return launch_scan_direct(p, num_sms, s);
   const int gpt = pick_gpt(p);
-  if (g_family >= 2 && gpt && p.ks == 256 && !p.rot_t) {
-    if (g_family >= 3 && p.probe_rec && p.P <= 256) return launch_scan_stream(p, p.dsub, gpt, num_sms, s);
-    return launch_scan_pipe(p, p.dsub, gpt, num_sms, s);
-  }
+  if (g_family >= 3 && gpt && p.ks == 256 && !p.rot_t && p.probe_rec && p.P <= 256)
+    return launch_scan_stream(p, p.dsub, gpt, num_sms, s);
   if (p.ks == 16) {
     if (use_four_warp(p, num_sms)) return launch_scan_four_warp(p, num_sms, s);
     return launch_scan_four(p, gpt ? p.dsub : 0, gpt, num_sms, s);
   }
   return launch_scan_eight(p, gpt ? p.dsub : 0, gpt, num_sms, s);
+}
+
+bool ivfpq_scan_warp_applies(const ScanParams &p) {
+  return p.k >= 1 && p.k <= 64 && !p.key_floor && (scan_direct_fits(p) || (p.ks == 16 && scan_four_warp_fits(p)));
 }
 
 cudaError_t launch_ivfpq_scan_generic(const ScanParams &p, int num_sms, cudaStream_t s) {
@@ -90,16 +81,11 @@ cudaError_t launch_ivfpq_scan_generic(const ScanParams &p, int num_sms, cudaStre
 }
 
 int ivfpq_scan_variant_name(const ScanParams &p, int num_sms, char *buf, size_t len) {
-  const int ws = p.rot_t || p.key_floor ? 0 : pick_ws_ept(p);
-  if (ws) return snprintf(buf, len, "ivfpq_ws_kernel<%d,%d,1,256>", p.dsub, ws);
-  if (g_family >= 4 && !p.key_floor && use_direct(p, num_sms))
+  if ((g_family >= 4 || p.force_warp) && !p.key_floor && use_direct(p, num_sms))
     return snprintf(buf, len, "ivfpq_direct_kernel<%d,%d>", p.dsub, p.k <= 32 ? 1 : 2);
   const int gpt = pick_gpt(p);
-  if (g_family >= 2 && gpt && p.ks == 256 && !p.rot_t && !p.key_floor) {
-    if (g_family >= 3 && p.probe_rec && p.P <= 256)
-      return snprintf(buf, len, "ivfpq_stream_kernel<%d,%d,1,256>", p.dsub, gpt);
-    return snprintf(buf, len, "ivfpq_pipe_kernel<%d,%d,1,256>", p.dsub, gpt);
-  }
+  if (g_family >= 3 && gpt && p.ks == 256 && !p.rot_t && !p.key_floor && p.probe_rec && p.P <= 256)
+    return snprintf(buf, len, "ivfpq_stream_kernel<%d,%d,1,256>", p.dsub, gpt);
   if (!p.key_floor && use_four_warp(p, num_sms)) return snprintf(buf, len, "ivfpq_four_warp_kernel<%d>", p.k <= 32 ? 1 : 2);
   if (p.ks == 16) return snprintf(buf, len, "ivfpq_four_kernel<%d>", p.k <= 32 ? 1 : p.k <= 64 ? 2 : p.k <= 128 ? 4 : 8);
   return snprintf(buf, len, "ivfpq_query_kernel<%d,%d,%d,%s>", gpt ? p.dsub : 0, gpt,

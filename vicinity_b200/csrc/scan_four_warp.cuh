@@ -74,8 +74,16 @@ __global__ void __launch_bounds__(kFourWarpThreads, 1) ivfpq_four_warp_kernel(co
     WarpTopK<R> tk;
     tk.init();
     uint32_t n_lists = 0, n_vecs = 0;  // scored after pruning (profiling)
-    uint64_t kth = kEmptyKey;
-    for (int pi = 0; pi < P; ++pi) {
+    // a ceiling key (a bound on the query's k-th key over every shard) keeps
+    // only keys at or below it
+    uint64_t kth0 = kEmptyKey;
+    if (p.key_ceiling) {
+      const uint64_t c = p.key_ceiling[q];
+      kth0 = c == kEmptyKey ? kEmptyKey : c + 1;
+    }
+    uint64_t kth = kth0;
+    const int pn = p.pscan ? p.pscan : P;
+    for (int pi = 0; pi < pn; ++pi) {
       const size_t pr = static_cast<size_t>(q) * P + pi;
       const uint32_t l = p.probes[pr];
       if (l == 0xffffffffu || (p.owner && !p.owner[l])) continue;
@@ -101,7 +109,7 @@ __global__ void __launch_bounds__(kFourWarpThreads, 1) ivfpq_four_warp_kernel(co
         const bool pass = alive && (kth == kEmptyKey || dk <= static_cast<uint32_t>(kth >> 32));
         const uint64_t key = pass ? ((static_cast<uint64_t>(dk) << 32) | ids[lane]) : kEmptyKey;
         tk.add(key < kth ? key : kEmptyKey);
-        kth = tk.get(k - 1);
+        kth = min(tk.get(k - 1), kth0);
         continue;
       }
       // the first codes of the list come in while the table is built
@@ -180,8 +188,12 @@ __global__ void __launch_bounds__(kFourWarpThreads, 1) ivfpq_four_warp_kernel(co
             if (kx < kth) topk_insert_one(tk, kx);
           }
         }
-        kth = tk.get(k - 1);
+        kth = min(tk.get(k - 1), kth0);
       }
+    }
+    if (p.out_kth) {
+      const uint64_t kk = tk.get(k - 1);
+      if (lane == 0) p.out_kth[q] = kk;
     }
     uint32_t count = 0;
 #pragma unroll

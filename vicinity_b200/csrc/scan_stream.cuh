@@ -23,10 +23,37 @@
 // is free again once its query has been written.
 #pragma once
 
+#include "f32x2.cuh"
 #include "pipeline.cuh"
-#include "scan_pipe.cuh"
+#include "scan_kernel.cuh"
 
 namespace vg {
+
+// Shared memory of the per-warp top-k rows and two sets of `batch` tables.
+__host__ __device__ inline size_t pipe_smem_bytes(int d, int M, int ks, int batch, int R) {
+  const size_t table = static_cast<size_t>((M * ks + 3) & ~3) * 4;
+  (void)d;
+  return static_cast<size_t>(kScanWarps) * 32 * R * 8 + 2 * static_cast<size_t>(batch) * table;
+}
+
+// D floats of row `a` minus row `b` at offset o, each an IEEE subtraction.
+template <int D>
+__device__ __forceinline__ void load_residual(const float *a, const float *b, int o, bool vec4, float (&r)[D]) {
+  if (D % 4 == 0 && vec4) {
+#pragma unroll
+    for (int j = 0; j < D; j += 4) {
+      const float4 x = *reinterpret_cast<const float4 *>(a + o + j);
+      const float4 y = *reinterpret_cast<const float4 *>(b + o + j);
+      r[j] = __fsub_rn(x.x, y.x);
+      r[j + 1] = __fsub_rn(x.y, y.y);
+      r[j + 2] = __fsub_rn(x.z, y.z);
+      r[j + 3] = __fsub_rn(x.w, y.w);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < D; ++j) r[j] = __fsub_rn(a[o + j], b[o + j]);
+  }
+}
 
 constexpr int kStreamSlots = 8;  // query slots (records in shared memory)
 constexpr int kStreamMaxP = 256;  // two 16-byte copies per record, one per thread

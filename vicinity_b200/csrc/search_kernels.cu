@@ -748,3 +748,59 @@ cudaError_t launch_rerank(const float *qn, const float *vectors, int d, const un
 }
 
 }  // namespace vg
+
+// ---------------------------------------------------------------------------
+// List-sharded search helpers.
+// ---------------------------------------------------------------------------
+namespace vg {
+namespace {
+__global__ void probe_records_kernel(const uint32_t *__restrict__ probes, const float *__restrict__ lb, size_t n,
+                                     const uint8_t *__restrict__ owner, const uint64_t *__restrict__ list_off,
+                                     const uint64_t *__restrict__ code_off, ProbeRec *__restrict__ rec) {
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t l = probes[i];
+  if (l == 0xffffffffu || (owner && !owner[l])) {
+    rec[i] = ProbeRec{0xffffffffu, 0u, 0ull, 0ull, 0.0f, 0u};
+    return;
+  }
+  const uint64_t beg = list_off[l];
+  rec[i] = ProbeRec{l, static_cast<uint32_t>(list_off[l + 1] - beg), beg, code_off[l], lb[i], 0u};
+}
+
+// block per segment: bytes[s] bytes from src + src_off[s] to dst + dst_off[s]
+__global__ void copy_segments_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst,
+                                     const uint64_t *__restrict__ src_off, const uint64_t *__restrict__ dst_off,
+                                     const uint64_t *__restrict__ bytes) {
+  const size_t sgm = blockIdx.x;
+  const uint8_t *a = src + src_off[sgm];
+  uint8_t *b = dst + dst_off[sgm];
+  const uint64_t nb = bytes[sgm];
+  if (((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15) == 0) {
+    const uint64_t n16 = nb >> 4;
+    for (uint64_t i = threadIdx.x; i < n16; i += blockDim.x)
+      reinterpret_cast<uint4 *>(b)[i] = reinterpret_cast<const uint4 *>(a)[i];
+    for (uint64_t i = (n16 << 4) + threadIdx.x; i < nb; i += blockDim.x) b[i] = a[i];
+  } else {
+    for (uint64_t i = threadIdx.x; i < nb; i += blockDim.x) b[i] = a[i];
+  }
+}
+}  // namespace
+
+cudaError_t launch_probe_records(const uint32_t *probes, const float *lb, size_t n, const uint8_t *owner,
+                                 const uint64_t *list_off, const uint64_t *code_off, ProbeRec *rec, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  probe_records_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(probes, lb, n, owner, list_off,
+                                                                              code_off, rec);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_copy_segments(const void *src, void *dst, const uint64_t *src_off, const uint64_t *dst_off,
+                                 const uint64_t *bytes, size_t count, cudaStream_t s) {
+  if (count == 0) return cudaSuccess;
+  copy_segments_kernel<<<static_cast<unsigned>(count), 256, 0, s>>>(static_cast<const uint8_t *>(src),
+                                                                    static_cast<uint8_t *>(dst), src_off, dst_off,
+                                                                    bytes);
+  return cudaGetLastError();
+}
+}  // namespace vg

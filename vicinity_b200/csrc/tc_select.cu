@@ -48,13 +48,14 @@ namespace {
 constexpr int kTile = 128;                            // UMMA M (query rows) and N (columns) per tile
 constexpr int kKBlock = 64;                           // binary16 elements per 128-byte swizzle row
 constexpr uint32_t kBlockBytes = kTile * 128;         // one K-block of one tile: 16 KB
-constexpr int kStages = 3;                            // column tiles in flight
+constexpr int kStages = 2;                            // column tiles in flight
 constexpr int kBins = 256;                            // histogram bins of 1 - s over [0, 2)
-constexpr int kWinThreads = 192;                      // 6 warps
+constexpr uint32_t kWarmTiles = 4;                    // tiles of a unit counted before any is gathered
+constexpr int kEpiWarps = 8;                          // two epilogue warpgroups, one per accumulator
+constexpr int kWinThreads = 64 + kEpiWarps * 32;      // copies, MMA, epilogue
 constexpr uint32_t kTmemCols = 2 * kTile;             // two f32 accumulators of 128 columns
 constexpr int kFinWarps = 8;
 constexpr int kFinBuf = 512;                          // re-scored candidates per row (finisher)
-constexpr uint32_t kMaxSplitCols = 511u * kTile;      // histogram counts are u16
 
 // tcgen05.mma instruction descriptor, kind::f16: D f32, A and B binary16,
 // both K-major, N = 128 (bits 17-22, N >> 3), M = 128 (bits 24-28, M >> 4).
@@ -95,8 +96,26 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
-// 32 consecutive f32 accumulator columns of this warp's 32 TMEM lanes.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+struct WinParams {
+  const uint8_t *a_img, *b_img;  // operand images (tile = kp * 256 bytes)
+  size_t rows, cols;
+  int kp, ksteps, P, top1;       // ksteps: MMA K-steps of 16 covering d; top1: running maximum
+  int splits;                    // column ranges per row block (work unit = row block x range)
+  uint32_t split_cols;           // columns per range, a multiple of 128
+  int cap;                       // candidates kept per (row, range, warpgroup)
+  const float *eps;              // [rows] error bound of the approximate products
+  uint2 *cand;                   // [rows][splits][2][cap] (column, bits of s)
+  uint32_t *count;               // [rows][splits][2] candidates found (> cap: overflow)
+  uint32_t *gbound;              // [rows] bound shared by every CTA of a row (zeroed before launch)
+  int *error;                    // set nonzero when a bounded wait gives up
+};
+
+__device__ __forceinline__ void win_fail(const WinParams &p, volatile int *abort_flag, int code) {
+  *abort_flag = 1;
+  if (p.error) *reinterpret_cast<volatile int *>(p.error) = code;
+}
+
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t *v) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
@@ -106,36 +125,60 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
         "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-__device__ __forceinline__ uint16_t lds_u16(uint32_t a) {
-  uint16_t x;
-  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(x) : "r"(a));
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+  uint32_t x;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(x) : "r"(a) : "memory");
   return x;
 }
-__device__ __forceinline__ void sts_u16(uint32_t a, uint16_t x) {
-  asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "h"(x) : "memory");
+
+// largest of 32 values (tree, no NaN propagation)
+__device__ __forceinline__ float max32(const uint32_t *v) {
+  float m[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) m[i] = fmaxf(__uint_as_float(v[i]), __uint_as_float(v[i + 16]));
+#pragma unroll
+  for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; ++i) m[i] = fmaxf(m[i], m[i + w]);
+  return m[0];
 }
 
-struct WinParams {
-  const uint8_t *a_img, *b_img;  // operand images (tile = kp * 256 bytes)
-  size_t rows, cols;
-  int kp, P, top1;               // top1: running maximum instead of the histogram
-  int splits;                    // column ranges per row block (work unit = row block x range)
-  uint32_t split_cols;           // columns per range, a multiple of 128, <= kMaxSplitCols
-  int cap;                       // candidates kept per (row, range)
-  const float *eps;              // [rows] error bound of the approximate products
-  uint2 *cand;                   // [rows][splits][cap] (column, bits of s)
-  uint32_t *count;               // [rows][splits] candidates found (> cap: overflow)
-  int *error;                    // set nonzero when a bounded wait gives up
-};
-
-__device__ __forceinline__ void win_fail(const WinParams &p, volatile int *abort_flag, int code) {
-  *abort_flag = 1;
-  if (p.error) *reinterpret_cast<volatile int *>(p.error) = code;
+// predicated helpers: no branch per value
+__device__ __forceinline__ void red_add_if(bool p, uint32_t addr) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %1, 0;\n\t@q red.shared.add.u32 [%0], 1;\n\t}" ::"r"(addr),
+      "r"(static_cast<uint32_t>(p))
+      : "memory");
+}
+__device__ __forceinline__ void st_cand_if(bool p, uint2 *dst, uint32_t col, uint32_t bits) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %3, 0;\n\t@q st.global.v2.u32 [%0], {%1, %2};\n\t}" ::"l"(dst),
+      "r"(col), "r"(bits), "r"(static_cast<uint32_t>(p))
+      : "memory");
 }
 
+// Window of one row (thread), a single sweep of the row's columns.  Per tile
+// of products (in registers):
+//   1. count: histogram mode -- hist[b][row] counts the row's products with
+//      bin b = round(128 (1 - s)) clamped to [0, 255] (shared by the row's two
+//      epilogue threads, red.shared.add).  h is a bin bound: every value with
+//      bin < h is counted exactly, so once the counts below h reach P the P-th
+//      smallest 1 - s of the row lies at or below (h - 0.5) / 128; values with
+//      bin >= h are skipped (those bins may be undercounted, which only delays
+//      the bound).  Top-1 mode -- a running maximum of s.
+//   2. refresh the bound (histogram mode: on a schedule): from the exact bins
+//      below h, and from the other column ranges of the row through
+//      gbound[row] (256 - h, atomicMax; a bound on the P-th smallest of any
+//      subset of the row's columns bounds the whole row's).
+//   3. gather: every column of the tile with 1 - s within twice the error
+//      bound of the current bound is appended to the row's candidates.  The
+//      bound only tightens, so every column of the final window has been
+//      appended; when the list fills up, candidates below the current window
+//      are dropped (compaction).  A list that still overflows marks the row
+//      for the exact re-score of every column.
 __global__ void __launch_bounds__(kWinThreads, 1) tc_window_kernel(const WinParams p) {
   extern __shared__ uint8_t win_raw[];
   const uint32_t raw = smem_u32(win_raw);
@@ -144,16 +187,377 @@ __global__ void __launch_bounds__(kWinThreads, 1) tc_window_kernel(const WinPara
   const uint32_t tile_bytes = static_cast<uint32_t>(nkb) * kBlockBytes;
   uint8_t *sA = sm;
   uint8_t *sB = sm + tile_bytes;
-  uint16_t *hist = reinterpret_cast<uint16_t *>(sB + kStages * tile_bytes);  // [kBins][128 rows]
-  uint64_t *bars = reinterpret_cast<uint64_t *>(hist + kBins * kTile);
+  uint32_t *hist = reinterpret_cast<uint32_t *>(sB + kStages * tile_bytes);  // [kBins][128 rows]
+  uint32_t *lowbin = hist + kBins * kTile;  // [128 rows] lowest bin counted in the unit
+  uint64_t *bars = reinterpret_cast<uint64_t *>(lowbin + kTile);
   uint64_t *full = bars, *empty = bars + kStages, *afull = bars + 2 * kStages, *aempty = afull + 1;
-  uint64_t *accfull = aempty + 1, *accempty = accfull + 2, *drain = accempty + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  uint64_t *accfull = aempty + 1, *accempty = accfull + 2, *drain = accempty + 2, *hzero = drain + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(hzero + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    mbar_init(afull, 1);
+    mbar_init(aempty, 1);
+    mbar_init(accfull, 1);
+    mbar_init(accfull + 1, 1);
+    mbar_init(accempty, 4);
+    mbar_init(accempty + 1, 4);
+    mbar_init(drain, 1);
+    mbar_init(hzero, kEpiWarps * 32);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // work units range-major: CTAs running at the same time mostly stream the
+  // same column range (its tiles shared in L2) for different row blocks
+  const size_t rblocks = (p.rows + kTile - 1) / kTile;
+  const size_t units = rblocks * static_cast<size_t>(p.splits);
+  auto unit_range = [&](size_t u, size_t &rb, int &sp, size_t &c0, uint32_t &ntiles) {
+    sp = static_cast<int>(u / rblocks);
+    rb = u - static_cast<size_t>(sp) * rblocks;
+    c0 = static_cast<size_t>(sp) * p.split_cols;
+    const size_t c1 = min(p.cols, c0 + p.split_cols);
+    ntiles = static_cast<uint32_t>((c1 - c0 + kTile - 1) / kTile);
+  };
+
+  if (warp == 0) {
+    // ---- producer: A tile per unit, then the unit's column tiles ----
+    if (lane == 0) {
+      uint32_t it = 0, ul = 0;
+      long long a_issued = -1;  // last unit whose A tile was issued
+      int last_stage_it[kStages];
+      for (int s = 0; s < kStages; ++s) last_stage_it[s] = -1;
+      bool ok = true;
+      for (size_t u = blockIdx.x; ok && u < units; u += gridDim.x, ++ul) {
+        size_t rb, c0;
+        int sp;
+        uint32_t ntiles;
+        unit_range(u, rb, sp, c0, ntiles);
+        if (*abort_flag || (ul > 0 && !mbar_wait_sleep(aempty, (ul - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(afull, tile_bytes);
+        bulk_copy_g2s(sA, p.a_img + rb * tile_bytes, tile_bytes, afull);
+        a_issued = ul;
+        const size_t t0 = c0 / kTile;
+        const uint32_t nvisit = ntiles + min(ntiles, kWarmTiles);
+        for (uint32_t i = 0; i < nvisit; ++i, ++it) {
+          const uint32_t t = i < ntiles ? i : i - ntiles;
+          const uint32_t stage = it % kStages, ph = (it / kStages) & 1;
+          if (*abort_flag || !mbar_wait_sleep(empty + stage, ph ^ 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full + stage, tile_bytes);
+          bulk_copy_g2s(sB + stage * tile_bytes, p.b_img + (t0 + t) * tile_bytes, tile_bytes, full + stage);
+          last_stage_it[stage] = static_cast<int>(it);
+        }
+      }
+      if (!ok) {
+        win_fail(p, abort_flag, 1);
+        // copies still in flight land in shared memory: wait for them (bounded)
+        for (int s = 0; s < kStages; ++s)
+          if (last_stage_it[s] >= 0) mbar_wait(full + s, (static_cast<uint32_t>(last_stage_it[s]) / kStages) & 1);
+        if (a_issued >= 0) mbar_wait(afull, static_cast<uint32_t>(a_issued) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      uint32_t it = 0, tc = 0, ul = 0;
+      bool ok = true;
+      for (size_t u = blockIdx.x; ok && u < units; u += gridDim.x, ++ul) {
+        size_t rb, c0;
+        int sp;
+        uint32_t ntiles;
+        unit_range(u, rb, sp, c0, ntiles);
+        if (!mbar_wait_sleep(afull, ul & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(sA);
+        const uint32_t nvisit = ntiles + min(ntiles, kWarmTiles);
+        for (uint32_t i = 0; i < nvisit; ++i, ++it, ++tc) {
+          const uint32_t stage = it % kStages, ph = (it / kStages) & 1;
+          const uint32_t acc = tc & 1, aph = (tc >> 1) & 1;
+          if (!mbar_wait_sleep(full + stage, ph) || !mbar_wait_sleep(accempty + acc, aph ^ 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t b_base = smem_u32(sB + stage * tile_bytes);
+          const uint32_t d_tmem = tmem + acc * kTile;
+          for (int ks = 0; ks < p.ksteps; ++ks) {
+            const uint32_t off = static_cast<uint32_t>(ks >> 2) * kBlockBytes + static_cast<uint32_t>(ks & 3) * 32u;
+            umma_f16(d_tmem, umma_desc(a_base + off), umma_desc(b_base + off), ks != 0);
+          }
+          umma_commit(empty + stage);
+          umma_commit(accfull + acc);
+        }
+        if (ok) umma_commit(aempty);
+      }
+      if (!ok) win_fail(p, abort_flag, 2);
+      // every MMA issued is complete before the accumulators are released
+      umma_commit(drain);
+      mbar_wait(drain, 0);
+    }
+  } else {
+    // ---- epilogue: warpgroup eg reads accumulator eg (the tiles with tile
+    // counter parity eg); warp w reads TMEM lanes 32 (w % 4) .. + 31 ----
+    const int eg = (warp - 2) >> 2;
+    const int ew = warp & 3;
+    const int rloc = ew * 32 + lane;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(eg) * kTile;
+    const uint32_t hbase = smem_u32(hist) + static_cast<uint32_t>(rloc) * 4u;
+    const uint32_t lbase = smem_u32(lowbin) + static_cast<uint32_t>(rloc) * 4u;
+    const float kInf = __int_as_float(0x7f800000);
+    const uint32_t cap = static_cast<uint32_t>(p.cap);
+    uint32_t tc = 0, ul = 0;
+    bool ok = true;
+    for (size_t u = blockIdx.x; ok && u < units; u += gridDim.x, ++ul) {
+      size_t rb, c0;
+      int sp;
+      uint32_t ntiles;
+      unit_range(u, rb, sp, c0, ntiles);
+      const size_t row = rb * kTile + rloc;
+      const bool rv = row < p.rows;
+      const double eps = rv ? static_cast<double>(p.eps[row]) : 0.0;
+      const bool bounded = rv && eps < 1.0;  // otherwise the finisher scores the row exactly
+      const size_t c1 = min(p.cols, c0 + p.split_cols);
+      uint32_t *gb = p.gbound + (rv ? row : 0);
+      if (!p.top1) {
+        // zero this row's bins (each warpgroup half of them); every epilogue
+        // thread arrives, and counting starts once the phase completes
+        for (int b = eg * (kBins / 2); b < (eg + 1) * (kBins / 2); ++b) hist[b * kTile + rloc] = 0;
+        if (eg == 0) lowbin[rloc] = kBins;
+        mbar_arrive(hzero);
+        if (!__all_sync(VG_FULL_MASK, mbar_wait_sleep(hzero, ul & 1))) {
+          ok = false;
+          break;
+        }
+      }
+      uint32_t h = kBins;  // bin bound (kBins: none yet)
+      uint32_t gseen = 0;  // largest gbound value seen
+      float s_h = -kInf;   // values with s > s_h are counted (1 - h / 128)
+      float smax = -kInf;  // top-1 mode: running maximum
+      float s_lo = -kInf;  // values with s >= s_lo are gathered
+      uint32_t n = 0, tp = 0;
+      bool over = false;
+      uint2 *cand = p.cand + ((row * p.splits + sp) * 2 + eg) * static_cast<size_t>(p.cap);
+
+      // s_lo of a bound T on the P-th smallest 1 - s: 1 - s <= T + 2 eps
+      auto set_window = [&](double T) {
+        const double lo = 1.0 - (T + 2.0 * eps) * (1.0 + 9.5367431640625e-7) - 9.5367431640625e-7;
+        s_lo = bounded ? __double2float_rd(lo) : -kInf;
+      };
+      // refresh h from the exact bins below it and from the other ranges
+      auto refresh = [&]() {
+        uint32_t cum = 0, found = h;
+        // bins below the lowest one counted are empty
+        for (uint32_t b0 = min(lds_u32(lbase), static_cast<uint32_t>(kBins)) & ~7u; b0 < found; b0 += 8) {
+          uint32_t c[8];
+#pragma unroll
+          for (int uu = 0; uu < 8; ++uu) c[uu] = lds_u32(hbase + ((b0 + uu) << 9));
+#pragma unroll
+          for (int uu = 0; uu < 8; ++uu) {
+            if (b0 + uu < found) {
+              cum += c[uu];
+              if (cum >= static_cast<uint32_t>(p.P)) found = b0 + uu + 1;
+            }
+          }
+        }
+        h = found;
+        if (rv) {
+          const uint32_t mine = kBins - h;
+          if (mine > gseen) atomicMax(gb, mine);
+          gseen = max(gseen, max(mine, *reinterpret_cast<volatile uint32_t *>(gb)));
+        }
+        h = min(h, kBins - gseen);
+        s_h = 1.0f - static_cast<float>(h) * (1.0f / 128.0f);
+        // bin b holds 128 (1 - s) rounded to nearest: 1 - s <= (b + 0.5) / 128
+        if (h < kBins) set_window((h - 0.5) / 128.0);
+      };
+      // drop candidates below the current window (16 loads in flight)
+      auto compact = [&]() {
+        const uint32_t m = min(n, cap);
+        uint32_t k = 0;
+        for (uint32_t i0 = 0; i0 < m; i0 += 16) {
+          uint2 e[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) e[j] = i0 + j < m ? cand[i0 + j] : make_uint2(0u, 0x7fc00000u);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const bool keep = __uint_as_float(e[j].y) >= s_lo;
+            st_cand_if(keep, cand + k, e[j].x, e[j].y);
+            k += keep ? 1u : 0u;
+          }
+        }
+        n = k;
+      };
+
+      // The first kWarmTiles tiles are only counted; the sweep then visits
+      // them again at its end and gathers them with the final bound.
+      const uint32_t warm = min(ntiles, kWarmTiles);
+      for (uint32_t i = 0; i < ntiles + warm; ++i, ++tc) {
+        const bool revisit = i >= ntiles;
+        const uint32_t t = revisit ? i - ntiles : i;
+        const uint32_t acc = tc & 1;
+        if (acc != static_cast<uint32_t>(eg)) continue;  // the other warpgroup's tile
+        const uint32_t aph = (tc >> 1) & 1;
+        if (!__all_sync(VG_FULL_MASK, mbar_wait_sleep(accfull + acc, aph))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const size_t col0 = c0 + static_cast<size_t>(t) * kTile;
+        const int nval = static_cast<int>(min(static_cast<size_t>(kTile), c1 - col0));
+        uint32_t v[kTile];
+#pragma unroll
+        for (int ch = 0; ch < kTile / 32; ++ch) tmem_ld32_nowait(t_lane + ch * 32, v + ch * 32);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(accempty + acc);  // the values are in registers
+        if (nval < kTile) {
+#pragma unroll
+          for (int j = 0; j < kTile; ++j)
+            if (j >= nval) v[j] = 0x7fc00000u;  // NaN: fails every comparison, ignored by fmaxf
+        }
+        float cmax[kTile / 32];
+#pragma unroll
+        for (int ch = 0; ch < kTile / 32; ++ch) cmax[ch] = max32(v + ch * 32);
+        // 1. count
+        if (revisit) {
+        } else if (p.top1) {
+#pragma unroll
+          for (int ch = 0; ch < kTile / 32; ++ch) smax = fmaxf(smax, cmax[ch]);
+        } else {
+#pragma unroll
+          for (int ch = 0; ch < kTile / 32; ++ch) {
+            if (cmax[ch] > s_h) {
+              uint32_t bmin = kBins;
+              const uint32_t *w = v + ch * 32;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float sv = __uint_as_float(w[j]);
+                const float tt = fmaf(sv, -128.0f, 8388736.0f);  // 2^23 + 128 (1 - s), rounded
+                int b = static_cast<int>(__float_as_uint(tt)) - 0x4B000000;
+                b = min(max(b, 0), kBins - 1);
+                red_add_if(sv > s_h, hbase + (static_cast<uint32_t>(b) << 9));
+                bmin = (sv > s_h) ? min(bmin, static_cast<uint32_t>(b)) : bmin;
+              }
+              asm volatile("red.shared.min.u32 [%0], %1;" ::"r"(lbase), "r"(bmin) : "memory");
+            }
+          }
+        }
+        // 2. refresh the bound
+        ++tp;
+        if (revisit) {
+        } else if (p.top1) {
+          if (rv && smax > -kInf) {
+            const uint32_t key = order_key(smax);
+            if (key > gseen) atomicMax(gb, key);
+            gseen = max(gseen, max(key, *reinterpret_cast<volatile uint32_t *>(gb)));
+            smax = fmaxf(smax, key_to_float(gseen));
+            const double lo = static_cast<double>(smax) - 2.0 * eps * (1.0 + 9.5367431640625e-7) -
+                              9.5367431640625e-7 * (1.0 + fabs(static_cast<double>(smax)));
+            s_lo = bounded ? __double2float_rd(lo) : -kInf;
+          }
+        } else if (t + 1 >= warm && ((tp & 1) == 0 || t + 2 >= ntiles || t + 1 == warm)) {
+          refresh();
+        }
+        // 3. gather
+        if (bounded && (revisit || t >= warm)) {
+#pragma unroll
+          for (int ch = 0; ch < kTile / 32; ++ch) {
+            if (cmax[ch] >= s_lo) {
+              if (n + 32 > cap && !over) {
+                compact();
+                // a window this wide is scored exactly by the finisher
+                if (n > cap / 2) over = true;
+              }
+              const uint32_t *w = v + ch * 32;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const bool g = __uint_as_float(w[j]) >= s_lo;
+                st_cand_if(g && !over, cand + n, static_cast<uint32_t>(col0 + ch * 32 + j), w[j]);
+                n += (g && !over) ? 1u : 0u;
+              }
+            }
+          }
+        }
+      }
+      if (rv && ok) p.count[(row * p.splits + sp) * 2 + eg] = over ? cap + 1 : n;
+    }
+    if (!ok) win_fail(p, abort_flag, 3);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+size_t win_smem_bytes(int kp) {
+  const size_t tile = static_cast<size_t>(kp / kKBlock) * kBlockBytes;
+  return 1024 + tile * (1 + kStages) + static_cast<size_t>(kBins) * kTile * 4 + kTile * 4 + 16 * 8 + 16;
+}
+
+// ---- tensor-core products to memory --------------------------------------
+
+// out[r][c] = binary16(q_r . x_c) for every row and column, rounded to
+// nearest from the f32 accumulator: the product matrix the probe shortlist
+// (shortlist.cu) ranks.  The same staged-operand pipeline as the window
+// kernel (warp 0 bulk copies, warp 1 issues tcgen05.mma into two TMEM
+// accumulators); the two epilogue warpgroups convert their accumulator and
+// store each row's 128 products of the tile as 16-byte vectors.
+constexpr int kGemmStages = 4;
+
+struct GemmParams {
+  const uint8_t *a_img, *b_img;
+  size_t rows, cols, ld;
+  int kp, ksteps, splits;
+  uint32_t split_cols;
+  __half *out;
+  int *error;
+};
+
+__global__ void __launch_bounds__(kWinThreads, 1) tc_gemm_f16_kernel(const GemmParams p) {
+  extern __shared__ uint8_t gemm_raw[];
+  const uint32_t raw = smem_u32(gemm_raw);
+  uint8_t *sm = gemm_raw + (((raw + 1023u) & ~1023u) - raw);
+  const int nkb = p.kp / kKBlock;
+  const uint32_t tile_bytes = static_cast<uint32_t>(nkb) * kBlockBytes;
+  uint8_t *sA = sm;
+  uint8_t *sB = sm + tile_bytes;
+  uint4 *stage_out = reinterpret_cast<uint4 *>(sB + kGemmStages * tile_bytes);  // [8 warps][32 rows][16 chunks]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(stage_out + kEpiWarps * 32 * 16);
+  uint64_t *full = bars, *empty = bars + kGemmStages, *afull = bars + 2 * kGemmStages, *aempty = afull + 1;
+  uint64_t *accfull = aempty + 1, *accempty = accfull + 2, *drain = accempty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGemmStages; ++s) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
@@ -178,215 +582,159 @@ __global__ void __launch_bounds__(kWinThreads, 1) tc_window_kernel(const WinPara
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
   const size_t rblocks = (p.rows + kTile - 1) / kTile;
   const size_t units = rblocks * static_cast<size_t>(p.splits);
-  auto unit_range = [&](size_t u, size_t &rb, int &sp, size_t &c0, uint32_t &ntiles) {
-    rb = u / p.splits;
-    sp = static_cast<int>(u - rb * p.splits);
-    c0 = static_cast<size_t>(sp) * p.split_cols;
+  auto unit_range = [&](size_t u, size_t &rb, size_t &c0, uint32_t &ntiles) {
+    const size_t sp = u / rblocks;
+    rb = u - sp * rblocks;
+    c0 = sp * p.split_cols;
     const size_t c1 = min(p.cols, c0 + p.split_cols);
     ntiles = static_cast<uint32_t>((c1 - c0 + kTile - 1) / kTile);
   };
+  auto fail = [&](int code) {
+    *abort_flag = 1;
+    if (p.error) *reinterpret_cast<volatile int *>(p.error) = code;
+  };
 
   if (warp == 0) {
-    // ---- producer: A tile per unit, then the unit's column tiles twice ----
     if (lane == 0) {
       uint32_t it = 0, ul = 0;
-      long long a_issued = -1;  // last unit whose A tile was issued
-      int last_stage_it[kStages];
-      for (int s = 0; s < kStages; ++s) last_stage_it[s] = -1;
+      long long a_issued = -1;
+      int last_stage_it[kGemmStages];
+      for (int s = 0; s < kGemmStages; ++s) last_stage_it[s] = -1;
       bool ok = true;
       for (size_t u = blockIdx.x; ok && u < units; u += gridDim.x, ++ul) {
         size_t rb, c0;
-        int sp;
         uint32_t ntiles;
-        unit_range(u, rb, sp, c0, ntiles);
-        if (*abort_flag || (ul > 0 && !mbar_wait(aempty, (ul - 1) & 1))) {
+        unit_range(u, rb, c0, ntiles);
+        if (*abort_flag || (ul > 0 && !mbar_wait_sleep(aempty, (ul - 1) & 1))) {
           ok = false;
           break;
         }
         mbar_arrive_expect_tx(afull, tile_bytes);
         bulk_copy_g2s(sA, p.a_img + rb * tile_bytes, tile_bytes, afull);
         a_issued = ul;
-        const size_t t0 = c0 / kTile;
-        for (int pass = 0; ok && pass < 2; ++pass) {
-          for (uint32_t t = 0; t < ntiles; ++t, ++it) {
-            const uint32_t stage = it % kStages, ph = (it / kStages) & 1;
-            if (*abort_flag || !mbar_wait(empty + stage, ph ^ 1)) {
-              ok = false;
-              break;
-            }
-            mbar_arrive_expect_tx(full + stage, tile_bytes);
-            bulk_copy_g2s(sB + stage * tile_bytes, p.b_img + (t0 + t) * tile_bytes, tile_bytes, full + stage);
-            last_stage_it[stage] = static_cast<int>(it);
+        for (uint32_t t = 0; t < ntiles; ++t, ++it) {
+          const uint32_t stage = it % kGemmStages, ph = (it / kGemmStages) & 1;
+          if (*abort_flag || !mbar_wait_sleep(empty + stage, ph ^ 1)) {
+            ok = false;
+            break;
           }
+          mbar_arrive_expect_tx(full + stage, tile_bytes);
+          bulk_copy_g2s(sB + stage * tile_bytes, p.b_img + (c0 / kTile + t) * tile_bytes, tile_bytes, full + stage);
+          last_stage_it[stage] = static_cast<int>(it);
         }
       }
       if (!ok) {
-        win_fail(p, abort_flag, 1);
-        // copies still in flight land in shared memory: wait for them (bounded)
-        for (int s = 0; s < kStages; ++s)
-          if (last_stage_it[s] >= 0) mbar_wait(full + s, (static_cast<uint32_t>(last_stage_it[s]) / kStages) & 1);
+        fail(1);
+        for (int s = 0; s < kGemmStages; ++s)
+          if (last_stage_it[s] >= 0) mbar_wait(full + s, (static_cast<uint32_t>(last_stage_it[s]) / kGemmStages) & 1);
         if (a_issued >= 0) mbar_wait(afull, static_cast<uint32_t>(a_issued) & 1);
       }
     }
   } else if (warp == 1) {
-    // ---- MMA issuer ----
     if (lane == 0) {
       uint32_t it = 0, tc = 0, ul = 0;
       bool ok = true;
       for (size_t u = blockIdx.x; ok && u < units; u += gridDim.x, ++ul) {
         size_t rb, c0;
-        int sp;
         uint32_t ntiles;
-        unit_range(u, rb, sp, c0, ntiles);
-        if (!mbar_wait(afull, ul & 1)) {
+        unit_range(u, rb, c0, ntiles);
+        if (!mbar_wait_sleep(afull, ul & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t a_base = smem_u32(sA);
-        for (int pass = 0; ok && pass < 2; ++pass) {
-          for (uint32_t t = 0; t < ntiles; ++t, ++it, ++tc) {
-            const uint32_t stage = it % kStages, ph = (it / kStages) & 1;
-            const uint32_t acc = tc & 1, aph = (tc >> 1) & 1;
-            if (!mbar_wait(full + stage, ph) || !mbar_wait(accempty + acc, aph ^ 1)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t b_base = smem_u32(sB + stage * tile_bytes);
-            const uint32_t d_tmem = tmem + acc * kTile;
-            for (int kb = 0; kb < nkb; ++kb) {
-#pragma unroll
-              for (int j = 0; j < kKBlock / 16; ++j) {
-                const uint32_t off = static_cast<uint32_t>(kb) * kBlockBytes + static_cast<uint32_t>(j) * 32u;
-                umma_f16(d_tmem, umma_desc(a_base + off), umma_desc(b_base + off), (kb | j) != 0);
-              }
-            }
-            umma_commit(empty + stage);
-            umma_commit(accfull + acc);
-          }
-        }
-        if (ok) umma_commit(aempty);
-      }
-      if (!ok) win_fail(p, abort_flag, 2);
-      // every MMA issued is complete before the accumulators are released
-      umma_commit(drain);
-      mbar_wait(drain, 0);
-    }
-  } else {
-    // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 ----
-    const int ew = warp & 3;
-    const int rloc = ew * 32 + lane;
-    const uint32_t t_lane = tmem + (static_cast<uint32_t>(ew * 32) << 16);
-    const uint32_t hbase = smem_u32(hist) + static_cast<uint32_t>(rloc) * 2u;
-    uint32_t tc = 0;
-    bool ok = true;
-    for (size_t u = blockIdx.x; ok && u < units; u += gridDim.x) {
-      size_t rb, c0;
-      int sp;
-      uint32_t ntiles;
-      unit_range(u, rb, sp, c0, ntiles);
-      const size_t row = rb * kTile + rloc;
-      const bool rv = row < p.rows;
-      const double eps = rv ? static_cast<double>(p.eps[row]) : 0.0;
-      const size_t c1 = min(p.cols, c0 + p.split_cols);
-      if (!p.top1)
-        for (int b = 0; b < kBins; ++b) hist[b * kTile + rloc] = 0;
-      float smax = -__int_as_float(0x7f800000);
-      float s_lo = 0.0f;
-      uint32_t n = 0;
-      uint2 *cand = p.cand + (row * p.splits + sp) * static_cast<size_t>(p.cap);
-      for (int pass = 0; ok && pass < 2; ++pass) {
-        if (pass == 1) {
-          // lower bound on s for 1 - s within 2 eps of the bound on the P-th smallest
-          double lo = -__longlong_as_double(0x7ff0000000000000ll);
-          if (p.top1) {
-            if (smax > -__int_as_float(0x7f800000))
-              lo = static_cast<double>(smax) - 2.0 * eps * (1.0 + 9.5367431640625e-7) -
-                   9.5367431640625e-7 * (1.0 + fabs(static_cast<double>(smax)));
-          } else {
-            uint32_t cum = 0;
-            int bstar = kBins - 1;
-            for (int b = 0; b < kBins - 1; ++b) {
-              cum += hist[b * kTile + rloc];
-              if (cum >= static_cast<uint32_t>(p.P)) {
-                bstar = b;
-                break;
-              }
-            }
-            // bin b holds 128 (1 - s) rounded to nearest: 1 - s <= (b + 0.5) / 128
-            if (bstar < kBins - 1) {
-              const double T = (bstar + 0.5) / 128.0;
-              lo = 1.0 - (T + 2.0 * eps) * (1.0 + 9.5367431640625e-7) - 9.5367431640625e-7;
-            }
-          }
-          s_lo = eps < 1.0 ? __double2float_rd(lo) : -__int_as_float(0x7f800000);
-        }
-        for (uint32_t t = 0; t < ntiles; ++t, ++tc) {
+        for (uint32_t t = 0; t < ntiles; ++t, ++it, ++tc) {
+          const uint32_t stage = it % kGemmStages, ph = (it / kGemmStages) & 1;
           const uint32_t acc = tc & 1, aph = (tc >> 1) & 1;
-          if (!__all_sync(VG_FULL_MASK, mbar_wait(accfull + acc, aph))) {
+          if (!mbar_wait_sleep(full + stage, ph) || !mbar_wait_sleep(accempty + acc, aph ^ 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const size_t col0 = c0 + static_cast<size_t>(t) * kTile;
-          const int nval = static_cast<int>(min(static_cast<size_t>(kTile), c1 - col0));
-#pragma unroll 1
-          for (int ch = 0; ch < kTile / 32; ++ch) {
-            if (ch * 32 >= nval) break;
-            uint32_t v[32];
-            tmem_ld32(t_lane + acc * kTile + ch * 32, v);
-            const int lim = nval - ch * 32;
-            if (pass == 0) {
-              if (p.top1) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  if (j < lim) smax = fmaxf(smax, __uint_as_float(v[j]));
-              } else {
-                // 8 counts loaded, then 8 stored: two equal bins in one group
-                // lose an increment, which only loosens the bound (a count
-                // never exceeds the true one; u16 wrap-around likewise)
-#pragma unroll
-                for (int g = 0; g < 4; ++g) {
-                  uint32_t a[8];
-                  uint16_t c[8];
-#pragma unroll
-                  for (int uu = 0; uu < 8; ++uu) {
-                    const int j = g * 8 + uu;
-                    const float tt = fmaf(__uint_as_float(v[j]), -128.0f, 8388736.0f);  // 2^23 + 128 (1 - s)
-                    int b = static_cast<int>(__float_as_uint(tt)) - 0x4B000000;
-                    b = min(max(b, 0), kBins - 1);
-                    if (j >= lim) b = kBins - 1;
-                    a[uu] = hbase + (static_cast<uint32_t>(b) << 8);
-                  }
-#pragma unroll
-                  for (int uu = 0; uu < 8; ++uu) c[uu] = lds_u16(a[uu]);
-#pragma unroll
-                  for (int uu = 0; uu < 8; ++uu) sts_u16(a[uu], static_cast<uint16_t>(c[uu] + 1));
-                }
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                if (j < lim && __uint_as_float(v[j]) >= s_lo) {
-                  if (rv && n < static_cast<uint32_t>(p.cap))
-                    cand[n] = make_uint2(static_cast<uint32_t>(col0 + ch * 32 + j), v[j]);
-                  ++n;
-                }
-              }
-            }
+          const uint32_t b_base = smem_u32(sB + stage * tile_bytes);
+          for (int ks = 0; ks < p.ksteps; ++ks) {
+            const uint32_t off = static_cast<uint32_t>(ks >> 2) * kBlockBytes + static_cast<uint32_t>(ks & 3) * 32u;
+            umma_f16(tmem + acc * kTile, umma_desc(a_base + off), umma_desc(b_base + off), ks != 0);
           }
-          tc_fence_before();
+          umma_commit(empty + stage);
+          umma_commit(accfull + acc);
+        }
+        if (ok) umma_commit(aempty);
+      }
+      if (!ok) fail(2);
+      umma_commit(drain);
+      mbar_wait(drain, 0);
+    }
+  } else {
+    const int eg = (warp - 2) >> 2, ew = warp & 3;
+    const int rloc = ew * 32 + lane;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(eg) * kTile;
+    const bool vec = (p.ld & 7) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
+    uint32_t tc = 0;
+    bool ok = true;
+    for (size_t u = blockIdx.x; ok && u < units; u += gridDim.x) {
+      size_t rb, c0;
+      uint32_t ntiles;
+      unit_range(u, rb, c0, ntiles);
+      const size_t row = rb * kTile + rloc;
+      const bool rv = row < p.rows;
+      for (uint32_t t = 0; t < ntiles; ++t, ++tc) {
+        const uint32_t acc = tc & 1;
+        if (acc != static_cast<uint32_t>(eg)) continue;
+        if (!__all_sync(VG_FULL_MASK, mbar_wait_sleep(accfull + acc, (tc >> 1) & 1))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t v[kTile];
+#pragma unroll
+        for (int ch = 0; ch < kTile / 32; ++ch) tmem_ld32_nowait(t_lane + ch * 32, v + ch * 32);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(accempty + acc);
+        const size_t col0 = c0 + static_cast<size_t>(t) * kTile;
+        const int nval = static_cast<int>(min(static_cast<size_t>(kTile), p.cols - col0));
+        if (vec && nval == kTile) {
+          // the warp's 32 rows x 256 bytes through shared memory (chunk j of
+          // row r at r * 16 + (j ^ (r & 15)): conflict-free both ways), then
+          // whole 128-byte lines: lanes 0-15 one row, lanes 16-31 the next
+          uint4 *stg = stage_out + static_cast<size_t>(warp - 2) * 32 * 16;
+#pragma unroll
+          for (int j = 0; j < kTile / 8; ++j) {
+            __half2 h0 = __floats2half2_rn(__uint_as_float(v[8 * j]), __uint_as_float(v[8 * j + 1]));
+            __half2 h1 = __floats2half2_rn(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3]));
+            __half2 h2 = __floats2half2_rn(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5]));
+            __half2 h3 = __floats2half2_rn(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7]));
+            uint4 o;
+            o.x = *reinterpret_cast<uint32_t *>(&h0);
+            o.y = *reinterpret_cast<uint32_t *>(&h1);
+            o.z = *reinterpret_cast<uint32_t *>(&h2);
+            o.w = *reinterpret_cast<uint32_t *>(&h3);
+            stg[lane * 16 + (j ^ (lane & 15))] = o;
+          }
           __syncwarp();
-          if (lane == 0) mbar_arrive(accempty + acc);
+          const int half = lane >> 4, j = lane & 15;
+#pragma unroll 4
+          for (int r2 = 0; r2 < 32; r2 += 2) {
+            const int r = r2 + half;
+            const size_t grow = rb * kTile + ew * 32 + r;
+            const uint4 o = stg[r * 16 + (j ^ (r & 15))];
+            if (grow < p.rows) *reinterpret_cast<uint4 *>(p.out + grow * p.ld + col0 + 8 * j) = o;
+          }
+          __syncwarp();
+        } else if (rv) {
+          __half *dst = p.out + row * p.ld + col0;
+#pragma unroll
+          for (int j = 0; j < kTile; ++j)
+            if (j < nval) dst[j] = __float2half_rn(__uint_as_float(v[j]));
         }
       }
-      if (rv && ok) p.count[row * p.splits + sp] = n;
     }
-    if (!ok) win_fail(p, abort_flag, 3);
+    if (!ok) fail(3);
   }
   tc_fence_before();
   __syncthreads();
@@ -394,11 +742,6 @@ __global__ void __launch_bounds__(kWinThreads, 1) tc_window_kernel(const WinPara
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
-}
-
-size_t win_smem_bytes(int kp) {
-  const size_t tile = static_cast<size_t>(kp / kKBlock) * kBlockBytes;
-  return 1024 + tile * (1 + kStages) + static_cast<size_t>(kBins) * kTile * 2 + 16 * 8 + 16;
 }
 
 // ---- operand images ------------------------------------------------------
@@ -611,21 +954,28 @@ cudaError_t launch_umma_image(const float *x, size_t rows, int d, int kp, void *
 }
 
 void tc_select_plan(size_t rows, size_t cols, int P, int num_sms, int *splits, uint32_t *split_cols, int *cap) {
-  const size_t rblocks = (rows + kTile - 1) / kTile;
-  size_t sp = (cols + kMaxSplitCols - 1) / kMaxSplitCols;
-  // few row blocks: more column ranges keep every SM busy, as long as each
-  // range stays wide enough for a tight bound on its P-th product
-  const size_t bal = rblocks ? static_cast<size_t>(num_sms) / rblocks : 1;
-  const size_t wide = std::max<size_t>(1, cols / 8192);
-  sp = std::max(sp, std::min(bal, wide));
-  if (sp < 1) sp = 1;
-  size_t per = (cols + sp - 1) / sp;
-  per = (per + kTile - 1) / kTile * kTile;
-  if (per == 0) per = kTile;
-  sp = (cols + per - 1) / per;
-  if (sp < 1) sp = 1;
-  *splits = static_cast<int>(sp);
-  *split_cols = static_cast<uint32_t>(per);
+  // Column ranges per row block: the split that finishes the work units in
+  // the fewest rounds of num_sms CTAs (relative to one whole row block),
+  // ranges of at least 512 columns.  The ranges of a row share their bound
+  // on the P-th product, so splitting costs little in window width.
+  const size_t rblocks = std::max<size_t>(1, (rows + kTile - 1) / kTile);
+  const size_t ctiles = (cols + kTile - 1) / kTile;
+  const size_t smax = std::max<size_t>(1, std::min<size_t>(64, ctiles / 4));
+  size_t best = 1;
+  double best_t = 1e30;
+  for (size_t sp = 1; sp <= smax; ++sp) {
+    const size_t per_tiles = (ctiles + sp - 1) / sp;
+    const size_t real_sp = (ctiles + per_tiles - 1) / per_tiles;
+    const size_t rounds = (rblocks * real_sp + num_sms - 1) / num_sms;
+    const double t = static_cast<double>(rounds) * per_tiles + 2.0 * rounds;  // + per-unit overhead
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = sp;
+    }
+  }
+  const size_t per_tiles = (ctiles + best - 1) / best;
+  *split_cols = static_cast<uint32_t>(per_tiles * kTile);
+  *splits = static_cast<int>((ctiles + per_tiles - 1) / per_tiles);
   *cap = P == 1 ? 32 : std::min(1024, (2 * P + 64 + 31) / 32 * 32);
 }
 
@@ -633,7 +983,7 @@ size_t tc_select_workspace_bytes(size_t rows, size_t cols, int P, int num_sms) {
   int sp, cap;
   uint32_t per;
   tc_select_plan(rows, cols, P, num_sms, &sp, &per, &cap);
-  return rows * sp * (static_cast<size_t>(cap) * 8 + 4) + 256;
+  return rows * sp * 2 * (static_cast<size_t>(cap) * 8 + 4) + rows * 4 + 256;
 }
 
 cudaError_t launch_tc_select(const TcSelect &t, int num_sms, cudaStream_t s) {
@@ -643,13 +993,17 @@ cudaError_t launch_tc_select(const TcSelect &t, int num_sms, cudaStream_t s) {
   uint32_t per;
   tc_select_plan(t.rows, t.cols, t.P, num_sms, &sp, &per, &cap);
   uint2 *cand = static_cast<uint2 *>(t.workspace);
-  uint32_t *count = reinterpret_cast<uint32_t *>(cand + t.rows * sp * static_cast<size_t>(cap));
+  uint32_t *count = reinterpret_cast<uint32_t *>(cand + t.rows * sp * 2 * static_cast<size_t>(cap));
+  uint32_t *gbound = count + t.rows * sp * 2;
+  cudaError_t e = cudaMemsetAsync(gbound, 0, t.rows * 4, s);
+  if (e != cudaSuccess) return e;
   WinParams wp{};
   wp.a_img = static_cast<const uint8_t *>(t.a_img);
   wp.b_img = static_cast<const uint8_t *>(t.b_img);
   wp.rows = t.rows;
   wp.cols = t.cols;
   wp.kp = t.kp;
+  wp.ksteps = (t.d + 15) / 16;
   wp.P = t.P;
   wp.top1 = t.P == 1;
   wp.splits = sp;
@@ -658,9 +1012,10 @@ cudaError_t launch_tc_select(const TcSelect &t, int num_sms, cudaStream_t s) {
   wp.eps = t.eps;
   wp.cand = cand;
   wp.count = count;
+  wp.gbound = gbound;
   wp.error = t.error;
   const size_t smem = win_smem_bytes(t.kp);
-  cudaError_t e = cudaFuncSetAttribute(tc_window_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  e = cudaFuncSetAttribute(tc_window_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const size_t units = (t.rows + kTile - 1) / kTile * static_cast<size_t>(sp);
@@ -673,7 +1028,7 @@ cudaError_t launch_tc_select(const TcSelect &t, int num_sms, cudaStream_t s) {
   FinParams fp{};
   fp.cand = cand;
   fp.count = count;
-  fp.splits = sp;
+  fp.splits = sp * 2;  // a candidate segment per (range, epilogue warpgroup)
   fp.cap = cap;
   fp.eps = t.eps;
   fp.q = t.q;
@@ -692,6 +1047,37 @@ cudaError_t launch_tc_select(const TcSelect &t, int num_sms, cudaStream_t s) {
       : t.P <= 128 ? launch_finish<4>(fp, s) : launch_finish<8>(fp, s);
   if (e == cudaSuccess && t.marks[2]) cudaEventRecord(t.marks[2], s);
   return e;
+}
+
+cudaError_t launch_tc_gemm_f16(const void *a_img, size_t rows, const void *b_img, size_t cols, int d, int kp,
+                               void *out, size_t ld, int *error, int num_sms, cudaStream_t s) {
+  if (rows == 0 || cols == 0) return cudaSuccess;
+  if ((kp != 64 && kp != 128) || d < 1 || d > kp) return cudaErrorInvalidValue;
+  const size_t rblocks = (rows + kTile - 1) / kTile, ctiles = (cols + kTile - 1) / kTile;
+  // column ranges of at least 8 tiles, enough work units for every SM twice
+  size_t sp = std::max<size_t>(1, (2 * static_cast<size_t>(num_sms) + rblocks - 1) / rblocks);
+  sp = std::min(sp, std::max<size_t>(1, ctiles / 8));
+  const size_t per = (ctiles + sp - 1) / sp;
+  GemmParams gp{};
+  gp.a_img = static_cast<const uint8_t *>(a_img);
+  gp.b_img = static_cast<const uint8_t *>(b_img);
+  gp.rows = rows;
+  gp.cols = cols;
+  gp.ld = ld;
+  gp.kp = kp;
+  gp.ksteps = (d + 15) / 16;
+  gp.splits = static_cast<int>((ctiles + per - 1) / per);
+  gp.split_cols = static_cast<uint32_t>(per * kTile);
+  gp.out = static_cast<__half *>(out);
+  gp.error = error;
+  const size_t smem = 1024 + static_cast<size_t>(kp / kKBlock) * kBlockBytes * (1 + kGemmStages) +
+                      static_cast<size_t>(kEpiWarps) * 32 * 16 * 16 + 16 * 8 + 16;
+  cudaError_t e = cudaFuncSetAttribute(tc_gemm_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  const size_t units = rblocks * gp.splits;
+  tc_gemm_f16_kernel<<<static_cast<unsigned>(std::min<size_t>(units, num_sms)), kWinThreads, smem, s>>>(gp);
+  return cudaGetLastError();
 }
 
 }  // namespace vg

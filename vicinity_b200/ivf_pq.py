@@ -446,7 +446,12 @@ class IVFPQIndex:
 
     # -- sharding ----------------------------------------------------------------
     def shard(self, rank: int, world_size: int, nccl_id: bytes, timeout_ms: int = 60000) -> None:
-        """Keep only this rank's inverted lists; searches all-gather top-k."""
+        """Make this built index rank ``rank`` of a list-sharded group: the
+        device keeps only this rank's inverted lists (greedy size-balanced
+        packing).  Afterwards every rank searches batches of its own -- the
+        same size on every rank, every search called on all ranks -- and gets
+        the results of its own queries; the ranks exchange queries, probes,
+        a pruning seed and per-rank top-k over NCCL."""
         if len(nccl_id) != 128:
             raise ValueError("nccl_id must be 128 bytes")
         buf = (C.c_uint8 * 128).from_buffer_copy(nccl_id)
