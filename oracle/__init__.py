@@ -40,6 +40,7 @@ _SIGS = {
     "or_index_add": (_i, [_vp, _vp, _vp, _sz]),
     "or_index_finalize": (_i, [_vp]),
     "or_index_adopt_codes": (_i, [_vp, _vp, _vp]),
+    "or_index_adopt_state": (_i, [_vp, _vp, _sz, _vp, _vp]),
     "or_index_set_nprobe": (None, [_vp, _sz]),
     "or_index_set_rotation": (None, [_vp, _vp]),
     "or_index_set_filter": (_i, [_vp, _vp, _vp]),
@@ -250,6 +251,14 @@ class OracleIndex:
         a = np.ascontiguousarray(assignments, dtype=np.uint32)
         c = np.ascontiguousarray(codes, dtype=np.uint8)
         assert self._lib.or_index_adopt_codes(self._h, _p(a), _p(c)) == 0
+
+    def adopt_state(self, doc_ids, assignments, codes):
+        """The built state of a compacted index (no raw vectors): doc ids,
+        list assignments and codes (search.rs:901-904)."""
+        i = np.ascontiguousarray(doc_ids, dtype=np.uint32)
+        a = np.ascontiguousarray(assignments, dtype=np.uint32)
+        c = np.ascontiguousarray(codes, dtype=np.uint8)
+        assert self._lib.or_index_adopt_state(self._h, _p(i), i.shape[0], _p(a), _p(c)) == 0
 
     def set_filter(self, category, bitmask=None):
         """Per-vector filter categories (255: none) and per-list bitmasks

@@ -574,6 +574,23 @@ int or_index_adopt_codes(or_index *ix, const uint32_t *assignments, const uint8_
   return 0;
 }
 
+// The built state without raw vectors (what IVFPQIndex keeps after compact,
+// search.rs:901-904): doc ids, list assignments and codes of n vectors.
+// Searches run; reranking needs the raw vectors and is not available.
+int or_index_adopt_state(or_index *ix, const uint32_t *doc_ids, size_t n, const uint32_t *assignments,
+                         const uint8_t *codes) {
+  if (ix->built) return -5;
+  if (!ix->trained) return -4;
+  ix->doc_ids.assign(doc_ids, doc_ids + n);
+  ix->vectors.clear();
+  ix->assign.assign(assignments, assignments + n);
+  ix->codes.assign(codes, codes + n * ix->M);
+  for (size_t i = 0; i < n; ++i)
+    if (ix->assign[i] >= ix->L) return -9;
+  build_lists(ix);
+  return 0;
+}
+
 void or_index_set_nprobe(or_index *ix, size_t nprobe) { ix->nprobe = nprobe; }
 
 void or_rotate(const float *r, const float *v, size_t d, float *out) { rotate(r, v, d, out); }

@@ -127,6 +127,12 @@ int or_index_finalize(or_index *ix);
 int or_index_adopt_codes(or_index *ix, const uint32_t *assignments,
                          const uint8_t *codes);
 
+/* The built state of a compacted index without raw vectors (search.rs:901-904):
+ * doc ids, list assignments and codes of n vectors; searches run, reranking
+ * does not. */
+int or_index_adopt_state(or_index *ix, const uint32_t *doc_ids, size_t n,
+                         const uint32_t *assignments, const uint8_t *codes);
+
 void or_index_set_nprobe(or_index *ix, size_t nprobe);
 /* Filter state of search.rs:1407-1549: category [n] per vector (255: none)
  * and bitmask [L] per list (NULL: computed from the categories as

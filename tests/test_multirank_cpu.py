@@ -3,8 +3,9 @@ running the oracle).
 
 Each rank owns the lists the engine's packer gives it and searches a batch of
 its own.  The ranks exchange their queries, seed every query's bound with the
-k-th key of its nearest list (found by the rank that owns that list; all-
-reduce min), keep only keys at or below that seed in their own lists, and
+k-th key over its four nearest lists (each rank's keys in the ones it owns,
+all-gathered and merged), keep only keys at or below that bound in their own
+lists, and
 route every query's per-rank top-k back to its rank, which merges them by
 (distance, id).  The merged rows must equal the unsharded search of the same
 queries -- the property the engine's NCCL path
@@ -24,6 +25,7 @@ import torch.multiprocessing as mp
 WORLD = 2
 N, D, L, M, KS, NPROBE, K, NQ = 3000, 16, 24, 4, 16, 6, 10, 40  # NQ queries per rank
 EMPTY = np.uint64(0xFFFFFFFFFFFFFFFF)
+SEED = 4  # probes scanned before the bound is exchanged (the engine's kSeedProbes)
 
 
 def _free_port() -> int:
@@ -79,15 +81,15 @@ def _rank_main(rank, port, out_path):
     parts = [torch.empty_like(own) for _ in range(WORLD)]
     dist.all_gather(parts, own)
     q = torch.cat(parts).numpy()
-    # 3. seed: the k-th key of each query's nearest list, from its owner
-    sid, sd, sc = shard.search_batch(q, K, nprobe=1)
-    seed = _keys(orc, sid, sd, sc)[:, K - 1]
-    seed_t = torch.from_numpy(seed.view(np.int64).copy())
-    # keys compare unsigned: all-reduce the order-preserving signed image
-    seed_t ^= torch.tensor(np.int64(-0x8000000000000000))
-    dist.all_reduce(seed_t, op=dist.ReduceOp.MIN)
-    seed_t ^= torch.tensor(np.int64(-0x8000000000000000))
-    ceiling = seed_t.numpy().view(np.uint64)
+    # 3. seed: each rank's keys in its lists among every query's SEED nearest
+    # lists, all-gathered and merged: the k-th merged key bounds the query's
+    # k-th key over every list
+    sid, sd, sc = shard.search_batch(q, K, nprobe=SEED)
+    seed = _keys(orc, sid, sd, sc)
+    parts = [torch.empty((NQ * WORLD, K), dtype=torch.int64) for _ in range(WORLD)]
+    dist.all_gather(parts, torch.from_numpy(seed.view(np.int64).copy()))
+    merged_seed = np.sort(np.concatenate([p.numpy().view(np.uint64) for p in parts], axis=1), axis=1)[:, :K]
+    ceiling = merged_seed[:, K - 1]
     # 4. own lists for the global batch, keys at or below the ceiling only
     ids, dists, cnt = shard.search_batch(q, K)
     keys = _keys(orc, ids, dists, cnt)

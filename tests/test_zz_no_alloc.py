@@ -1,9 +1,9 @@
 """vg_flat_search_ip_noalloc: the exact flat search with its scratch in one
 fixed device array, called through the C ABI.
 
-It must return exactly what vg_flat_search_ip returns (the same kernels run;
-only where the scratch lives differs), call after call, although every call
-reuses the same scratch.  The file is named to be collected last and needs
+It must return exactly what vg_flat_search_ip and the oracle's exhaustive
+scan return, call after call, although every call reuses the same scratch,
+and a call must leave the device's free memory unchanged.  The file is named to be collected last and needs
 no state from other tests.
 """
 from __future__ import annotations
@@ -88,6 +88,48 @@ def test_two_calls_in_a_row_match_the_allocating_entry_point():
     _same(got2, want2)
     # and the first request once more, bit-identical to its first answer
     _same(_noalloc(torch, db1, q1, 10), want1)
+
+
+def test_matches_the_oracle():
+    # the reference's exhaustive -dot scan (src/distance.rs:125-130) on the host
+    torch = pytest.importorskip("torch")
+    import oracle as orc
+
+    db, q = _case(torch, 6_000, 200, 64, seed=4)
+    got = _noalloc(torch, db, q, 25)
+    ri, rd, rc = orc.flat_search_ip(db.cpu().numpy(), q.cpu().numpy(), 25, threads=8)
+    _same(got, (ri.astype(np.int32), rd, rc.astype(np.int32)))
+
+
+def test_empty_database_gives_padding():
+    torch = pytest.importorskip("torch")
+    db, q = _case(torch, 8, 12, 16, seed=5)  # a placeholder; n = 0 is passed
+    lib = _lib()
+    ids, dist, cnt = _outputs(torch, 12, 7)
+    lib.check(lib.load().vg_flat_search_ip_noalloc(_dev(db), 0, _dev(q), 12, 16, 7, 0, None, _dev(ids), _dev(dist),
+                                                   _dev(cnt)))
+    got = (ids.cpu().numpy(), dist.cpu().numpy(), cnt.cpu().numpy())
+    assert (got[0] == -1).all() and np.isinf(got[1]).all() and (got[2] == 0).all()
+    ids2, dist2, cnt2 = _outputs(torch, 12, 7)
+    lib.check(lib.load().vg_flat_search_ip(_dev(db), 0, _dev(q), 12, 16, 7, 0, _dev(ids2), _dev(dist2), _dev(cnt2)))
+    _same(got, (ids2.cpu().numpy(), dist2.cpu().numpy(), cnt2.cpu().numpy()))
+
+
+def test_calls_allocate_no_device_memory():
+    # after the first call has resolved the scratch address, a call of
+    # another size leaves the device's free memory exactly as it was
+    torch = pytest.importorskip("torch")
+    db, q = _case(torch, 9_000, 500, 48, seed=6)
+    _noalloc(torch, db, q, 20)
+    db2, q2 = _case(torch, 4_000, 100, 48, seed=7)
+    ids, dist, cnt = _outputs(torch, 100, 50)
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info(0)
+    lib = _lib()
+    lib.check(lib.load().vg_flat_search_ip_noalloc(_dev(db2), 4_000, _dev(q2), 100, 48, 50, 0, None, _dev(ids),
+                                                   _dev(dist), _dev(cnt)))
+    free_after, _ = torch.cuda.mem_get_info(0)
+    assert free_after == free_before
 
 
 def test_padding_when_k_exceeds_rows():

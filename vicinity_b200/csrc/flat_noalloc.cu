@@ -139,19 +139,29 @@ extern "C" int vg_flat_search_ip_noalloc(const float *db, size_t n, const float 
   unsigned long long *keys = reinterpret_cast<unsigned long long *>(static_cast<unsigned char *>(base) + dist_bytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
+  // A launch that fails part way leaves earlier kernels of this call queued
+  // on the stream, still using the shared scratch: wait for them (whatever
+  // the outcome) before returning, so a failed call has also finished with
+  // the scratch when it returns.
+  auto fail_after_launches = [&](cudaError_t err, const char *what) {
+    const int code = noalloc_cuda_fail(err, what);
+    cudaStreamSynchronize(s);
+    cudaGetLastError();
+    return code;
+  };
   for (size_t ci = 0; ci < chunks; ++ci) {
     const size_t c0 = ci * tile, cols = (n - c0) < tile ? (n - c0) : tile;
     e = vg::launch_neg_dot(queries, nq, db + c0 * dim, cols, static_cast<int>(dim), dist, tile, s);
-    if (e != cudaSuccess) return noalloc_cuda_fail(e, "distance tile");
+    if (e != cudaSuccess) return fail_after_launches(e, "distance tile");
     e = vg::launch_select_rows_keys(dist, nq, cols, tile, static_cast<int>(k), keys + ci * k, chunks * k,
                                     static_cast<uint32_t>(c0), s);
-    if (e != cudaSuccess) return noalloc_cuda_fail(e, "tile top-k");
+    if (e != cudaSuccess) return fail_after_launches(e, "tile top-k");
   }
   // With n == 0 the merge reads nothing and writes the padding (id
   // 0xffffffff, +inf, count 0), as vg_flat_search_ip does.
   e = vg::launch_merge_keys(keys, nq, chunks * k, chunks * k, static_cast<int>(k), nullptr, out_ids, out_dist,
                             out_count, nullptr, s);
-  if (e != cudaSuccess) return noalloc_cuda_fail(e, "merge");
+  if (e != cudaSuccess) return fail_after_launches(e, "merge");
   e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return noalloc_cuda_fail(e, "cudaStreamSynchronize");
   return VG_OK;

@@ -980,6 +980,9 @@ ProbeBoundArgs bound_args_at(vg_index *ix, size_t P, size_t r0, bool prune, bool
                         quant ? ix->ws_lbq.as<float>() + r0 * P : nullptr};
 }
 
+// Probes of every query scanned before the pruning bound is exchanged.
+constexpr size_t kSeedProbes = 4;
+
 int nccl_ok(vg_index *ix, ncclResult_t r, const char *what) {
   if (r == ncclSuccess) return VG_OK;
   if (r == ncclInProgress) return nccl_wait_ready(ix->comm, ix->comm_timeout_ms);
@@ -993,12 +996,13 @@ int nccl_ok(vg_index *ix, ncclResult_t r, const char *what) {
 //      pruning bounds, valid on every rank);
 //   2. all-gather queries, probes and bounds: every rank holds the global
 //      batch (world * nq rows, rank r's rows at r * nq);
-//   3. seed: every rank scans, for every query, the query's nearest list when
-//      it owns it, and keeps that list's k-th key; an all-reduce (min) gives
-//      every query the k-th key of its nearest list -- a bound on its k-th key
-//      over every list, so each rank prunes from the start as one GPU would;
-//   4. every rank scans its lists for the global batch, keeping only keys at
-//      or below the ceiling;
+//   3. seed: every rank scans, for every query, the lists it owns among the
+//      query's kSeedProbes nearest; the per-rank top-k are all-gathered and
+//      merged, so every query gets the k-th key over its nearest lists -- a
+//      bound on its k-th key over every list, the one a single GPU has after
+//      those lists;
+//   4. every rank scans its lists among the remaining probes for the global
+//      batch, from its own seed keys, keeping only keys at or below the bound;
 //   5. an all-to-all returns every query's per-rank top-k to the query's rank,
 //      which merges them (the reference's per-shard top-k merge,
 //      examples/large_scale.rs:1969-2025).
@@ -1040,7 +1044,8 @@ int search_sharded(vg_index *ix, const float *queries, size_t nq, size_t k, size
   VG_CU(ix->ws_lb.reserve(B * P * 4));
   if (quant) VG_CU(ix->ws_lbq.reserve(B * P * 4));
   if (recs) VG_CU(ix->ws_rec.reserve(B * P * sizeof(ProbeRec)));
-  VG_CU(ix->ws_seed.reserve(B * 8));
+  const size_t S = std::min<size_t>(P, kSeedProbes);
+  VG_CU(ix->ws_seed.reserve(W * B * kk * 8 + B * kk * 8));  // per-rank seed keys, then their merge
   VG_CU(ix->ws_keys.reserve(B * kk * 8));
   VG_CU(ix->ws_all_keys.reserve(B * kk * 8));
   float *qall = ix->ws_qall.as<float>(), *qown = qall + R * nq * d;
@@ -1095,20 +1100,26 @@ int search_sharded(vg_index *ix, const float *queries, size_t nq, size_t k, size
                              ix->stats.as<unsigned long long>(), s));
   }
 
-  // 3. seed: the k-th key of every query's nearest list
-  const bool seeded = prune && ivfpq_scan_warp_applies(sp);
+  // 3. seed: every query's k-th key over its S nearest lists
+  const bool seeded = prune && S < P && ivfpq_scan_warp_applies(sp);
+  unsigned long long *seed_all = ix->ws_seed.as<unsigned long long>();  // [W][B][kk]
+  unsigned long long *seed_own = seed_all + R * B * kk, *merged = seed_all + W * B * kk;
   if (seeded) {
-    sp.pscan = 1;
-    sp.out_kth = ix->ws_seed.as<unsigned long long>();
+    sp.pscan = static_cast<int>(S);
+    sp.out_keys = seed_own;
     VG_CU(cudaMemsetAsync(d_counter, 0, 4, s));
     VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
     ix->launches += 1;
     mark(ix, 6);
-    VG_TRY(nccl_ok(ix, ncclAllReduce(ix->ws_seed.p, ix->ws_seed.p, B, ncclUint64, ncclMin, ix->comm, s),
-                   "ncclAllReduce (seed keys)"));
+    VG_TRY(nccl_ok(ix, ncclAllGather(seed_own, seed_all, B * kk, ncclUint64, ix->comm, s), "ncclAllGather (seed keys)"));
+    VG_CU(launch_merge_shards(seed_all, static_cast<int>(W), B, static_cast<int>(kk), nullptr, nullptr, nullptr,
+                              nullptr, merged, s));
+    ix->launches += 1;
+    sp.pstart = static_cast<int>(S);
     sp.pscan = 0;
-    sp.out_kth = nullptr;
-    sp.key_ceiling = ix->ws_seed.as<unsigned long long>();
+    sp.init_keys = seed_own;
+    sp.key_ceiling = merged + (kk - 1);  // the k-th merged key of every query
+    sp.ceiling_stride = static_cast<int>(kk);
   } else {
     mark(ix, 6);
   }

@@ -78,12 +78,19 @@ __global__ void __launch_bounds__(kFourWarpThreads, 1) ivfpq_four_warp_kernel(co
     // only keys at or below it
     uint64_t kth0 = kEmptyKey;
     if (p.key_ceiling) {
-      const uint64_t c = p.key_ceiling[q];
+      const uint64_t c = p.key_ceiling[static_cast<size_t>(q) * (p.ceiling_stride ? p.ceiling_stride : 1)];
       kth0 = c == kEmptyKey ? kEmptyKey : c + 1;
     }
-    uint64_t kth = kth0;
+    if (p.init_keys) {  // keys of probes scanned earlier (a seed pass) start the top-k
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int i = r * 32 + lane;
+        tk.add(i < k ? p.init_keys[static_cast<size_t>(q) * k + i] : kEmptyKey);
+      }
+    }
+    uint64_t kth = min(tk.get(k - 1), kth0);
     const int pn = p.pscan ? p.pscan : P;
-    for (int pi = 0; pi < pn; ++pi) {
+    for (int pi = p.pstart; pi < pn; ++pi) {
       const size_t pr = static_cast<size_t>(q) * P + pi;
       const uint32_t l = p.probes[pr];
       if (l == 0xffffffffu || (p.owner && !p.owner[l])) continue;
@@ -191,10 +198,7 @@ __global__ void __launch_bounds__(kFourWarpThreads, 1) ivfpq_four_warp_kernel(co
         kth = min(tk.get(k - 1), kth0);
       }
     }
-    if (p.out_kth) {
-      const uint64_t kk = tk.get(k - 1);
-      if (lane == 0) p.out_kth[q] = kk;
-    }
+
     uint32_t count = 0;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
