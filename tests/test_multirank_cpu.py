@@ -3,10 +3,10 @@ running the oracle).
 
 Each rank owns the lists the engine's packer gives it and searches a batch of
 its own.  The ranks exchange their queries, seed every query's bound with the
-k-th key over its four nearest lists (each rank's keys in the ones it owns,
-all-gathered and merged), keep only keys at or below that bound in their own
-lists, and
-route every query's per-rank top-k back to its rank, which merges them by
+k-th key of its nearest list (scored by the rank that owns it; per-rank seed
+keys all-gathered and merged), keep only keys at or below that bound in their
+own lists, and route every query's per-rank top-k back to its rank, which
+merges them by
 (distance, id).  The merged rows must equal the unsharded search of the same
 queries -- the property the engine's NCCL path
 (vg_ivfpq_shard / vg_ivfpq_search_batch) relies on.  The partition comes from
@@ -25,7 +25,7 @@ import torch.multiprocessing as mp
 WORLD = 2
 N, D, L, M, KS, NPROBE, K, NQ = 3000, 16, 24, 4, 16, 6, 10, 40  # NQ queries per rank
 EMPTY = np.uint64(0xFFFFFFFFFFFFFFFF)
-SEED = 4  # probes scanned before the bound is exchanged (the engine's kSeedProbes)
+SEED = 1  # probes scanned before the bound is exchanged (the engine's kSeedProbes)
 
 
 def _free_port() -> int:

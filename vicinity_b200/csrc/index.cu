@@ -980,8 +980,11 @@ ProbeBoundArgs bound_args_at(vg_index *ix, size_t P, size_t r0, bool prune, bool
                         quant ? ix->ws_lbq.as<float>() + r0 * P : nullptr};
 }
 
-// Probes of every query scanned before the pruning bound is exchanged.
-constexpr size_t kSeedProbes = 4;
+// Probes of every query scanned before the pruning bound is exchanged: the
+// nearest list only.  It belongs to one rank, which scores it as one GPU
+// would (with no bound yet); with more seed probes every rank would also
+// score its first owned list without a bound, work one GPU never does.
+constexpr size_t kSeedProbes = 1;
 
 int nccl_ok(vg_index *ix, ncclResult_t r, const char *what) {
   if (r == ncclSuccess) return VG_OK;
