@@ -6,8 +6,8 @@ its own.  The ranks exchange their queries, seed every query's bound with the
 k-th key of its nearest list (scored by the rank that owns it; per-rank seed
 keys all-gathered and merged), keep only keys at or below that bound in their
 own lists, and route every query's per-rank top-k back to its rank, which
-merges them by
-(distance, id).  The merged rows must equal the unsharded search of the same
+merges them by (distance, id).  The merged rows must equal the unsharded
+search of the same
 queries -- the property the engine's NCCL path
 (vg_ivfpq_shard / vg_ivfpq_search_batch) relies on.  The partition comes from
 the engine library's host-only vg_shard_assign_lists.

@@ -999,11 +999,10 @@ int nccl_ok(vg_index *ix, ncclResult_t r, const char *what) {
 //      pruning bounds, valid on every rank);
 //   2. all-gather queries, probes and bounds: every rank holds the global
 //      batch (world * nq rows, rank r's rows at r * nq);
-//   3. seed: every rank scans, for every query, the lists it owns among the
-//      query's kSeedProbes nearest; the per-rank top-k are all-gathered and
-//      merged, so every query gets the k-th key over its nearest lists -- a
-//      bound on its k-th key over every list, the one a single GPU has after
-//      those lists;
+//   3. seed: the rank owning a query's nearest list scores it; an all-reduce
+//      (min) of every query's k-th key gives every rank the k-th key of the
+//      query's nearest list -- a bound on its k-th key over every list, the
+//      one a single GPU has after that list;
 //   4. every rank scans its lists among the remaining probes for the global
 //      batch, from its own seed keys, keeping only keys at or below the bound;
 //   5. an all-to-all returns every query's per-rank top-k to the query's rank,
@@ -1048,7 +1047,7 @@ int search_sharded(vg_index *ix, const float *queries, size_t nq, size_t k, size
   if (quant) VG_CU(ix->ws_lbq.reserve(B * P * 4));
   if (recs) VG_CU(ix->ws_rec.reserve(B * P * sizeof(ProbeRec)));
   const size_t S = std::min<size_t>(P, kSeedProbes);
-  VG_CU(ix->ws_seed.reserve(W * B * kk * 8 + B * kk * 8));  // per-rank seed keys, then their merge
+  VG_CU(ix->ws_seed.reserve(B * kk * 8 + B * 8));  // this rank's seed keys, then every query's k-th key
   VG_CU(ix->ws_keys.reserve(B * kk * 8));
   VG_CU(ix->ws_all_keys.reserve(B * kk * 8));
   float *qall = ix->ws_qall.as<float>(), *qown = qall + R * nq * d;
@@ -1105,24 +1104,24 @@ int search_sharded(vg_index *ix, const float *queries, size_t nq, size_t k, size
 
   // 3. seed: every query's k-th key over its S nearest lists
   const bool seeded = prune && S < P && ivfpq_scan_warp_applies(sp);
-  unsigned long long *seed_all = ix->ws_seed.as<unsigned long long>();  // [W][B][kk]
-  unsigned long long *seed_own = seed_all + R * B * kk, *merged = seed_all + W * B * kk;
+  unsigned long long *seed_own = ix->ws_seed.as<unsigned long long>();  // [B][kk]
+  unsigned long long *ceiling = seed_own + B * kk;                       // [B]
   if (seeded) {
     sp.pscan = static_cast<int>(S);
     sp.out_keys = seed_own;
+    sp.out_kth = ceiling;
     VG_CU(cudaMemsetAsync(d_counter, 0, 4, s));
     VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
     ix->launches += 1;
     mark(ix, 6);
-    VG_TRY(nccl_ok(ix, ncclAllGather(seed_own, seed_all, B * kk, ncclUint64, ix->comm, s), "ncclAllGather (seed keys)"));
-    VG_CU(launch_merge_shards(seed_all, static_cast<int>(W), B, static_cast<int>(kk), nullptr, nullptr, nullptr,
-                              nullptr, merged, s));
-    ix->launches += 1;
+    // one rank holds each query's seed keys (kEmptyKey elsewhere): min over ranks
+    VG_TRY(nccl_ok(ix, ncclAllReduce(ceiling, ceiling, B, ncclUint64, ncclMin, ix->comm, s),
+                   "ncclAllReduce (seed bounds)"));
     sp.pstart = static_cast<int>(S);
     sp.pscan = 0;
+    sp.out_kth = nullptr;
     sp.init_keys = seed_own;
-    sp.key_ceiling = merged + (kk - 1);  // the k-th merged key of every query
-    sp.ceiling_stride = static_cast<int>(kk);
+    sp.key_ceiling = ceiling;
   } else {
     mark(ix, 6);
   }

@@ -294,6 +294,7 @@ struct ScanParams {
   // list-sharded search (warp-per-query kernels only; zero-initialised = off):
   int pstart, pscan;                     // probes [pstart, pscan) are visited (pscan 0: P); row stride stays P
   const unsigned long long *init_keys;   // [nq][k] keys the query's top-k starts from (nullable)
+  unsigned long long *out_kth;           // [nq] the query's k-th kept key (kEmptyKey: fewer than k) (nullable)
   const unsigned long long *key_ceiling; // keys above the query's ceiling are never kept (nullable) ...
   int ceiling_stride;                    // ... read at key_ceiling[q * ceiling_stride] (0: stride 1)
   int force_warp;                        // use the warp-per-query kernels at any batch size
@@ -310,7 +311,7 @@ cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms,
 cudaError_t launch_ivfpq_scan_generic(const ScanParams &p, int num_sms, cudaStream_t s);
 
 // Whether launch_ivfpq_scan with force_warp runs a warp-per-query kernel for
-// p (the kernels that honour pstart, pscan, init_keys and key_ceiling).
+// p (the kernels that honour pstart, pscan, init_keys, out_kth and key_ceiling).
 bool ivfpq_scan_warp_applies(const ScanParams &p);
 
 // Name of the kernel variant launch_ivfpq_scan would run for p.

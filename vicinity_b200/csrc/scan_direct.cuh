@@ -180,6 +180,10 @@ __global__ void __launch_bounds__(kDirectThreads, 1) ivfpq_direct_kernel(const S
       }
     }
 
+    if (p.out_kth) {
+      const uint64_t kk = tk.get(k - 1);
+      if (lane == 0) p.out_kth[q] = kk;
+    }
     uint32_t count = 0;
 #pragma unroll
     for (int r = 0; r < R; ++r) {

@@ -199,6 +199,10 @@ __global__ void __launch_bounds__(kFourWarpThreads, 1) ivfpq_four_warp_kernel(co
       }
     }
 
+    if (p.out_kth) {
+      const uint64_t kk = tk.get(k - 1);
+      if (lane == 0) p.out_kth[q] = kk;
+    }
     uint32_t count = 0;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
