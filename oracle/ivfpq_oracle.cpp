@@ -106,13 +106,13 @@ void or_normalize(const float *x, size_t n, size_t d, float *out) {
   }
 }
 
-// pq.rs:573-643.  The three branches (dsub == 1, dsub <= 8, general) compute
+// pq.rs:196-267.  The three branches (dsub == 1, dsub <= 8, general) compute
 // the same sequential sum; they are kept separate to mirror the reference.
 int or_adc_table(const float *q, size_t d, size_t M, size_t ks,
                  const float *cb, float *table) {
   if (M == 0 || d % M != 0) return -1;
   size_t dsub = d / M;
-  if (dsub == 1) {  // pq.rs:588-605
+  if (dsub == 1) {  // pq.rs:210-229
     for (size_t m = 0; m < M; ++m)
       for (size_t c = 0; c < ks; ++c) {
         float diff = q[m] - cb[m * ks + c];
@@ -120,7 +120,7 @@ int or_adc_table(const float *q, size_t d, size_t M, size_t ks,
       }
     return 0;
   }
-  if (dsub <= 8) {  // pq.rs:609-627
+  if (dsub <= 8) {  // pq.rs:232-251
     for (size_t m = 0; m < M; ++m) {
       const float *qs = q + m * dsub;
       for (size_t c = 0; c < ks; ++c) {
@@ -135,13 +135,13 @@ int or_adc_table(const float *q, size_t d, size_t M, size_t ks,
     }
     return 0;
   }
-  for (size_t m = 0; m < M; ++m)  // pq.rs:630-640
+  for (size_t m = 0; m < M; ++m)  // pq.rs:253-265
     for (size_t c = 0; c < ks; ++c)
       table[m * ks + c] = l2sq_seq(q + m * dsub, cb + (m * ks + c) * dsub, dsub);
   return 0;
 }
 
-// pq.rs:649-656.
+// pq.rs:272-279.
 float or_distance_with_table(const float *table, size_t M, size_t ks,
                              const uint8_t *codes) {
   float total = 0.0f;
@@ -158,7 +158,7 @@ void or_adc_batch(const uint8_t *codes, size_t n, size_t M, const float *lut,
     out[i] = or_distance_with_table(lut, M, ks, codes + i * M);
 }
 
-// pq.rs:513-538: per subspace, the first codeword with the strictly smallest
+// pq.rs:136-160: per subspace, the first codeword with the strictly smallest
 // squared L2 distance wins.
 void or_pq_quantize(const float *x, size_t n, size_t d, size_t M, size_t ks,
                     const float *cb, uint8_t *codes) {
@@ -180,7 +180,7 @@ void or_pq_quantize(const float *x, size_t n, size_t d, size_t M, size_t ks,
   }
 }
 
-// pq.rs:680-687.
+// pq.rs:284-290.
 void or_pq_reconstruct(const uint8_t *codes, size_t d, size_t M, size_t ks,
                        const float *cb, float *out) {
   size_t dsub = d / M;

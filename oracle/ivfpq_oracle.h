@@ -33,11 +33,11 @@ extern "C" {
 /* search.rs:55-62 (normalize_query) and search.rs:503-508 (add_slice). */
 void or_normalize(const float *x, size_t n, size_t d, float *out);
 
-/* pq.rs:573-643 (compute_adc_table_into). Returns 0, or -1 on a bad shape. */
+/* pq.rs:196-267 (compute_adc_table_into). Returns 0, or -1 on a bad shape. */
 int or_adc_table(const float *query_residual, size_t d, size_t num_codebooks,
                  size_t codebook_size, const float *codebooks, float *table);
 
-/* pq.rs:649-656 (distance_with_table). */
+/* pq.rs:272-279 (distance_with_table). */
 float or_distance_with_table(const float *table, size_t num_codebooks,
                              size_t codebook_size, const uint8_t *codes);
 
@@ -45,12 +45,12 @@ float or_distance_with_table(const float *table, size_t num_codebooks,
 void or_adc_batch(const uint8_t *codes, size_t n, size_t num_codebooks,
                   const float *lut, size_t codebook_size, float *out);
 
-/* pq.rs:513-538 (quantize), row by row. */
+/* pq.rs:136-160 (quantize), row by row. */
 void or_pq_quantize(const float *x, size_t n, size_t d, size_t num_codebooks,
                     size_t codebook_size, const float *codebooks,
                     uint8_t *codes);
 
-/* pq.rs:680-687 (reconstruct). */
+/* pq.rs:284-290 (reconstruct). */
 void or_pq_reconstruct(const uint8_t *codes, size_t d, size_t num_codebooks,
                        size_t codebook_size, const float *codebooks,
                        float *out);

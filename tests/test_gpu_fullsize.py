@@ -37,7 +37,7 @@ def _check(cfg_id: int):
 
     # list assignments and codes of sampled rows, computed by the oracle from
     # the engine's trained centroids and codebooks (kmeans.rs:97-107,
-    # pq.rs:136-180): bit-identical
+    # pq.rs:136-160): bit-identical
     Lc = int(ix.info().num_centroids)
     srows = np.linspace(0, x.shape[0] - 1, 4000).astype(np.int64)
     sub = orc.OracleIndex(cfg["d"], Lc, cfg["M"], cfg["ks"], cfg["nprobe"])

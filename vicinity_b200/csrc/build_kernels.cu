@@ -3,7 +3,7 @@
 //
 // Reference behaviour restated here (vicinity 0.12.0):
 //   residuals                 src/ivf_pq/search.rs:720-729
-//   ProductQuantizer::quantize src/ivf_pq/pq.rs:513-538 (strict <, first
+//   ProductQuantizer::quantize src/ivf_pq/pq.rs:136-160 (strict <, first
 //                             minimum wins; sequential squared-L2 sum)
 //   lists in vector order     src/ivf_pq/search.rs:623-718
 //   list-contiguous codes     src/ivf_pq/file_storage.rs:39-72

@@ -6,7 +6,7 @@
 //   vectors    f32 [n][d]          L2-normalised rows (dropped by compact)
 //   doc_ids    u32 [n]             caller ids by insertion index
 //   centroids  f32 [Lc][d]         coarse centroids (Lc <= num_clusters)
-//   codebooks  f32 [M][ks][dsub]   product quantizer (pq.rs:396-398 layout)
+//   codebooks  f32 [M][ks][dsub]   product quantizer (pq.rs:19-21 layout)
 //   assign     u32 [n]             list of each insertion index
 //   codes      u8  [n][M]          codes in insertion order (codes.bin)
 //   list_off   u64 [Lc+1]          CSR offsets of the inverted lists
@@ -506,7 +506,7 @@ int train(vg_index *ix, size_t n_train, size_t max_iter) {
     if (it == 0) changed = 1;
   }
 
-  // PQ: Euclidean Lloyd per subspace on training residuals (pq.rs:452-501)
+  // PQ: Euclidean Lloyd per subspace on training residuals (pq.rs:75-124)
   VG_TRY(assign_rows_to_lists(ix, X, n_train, ix->centroids.as<float>(), Lc, assign_t.as<uint32_t>(), nullptr,
                               nullptr));
   DevBuf resid, codes_t, codes_prev, pkeys;

@@ -327,7 +327,7 @@ void set_scan_family(int family);
 // ---- build_kernels.cu -----------------------------------------------------
 
 // codes[i][m] = first argmin_c ||(x[i] - cent[assign[i]])_m - cw[m][c]||^2
-// (search.rs:720-729 residuals, pq.rs:513-538 quantize).
+// (search.rs:720-729 residuals, pq.rs:136-160 quantize).
 cudaError_t launch_encode(const float *xn, size_t n, int d,
                           const uint32_t *assign, const float *cent,
                           const float *codebooks, int M, int ks,

@@ -3,7 +3,7 @@
 // The reference scores a candidate by summing, over subspaces in order, the
 // entry of its code in a per-(query, list) table, each entry being the
 // sequential f32 sum sum_j (r_j - w_j)^2 over the subvector
-// (search.rs:1175-1391, pq.rs:396-398).  This kernel evaluates exactly those
+// (search.rs:1175-1391, pq.rs:19-21).  This kernel evaluates exactly those
 // entries, in the same order and with the same roundings, for the codes a
 // candidate actually has, reading the codewords from a shared-memory copy of
 // the codebook -- so it returns the same ids and distances without building a

@@ -1,7 +1,7 @@
 // Fused IVF-PQ search kernel: one block owns one query at a time and runs
 // the reference's per-query loop (search.rs:1175-1391) over its probed lists:
 //   1. query residual  q - c_list                      (search.rs:1239-1245)
-//   2. ADC table       T[m][c] = sum_j (r_mj - cw_mcj)^2 (pq.rs:573-643)
+//   2. ADC table       T[m][c] = sum_j (r_mj - cw_mcj)^2 (pq.rs:196-267)
 //   3. code scan       dist = sum_m T[m][code_m]       (pq_simd.rs:314-369)
 //      (16-entry codebooks run ivfpq_four_kernel, scan_fourbit.cuh)
 //   4. top-k by (distance, vector id)                  (search.rs:64-75)

@@ -20,7 +20,7 @@ struct SnapshotState {
   size_t dim = 0, num_vectors = 0, num_centroids = 0;
   vg_ivfpq_params params{};
   std::vector<float> centroids;         // [num_centroids][dim]
-  std::vector<float> codebooks;         // [M][ks][dsub] (pq.rs:396-398)
+  std::vector<float> codebooks;         // [M][ks][dsub] (pq.rs:19-21)
   bool optimized = false;               // quantizer is Quantizer::Optimized
   std::vector<float> rotation;          // [dim][dim] row-major; empty = none
   std::vector<uint32_t> doc_ids;        // [num_vectors]
