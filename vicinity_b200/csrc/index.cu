@@ -211,7 +211,7 @@ struct vg_index {
   // search workspace
   DevBuf ws_q, ws_qn, ws_dist, ws_probes, ws_pdist, ws_scalars,
       ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_lb, ws_rec, ws_lbq, ws_qimg, ws_eps, ws_tc,
-      ws_floor, ws_qall;
+      ws_floor, ws_qall, ws_cmax;
   DevBuf stats;  // u64 [pairs, vectors, code bytes, scored lists, scored vectors] while profiling
 
   // error flag of bounded device waits, in mapped pinned host memory
@@ -856,13 +856,16 @@ int coarse_probes(vg_index *ix, const float *qn, size_t rows, size_t P, uint32_t
     rel += 1.0 / 2048;
     VG_CU(ix->ws_qimg.reserve(umma_image_bytes(rows, kp)));
     VG_CU(ix->ws_dist.reserve(std::max<size_t>(rows * Lc, 1) * 2));
+    const size_t cstride = (Lc + 127) / 128 * 4;  // chunk maxima of 32 products per row
+    VG_CU(ix->ws_cmax.reserve(std::max<size_t>(rows * cstride, 1) * 2));
     VG_CU(launch_umma_image(qn, rows, static_cast<int>(d), kp, ix->ws_qimg.p, nullptr, 0.0, 0.0, nullptr, s));
     VG_CU(launch_tc_gemm_f16(ix->ws_qimg.p, rows, ix->cent_img.p, Lc, static_cast<int>(d), kp, ix->ws_dist.p, Lc,
-                             ix->d_err, ix->num_sms, s));
+                             ix->ws_cmax.p, cstride, ix->d_err, ix->num_sms, s));
     mark(ix, 3);
     VG_CU(launch_probe_shortlist(ix->ws_dist.p, true, rows, Lc, Lc, qn, static_cast<int>(d),
                                  ix->centroids.as<float>(), ix->cent_norm.as<float>(), rel, abs_coef,
-                                 static_cast<int>(P), probes, pdist, P, bounds ? *bounds : ProbeBoundArgs{}, s));
+                                 static_cast<int>(P), probes, pdist, P, bounds ? *bounds : ProbeBoundArgs{}, s,
+                                 ix->ws_cmax.p, cstride));
     *launches += 3;
     if (bounds_done) *bounds_done = bounds != nullptr;
     return VG_OK;
@@ -1770,7 +1773,7 @@ int vg_ivfpq_destroy(vg_index *ix) {
                       &ix->owner, &ix->ws_q, &ix->ws_qn, &ix->ws_dist, &ix->ws_probes, &ix->ws_pdist,
                       &ix->ws_scalars, &ix->ws_keys, &ix->ws_all_keys, &ix->ws_out_ids, &ix->ws_out_dist,
                       &ix->ws_out_count, &ix->stats, &ix->ws_lb, &ix->ws_rec, &ix->ws_lbq, &ix->ws_qimg,
-                      &ix->ws_eps, &ix->ws_tc, &ix->ws_floor, &ix->cent_img, &ix->ws_seed, &ix->ws_qall})
+                      &ix->ws_eps, &ix->ws_tc, &ix->ws_floor, &ix->cent_img, &ix->ws_seed, &ix->ws_qall, &ix->ws_cmax})
       b->release();
     for (int i = 0; i < kPhaseEvents; ++i)
       if (ix->ev[i]) cudaEventDestroy(ix->ev[i]);

@@ -131,9 +131,12 @@ size_t tc_select_workspace_bytes(size_t rows, size_t cols, int P, int num_sms);
 
 // out[r][c] (binary16, row stride ld) = q_r . x_c from the tensor cores
 // (binary16 operand images, f32 accumulation, rounded to nearest): the
-// approximate coarse products the probe shortlist ranks.
+// approximate coarse products the probe shortlist ranks.  With cmax set,
+// also cmax[r][j] (binary16, row stride cstride >= 4 ceil(cols / 128)) = the
+// largest product of columns [32 j, 32 j + 32) of row r (-inf past cols).
 cudaError_t launch_tc_gemm_f16(const void *a_img, size_t rows, const void *b_img, size_t cols, int d, int kp,
-                               void *out, size_t ld, int *error, int num_sms, cudaStream_t s);
+                               void *out, size_t ld, void *cmax, size_t cstride, int *error, int num_sms,
+                               cudaStream_t s);
 
 // Exact top-k probes per row from approximate products s[row][l] ~ q . c_l
 // (binary16 with s_half, else f32): candidates within eps = rel |q| cmax +
@@ -142,10 +145,13 @@ cudaError_t launch_tc_gemm_f16(const void *a_img, size_t rows, const void *b_img
 // scored exactly over all L.  Same output as launch_select_rows on exact
 // 1 - dot distances; with bounds.lb set, the probes' pruning bounds and
 // records are written beside them (shortlist.cu).
+// With chunk_max set (binary16 products only, row stride chunk_stride: the
+// GEMM's chunk maxima), the bound comes from the chunk maxima and only chunks
+// whose maximum reaches the window are read.
 cudaError_t launch_probe_shortlist(const void *s, bool s_half, size_t rows, size_t L, size_t ld, const float *qn,
                                    int d, const float *cent, const float *cmax, double rel, double abs_coef, int k,
                                    uint32_t *out_ids, float *out_dist, size_t out_ld, const ProbeBoundArgs &bounds,
-                                   cudaStream_t st);
+                                   cudaStream_t st, const void *chunk_max = nullptr, size_t chunk_stride = 0);
 cudaError_t launch_tc_select(const TcSelect &t, int num_sms, cudaStream_t s);
 
 // Same selection, but writing packed keys (for later merging).

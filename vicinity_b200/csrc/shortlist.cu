@@ -33,6 +33,7 @@ constexpr int kSelectWarps = 8;
 // ---------------------------------------------------------------------------
 namespace {
 constexpr int kShortBuf = 512;  // gathered candidates per warp
+constexpr int kChunkBuf = 256;  // candidate chunks per warp (chunk-maxima path)
 
 // 1 - sum_j q_j c_j in the reference's order (the exact coarse distance).
 __device__ __forceinline__ float exact_one_minus_dot(const float *q, const float *__restrict__ c, int d, bool vec) {
@@ -133,7 +134,7 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
     shortlist_kernel(const TS *__restrict__ s, size_t rows, size_t L, size_t ld, const float *__restrict__ qn,
                      int d, const float *__restrict__ cent, const float *__restrict__ cmax_p, double rel,
                      double abs_coef, int k, uint32_t *__restrict__ out_ids, float *__restrict__ out_dist,
-                     size_t out_ld, const ProbeBoundArgs bnd) {
+                     size_t out_ld, const ProbeBoundArgs bnd, const __half *__restrict__ cmx, size_t cstride) {
   extern __shared__ __align__(16) unsigned char sh[];
   constexpr int R2 = 2 * R;
   const int lane = lane_id(), warp = threadIdx.x >> 5;
@@ -143,6 +144,10 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
   const int dpad = (d + 3) & ~3;
   float *qs = reinterpret_cast<float *>(reinterpret_cast<uint32_t *>(sh) + kSelectWarps * kShortBuf) +
               static_cast<size_t>(warp) * dpad;
+  uint32_t *cl = reinterpret_cast<uint32_t *>(reinterpret_cast<float *>(reinterpret_cast<uint32_t *>(sh) +
+                                                                        kSelectWarps * kShortBuf) +
+                                              static_cast<size_t>(kSelectWarps) * dpad) +
+                 static_cast<size_t>(warp) * kChunkBuf;  // candidate chunk ids
   const TS *srow = s + row * ld;
   const float *qrow = qn + row * d;
   for (int j = lane; j < d; j += 32) qs[j] = qrow[j];
@@ -173,6 +178,12 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
   };
   bool half_fast = false;
   if constexpr (std::is_same<TS, __half>::value) half_fast = svec;
+  // chunk maxima: the largest product of every 32 columns, a subset of the
+  // products, so their P-th largest still bounds A_P, and a chunk whose
+  // maximum is below the window holds no candidate
+  const __half *crow = cmx ? cmx + row * cstride : nullptr;
+  const size_t nch = ((L + 127) / 128) * 4;  // chunk maxima per row, whole tiles of 4
+  const bool chunked = half_fast && crow != nullptr;
   if (!exact_all && half_fast) {
     if constexpr (std::is_same<TS, __half>::value) {
       // the largest products are the smallest distances: keep the 2R largest
@@ -190,10 +201,11 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
           a2[r] = hi;
         }
       };
-      for_each_half_quad<false>(srow, L, lane, [&](size_t, __half2 lo, __half2 hi, bool ok) {
-        insert2(ok ? lo : ninf);
-        insert2(ok ? hi : ninf);
-      });
+      for_each_half_quad<false>(chunked ? crow : srow, chunked ? nch : L, lane,
+                                [&](size_t, __half2 lo, __half2 hi, bool ok) {
+                                  insert2(ok ? lo : ninf);
+                                  insert2(ok ? hi : ninf);
+                                });
 #pragma unroll
       for (int r = 0; r < R2; ++r) {
         const float s = fmaxf(__low2float(a2[r]), __high2float(a2[R2 - 1 - r]));
@@ -240,12 +252,83 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
       const float s_lo = __double2float_rd(1.0 - static_cast<double>(limit) -
                                            1e-6 * (1.0 + fabs(static_cast<double>(limit))));
       const __half2 slo2 = __half2half2(__float2half_rd(s_lo));
+      if (chunked) {
+        // the ids of chunks whose maximum reaches s_lo (no product read yet),
+        // then one chunk per lane, its 64 bytes in flight at once
+        const __half slo = __float2half_rd(s_lo);
+        int nc = 0;
+        for_each_half_quad<false>(crow, nch, lane, [&](size_t c4, __half2 lo, __half2 hi, bool ok) {
+          const bool mt[4] = {ok && !__hlt(__low2half(lo), slo), ok && !__hlt(__high2half(lo), slo),
+                              ok && !__hlt(__low2half(hi), slo), ok && !__hlt(__high2half(hi), slo)};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const unsigned m = __ballot_sync(VG_FULL_MASK, mt[h]);
+            const int pos = nc + __popc(m & ((1u << lane) - 1u));
+            if (mt[h] && pos < kChunkBuf) cl[pos] = static_cast<uint32_t>(c4 + h);
+            nc += __popc(m);
+          }
+        });
+        __syncwarp();
+        if (nc > kChunkBuf) {
+          exact_all = true;  // a window this wide: every list scored exactly
+        } else {
+          const bool vload = (L & 7) == 0 && (reinterpret_cast<uintptr_t>(srow) & 15) == 0;
+          for (int i0 = 0; i0 < nc; i0 += 32) {
+            const bool have = i0 + lane < nc;
+            const size_t c0 = have ? static_cast<size_t>(cl[i0 + lane]) * 32 : 0;
+            uint32_t w[16];  // 32 binary16 products
+            if (have && vload && c0 + 32 <= L) {
+              const uint4 *src = reinterpret_cast<const uint4 *>(srow + c0);
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const uint4 x = __ldcs(src + u);
+                w[4 * u] = x.x;
+                w[4 * u + 1] = x.y;
+                w[4 * u + 2] = x.z;
+                w[4 * u + 3] = x.w;
+              }
+            } else {
+#pragma unroll
+              for (int u = 0; u < 16; ++u) {
+                const size_t a = c0 + 2 * u, b = a + 1;
+                const unsigned short lo16 = have && a < L ? __half_as_ushort(srow[a]) : 0xFC00u;  // -inf past L
+                const unsigned short hi16 = have && b < L ? __half_as_ushort(srow[b]) : 0xFC00u;
+                w[u] = static_cast<uint32_t>(lo16) | (static_cast<uint32_t>(hi16) << 16);
+              }
+            }
+            uint32_t take = 0;
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[u]));
+              take |= (have && !(__fsub_rn(1.0f, f.x) > limit) ? 1u : 0u) << (2 * u);
+              take |= (have && !(__fsub_rn(1.0f, f.y) > limit) ? 1u : 0u) << (2 * u + 1);
+            }
+            // lanes' candidates side by side: exclusive prefix sum of the counts
+            const int cnt = __popc(take);
+            int incl = cnt;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+              const int y = __shfl_up_sync(VG_FULL_MASK, incl, off);
+              if (lane >= off) incl += y;
+            }
+            int pos = n + incl - cnt;
+            while (take) {
+              const int j = __ffs(take) - 1;
+              take &= take - 1;
+              if (pos < kShortBuf) buf[pos] = static_cast<uint32_t>(c0 + j);
+              ++pos;
+            }
+            n += __shfl_sync(VG_FULL_MASK, incl, 31);
+          }
+        }
+      } else {
       for_each_half_quad<true>(srow, L, lane, [&](size_t c, __half2 lo, __half2 hi, bool ok) {
         const bool maybe = ok && (!__hblt2(lo, slo2) || !__hblt2(hi, slo2));
         if (!__any_sync(VG_FULL_MASK, maybe)) return;
         const float2 fl = __half22float2(lo), fh = __half22float2(hi);
         gather(c, make_float4(fl.x, fl.y, fh.x, fh.y), ok, ok, ok, ok);
       });
+      }
     }
   } else if (!exact_all) {
     for_each_quad<true, TS>(srow, L, svec, lane, gather);
@@ -296,8 +379,9 @@ template <int R, typename TS>
 cudaError_t launch_shortlist_impl(const TS *s, size_t rows, size_t L, size_t ld, const float *qn, int d,
                                   const float *cent, const float *cmax, double rel, double abs_coef, int k,
                                   uint32_t *ids, float *dst, size_t out_ld, const ProbeBoundArgs &bnd,
-                                  cudaStream_t st) {
-  const size_t smem = static_cast<size_t>(kSelectWarps) * (kShortBuf * 4 + static_cast<size_t>((d + 3) & ~3) * 4);
+                                  cudaStream_t st, const __half *cmx, size_t cstride) {
+  const size_t smem =
+      static_cast<size_t>(kSelectWarps) * (kShortBuf * 4 + static_cast<size_t>((d + 3) & ~3) * 4 + kChunkBuf * 4);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(shortlist_kernel<R, TS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
@@ -305,18 +389,19 @@ cudaError_t launch_shortlist_impl(const TS *s, size_t rows, size_t L, size_t ld,
   }
   dim3 grid(static_cast<unsigned>((rows + kSelectWarps - 1) / kSelectWarps));
   shortlist_kernel<R, TS><<<grid, kSelectWarps * 32, smem, st>>>(s, rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k,
-                                                                  ids, dst, out_ld, bnd);
+                                                                  ids, dst, out_ld, bnd, cmx, cstride);
   return cudaGetLastError();
 }
 
 template <typename TS>
 cudaError_t shortlist_dispatch(const TS *s, size_t rows, size_t L, size_t ld, const float *qn, int d,
                                const float *cent, const float *cmax, double rel, double abs_coef, int k,
-                               uint32_t *ids, float *dst, size_t out_ld, const ProbeBoundArgs &bnd, cudaStream_t st) {
-  if (k <= 32) return launch_shortlist_impl<1>(s, rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k, ids, dst, out_ld, bnd, st);
-  if (k <= 64) return launch_shortlist_impl<2>(s, rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k, ids, dst, out_ld, bnd, st);
-  if (k <= 128) return launch_shortlist_impl<4>(s, rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k, ids, dst, out_ld, bnd, st);
-  if (k <= 256) return launch_shortlist_impl<8>(s, rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k, ids, dst, out_ld, bnd, st);
+                               uint32_t *ids, float *dst, size_t out_ld, const ProbeBoundArgs &bnd, cudaStream_t st,
+                               const __half *cmx, size_t cstride) {
+  if (k <= 32) return launch_shortlist_impl<1>(s, rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k, ids, dst, out_ld, bnd, st, cmx, cstride);
+  if (k <= 64) return launch_shortlist_impl<2>(s, rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k, ids, dst, out_ld, bnd, st, cmx, cstride);
+  if (k <= 128) return launch_shortlist_impl<4>(s, rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k, ids, dst, out_ld, bnd, st, cmx, cstride);
+  if (k <= 256) return launch_shortlist_impl<8>(s, rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k, ids, dst, out_ld, bnd, st, cmx, cstride);
   return cudaErrorInvalidValue;
 }
 
@@ -325,13 +410,13 @@ cudaError_t shortlist_dispatch(const TS *s, size_t rows, size_t L, size_t ld, co
 cudaError_t launch_probe_shortlist(const void *s, bool s_half, size_t rows, size_t L, size_t ld, const float *qn,
                                    int d, const float *cent, const float *cmax, double rel, double abs_coef, int k,
                                    uint32_t *out_ids, float *out_dist, size_t out_ld, const ProbeBoundArgs &bnd,
-                                   cudaStream_t st) {
+                                   cudaStream_t st, const void *chunk_max, size_t chunk_stride) {
   if (rows == 0 || k <= 0) return cudaSuccess;
   if (s_half)
     return shortlist_dispatch(static_cast<const __half *>(s), rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k,
-                              out_ids, out_dist, out_ld, bnd, st);
+                              out_ids, out_dist, out_ld, bnd, st, static_cast<const __half *>(chunk_max), chunk_stride);
   return shortlist_dispatch(static_cast<const float *>(s), rows, L, ld, qn, d, cent, cmax, rel, abs_coef, k, out_ids,
-                            out_dist, out_ld, bnd, st);
+                            out_dist, out_ld, bnd, st, nullptr, 0);
 }
 
 

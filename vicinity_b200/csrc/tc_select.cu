@@ -538,6 +538,8 @@ struct GemmParams {
   int kp, ksteps, splits;
   uint32_t split_cols;
   __half *out;
+  __half *cmax;   // [rows][cstride] largest product of every 32-column chunk (nullable)
+  size_t cstride;
   int *error;
 };
 
@@ -698,6 +700,29 @@ __global__ void __launch_bounds__(kWinThreads, 1) tc_gemm_f16_kernel(const GemmP
         if (lane == 0) mbar_arrive(accempty + acc);
         const size_t col0 = c0 + static_cast<size_t>(t) * kTile;
         const int nval = static_cast<int>(min(static_cast<size_t>(kTile), p.cols - col0));
+        if (p.cmax && rv) {
+          // the largest product of each 32-column chunk, rounded as the
+          // products are (rounding is monotone: the largest rounded product)
+          float m4[4];
+          if (nval == kTile) {
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) m4[ch] = max32(v + ch * 32);
+          } else {
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+              float m = -__int_as_float(0x7f800000);
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (ch * 32 + j < nval) m = fmaxf(m, __uint_as_float(v[ch * 32 + j]));
+              m4[ch] = m;
+            }
+          }
+          __half2 mh[2] = {__floats2half2_rn(m4[0], m4[1]), __floats2half2_rn(m4[2], m4[3])};
+          uint2 o;
+          o.x = *reinterpret_cast<uint32_t *>(&mh[0]);
+          o.y = *reinterpret_cast<uint32_t *>(&mh[1]);
+          *reinterpret_cast<uint2 *>(p.cmax + row * p.cstride + (col0 / kTile) * 4) = o;
+        }
         if (vec && nval == kTile) {
           // the warp's 32 rows x 256 bytes through shared memory (chunk j of
           // row r at r * 16 + (j ^ (r & 15)): conflict-free both ways), then
@@ -1050,7 +1075,8 @@ cudaError_t launch_tc_select(const TcSelect &t, int num_sms, cudaStream_t s) {
 }
 
 cudaError_t launch_tc_gemm_f16(const void *a_img, size_t rows, const void *b_img, size_t cols, int d, int kp,
-                               void *out, size_t ld, int *error, int num_sms, cudaStream_t s) {
+                               void *out, size_t ld, void *cmax, size_t cstride, int *error, int num_sms,
+                               cudaStream_t s) {
   if (rows == 0 || cols == 0) return cudaSuccess;
   if ((kp != 64 && kp != 128) || d < 1 || d > kp) return cudaErrorInvalidValue;
   const size_t rblocks = (rows + kTile - 1) / kTile, ctiles = (cols + kTile - 1) / kTile;
@@ -1069,6 +1095,8 @@ cudaError_t launch_tc_gemm_f16(const void *a_img, size_t rows, const void *b_img
   gp.splits = static_cast<int>((ctiles + per - 1) / per);
   gp.split_cols = static_cast<uint32_t>(per * kTile);
   gp.out = static_cast<__half *>(out);
+  gp.cmax = static_cast<__half *>(cmax);
+  gp.cstride = cstride;
   gp.error = error;
   const size_t smem = 1024 + static_cast<size_t>(kp / kKBlock) * kBlockBytes * (1 + kGemmStages) +
                       static_cast<size_t>(kEpiWarps) * 32 * 16 * 16 + 16 * 8 + 16;
