@@ -41,6 +41,49 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "IVF-PQ queries/sec at recall@10 (1/2/4/8 B200); ADC scan HBM GB/s vs peak"
 FALLBACK_HBM_GBS = 6650.0
+RECALL_QUERIES = 1000  # both arms report recall@10 on the batch's first 1,000 queries
+
+
+def workload_config(cfg, nq: int, train_sample: int, train_iters: int) -> dict:
+    """The workload, identical in the engine and reference lines."""
+    if cfg["centre"] == "flat":
+        return {"workload": cfg["name"], "n": cfg["n"], "d": cfg["d"], "k": cfg["k"], "batch_per_rank": nq,
+                "l2": "not flushed: the database (400 MB of f32 rows, 256 MB binary16 image) exceeds L2"}
+    return {"workload": cfg["name"], "n": cfg["n"], "d": cfg["d"], "nlist": cfg["nlist"], "M": cfg["M"],
+            "codebook_size": cfg["ks"], "nprobe": cfg["nprobe"], "k": cfg["k"], "batch_per_rank": nq,
+            "train_sample": train_sample, "train_iters": train_iters,
+            "training": "seeded sample, spherical Lloyd (lists) + Euclidean Lloyd per subspace, to convergence "
+                        "or train_iters",
+            "l2": "flushed between the GPU arm's timed steps (512 MiB write, then 512 MiB read of another buffer)"}
+
+
+def exact_top_k_cpu(xn: np.ndarray, q: np.ndarray, k: int) -> np.ndarray:
+    """Exact top-k rows of normalised `xn` by inner product with the
+    normalised queries (CPU matmul in blocks): the recall ground truth."""
+    import torch
+
+    qs = q / np.maximum(np.linalg.norm(q, axis=1, keepdims=True), 1e-30)
+    qt = torch.from_numpy(np.ascontiguousarray(qs.astype(np.float32)).T.copy())
+    best_v = torch.full((q.shape[0], k), -1e30)
+    best_i = torch.zeros((q.shape[0], k), dtype=torch.int64)
+    for s0 in range(0, xn.shape[0], 1 << 20):
+        sc = torch.from_numpy(xn[s0:s0 + (1 << 20)]) @ qt
+        v, i = torch.topk(sc, min(k, sc.shape[0]), dim=0)
+        allv = torch.cat([best_v, v.T], dim=1)
+        alli = torch.cat([best_i, (i + s0).T], dim=1)
+        top = torch.topk(allv, k, dim=1)
+        best_v, best_i = top.values, torch.gather(alli, 1, top.indices)
+    return best_i.numpy()
+
+
+def recall_at_k(ids: np.ndarray, counts, truth: np.ndarray) -> float:
+    """Mean |returned ∩ true top-k| / k over the rows of `truth`."""
+    k = truth.shape[1]
+    hits = 0
+    for r in range(truth.shape[0]):
+        c = k if counts is None else int(counts[r])
+        hits += len(set(ids[r, :c].tolist()) & set(truth[r].tolist()))
+    return hits / truth.size
 
 
 def parse_args():
@@ -332,10 +375,13 @@ def run_engine(args):
     e2e_ms = reduce(timed(step_e2e, args.steps), dist.ReduceOp.MAX if world > 1 else None)
     e2e_value = queries_total * args.steps / (e2e_ms / 1e3)
 
-    # recall@10 of this rank's rows, averaged over ranks
+    # recall@10 of this rank's rows, averaged over ranks: on the first
+    # RECALL_QUERIES queries (the reference arm's recall queries at N = 1) and
+    # on every row with a ground truth
     got = ids_h.numpy()[:rq].astype(np.int64)
-    hits = sum(len(set(a) & set(b)) for a, b in zip(got.tolist(), truth.tolist()))
-    recall = reduce(hits / truth.size, dist.ReduceOp.SUM if world > 1 else None) / world
+    rs = min(RECALL_QUERIES, rq)
+    recall = reduce(recall_at_k(got[:rs], None, truth[:rs]), dist.ReduceOp.SUM if world > 1 else None) / world
+    recall_batch = reduce(recall_at_k(got, None, truth), dist.ReduceOp.SUM if world > 1 else None) / world
 
     # roofline of the scan kernel (live CUDA events on the launching stream)
     peaks, peak_kind = measured_peaks()
@@ -369,18 +415,16 @@ def run_engine(args):
             "data": ("synthetic: seeded Gaussian mixture drawn on the GPU chunk by chunk (torch generator), "
                      "never held on the host" if on_device else
                      "synthetic: seeded Gaussian mixture with the configuration's generator (no dataset)"),
-            "config": {
-                "workload": cfg["name"], "n": n, "d": d, "nlist": cfg["nlist"], "M": cfg["M"],
-                "codebook_size": cfg["ks"], "nprobe": cfg["nprobe"], "k": k, "batch_per_rank": nq,
-                "recall_at_10": round(recall, 4), "recall_queries_per_rank": rq,
-                "train_sample": train_sample, "train_iters": args.train_iters,
-                "l2": "flushed between timed steps (512 MiB write, then 512 MiB read of another buffer)",
-                "parallelism": ("single GPU" if world == 1 else
-                                f"inverted lists sharded by list x{world}, {nq} queries per rank" if by_lists
-                                else f"index replica per GPU, {nq} queries per rank x{world}"),
-                "index_bytes_one_gpu": bytes_full, "index_bytes_per_rank": bytes_rank,
-                "build_s": round(build_s, 1),
-            },
+            "config": workload_config(cfg, nq, train_sample, args.train_iters),
+            "recall_at_10": round(recall, 4),
+            "recall_queries": rs,
+            "recall_at_10_batch": round(recall_batch, 4),
+            "recall_queries_batch": rq,
+            "parallelism": ("single GPU" if world == 1 else
+                            f"inverted lists sharded by list x{world}, {nq} queries per rank" if by_lists
+                            else f"index replica per GPU, {nq} queries per rank x{world}"),
+            "index_bytes_one_gpu": bytes_full, "index_bytes_per_rank": bytes_rank,
+            "index_build_s": round(build_s, 1),
             "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
                     "h2d_bytes_per_step": nq * d * 4, "d2h_bytes_per_step": nq * k * 8 + nq * 4},
             "roofline": {
@@ -402,6 +446,10 @@ def run_engine(args):
             "phases_ms_per_step": {key: round(prof[key] / calls, 4) for key in
                                    ("normalize_ms", "coarse_ms", "select_ms", "pairs_ms", "scan_ms", "merge_ms",
                                     "collective_ms", "total_ms")},
+            "scan_counters_per_step": {key: round(prof[key] / calls, 1) for key in
+                                       ("scored_lists", "scored_vectors", "tables_built", "code_groups",
+                                        "seed_scored_lists", "seed_scored_vectors", "seed_tables_built",
+                                        "seed_code_groups")},
             "gpu_launches": int(prof["kernel_launches"]),
             "clocks": clock_info,
             "cpu_baseline": cpu_baseline,
@@ -519,10 +567,9 @@ def run_flat(args, cfg, world, rank, local):
             "vs_baseline": None,
             "dtype": "f32",
             "data": "synthetic: N(0,1) rows L2-normalised, seeded (no dataset)",
-            "config": {"workload": cfg["name"], "n": n, "d": d, "k": k, "batch": nq,
-                       "l2": "not flushed: the database (400 MB f32 rows, 256 MB binary16 image) exceeds L2",
-                       "parallelism": "single GPU" if world == 1 else f"database replica per GPU, {nq} queries per rank x{world}",
-                       "build_s": round(build_s, 1)},
+            "config": workload_config(cfg, nq, 0, 0),
+            "parallelism": "single GPU" if world == 1 else f"database replica per GPU, {nq} queries per rank x{world}",
+            "index_build_s": round(build_s, 1),
             "e2e": {"value": round(e2e_value, 1), "unit": "queries/s", "h2d_bytes_per_step": nq * d * 4,
                     "d2h_bytes_per_step": nq * k * 8 + nq * 4},
             "roofline": {
@@ -647,65 +694,132 @@ def cpu_baseline_port(ix, x, q, cfg, budget_s, truth):
 # reference arm: the reference's CPU algorithm (oracle port) on host cores
 # --------------------------------------------------------------------------
 
-def numpy_train_and_encode(x, cfg, sample, iters, seed=42):
-    """CPU index construction for the reference arm (untimed): spherical
-    Lloyd for the coarse lists and Euclidean Lloyd per PQ subspace, with
-    BLAS matmuls; returns centroids, codebooks, assignments and codes."""
-    rng = np.random.default_rng(seed)
-    n, d = x.shape
-    L, M, ks = cfg["nlist"], cfg["M"], cfg["ks"]
-    dsub = d // M
-    xn = x / np.maximum(np.linalg.norm(x, axis=1, keepdims=True), 1e-10)
-    xn = xn.astype(np.float32)
-    tr = xn[np.sort(rng.choice(n, min(sample, n), replace=False))]
-    cent = tr[rng.choice(tr.shape[0], L, replace=False)].copy()
+_MASK64 = (1 << 64) - 1
 
-    import torch  # CPU matmul and argmax on every host thread (index construction only)
+
+def seeded_prefix(n: int, take: int, seed: int) -> np.ndarray:
+    """First `take` entries of a seeded Fisher-Yates permutation of [0, n),
+    one splitmix64 draw per swap: how the engine picks its training rows and
+    initial centroids (index.cu seeded_prefix)."""
+    idx = np.arange(n, dtype=np.int64)
+    s = seed & _MASK64
+    for i in range(min(take, n - 1)):
+        s = (s + 0x9E3779B97F4A7C15) & _MASK64
+        z = ((s ^ (s >> 30)) * 0xBF58476D1CE4E5B9) & _MASK64
+        z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & _MASK64
+        z ^= z >> 31
+        j = i + z % (n - i)
+        idx[i], idx[j] = idx[j], idx[i]
+    return idx[:take]
+
+
+def _segment_means(rows: np.ndarray, labels: np.ndarray, nseg: int, old: np.ndarray) -> np.ndarray:
+    """Per-label means of `rows` (sums in double); labels without rows keep
+    `old`."""
+    counts = np.bincount(labels, minlength=nseg)
+    nz = counts > 0
+    out = old.copy()
+    for j in range(rows.shape[1]):
+        sums = np.bincount(labels, weights=rows[:, j], minlength=nseg)
+        out[nz, j] = (sums[nz] / counts[nz]).astype(np.float32)
+    return out
+
+
+def host_train_like_engine(xn: np.ndarray, cfg, sample: int, iters: int, seed: int = 42):
+    """CPU restatement of the engine's index training, for the reference arm
+    (untimed): the same seeded training rows and initial centroids, spherical
+    Lloyd for the coarse lists and Euclidean Lloyd per PQ subspace from seeded
+    rows, each stopping when no assignment changes (index.cu train()).  The
+    reference trains with the third-party `clump` k-means; restating the
+    engine's training instead gives both arms the same index recipe, so their
+    recalls are comparable.  Returns centroids, codebooks, assignments and codes
+    of every row of `xn` (L2-normalised)."""
+    import torch  # CPU matmuls on every host thread (index construction only)
 
     torch.set_num_threads(host_threads())
+    n, d = xn.shape
+    M, ks = cfg["M"], cfg["ks"]
+    dsub = d // M
+    n_train = min(sample, n)
+    rows = np.sort(seeded_prefix(n, n_train, seed)) if n_train < n else np.arange(n)
+    X = np.ascontiguousarray(xn[rows])
+    Lc = min(cfg["nlist"], n_train)
+    cent = np.ascontiguousarray(X[seeded_prefix(n_train, Lc, seed)])
 
-    def assign(rows, c):
-        out = np.empty(rows.shape[0], np.int64)
+    def assign(data: np.ndarray, c: np.ndarray) -> np.ndarray:
+        # nearest centroid by cosine distance 1 - dot (kmeans.rs:97-107): the
+        # largest dot, the lowest list on ties.  One score buffer is reused
+        # (a fresh 100 MB block per matmul costs more in page faults than the
+        # matmul itself)
+        out = torch.empty(data.shape[0], dtype=torch.int64)
         ct = torch.from_numpy(np.ascontiguousarray(c.T))
-        blk = max(1, (1 << 26) // c.shape[0])
-        for s in range(0, rows.shape[0], blk):
-            out[s:s + blk] = torch.argmax(torch.from_numpy(rows[s:s + blk]) @ ct, dim=1).numpy()
-        return out
+        blk = max(1, (1 << 25) // c.shape[0])
+        buf = torch.empty((blk, c.shape[0]), dtype=torch.float32)
+        for s0 in range(0, data.shape[0], blk):
+            rows = min(blk, data.shape[0] - s0)
+            torch.mm(torch.from_numpy(data[s0:s0 + rows]), ct, out=buf[:rows])
+            torch.argmax(buf[:rows], dim=1, out=out[s0:s0 + rows])
+        return out.numpy()
 
+    prev = None
     for _ in range(iters):
-        a = assign(tr, cent)
-        sums = np.zeros_like(cent)
-        np.add.at(sums, a, tr)
-        cnt = np.bincount(a, minlength=L)
-        nz = cnt > 0
-        sums[nz] /= cnt[nz, None]
-        norms = np.linalg.norm(sums[nz], axis=1, keepdims=True)
-        cent[nz] = sums[nz] / np.maximum(norms, 1e-10)
-    a_tr = assign(tr, cent)
-    res = tr - cent[a_tr]
+        a = assign(X, cent)
+        mean = _segment_means(X, a, Lc, cent)
+        norm = np.sqrt((mean.astype(np.float64) ** 2).sum(axis=1)).astype(np.float32)
+        moved = (np.bincount(a, minlength=Lc) > 0) & (norm > 1e-10)
+        mean[moved] /= norm[moved, None]
+        cent = mean
+        done = prev is not None and np.array_equal(a, prev)
+        prev = a
+        if done:
+            break
+
+    def encode(res: np.ndarray, cb: np.ndarray) -> np.ndarray:
+        # argmin over codewords of the squared distance (pq.rs:136-160), the
+        # lowest codeword on ties: summed in coordinate order for small
+        # codebooks; |c|^2 - 2 r.c by CPU matmul for 256-word codebooks (equal
+        # but for near-ties, which do not move recall)
+        codes = np.empty((res.shape[0], M), np.uint8)
+        if ks * dsub <= 64:
+            blk = max(1, (1 << 20) // (ks * dsub))
+            for s0 in range(0, res.shape[0], blk):
+                r = res[s0:s0 + blk]
+                for m in range(M):
+                    diff = r[:, None, m * dsub:(m + 1) * dsub] - cb[m][None, :, :]
+                    dd = diff[..., 0] * diff[..., 0]
+                    for j in range(1, dsub):
+                        dd = dd + diff[..., j] * diff[..., j]
+                    codes[s0:s0 + blk, m] = np.argmin(dd, axis=1)
+            return codes
+        cbt = torch.from_numpy(np.ascontiguousarray(cb.transpose(0, 2, 1)))  # [M][dsub][ks]
+        cn = torch.from_numpy((cb.astype(np.float32) ** 2).sum(axis=2))[:, None, :]  # [M][1][ks]
+        blk = max(1, (1 << 25) // (M * ks))
+        for s0 in range(0, res.shape[0], blk):
+            sub = torch.from_numpy(np.ascontiguousarray(res[s0:s0 + blk])).view(-1, M, dsub).transpose(0, 1)
+            dd = torch.baddbmm(cn, sub, cbt, alpha=-2.0)  # [M][rows][ks]
+            codes[s0:s0 + blk] = torch.argmin(dd, dim=2).T.numpy()
+        return codes
+
+    res = X - cent[assign(X, cent)]
     cb = np.empty((M, ks, dsub), np.float32)
     for m in range(M):
-        sub = res[:, m * dsub:(m + 1) * dsub]
-        cw = sub[rng.choice(sub.shape[0], ks, replace=False)].copy()
-        for _ in range(iters):
-            dd = (sub ** 2).sum(1, keepdims=True) - 2 * sub @ cw.T + (cw ** 2).sum(1)[None]
-            lab = np.argmin(dd, axis=1)
-            s2 = np.zeros_like(cw)
-            np.add.at(s2, lab, sub)
-            c2 = np.bincount(lab, minlength=ks)
-            nz = c2 > 0
-            cw[nz] = s2[nz] / c2[nz, None]
-        cb[m] = cw
-    assign_all = assign(xn, cent).astype(np.uint32)
-    codes = np.empty((n, M), np.uint8)
-    blk = 1 << 18
-    for s in range(0, n, blk):
-        r = xn[s:s + blk] - cent[assign_all[s:s + blk]]
+        cb[m] = res[seeded_prefix(n_train, ks, seed + m), m * dsub:(m + 1) * dsub]
+    prev = None
+    for _ in range(iters):
+        codes = encode(res, cb)
         for m in range(M):
-            sub = r[:, m * dsub:(m + 1) * dsub]
-            dd = (sub ** 2).sum(1, keepdims=True) - 2 * sub @ cb[m].T + (cb[m] ** 2).sum(1)[None]
-            codes[s:s + blk, m] = np.argmin(dd, axis=1)
-    return cent, cb, assign_all, codes
+            cb[m] = _segment_means(res[:, m * dsub:(m + 1) * dsub], codes[:, m].astype(np.int64), ks, cb[m])
+        done = prev is not None and np.array_equal(codes, prev)
+        prev = codes
+        if done:
+            break
+    assign_all = assign(xn, cent)
+    codes_all = np.empty((n, M), np.uint8)
+    blk = 1 << 20
+    blk = 1 << 16
+    for s0 in range(0, n, blk):
+        codes_all[s0:s0 + blk] = encode(xn[s0:s0 + blk] - cent[assign_all[s0:s0 + blk]], cb)
+    return cent, cb, assign_all.astype(np.uint32), codes_all
 
 
 def run_reference(args):
@@ -726,32 +840,23 @@ def run_reference(args):
     x, q = config_data(args.config, seed=0, nq=cfg["nq"])
     if cfg["centre"] == "flat":
         return run_reference_flat(args, cfg, x, q, threads)
-    cent, cb, assign, codes = numpy_train_and_encode(x, cfg, min(args.train_sample or 65_536, 65_536), 8)
+    train_sample = min(args.train_sample or cfg.get("train_sample", 131_072), x.shape[0])
+    t0 = time.time()
+    xn = orc.normalize(x)
+    cent, cb, assign, codes = host_train_like_engine(xn, cfg, train_sample, args.train_iters)
     ref = orc.OracleIndex(cfg["d"], cfg["nlist"], cfg["M"], cfg["ks"], cfg["nprobe"])
     ref.set_trained(cent, cb)
     ref.add(np.arange(x.shape[0], dtype=np.uint32), x)
     ref.adopt_codes(assign, codes)
-    # recall@10 of this index on a sample of the batch (exact top-10 of the
-    # normalised rows, CPU matmul)
-    import torch
-
-    rs = min(200, q.shape[0])
-    xn = torch.from_numpy(x / np.maximum(np.linalg.norm(x, axis=1, keepdims=True), 1e-10).astype(np.float32))
-    qs = q[:rs] / np.maximum(np.linalg.norm(q[:rs], axis=1, keepdims=True), 1e-30)
-    best = torch.full((rs, cfg["k"]), -1e30), torch.zeros((rs, cfg["k"]), dtype=torch.int64)
-    qt = torch.from_numpy(qs.astype(np.float32)).T.contiguous()
-    for s0 in range(0, xn.shape[0], 1 << 20):
-        sc = xn[s0:s0 + (1 << 20)] @ qt
-        v, i = torch.topk(sc, min(cfg["k"], sc.shape[0]), dim=0)
-        allv = torch.cat([best[0], v.T], dim=1)
-        alli = torch.cat([best[1], (i + s0).T], dim=1)
-        top = torch.topk(allv, cfg["k"], dim=1)
-        best = top.values, torch.gather(alli, 1, top.indices)
+    build_s = time.time() - t0
+    # recall@10 of this index on the batch's first RECALL_QUERIES queries
+    # (exact top-10 of the normalised rows by CPU matmul), the same queries
+    # the engine arm reports its recall on
+    rs = min(RECALL_QUERIES, q.shape[0])
+    truth = exact_top_k_cpu(xn, q[:rs], cfg["k"])
     del xn
     rid, _, rcnt = ref.search_batch(q[:rs], cfg["k"], threads=threads)
-    truth = best[1].numpy()
-    ref_recall = float(np.mean([len(set(a[:c].tolist()) & set(b.tolist())) / cfg["k"]
-                                for a, c, b in zip(rid.astype(np.int64), rcnt, truth)]))
+    ref_recall = recall_at_k(rid.astype(np.int64), rcnt, truth)
     probe = q[: max(2 * threads, 16)]
     t = time.time()
     ref.search_batch(probe, cfg["k"], threads=threads)
@@ -782,11 +887,11 @@ def run_reference(args):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic: seeded Gaussian mixture with the configuration's generator (no dataset)",
-        "config": {"workload": cfg["name"], "n": cfg["n"], "d": cfg["d"], "nlist": cfg["nlist"],
-                   "M": cfg["M"], "codebook_size": cfg["ks"], "nprobe": cfg["nprobe"], "k": cfg["k"],
-                   "batch": cfg["nq"], "step_sample": s, "recall_at_10": round(ref_recall, 4),
-                   "recall_queries": rs,
-                   "index": "spherical Lloyd on 65,536 rows, 8 iterations (CPU, untimed)"},
+        "config": workload_config(cfg, cfg["nq"], train_sample, args.train_iters),
+        "recall_at_10": round(ref_recall, 4),
+        "recall_queries": rs,
+        "step_sample": s,
+        "index_build_s": round(build_s, 1),
         "cpu_baseline": {"value": round(value, 1), "unit": "queries/s", "cores": threads, "kind": "port",
                          "sample": f"{s} queries per step of the {cfg['nq']}-query batch, oracle port of the reference search on all host threads"},
         "e2e": {"value": round(value, 1), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -820,8 +925,8 @@ def run_reference_flat(args, cfg, x, q, threads):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic: N(0,1) rows L2-normalised, seeded (no dataset)",
-        "config": {"workload": cfg["name"], "n": cfg["n"], "d": cfg["d"], "k": k, "batch": cfg["nq"],
-                   "step_sample": s},
+        "config": workload_config(cfg, cfg["nq"], 0, 0),
+        "step_sample": s,
         "cpu_baseline": {"value": round(value, 1), "unit": "queries/s", "cores": threads, "kind": "port",
                          "sample": f"{s} queries per step, oracle exhaustive scan on all host threads"},
         "e2e": {"value": round(value, 1), "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -79,6 +79,12 @@ typedef struct vg_search_profile {
    * warp-per-query kernels; 0 where another kernel ran); probed_pairs and
    * scanned_vectors count every probed list */
   uint64_t scored_lists, scored_vectors;
+  /* 4-bit warp-per-query kernel: tables built (lists past the pre-table
+   * bound) and 16-code groups summed (candidates x groups before early exit);
+   * seed_*: the same counters of a list-sharded search's seed pass, which the
+   * fields above do not include */
+  uint64_t tables_built, code_groups;
+  uint64_t seed_scored_lists, seed_scored_vectors, seed_tables_built, seed_code_groups;
 } vg_search_profile;
 
 typedef struct vg_index vg_index;

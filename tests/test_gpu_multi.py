@@ -2,8 +2,10 @@
 
 After vg_ivfpq_shard every rank keeps only the inverted lists it owns, and
 each rank searches a batch of its own.  The ranks all-gather queries, probes
-and pruning bounds, seed every query's pruning bound with the k-th key of its
-nearest list (all-reduce min), scan their own lists for the global batch and
+and pruning bounds, seed every query's pruning bound on the rank that owns its
+nearest list (that rank's lists of the query's probes, in order, until it holds
+k keys; the k-th key travels as an all-reduce min), scan their own lists for
+the global batch and
 return every query's per-rank top-k to its rank (all-to-all), which merges
 them -- the reference's per-shard top-k merge
 (examples/large_scale.rs:1969-2025).  Each rank's results must equal, bit for

@@ -2,11 +2,13 @@
 running the oracle).
 
 Each rank owns the lists the engine's packer gives it and searches a batch of
-its own.  The ranks exchange their queries, seed every query's bound with the
-k-th key of its nearest list (scored by the rank that owns it; per-rank seed
-keys all-gathered and merged), keep only keys at or below that bound in their
-own lists, and route every query's per-rank top-k back to its rank, which
-merges them by (distance, id).  The merged rows must equal the unsharded
+its own.  The ranks exchange their queries; the rank that owns a query's
+nearest list seeds the query's bound: it scores its own lists of the query's
+probes in order until it holds k keys, and its k-th key (the minimum over
+ranks, the other ranks holding none) bounds the query's k-th key over every
+list.  Each rank keeps only keys at or below that bound in its own lists and
+routes every query's per-rank top-k back to its rank, which merges them by
+(distance, id).  The merged rows must equal the unsharded
 search of the same
 queries -- the property the engine's NCCL path
 (vg_ivfpq_shard / vg_ivfpq_search_batch) relies on.  The partition comes from
@@ -25,7 +27,6 @@ import torch.multiprocessing as mp
 WORLD = 2
 N, D, L, M, KS, NPROBE, K, NQ = 3000, 16, 24, 4, 16, 6, 10, 40  # NQ queries per rank
 EMPTY = np.uint64(0xFFFFFFFFFFFFFFFF)
-SEED = 1  # probes scanned before the bound is exchanged (the engine's kSeedProbes)
 
 
 def _free_port() -> int:
@@ -81,15 +82,27 @@ def _rank_main(rank, port, out_path):
     parts = [torch.empty_like(own) for _ in range(WORLD)]
     dist.all_gather(parts, own)
     q = torch.cat(parts).numpy()
-    # 3. seed: each rank's keys in its lists among every query's SEED nearest
-    # lists, all-gathered and merged: the k-th merged key bounds the query's
-    # k-th key over every list
-    sid, sd, sc = shard.search_batch(q, K, nprobe=SEED)
-    seed = _keys(orc, sid, sd, sc)
-    parts = [torch.empty((NQ * WORLD, K), dtype=torch.int64) for _ in range(WORLD)]
-    dist.all_gather(parts, torch.from_numpy(seed.view(np.int64).copy()))
-    merged_seed = np.sort(np.concatenate([p.numpy().view(np.uint64) for p in parts], axis=1), axis=1)[:, :K]
-    ceiling = merged_seed[:, K - 1]
+    # 3. seed: the owner of a query's nearest list scores its own lists of the
+    # query's probes in order until it holds K keys; the minimum over ranks of
+    # the seed k-th keys (EMPTY where a rank seeded nothing) is the ceiling
+    qn = orc.normalize(q)
+    sc_cent = qn @ cent.T
+    nearest = np.argmax(sc_cent, axis=1)
+    top2 = np.sort(sc_cent, axis=1)[:, -2:]
+    assert (top2[:, 1] - top2[:, 0] > 1e-5).all()  # no near-tie for the nearest list
+    kth = np.full(q.shape[0], EMPTY, dtype=np.uint64)
+    for i in range(q.shape[0]):
+        if owner[nearest[i]] != rank:
+            continue
+        for s in range(1, NPROBE + 1):
+            sid, sd, sc = shard.search_batch(q[i:i + 1], K, nprobe=s)
+            if sc[0] >= K:
+                kth[i] = _keys(orc, sid, sd, sc)[0, K - 1]
+                break
+    t = torch.from_numpy(kth.view(np.int64).copy())
+    parts = [torch.empty_like(t) for _ in range(WORLD)]
+    dist.all_gather(parts, t)
+    ceiling = np.min(np.stack([p.numpy().view(np.uint64) for p in parts]), axis=0)
     # 4. own lists for the global batch, keys at or below the ceiling only
     ids, dists, cnt = shard.search_batch(q, K)
     keys = _keys(orc, ids, dists, cnt)

@@ -99,6 +99,12 @@ class VgProfile(C.Structure):
             "scan_launches",
             "scored_lists",
             "scored_vectors",
+            "tables_built",
+            "code_groups",
+            "seed_scored_lists",
+            "seed_scored_vectors",
+            "seed_tables_built",
+            "seed_code_groups",
         )
     ]
 

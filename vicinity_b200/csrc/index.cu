@@ -156,6 +156,7 @@ std::vector<uint32_t> seeded_prefix(size_t n, size_t take, uint64_t seed) {
 constexpr size_t kDistBudgetBytes = size_t(1) << 30;  // coarse distance tile
 constexpr size_t kAssignChunk = size_t(4) << 20;      // rows per argmin launch
 constexpr int kPhaseEvents = 12;
+constexpr int kStats = 11;  // profiling counters (vg_index::stats)
 
 }  // namespace
 
@@ -212,7 +213,7 @@ struct vg_index {
   DevBuf ws_q, ws_qn, ws_dist, ws_probes, ws_pdist, ws_scalars,
       ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_lb, ws_rec, ws_lbq, ws_qimg, ws_eps, ws_tc,
       ws_floor, ws_qall, ws_cmax;
-  DevBuf stats;  // u64 [pairs, vectors, code bytes, scored lists, scored vectors] while profiling
+  DevBuf stats;  // u64 [pairs, vectors, code bytes, scan counters [4], seed scan counters [4]] while profiling
 
   // error flag of bounded device waits, in mapped pinned host memory
   int *h_err = nullptr, *d_err = nullptr;
@@ -983,11 +984,6 @@ ProbeBoundArgs bound_args_at(vg_index *ix, size_t P, size_t r0, bool prune, bool
                         quant ? ix->ws_lbq.as<float>() + r0 * P : nullptr};
 }
 
-// Probes of every query scanned before the pruning bound is exchanged: the
-// nearest list only.  It belongs to one rank, which scores it as one GPU
-// would (with no bound yet); with more seed probes every rank would also
-// score its first owned list without a bound, work one GPU never does.
-constexpr size_t kSeedProbes = 1;
 
 int nccl_ok(vg_index *ix, ncclResult_t r, const char *what) {
   if (r == ncclSuccess) return VG_OK;
@@ -1049,8 +1045,9 @@ int search_sharded(vg_index *ix, const float *queries, size_t nq, size_t k, size
   VG_CU(ix->ws_lb.reserve(B * P * 4));
   if (quant) VG_CU(ix->ws_lbq.reserve(B * P * 4));
   if (recs) VG_CU(ix->ws_rec.reserve(B * P * sizeof(ProbeRec)));
-  const size_t S = std::min<size_t>(P, kSeedProbes);
-  VG_CU(ix->ws_seed.reserve(B * kk * 8 + B * 8));  // this rank's seed keys, then every query's k-th key
+  // this rank's seed keys, every query's k-th key, the probe each query's
+  // main pass starts from
+  VG_CU(ix->ws_seed.reserve(B * kk * 8 + B * 8 + B * 4));
   VG_CU(ix->ws_keys.reserve(B * kk * 8));
   VG_CU(ix->ws_all_keys.reserve(B * kk * 8));
   float *qall = ix->ws_qall.as<float>(), *qown = qall + R * nq * d;
@@ -1105,14 +1102,22 @@ int search_sharded(vg_index *ix, const float *queries, size_t nq, size_t k, size
                              ix->stats.as<unsigned long long>(), s));
   }
 
-  // 3. seed: every query's k-th key over its S nearest lists
-  const bool seeded = prune && S < P && ivfpq_scan_warp_applies(sp);
+  // 3. seed: the rank that owns a query's nearest list scores it as one GPU
+  // would (no bound yet), and its own next lists until it keeps k keys -- any
+  // k keys bound the query's k-th key over every list.  The other ranks score
+  // nothing here (an unbounded first list on every rank would be work one GPU
+  // never does).  The bound travels as a min over ranks of every query's k-th
+  // key; each query's main pass resumes after the lists its seed scored.
+  const bool seeded = prune && P > 1 && ivfpq_scan_warp_applies(sp);
   unsigned long long *seed_own = ix->ws_seed.as<unsigned long long>();  // [B][kk]
   unsigned long long *ceiling = seed_own + B * kk;                       // [B]
+  uint32_t *resume = reinterpret_cast<uint32_t *>(ceiling + B);          // [B]
   if (seeded) {
-    sp.pscan = static_cast<int>(S);
+    sp.seed_next = resume;
     sp.out_keys = seed_own;
     sp.out_kth = ceiling;
+    unsigned long long *main_counters = sp.scored;
+    if (prof) sp.scored = ix->stats.as<unsigned long long>() + 7;
     VG_CU(cudaMemsetAsync(d_counter, 0, 4, s));
     VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
     ix->launches += 1;
@@ -1120,11 +1125,12 @@ int search_sharded(vg_index *ix, const float *queries, size_t nq, size_t k, size
     // one rank holds each query's seed keys (kEmptyKey elsewhere): min over ranks
     VG_TRY(nccl_ok(ix, ncclAllReduce(ceiling, ceiling, B, ncclUint64, ncclMin, ix->comm, s),
                    "ncclAllReduce (seed bounds)"));
-    sp.pstart = static_cast<int>(S);
-    sp.pscan = 0;
+    sp.seed_next = nullptr;
+    sp.probe_from = resume;
     sp.out_kth = nullptr;
     sp.init_keys = seed_own;
     sp.key_ceiling = ceiling;
+    sp.scored = main_counters;
   } else {
     mark(ix, 6);
   }
@@ -2086,8 +2092,8 @@ int vg_ivfpq_set_profiling(vg_index *ix, int on) {
   if (!ix) return fail(VG_ERR_INVALID_PARAMETER, "null index");
   DeviceGuard g(ix->device);
   if (on && !ix->stats.p) {
-    VG_CU(ix->stats.reserve(5 * 8));
-    VG_CU(cudaMemset(ix->stats.p, 0, 5 * 8));
+    VG_CU(ix->stats.reserve(kStats * 8));
+    VG_CU(cudaMemset(ix->stats.p, 0, kStats * 8));
   }
   ix->profiling = on != 0;
   return VG_OK;
@@ -2098,13 +2104,19 @@ int vg_ivfpq_get_profile(const vg_index *ix, vg_search_profile *out) {
   *out = ix->prof;
   if (ix->stats.p) {
     DeviceGuard g(ix->device);
-    unsigned long long st[5] = {0, 0, 0, 0, 0};
+    unsigned long long st[kStats] = {};
     VG_CU(cudaMemcpy(st, ix->stats.p, sizeof(st), cudaMemcpyDeviceToHost));
     out->probed_pairs = st[0];
     out->scanned_vectors = st[1];
     out->scanned_code_bytes = st[2];
     out->scored_lists = st[3];
     out->scored_vectors = st[4];
+    out->tables_built = st[5];
+    out->code_groups = st[6];
+    out->seed_scored_lists = st[7];
+    out->seed_scored_vectors = st[8];
+    out->seed_tables_built = st[9];
+    out->seed_code_groups = st[10];
   }
   return VG_OK;
 }
@@ -2114,7 +2126,7 @@ int vg_ivfpq_reset_profile(vg_index *ix) {
   ix->prof = vg_search_profile{};
   if (ix->stats.p) {
     DeviceGuard g(ix->device);
-    VG_CU(cudaMemset(ix->stats.p, 0, 5 * 8));
+    VG_CU(cudaMemset(ix->stats.p, 0, kStats * 8));
   }
   return VG_OK;
 }

@@ -292,13 +292,20 @@ struct ScanParams {
   const float *probe_lb;         // [nq][P] distance lower bound per probe (nullable: no list pruning)
   const ProbeRec *probe_rec;     // [nq][P] probe records (streaming 8-bit kernel; nullable)
   const float *probe_lbq;        // [nq][P] bound on quantised 4-bit distances before the table (nullable)
-  unsigned long long *scored;    // [2]: lists and vectors scored after pruning (nullable; warp-per-query kernels)
+  unsigned long long *scored;    // [4]: lists and vectors scored after pruning, tables built and 16-code
+                                 // groups summed (4-bit) (nullable; warp-per-query kernels)
   // [nq] keys already selected by an earlier pass: only keys above a query's
   // floor compete (nullable; query-major and 4-bit block kernels, which serve
   // k up to 256: top-k beyond 256 in passes)
   const unsigned long long *key_floor;
   // list-sharded search (warp-per-query kernels only; zero-initialised = off):
-  int pstart, pscan;                     // probes [pstart, pscan) are visited (pscan 0: P); row stride stays P
+  // seed pass (seed_next set): a query whose probe 0 is this rank's list
+  // visits this rank's lists of probes 0, 1, ... and stops before the first
+  // list it reaches with k keys already kept; seed_next[q] = that probe (P
+  // when every probe was visited, 1 when probe 0 is another rank's: nothing
+  // visited).  Main pass: probe_from[q] = the query's first probe (nullable: 0)
+  uint32_t *seed_next;
+  const uint32_t *probe_from;
   const unsigned long long *init_keys;   // [nq][k] keys the query's top-k starts from (nullable)
   unsigned long long *out_kth;           // [nq] the query's k-th kept key (kEmptyKey: fewer than k) (nullable)
   const unsigned long long *key_ceiling; // keys above the query's ceiling are never kept (nullable) ...
@@ -317,7 +324,7 @@ cudaError_t launch_ivfpq_scan(const ScanParams &p, int num_sms,
 cudaError_t launch_ivfpq_scan_generic(const ScanParams &p, int num_sms, cudaStream_t s);
 
 // Whether launch_ivfpq_scan with force_warp runs a warp-per-query kernel for
-// p (the kernels that honour pstart, pscan, init_keys, out_kth and key_ceiling).
+// p (the kernels that honour seed_next, probe_from, init_keys, out_kth and key_ceiling).
 bool ivfpq_scan_warp_applies(const ScanParams &p);
 
 // Name of the kernel variant launch_ivfpq_scan would run for p.

@@ -140,43 +140,79 @@ __global__ void __launch_bounds__(kDirectThreads, 1) ivfpq_direct_kernel(const S
         tk.add(i < k ? p.init_keys[static_cast<size_t>(q) * k + i] : kEmptyKey);
       }
     }
-    const int pn = p.pscan ? p.pscan : P;
-    for (int pi = p.pstart; pi < pn; ++pi) {
-      const ProbeRec rec = p.probe_rec[static_cast<size_t>(q) * P + pi];
-      if (rec.list == 0xffffffffu) continue;
-      uint64_t kth = min(tk.get(k - 1), kth0);
-      if (kth != kEmptyKey && rec.lb > key_dist(kth)) continue;  // list pruning
-      const float *cent = p.centroids + static_cast<size_t>(rec.list) * d;
-      const uint8_t *lcodes = p.list_codes + rec.coff;
-      if (static_cast<uint32_t>(lane) < rec.len) prefetch_codes(lcodes + static_cast<uint64_t>(lane) * M);
-      __syncwarp();
-      for (int j = lane; j < d; j += 32) rb[(j / DSUB) * DP + j % DSUB] = __fsub_rn(qv[j], cent[j]);
-      __syncwarp();
-      ++n_lists;
-      n_vecs += rec.len;
-      for (uint32_t x0 = 0; x0 < rec.len; x0 += 32) {
-        const uint32_t c = x0 + lane;
-        bool alive = c < rec.len;
-        if (c + 32 < rec.len) prefetch_codes(lcodes + static_cast<uint64_t>(c + 32) * M);  // next chunk
-        const uint32_t tkey = static_cast<uint32_t>(kth >> 32);
-        const uint8_t *cp = lcodes + static_cast<uint64_t>(alive ? c : 0u) * M;
-        const float dist = direct_row_sum<DSUB, DP>(cp, cbk, rb, M, tkey, alive);
-        const uint32_t dk = order_key(dist);
-        const bool pass = alive && dk <= tkey;
-        unsigned mask = __ballot_sync(VG_FULL_MASK, pass);
-        if (!mask) continue;
-        const uint64_t key = pass ? ((static_cast<uint64_t>(dk) << 32) | p.list_ids[rec.lbeg + c]) : kEmptyKey;
-        if (__popc(mask) > 4) {
-          tk.add(key < kth ? key : kEmptyKey);
-        } else {
-          while (mask) {
-            const int src = __ffs(mask) - 1;
-            mask &= mask - 1;
-            const uint64_t kx = shfl64(key, src);
-            if (kx < kth) topk_insert_one(tk, kx);
-          }
+    const bool seed = p.seed_next != nullptr;
+    int first = p.probe_from ? static_cast<int>(p.probe_from[q]) : 0;
+    int seed_stop = P;
+    bool stopped = false;
+    // a seed pass scores only queries whose nearest list is this rank's (the
+    // records of other ranks' lists hold no list)
+    if (seed && p.probe_rec[static_cast<size_t>(q) * P].list == 0xffffffffu) {
+      seed_stop = 1;
+      first = P;
+    }
+    // probe records in groups of 32, in order: lane i loads record c0 + i so
+    // the warp walks only the live ones with no global load on its serial
+    // path; a list the group's starting bound prunes stays pruned (the bound
+    // only tightens)
+    for (int c0 = first; c0 < P; c0 += 32) {
+      if (stopped) break;
+      if (seed && tk.get(k - 1) != kEmptyKey) {
+        seed_stop = c0;
+        break;
+      }
+      ProbeRec rec_l{0xffffffffu, 0u, 0ull, 0ull, 0.0f, 0u};
+      if (c0 + lane < P) rec_l = p.probe_rec[static_cast<size_t>(q) * P + c0 + lane];
+      const uint64_t kth_g = min(tk.get(k - 1), kth0);
+      const bool pruned0 = kth_g != kEmptyKey && rec_l.lb > key_dist(kth_g);
+      unsigned todo = __ballot_sync(VG_FULL_MASK, rec_l.list != 0xffffffffu && rec_l.len > 0 && !pruned0);
+      while (todo) {
+        const int pj = __ffs(todo) - 1;
+        todo &= todo - 1;
+        if (seed && tk.get(k - 1) != kEmptyKey) {
+          seed_stop = c0 + pj;
+          stopped = true;
+          break;
         }
-        kth = min(tk.get(k - 1), kth0);
+        ProbeRec rec;
+        rec.list = __shfl_sync(VG_FULL_MASK, rec_l.list, pj);
+        rec.len = __shfl_sync(VG_FULL_MASK, rec_l.len, pj);
+        rec.lbeg = shfl64(rec_l.lbeg, pj);
+        rec.coff = shfl64(rec_l.coff, pj);
+        rec.lb = __shfl_sync(VG_FULL_MASK, rec_l.lb, pj);
+        uint64_t kth = min(tk.get(k - 1), kth0);
+        if (kth != kEmptyKey && rec.lb > key_dist(kth)) continue;  // list pruning
+        const float *cent = p.centroids + static_cast<size_t>(rec.list) * d;
+        const uint8_t *lcodes = p.list_codes + rec.coff;
+        if (static_cast<uint32_t>(lane) < rec.len) prefetch_codes(lcodes + static_cast<uint64_t>(lane) * M);
+        __syncwarp();
+        for (int j = lane; j < d; j += 32) rb[(j / DSUB) * DP + j % DSUB] = __fsub_rn(qv[j], cent[j]);
+        __syncwarp();
+        ++n_lists;
+        n_vecs += rec.len;
+        for (uint32_t x0 = 0; x0 < rec.len; x0 += 32) {
+          const uint32_t c = x0 + lane;
+          bool alive = c < rec.len;
+          if (c + 32 < rec.len) prefetch_codes(lcodes + static_cast<uint64_t>(c + 32) * M);  // next chunk
+          const uint32_t tkey = static_cast<uint32_t>(kth >> 32);
+          const uint8_t *cp = lcodes + static_cast<uint64_t>(alive ? c : 0u) * M;
+          const float dist = direct_row_sum<DSUB, DP>(cp, cbk, rb, M, tkey, alive);
+          const uint32_t dk = order_key(dist);
+          const bool pass = alive && dk <= tkey;
+          unsigned mask = __ballot_sync(VG_FULL_MASK, pass);
+          if (!mask) continue;
+          const uint64_t key = pass ? ((static_cast<uint64_t>(dk) << 32) | p.list_ids[rec.lbeg + c]) : kEmptyKey;
+          if (__popc(mask) > 4) {
+            tk.add(key < kth ? key : kEmptyKey);
+          } else {
+            while (mask) {
+              const int src = __ffs(mask) - 1;
+              mask &= mask - 1;
+              const uint64_t kx = shfl64(key, src);
+              if (kx < kth) topk_insert_one(tk, kx);
+            }
+          }
+          kth = min(tk.get(k - 1), kth0);
+        }
       }
     }
 
@@ -184,6 +220,7 @@ __global__ void __launch_bounds__(kDirectThreads, 1) ivfpq_direct_kernel(const S
       const uint64_t kk = tk.get(k - 1);
       if (lane == 0) p.out_kth[q] = kk;
     }
+    if (seed && lane == 0) p.seed_next[q] = static_cast<uint32_t>(seed_stop);
     uint32_t count = 0;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
