@@ -157,6 +157,11 @@ constexpr size_t kDistBudgetBytes = size_t(1) << 30;  // coarse distance tile
 constexpr size_t kAssignChunk = size_t(4) << 20;      // rows per argmin launch
 constexpr int kPhaseEvents = 12;
 constexpr int kStats = 11;  // profiling counters (vg_index::stats)
+// A list-sharded search's main pass runs units of this many probes of one
+// query (a query with many unpruned lists spreads over several warps); items
+// whose lists hold at least kHeavyVectors vectors are started first.
+constexpr int kUnitProbes = 8;
+constexpr uint32_t kHeavyVectors = 1024;
 
 }  // namespace
 
@@ -212,7 +217,7 @@ struct vg_index {
   // search workspace
   DevBuf ws_q, ws_qn, ws_dist, ws_probes, ws_pdist, ws_scalars,
       ws_keys, ws_all_keys, ws_out_ids, ws_out_dist, ws_out_count, ws_lb, ws_rec, ws_lbq, ws_qimg, ws_eps, ws_tc,
-      ws_floor, ws_qall, ws_cmax;
+      ws_floor, ws_qall, ws_cmax, ws_units, ws_work;
   DevBuf stats;  // u64 [pairs, vectors, code bytes, scan counters [4], seed scan counters [4]] while profiling
 
   // error flag of bounded device waits, in mapped pinned host memory
@@ -1045,9 +1050,12 @@ int search_sharded(vg_index *ix, const float *queries, size_t nq, size_t k, size
   VG_CU(ix->ws_lb.reserve(B * P * 4));
   if (quant) VG_CU(ix->ws_lbq.reserve(B * P * 4));
   if (recs) VG_CU(ix->ws_rec.reserve(B * P * sizeof(ProbeRec)));
-  // this rank's seed keys, every query's k-th key, the probe each query's
-  // main pass starts from
-  VG_CU(ix->ws_seed.reserve(B * kk * 8 + B * 8 + B * 4));
+  // every query's k-th key and the probe its main pass starts from; the
+  // per-unit keys [1 + U][B][kk] (row 0: the seed's); the work lists
+  const size_t U = (P + kUnitProbes - 1) / kUnitProbes;
+  VG_CU(ix->ws_seed.reserve(B * 8 + B * 4));
+  VG_CU(ix->ws_units.reserve((U + 1) * B * kk * 8));
+  VG_CU(ix->ws_work.reserve(B * U * 4));
   VG_CU(ix->ws_keys.reserve(B * kk * 8));
   VG_CU(ix->ws_all_keys.reserve(B * kk * 8));
   float *qall = ix->ws_qall.as<float>(), *qown = qall + R * nq * d;
@@ -1089,6 +1097,7 @@ int search_sharded(vg_index *ix, const float *queries, size_t nq, size_t k, size
   }
   VG_CU(ix->ws_scalars.reserve(64));
   uint32_t *d_counter = ix->ws_scalars.as<uint32_t>();
+  uint32_t *d_wcount = d_counter + 2;  // the work list's two counts
   vg::ScanParams sp = base_scan_params(ix, P, kk, prune, recs, quant);
   sp.qn = qall;
   sp.owner = ix->owner.as<uint8_t>();
@@ -1109,38 +1118,59 @@ int search_sharded(vg_index *ix, const float *queries, size_t nq, size_t k, size
   // never does).  The bound travels as a min over ranks of every query's k-th
   // key; each query's main pass resumes after the lists its seed scored.
   const bool seeded = prune && P > 1 && ivfpq_scan_warp_applies(sp);
-  unsigned long long *seed_own = ix->ws_seed.as<unsigned long long>();  // [B][kk]
-  unsigned long long *ceiling = seed_own + B * kk;                       // [B]
+  unsigned long long *unit_keys = ix->ws_units.as<unsigned long long>();  // [1 + U][B][kk]
+  unsigned long long *ceiling = ix->ws_seed.as<unsigned long long>();    // [B]
   uint32_t *resume = reinterpret_cast<uint32_t *>(ceiling + B);          // [B]
+  uint32_t *work = ix->ws_work.as<uint32_t>();
   if (seeded) {
+    // 3. seed pass over the queries whose nearest list is this rank's
+    VG_CU(cudaMemsetAsync(unit_keys, 0xff, (U + 1) * B * kk * 8, s));
+    VG_CU(cudaMemsetAsync(ceiling, 0xff, B * 8, s));
+    VG_CU(cudaMemsetAsync(d_counter, 0, 16, s));
+    VG_CU(launch_order_seed(ix->ws_probes.as<uint32_t>(), static_cast<int>(P), ix->owner.as<uint8_t>(),
+                            ix->list_off.as<uint64_t>(), B, kHeavyVectors, work, d_wcount,
+                            static_cast<uint32_t>(B * U), resume, s));
+    sp.work = work;
+    sp.work_count = d_wcount;
+    sp.work_cap = static_cast<uint32_t>(B * U);
     sp.seed_next = resume;
-    sp.out_keys = seed_own;
+    sp.out_keys = unit_keys;
     sp.out_kth = ceiling;
     unsigned long long *main_counters = sp.scored;
     if (prof) sp.scored = ix->stats.as<unsigned long long>() + 7;
-    VG_CU(cudaMemsetAsync(d_counter, 0, 4, s));
     VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
-    ix->launches += 1;
+    ix->launches += 2;
     mark(ix, 6);
     // one rank holds each query's seed keys (kEmptyKey elsewhere): min over ranks
     VG_TRY(nccl_ok(ix, ncclAllReduce(ceiling, ceiling, B, ncclUint64, ncclMin, ix->comm, s),
                    "ncclAllReduce (seed bounds)"));
+    mark(ix, 7);
+    // 4. units of this rank's lists for the global batch, bounded by the
+    // ceiling, heavy ones first; then every query's keys merged over its units
+    VG_CU(cudaMemsetAsync(d_counter, 0, 16, s));
+    VG_CU(launch_order_units(ix->ws_probes.as<uint32_t>(), static_cast<int>(P), kUnitProbes,
+                             ix->owner.as<uint8_t>(), ix->list_off.as<uint64_t>(),
+                             quant ? ix->ws_lbq.as<float>() : ix->ws_lb.as<float>(), ceiling, resume, B,
+                             kHeavyVectors, work, d_wcount, static_cast<uint32_t>(B * U), s));
     sp.seed_next = nullptr;
-    sp.probe_from = resume;
     sp.out_kth = nullptr;
-    sp.init_keys = seed_own;
+    sp.probe_from = resume;
+    sp.unit_probes = kUnitProbes;
     sp.key_ceiling = ceiling;
     sp.scored = main_counters;
+    VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
+    VG_CU(launch_merge_shards(unit_keys, static_cast<int>(U + 1), B, static_cast<int>(kk), nullptr, nullptr,
+                              nullptr, nullptr, ix->ws_keys.as<unsigned long long>(), s));
+    ix->launches += 3;
   } else {
     mark(ix, 6);
+    mark(ix, 7);
+    // 4. this rank's lists for the global batch
+    sp.out_keys = ix->ws_keys.as<unsigned long long>();
+    VG_CU(cudaMemsetAsync(d_counter, 0, 4, s));
+    VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
+    ix->launches += 1;
   }
-  mark(ix, 7);
-
-  // 4. this rank's lists for the global batch
-  sp.out_keys = ix->ws_keys.as<unsigned long long>();
-  VG_CU(cudaMemsetAsync(d_counter, 0, 4, s));
-  VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
-  ix->launches += 1;
   mark(ix, 8);
 
   // 5. every query's per-rank keys to its rank: [W][nq][kk]
@@ -1779,7 +1809,8 @@ int vg_ivfpq_destroy(vg_index *ix) {
                       &ix->owner, &ix->ws_q, &ix->ws_qn, &ix->ws_dist, &ix->ws_probes, &ix->ws_pdist,
                       &ix->ws_scalars, &ix->ws_keys, &ix->ws_all_keys, &ix->ws_out_ids, &ix->ws_out_dist,
                       &ix->ws_out_count, &ix->stats, &ix->ws_lb, &ix->ws_rec, &ix->ws_lbq, &ix->ws_qimg,
-                      &ix->ws_eps, &ix->ws_tc, &ix->ws_floor, &ix->cent_img, &ix->ws_seed, &ix->ws_qall, &ix->ws_cmax})
+                      &ix->ws_eps, &ix->ws_tc, &ix->ws_floor, &ix->cent_img, &ix->ws_seed, &ix->ws_qall, &ix->ws_cmax, &ix->ws_units,
+                      &ix->ws_work})
       b->release();
     for (int i = 0; i < kPhaseEvents; ++i)
       if (ix->ev[i]) cudaEventDestroy(ix->ev[i]);

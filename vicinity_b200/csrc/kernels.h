@@ -248,6 +248,21 @@ cudaError_t launch_probe_lb(const float *qn, size_t nq, int d, const uint32_t *p
 cudaError_t launch_probe_records(const uint32_t *probes, const float *lb, size_t n, const uint8_t *owner,
                                  const uint64_t *list_off, const uint64_t *code_off, ProbeRec *rec, cudaStream_t s);
 
+// Work lists of a list-sharded search's two scan passes (ScanParams::work).
+// Seed pass: the queries whose probe 0 is an owned list (seed_next[q] = 1 for
+// the others, which the pass skips).  Main pass: the units (query, G probes
+// from first[q] on) with an owned list whose bound (lbq for 4-bit codes, lb
+// for 8-bit) lies at or below the query's ceiling key.  An item whose lists
+// hold at least `heavy` vectors goes to the front (count[0]), the others to
+// the back (count[1], from work[cap - 1] down); count is zeroed first.
+cudaError_t launch_order_seed(const uint32_t *probes, int P, const uint8_t *owner, const uint64_t *list_off,
+                              size_t nq, uint32_t heavy, uint32_t *work, uint32_t *count, uint32_t cap,
+                              uint32_t *seed_next, cudaStream_t s);
+cudaError_t launch_order_units(const uint32_t *probes, int P, int G, const uint8_t *owner, const uint64_t *list_off,
+                               const float *bound, const unsigned long long *ceiling, const uint32_t *first,
+                               size_t nq, uint32_t heavy, uint32_t *work, uint32_t *count, uint32_t cap,
+                               cudaStream_t s);
+
 // dst + dst_off[i] <- bytes[i] bytes of src + src_off[i], i < count (a block
 // per segment; offsets and sizes in device memory).
 cudaError_t launch_copy_segments(const void *src, void *dst, const uint64_t *src_off, const uint64_t *dst_off,
@@ -306,6 +321,16 @@ struct ScanParams {
   // visited).  Main pass: probe_from[q] = the query's first probe (nullable: 0)
   uint32_t *seed_next;
   const uint32_t *probe_from;
+  // work items: with unit_probes = G > 0 an item is a unit (query q, probes
+  // [g G, (g + 1) G) from probe_from[q] on) whose top-k, bounded by the key
+  // ceiling, goes to out_keys[((1 + g) nq + q) k ...]; otherwise an item is a
+  // query.  work (nullable: every item, in order) lists the items to run:
+  // work_count[0] of them from work[0] up, then work_count[1] from
+  // work[work_cap - 1] down (a list built heavy items first)
+  int unit_probes;
+  const uint32_t *work;
+  const uint32_t *work_count;
+  uint32_t work_cap;
   const unsigned long long *init_keys;   // [nq][k] keys the query's top-k starts from (nullable)
   unsigned long long *out_kth;           // [nq] the query's k-th kept key (kEmptyKey: fewer than k) (nullable)
   const unsigned long long *key_ceiling; // keys above the query's ceiling are never kept (nullable) ...

@@ -19,6 +19,7 @@
 #pragma once
 
 #include "scan_kernel.cuh"
+#include "scan_work.cuh"
 
 namespace vg {
 
@@ -117,11 +118,17 @@ __global__ void __launch_bounds__(kDirectThreads, 1) ivfpq_direct_kernel(const S
   for (int i = lane; i < M * DP; i += 32) rb[i] = 0.0f;  // padding lanes of the residual stay 0
   __syncthreads();
 
+  ScanWork work;
+  work.init(p);
   for (;;) {
-    uint32_t q = 0;
-    if (lane == 0) q = atomicAdd(p.counter, 1u);
-    q = __shfl_sync(VG_FULL_MASK, q, 0);
-    if (q >= static_cast<uint32_t>(p.nq)) break;
+    uint32_t w = 0;
+    if (lane == 0) w = atomicAdd(p.counter, 1u);
+    w = __shfl_sync(VG_FULL_MASK, w, 0);
+    if (w >= work.total) break;
+    uint32_t q;
+    int first, last;
+    size_t orow;
+    work.item(p, w, q, first, last, orow);
     const float *qv = p.qn + static_cast<size_t>(q) * d;
     WarpTopK<R> tk;
     tk.init();
@@ -141,27 +148,26 @@ __global__ void __launch_bounds__(kDirectThreads, 1) ivfpq_direct_kernel(const S
       }
     }
     const bool seed = p.seed_next != nullptr;
-    int first = p.probe_from ? static_cast<int>(p.probe_from[q]) : 0;
     int seed_stop = P;
     bool stopped = false;
     // a seed pass scores only queries whose nearest list is this rank's (the
     // records of other ranks' lists hold no list)
     if (seed && p.probe_rec[static_cast<size_t>(q) * P].list == 0xffffffffu) {
       seed_stop = 1;
-      first = P;
+      first = last;
     }
     // probe records in groups of 32, in order: lane i loads record c0 + i so
     // the warp walks only the live ones with no global load on its serial
     // path; a list the group's starting bound prunes stays pruned (the bound
     // only tightens)
-    for (int c0 = first; c0 < P; c0 += 32) {
+    for (int c0 = first; c0 < last; c0 += 32) {
       if (stopped) break;
       if (seed && tk.get(k - 1) != kEmptyKey) {
         seed_stop = c0;
         break;
       }
       ProbeRec rec_l{0xffffffffu, 0u, 0ull, 0ull, 0.0f, 0u};
-      if (c0 + lane < P) rec_l = p.probe_rec[static_cast<size_t>(q) * P + c0 + lane];
+      if (c0 + lane < last) rec_l = p.probe_rec[static_cast<size_t>(q) * P + c0 + lane];
       const uint64_t kth_g = min(tk.get(k - 1), kth0);
       const bool pruned0 = kth_g != kEmptyKey && rec_l.lb > key_dist(kth_g);
       unsigned todo = __ballot_sync(VG_FULL_MASK, rec_l.list != 0xffffffffu && rec_l.len > 0 && !pruned0);
@@ -229,7 +235,7 @@ __global__ void __launch_bounds__(kDirectThreads, 1) ivfpq_direct_kernel(const S
       const bool real = i < k && key != kEmptyKey;
       count += __popc(__ballot_sync(VG_FULL_MASK, real));
       if (i < k) {
-        const size_t o = static_cast<size_t>(q) * k + i;
+        const size_t o = orow * k + i;
         if (p.out_keys) p.out_keys[o] = key;
         if (p.out_ids) {
           p.out_ids[o] = real ? p.doc_ids[key_id(key)] : 0xffffffffu;

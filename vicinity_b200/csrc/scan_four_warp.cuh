@@ -19,6 +19,7 @@
 #include <cfloat>
 
 #include "scan_fourbit.cuh"
+#include "scan_work.cuh"
 
 namespace vg {
 
@@ -64,12 +65,18 @@ __global__ void __launch_bounds__(kFourWarpThreads, 1) ivfpq_four_warp_kernel(co
 
   for (int i = tid; i < nent * dsub; i += kFourWarpThreads) cbs[i] = p.codebooks[i];
   __syncthreads();
+  ScanWork work;
+  work.init(p);
 
   for (;;) {
-    uint32_t q = 0;
-    if (lane == 0) q = atomicAdd(p.counter, 1u);
-    q = __shfl_sync(VG_FULL_MASK, q, 0);
-    if (q >= static_cast<uint32_t>(p.nq)) break;
+    uint32_t w = 0;
+    if (lane == 0) w = atomicAdd(p.counter, 1u);
+    w = __shfl_sync(VG_FULL_MASK, w, 0);
+    if (w >= work.total) break;
+    uint32_t q;
+    int first, last;
+    size_t orow;
+    work.item(p, w, q, first, last, orow);
     const float *qv = p.qn + static_cast<size_t>(q) * d;
     WarpTopK<R> tk;
     tk.init();
@@ -90,21 +97,20 @@ __global__ void __launch_bounds__(kFourWarpThreads, 1) ivfpq_four_warp_kernel(co
     }
     uint64_t kth = min(tk.get(k - 1), kth0);
     const bool seed = p.seed_next != nullptr;
-    int first = p.probe_from ? static_cast<int>(p.probe_from[q]) : 0;
     int seed_stop = P;
     bool stopped = false;
     if (seed) {  // a seed pass scores only queries whose nearest list is this rank's
       const uint32_t l0 = p.probes[static_cast<size_t>(q) * P];
       if (l0 == 0xffffffffu || (p.owner && !p.owner[l0])) {
         seed_stop = 1;
-        first = P;
+        first = last;
       }
     }
     // probes in groups of 32, in order: lane i loads probe c0 + i (list,
     // ownership, bounds, extent) so the warp walks only the live ones with no
     // global load on its serial path; a list the group's starting bound
     // prunes stays pruned (the bound only tightens)
-    for (int c0 = first; c0 < P; c0 += 32) {
+    for (int c0 = first; c0 < last; c0 += 32) {
       if (stopped) break;
       if (seed && tk.get(k - 1) != kEmptyKey) {
         seed_stop = c0;
@@ -114,7 +120,7 @@ __global__ void __launch_bounds__(kFourWarpThreads, 1) ivfpq_four_warp_kernel(co
       uint32_t l_l = 0xffffffffu, len_l = 0;
       uint64_t lbeg_l = 0, off_l = 0;
       float lbq_l = 0.0f, lb_l = 0.0f;
-      if (c0 + lane < P) {
+      if (c0 + lane < last) {
         l_l = p.probes[pr_l];
         if (l_l != 0xffffffffu && p.owner && !p.owner[l_l]) l_l = 0xffffffffu;
         if (l_l != 0xffffffffu) {
@@ -259,7 +265,7 @@ __global__ void __launch_bounds__(kFourWarpThreads, 1) ivfpq_four_warp_kernel(co
       const bool real = i < k && key != kEmptyKey;
       count += __popc(__ballot_sync(VG_FULL_MASK, real));
       if (i < k) {
-        const size_t o = static_cast<size_t>(q) * k + i;
+        const size_t o = orow * k + i;
         if (p.out_keys) p.out_keys[o] = key;
         if (p.out_ids) {
           p.out_ids[o] = real ? p.doc_ids[key_id(key)] : 0xffffffffu;

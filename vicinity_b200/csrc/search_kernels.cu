@@ -563,6 +563,75 @@ cudaError_t launch_merge_keys(const unsigned long long *keys, size_t rows, size_
                         out_keys, s);
 }
 
+namespace {
+__device__ __forceinline__ void push_work(uint32_t item, bool heavy, uint32_t *work, uint32_t *count,
+                                          uint32_t cap) {
+  if (heavy)
+    work[atomicAdd(count, 1u)] = item;
+  else
+    work[cap - 1 - atomicAdd(count + 1, 1u)] = item;
+}
+
+__global__ void order_seed_kernel(const uint32_t *__restrict__ probes, int P, const uint8_t *__restrict__ owner,
+                                  const uint64_t *__restrict__ list_off, size_t nq, uint32_t heavy,
+                                  uint32_t *__restrict__ work, uint32_t *__restrict__ count, uint32_t cap,
+                                  uint32_t *__restrict__ seed_next) {
+  const size_t q = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (q >= nq) return;
+  const uint32_t l = probes[q * P];
+  if (l == 0xffffffffu || (owner && !owner[l])) {
+    seed_next[q] = 1;
+    return;
+  }
+  push_work(static_cast<uint32_t>(q), list_off[l + 1] - list_off[l] >= heavy, work, count, cap);
+}
+
+__global__ void order_units_kernel(const uint32_t *__restrict__ probes, int P, int G,
+                                   const uint8_t *__restrict__ owner, const uint64_t *__restrict__ list_off,
+                                   const float *__restrict__ bound, const unsigned long long *__restrict__ ceiling,
+                                   const uint32_t *__restrict__ first, size_t nq, uint32_t heavy,
+                                   uint32_t *__restrict__ work, uint32_t *__restrict__ count, uint32_t cap) {
+  const uint32_t U = static_cast<uint32_t>((P + G - 1) / G);
+  const size_t it = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (it >= nq * U) return;
+  const size_t q = it / U;
+  const int g = static_cast<int>(it - q * U);
+  const int lo = max(first ? static_cast<int>(first[q]) : 0, g * G), hi = min(P, (g + 1) * G);
+  const uint64_t c = ceiling ? ceiling[q] : kEmptyKey;
+  uint64_t vecs = 0;
+  for (int i = lo; i < hi; ++i) {
+    const uint32_t l = probes[q * P + i];
+    if (l == 0xffffffffu || (owner && !owner[l])) continue;
+    if (bound && c != kEmptyKey && bound[q * P + i] > key_dist(c + 1)) continue;  // the scan prunes it
+    vecs += list_off[l + 1] - list_off[l];
+  }
+  if (vecs) push_work(static_cast<uint32_t>(it), vecs >= heavy, work, count, cap);
+}
+}  // namespace
+
+cudaError_t launch_order_seed(const uint32_t *probes, int P, const uint8_t *owner, const uint64_t *list_off,
+                              size_t nq, uint32_t heavy, uint32_t *work, uint32_t *count, uint32_t cap,
+                              uint32_t *seed_next, cudaStream_t s) {
+  if (nq == 0) return cudaSuccess;
+  if (nq > cap) return cudaErrorInvalidValue;
+  order_seed_kernel<<<static_cast<unsigned>((nq + 255) / 256), 256, 0, s>>>(probes, P, owner, list_off, nq, heavy,
+                                                                            work, count, cap, seed_next);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_order_units(const uint32_t *probes, int P, int G, const uint8_t *owner, const uint64_t *list_off,
+                               const float *bound, const unsigned long long *ceiling, const uint32_t *first,
+                               size_t nq, uint32_t heavy, uint32_t *work, uint32_t *count, uint32_t cap,
+                               cudaStream_t s) {
+  if (G < 1 || P < 1) return cudaErrorInvalidValue;
+  const size_t items = nq * static_cast<size_t>((P + G - 1) / G);
+  if (items == 0) return cudaSuccess;
+  if (items > cap) return cudaErrorInvalidValue;
+  order_units_kernel<<<static_cast<unsigned>((items + 255) / 256), 256, 0, s>>>(
+      probes, P, G, owner, list_off, bound, ceiling, first, nq, heavy, work, count, cap);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_merge_shards(const unsigned long long *keys, int G, size_t rows, int k,
                                 const uint32_t *ids_map, uint32_t *out_ids, float *out_dist,
                                 uint32_t *out_count, unsigned long long *out_keys, cudaStream_t s) {
