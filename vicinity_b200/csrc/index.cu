@@ -1316,7 +1316,7 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   // per-query fused scan: probes -> (residual, table, scan, top-k) on chip
   VG_CU(ix->ws_scalars.reserve(64));
   uint32_t *d_counter = ix->ws_scalars.as<uint32_t>();
-  VG_CU(cudaMemsetAsync(d_counter, 0, 4, s));
+  VG_CU(cudaMemsetAsync(d_counter, 0, 16, s));  // the kernel's item counter, the work list's counts
   if (prof) {
     VG_CU(launch_probe_stats(ix->ws_probes.as<uint32_t>(), nq, static_cast<int>(P),
                              ix->world > 1 ? ix->owner.as<uint8_t>() : nullptr, Lc, ix->list_off.as<uint64_t>(),
@@ -1359,6 +1359,18 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
     sp.out_keys = ix->ws_keys.as<unsigned long long>();
   }
   if (kk <= 256) {
+    if (prune && ivfpq_scan_warp_applies(sp)) {
+      // queries whose nearest list is long (scored with no bound yet) first:
+      // a warp that takes one late sets the kernel's end
+      VG_CU(ix->ws_work.reserve(nq * 4));
+      VG_CU(launch_order_seed(ix->ws_probes.as<uint32_t>(), static_cast<int>(P), nullptr,
+                              ix->list_off.as<uint64_t>(), nq, kHeavyVectors, ix->ws_work.as<uint32_t>(),
+                              d_counter + 2, static_cast<uint32_t>(nq), nullptr, s));
+      sp.work = ix->ws_work.as<uint32_t>();
+      sp.work_count = d_counter + 2;
+      sp.work_cap = static_cast<uint32_t>(nq);
+      ix->launches += 1;
+    }
     VG_CU(vg::launch_ivfpq_scan(sp, ix->num_sms, s));
     ix->launches += 1;
   } else {

@@ -250,7 +250,8 @@ cudaError_t launch_probe_records(const uint32_t *probes, const float *lb, size_t
 
 // Work lists of a list-sharded search's two scan passes (ScanParams::work).
 // Seed pass: the queries whose probe 0 is an owned list (seed_next[q] = 1 for
-// the others, which the pass skips).  Main pass: the units (query, G probes
+// the others, which the pass skips); with seed_next null, every query, heavy
+// ones (long probe-0 list) first -- the order of a single-GPU scan.  Main pass: the units (query, G probes
 // from first[q] on) with an owned list whose bound (lbq for 4-bit codes, lb
 // for 8-bit) lies at or below the query's ceiling key.  An item whose lists
 // hold at least `heavy` vectors goes to the front (count[0]), the others to

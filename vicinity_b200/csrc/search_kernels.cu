@@ -580,7 +580,10 @@ __global__ void order_seed_kernel(const uint32_t *__restrict__ probes, int P, co
   if (q >= nq) return;
   const uint32_t l = probes[q * P];
   if (l == 0xffffffffu || (owner && !owner[l])) {
-    seed_next[q] = 1;
+    if (seed_next)
+      seed_next[q] = 1;
+    else
+      push_work(static_cast<uint32_t>(q), false, work, count, cap);
     return;
   }
   push_work(static_cast<uint32_t>(q), list_off[l + 1] - list_off[l] >= heavy, work, count, cap);
