@@ -98,6 +98,13 @@ const char *vg_version(void);
 /* Number of CUDA devices visible (0 when none). */
 int vg_device_count(int *out);
 
+/* No counterpart in the reference: runs, on `device`, the bounded-wait path
+ * of the pipelined tensor-core kernels on its own -- a wait of at most
+ * limit_us (1..1e6) microseconds on a barrier phase nothing completes, which
+ * must expire and report through the device error flag.  *out_expired = 1
+ * when it did; the device stays usable afterwards. */
+int vg_selftest_bounded_wait(int device, uint32_t limit_us, int *out_expired);
+
 /* src/ivf_pq/search.rs:382-413 (IVFPQIndex::new): InvalidConfig for a zero
  * dimension, codebook_size > 256, or num_codebooks not dividing dim. */
 int vg_ivfpq_create(size_t dim, const vg_ivfpq_params *params, int device,

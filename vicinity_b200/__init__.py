@@ -15,6 +15,7 @@ from .ivf_pq import (
     default_ivfpq_codebooks,
     flat_search_ip,
     nccl_unique_id,
+    selftest_bounded_wait,
     shard_assign_lists,
     verify_generation,
 )
@@ -31,6 +32,7 @@ __all__ = [
     "device_count",
     "flat_search_ip",
     "nccl_unique_id",
+    "selftest_bounded_wait",
     "shard_assign_lists",
     "verify_generation",
 ]

@@ -118,6 +118,7 @@ SIGNATURES = {
     "vg_last_error": (_i, [C.c_char_p, _sz]),
     "vg_version": (C.c_char_p, []),
     "vg_device_count": (_i, [C.POINTER(_i)]),
+    "vg_selftest_bounded_wait": (_i, [_i, C.c_uint32, C.POINTER(_i)]),
     "vg_ivfpq_create": (_i, [_sz, C.POINTER(VgParams), _i, C.POINTER(_vp)]),
     "vg_ivfpq_destroy": (_i, [_vp]),
     "vg_ivfpq_add": (_i, [_vp, _vp, _vp, _sz]),

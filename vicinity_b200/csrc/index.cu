@@ -1003,12 +1003,13 @@ int nccl_ok(vg_index *ix, ncclResult_t r, const char *what) {
 //      pruning bounds, valid on every rank);
 //   2. all-gather queries, probes and bounds: every rank holds the global
 //      batch (world * nq rows, rank r's rows at r * nq);
-//   3. seed: the rank owning a query's nearest list scores it; an all-reduce
-//      (min) of every query's k-th key gives every rank the k-th key of the
-//      query's nearest list -- a bound on its k-th key over every list, the
-//      one a single GPU has after that list;
+//   3. seed: the rank owning a query's nearest list scores it (and its own
+//      next lists until it keeps k keys); an all-reduce (min) of every
+//      query's k-th key gives every rank a bound on the query's k-th key over
+//      every list, the one a single GPU has after those lists;
 //   4. every rank scans its lists among the remaining probes for the global
-//      batch, from its own seed keys, keeping only keys at or below the bound;
+//      batch in units of kUnitProbes probes per query, keeping only keys at or
+//      below the bound, and merges each query's units with its seed keys;
 //   5. an all-to-all returns every query's per-rank top-k to the query's rank,
 //      which merges them (the reference's per-shard top-k merge,
 //      examples/large_scale.rs:1969-2025).
@@ -1759,6 +1760,25 @@ int vg_last_error(char *buf, size_t len) {
 }
 
 const char *vg_version(void) { return "vicinity-b200 0.1.0 (sm_100a)"; }
+
+int vg_selftest_bounded_wait(int device, uint32_t limit_us, int *out_expired) {
+  if (!out_expired) return fail(VG_ERR_INVALID_PARAMETER, "null output");
+  if (limit_us == 0 || limit_us > 1000000u) return fail(VG_ERR_INVALID_PARAMETER, "limit_us must be in 1..1000000");
+  DeviceGuard g(device);
+  int clock_khz = 0;
+  VG_CU(cudaDeviceGetAttribute(&clock_khz, cudaDevAttrClockRate, device));
+  // the limit in cycles at the part's highest clock: at any lower clock the
+  // wait lasts longer, never shorter
+  const long long cycles = static_cast<long long>(limit_us) * std::max(clock_khz, 1) / 1000;
+  DevBuf flag_d;
+  VG_CU(flag_d.reserve(sizeof(int)));
+  VG_CU(cudaMemset(flag_d.p, 0, sizeof(int)));
+  VG_CU(launch_bounded_wait_check(cycles, flag_d.as<int>(), nullptr));
+  int flag = 0;
+  VG_CU(cudaMemcpy(&flag, flag_d.p, sizeof(int), cudaMemcpyDeviceToHost));
+  *out_expired = flag == 4 ? 1 : 0;
+  return VG_OK;
+}
 
 int vg_device_count(int *out) {
   if (!out) return fail(VG_ERR_INVALID_PARAMETER, "null output");

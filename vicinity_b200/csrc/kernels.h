@@ -134,6 +134,11 @@ size_t tc_select_workspace_bytes(size_t rows, size_t cols, int P, int num_sms);
 // approximate coarse products the probe shortlist ranks.  With cmax set,
 // also cmax[r][j] (binary16, row stride cstride >= 4 ceil(cols / 128)) = the
 // largest product of columns [32 j, 32 j + 32) of row r (-inf past cols).
+// Waits on an mbarrier phase nothing completes, for at most limit_cycles SM
+// cycles (at most the pipelined kernels' own limit), then sets *error = 4:
+// the bounded-wait path of the tensor-core kernels, run on its own.
+cudaError_t launch_bounded_wait_check(long long limit_cycles, int *error, cudaStream_t s);
+
 cudaError_t launch_tc_gemm_f16(const void *a_img, size_t rows, const void *b_img, size_t cols, int d, int kp,
                                void *out, size_t ld, void *cmax, size_t cstride, int *error, int num_sms,
                                cudaStream_t s);

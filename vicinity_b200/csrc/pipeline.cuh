@@ -59,13 +59,17 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t *bar, uint32_t parit
   return ok != 0;
 }
 
-__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_sleep_for(uint64_t *bar, uint32_t parity, long long limit_cycles) {
   if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
   const long long start = clock64();
   while (!mbar_try_wait_hint(bar, parity, 20000u)) {
-    if (clock64() - start > kWaitCycles) return false;
+    if (clock64() - start > limit_cycles) return false;
   }
   return true;
+}
+
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity) {
+  return mbar_wait_sleep_for(bar, parity, kWaitCycles);
 }
 
 // Add `bytes` of expected transaction count to the current phase of *bar.

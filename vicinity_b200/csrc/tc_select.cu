@@ -1109,3 +1109,27 @@ cudaError_t launch_tc_gemm_f16(const void *a_img, size_t rows, const void *b_img
 }
 
 }  // namespace vg
+
+// ---------------------------------------------------------------------------
+// Self-check of the bounded-wait path every pipelined kernel above uses: one
+// thread waits, with the given cycle limit, on an mbarrier phase that nothing
+// completes, then reports through the error flag exactly as a kernel role
+// does when a wait runs out (code 4) and returns.
+// ---------------------------------------------------------------------------
+namespace vg {
+namespace {
+__global__ void bounded_wait_check_kernel(long long limit_cycles, int *error) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  if (!mbar_wait_sleep_for(&bar, 0, limit_cycles)) atomicExch(error, 4);
+}
+}  // namespace
+
+cudaError_t launch_bounded_wait_check(long long limit_cycles, int *error, cudaStream_t s) {
+  if (limit_cycles <= 0 || limit_cycles > kWaitCycles) return cudaErrorInvalidValue;
+  bounded_wait_check_kernel<<<1, 32, 0, s>>>(limit_cycles, error);
+  return cudaGetLastError();
+}
+}  // namespace vg

@@ -504,6 +504,15 @@ def nccl_unique_id() -> bytes:
     return bytes(buf)
 
 
+def selftest_bounded_wait(limit_us: int = 20_000, device: int = 0) -> bool:
+    """Run the tensor-core kernels' bounded-wait path on its own: a device
+    wait of at most ``limit_us`` on a barrier nothing completes.  True when
+    it expired and was reported through the device error flag."""
+    out = C.c_int(0)
+    _lib.check(_lib.load().vg_selftest_bounded_wait(device, limit_us, C.byref(out)))
+    return bool(out.value)
+
+
 def shard_assign_lists(sizes, world_size: int) -> np.ndarray:
     """Owner rank of every list (greedy size-balanced packing, host only)."""
     s = np.ascontiguousarray(sizes, dtype=np.uint64)
