@@ -336,10 +336,10 @@ int vg_flat_get_profile(const vg_flat *f, vg_search_profile *out);
  * 32 MiB device array per GPU, shared by every call: requests whose scratch
  * would exceed it (nq > 32768, or nq * k * tiles too large) return
  * VG_ERR_INVALID_PARAMETER -- split the batch.  The first call on a device
- * resolves the array's address (cudaGetSymbolAddress); make it before any
- * stream capture.  Every call, failed ones included, returns only after its
- * GPU work on the scratch is done.  Calls whose GPU work overlaps race on
- * the scratch and must be serialised by the caller. */
+ * resolves the array's address (cudaGetSymbolAddress) and caches it.  Every
+ * call, failed ones included, returns only after its GPU work on the
+ * scratch is done.  Calls whose GPU work overlaps race on the scratch and
+ * must be serialised by the caller. */
 int vg_flat_search_ip_noalloc(const float *db, size_t n, const float *queries,
                               size_t nq, size_t dim, size_t k, int device,
                               void *stream, uint32_t *out_ids, float *out_dist,

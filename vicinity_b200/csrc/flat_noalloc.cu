@@ -21,8 +21,7 @@
 //   - Host code cannot hand the array's name to a kernel (on the host it is a
 //     shadow symbol, not a device address).  The first call on each device
 //     resolves the address with cudaGetSymbolAddress while that device is
-//     current, checks the result and caches it; later calls reuse it.  Make
-//     that first call before any stream capture.
+//     current, checks the result and caches it; later calls reuse it.
 //   - Every call shares the one array and the array keeps whatever the last
 //     call left there.  Each scratch element a call reads was written earlier
 //     in the same call, so nothing has to start at zero and nothing is
