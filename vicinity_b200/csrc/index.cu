@@ -161,6 +161,9 @@ constexpr int kStats = 11;  // profiling counters (vg_index::stats)
 // query (a query with many unpruned lists spreads over several warps); items
 // whose lists hold at least kHeavyVectors vectors are started first.
 constexpr int kUnitProbes = 8;
+// Host query batches from this many rows on are uploaded in tiles that the
+// coarse stage consumes as they arrive.
+constexpr size_t kPipeMinRows = 4096;
 constexpr uint32_t kHeavyVectors = 1024;
 
 }  // namespace
@@ -230,6 +233,11 @@ struct vg_index {
   // per-tile (start, coarse done, select done) events of a tiled coarse stage,
   // read after the call's final synchronisation; tile_marks redirects marks 2-4
   std::vector<cudaEvent_t> tile_ev;
+  // host queries copied in tiles on their own stream, each tile's coarse
+  // stage waiting only for its rows (no timing on these events)
+  cudaStream_t copy_stream = nullptr;
+  cudaEvent_t copy_start = nullptr;
+  std::vector<cudaEvent_t> copy_ev;
   cudaEvent_t *tile_marks = nullptr;
   vg_search_profile prof{};
   uint64_t launches = 0;
@@ -305,6 +313,24 @@ int nccl_wait_ready(ncclComm_t comm, int timeout_ms) {
 void mark(vg_index *ix, int i) {
   if (!ix->profiling) return;
   cudaEventRecord(ix->tile_marks && i >= 2 && i <= 4 ? ix->tile_marks[i - 2] : ix->ev[i], ix->stream);
+}
+
+cudaError_t reserve_copy_pipeline(vg_index *ix, size_t tiles) {
+  if (!ix->copy_stream) {
+    cudaError_t e = cudaStreamCreateWithFlags(&ix->copy_stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return e;
+  }
+  if (!ix->copy_start) {
+    cudaError_t e = cudaEventCreateWithFlags(&ix->copy_start, cudaEventDisableTiming);
+    if (e != cudaSuccess) return e;
+  }
+  while (ix->copy_ev.size() < tiles) {
+    cudaEvent_t e = nullptr;
+    cudaError_t err = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+    if (err != cudaSuccess) return err;
+    ix->copy_ev.push_back(e);
+  }
+  return cudaSuccess;
 }
 
 cudaError_t reserve_tile_events(vg_index *ix, size_t count) {
@@ -1264,21 +1290,42 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   uint64_t launches0 = ix->launches;
 
   *reinterpret_cast<volatile int *>(ix->h_err) = 0;
+  // coarse distances + top-nprobe, tiled over queries.  Host queries of a
+  // large batch arrive in (at least two) tiles on the copy stream: a tile's
+  // coarse stage waits only for its own rows, so the upload of the later
+  // rows runs under the products and shortlist of the earlier ones.
+  const bool host_q = !is_device_ptr(queries);
+  size_t tile = coarse_tile(ix, nq, P);
+  const bool pipe = host_q && nq >= kPipeMinRows;
+  if (pipe) tile = std::min(tile, ((nq + 1) / 2 + 127) / 128 * 128);
+  const size_t ntiles = (nq + tile - 1) / tile;
   mark(ix, 0);
   const float *dq = queries;
-  if (!is_device_ptr(queries)) {
+  if (host_q) {
     VG_CU(ix->ws_q.reserve(nq * d * 4));
-    VG_CU(cudaMemcpyAsync(ix->ws_q.p, queries, nq * d * 4, cudaMemcpyHostToDevice, s));
     dq = ix->ws_q.as<float>();
+    if (pipe) {
+      VG_CU(reserve_copy_pipeline(ix, ntiles));
+      // the copies start when the stream reaches this call, not earlier
+      VG_CU(cudaEventRecord(ix->copy_start, s));
+      VG_CU(cudaStreamWaitEvent(ix->copy_stream, ix->copy_start, 0));
+      for (size_t t = 0; t < ntiles; ++t) {
+        const size_t r0 = t * tile, rows = std::min(tile, nq - r0);
+        VG_CU(cudaMemcpyAsync(ix->ws_q.as<float>() + r0 * d, queries + r0 * d, rows * d * 4, cudaMemcpyHostToDevice,
+                              ix->copy_stream));
+        VG_CU(cudaEventRecord(ix->copy_ev[t], ix->copy_stream));
+      }
+    } else {
+      VG_CU(cudaMemcpyAsync(ix->ws_q.p, queries, nq * d * 4, cudaMemcpyHostToDevice, s));
+    }
   }
-  mark(ix, 1);
   VG_CU(ix->ws_qn.reserve(nq * d * 4));
-  VG_CU(launch_normalize_rows(dq, nq, static_cast<int>(d), ix->ws_qn.as<float>(), s));
-  ix->launches += 1;
-  mark(ix, 2);
-
-  // coarse distances + top-nprobe, tiled over queries
-  const size_t tile = coarse_tile(ix, nq, P);
+  if (!pipe) {
+    mark(ix, 1);
+    VG_CU(launch_normalize_rows(dq, nq, static_cast<int>(d), ix->ws_qn.as<float>(), s));
+    ix->launches += 1;
+    mark(ix, 2);
+  }
   VG_CU(ix->ws_probes.reserve(nq * P * 4));
   VG_CU(ix->ws_pdist.reserve(nq * P * 4));
   // list pruning bounds (tables without a rotation; see launch_probe_lb)
@@ -1294,12 +1341,21 @@ int search_impl(vg_index *ix, const float *queries, size_t nq, size_t k, size_t 
   }
   auto bound_args = [&](size_t r0) { return bound_args_at(ix, P, r0, prune, recs, quant); };
   bool bounds_done = prune;
-  // a profiled tiled stage times each tile on its own events (no host wait between tiles)
-  const size_t ntiles = (nq + tile - 1) / tile;
+  // a profiled tiled stage times each tile on its own events (no host wait
+  // between tiles); with the copy pipeline, normalising a later tile's rows
+  // falls between those events
   const bool tiled_prof = prof && ntiles > 1;
   if (tiled_prof) VG_CU(reserve_tile_events(ix, 3 * ntiles));
   for (size_t r0 = 0, t = 0; r0 < nq; r0 += tile, ++t) {
     size_t rows = std::min(tile, nq - r0);
+    if (pipe) {
+      ix->tile_marks = nullptr;
+      VG_CU(cudaStreamWaitEvent(s, ix->copy_ev[t], 0));
+      if (t == 0) mark(ix, 1);
+      VG_CU(launch_normalize_rows(dq + r0 * d, rows, static_cast<int>(d), ix->ws_qn.as<float>() + r0 * d, s));
+      ix->launches += 1;
+      if (t == 0) mark(ix, 2);
+    }
     const ProbeBoundArgs ba = bound_args(r0);
     bool tile_done = false;
     if (tiled_prof) {
@@ -1847,6 +1903,9 @@ int vg_ivfpq_destroy(vg_index *ix) {
     for (int i = 0; i < kPhaseEvents; ++i)
       if (ix->ev[i]) cudaEventDestroy(ix->ev[i]);
     for (cudaEvent_t e : ix->tile_ev) cudaEventDestroy(e);
+    for (cudaEvent_t e : ix->copy_ev) cudaEventDestroy(e);
+    if (ix->copy_start) cudaEventDestroy(ix->copy_start);
+    if (ix->copy_stream) cudaStreamDestroy(ix->copy_stream);
     if (ix->h_err) cudaFreeHost(ix->h_err);
     if (ix->own_stream) cudaStreamDestroy(ix->own_stream);
     delete ix;
