@@ -527,23 +527,27 @@ size_t win_smem_bytes(int kp) {
 // out[r][c] = binary16(q_r . x_c) for every row and column, rounded to
 // nearest from the f32 accumulator: the product matrix the probe shortlist
 // (shortlist.cu) ranks.  The same staged-operand pipeline as the window
-// kernel (warp 0 bulk copies, warp 1 issues tcgen05.mma into two TMEM
-// accumulators); the two epilogue warpgroups convert their accumulator and
-// store each row's 128 products of the tile as 16-byte vectors.
+// kernel (warp 0 bulk copies, warp 1 issues tcgen05.mma into four TMEM
+// accumulators, all 512 columns); four epilogue warpgroups, one per
+// accumulator, convert theirs 64 columns at a time and store each row's
+// products of the tile as whole 128-byte lines.
 constexpr int kGemmStages = 4;
+constexpr int kGemmAcc = 4;                              // TMEM accumulators (and epilogue warpgroups)
+constexpr int kGemmEpiWarps = 4 * kGemmAcc;
+constexpr int kGemmThreads = 64 + kGemmEpiWarps * 32;    // copies, MMA, epilogue
+constexpr uint32_t kGemmTmemCols = kGemmAcc * kTile;     // 512: the whole TMEM
 
 struct GemmParams {
   const uint8_t *a_img, *b_img;
   size_t rows, cols, ld;
-  int kp, ksteps, splits;
-  uint32_t split_cols;
+  int kp, ksteps;
   __half *out;
   __half *cmax;   // [rows][cstride] largest product of every 32-column chunk (nullable)
   size_t cstride;
   int *error;
 };
 
-__global__ void __launch_bounds__(kWinThreads, 1) tc_gemm_f16_kernel(const GemmParams p) {
+__global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_f16_kernel(const GemmParams p) {
   extern __shared__ uint8_t gemm_raw[];
   const uint32_t raw = smem_u32(gemm_raw);
   uint8_t *sm = gemm_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -551,10 +555,10 @@ __global__ void __launch_bounds__(kWinThreads, 1) tc_gemm_f16_kernel(const GemmP
   const uint32_t tile_bytes = static_cast<uint32_t>(nkb) * kBlockBytes;
   uint8_t *sA = sm;
   uint8_t *sB = sm + tile_bytes;
-  uint4 *stage_out = reinterpret_cast<uint4 *>(sB + kGemmStages * tile_bytes);  // [8 warps][32 rows][16 chunks]
-  uint64_t *bars = reinterpret_cast<uint64_t *>(stage_out + kEpiWarps * 32 * 16);
+  uint4 *stage_out = reinterpret_cast<uint4 *>(sB + kGemmStages * tile_bytes);  // [16 warps][32 rows][4 chunks]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(stage_out + kGemmEpiWarps * 32 * 4);
   uint64_t *full = bars, *empty = bars + kGemmStages, *afull = bars + 2 * kGemmStages, *aempty = afull + 1;
-  uint64_t *accfull = aempty + 1, *accempty = accfull + 2, *drain = accempty + 2;
+  uint64_t *accfull = aempty + 1, *accempty = accfull + kGemmAcc, *drain = accempty + kGemmAcc;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -565,10 +569,10 @@ __global__ void __launch_bounds__(kWinThreads, 1) tc_gemm_f16_kernel(const GemmP
     }
     mbar_init(afull, 1);
     mbar_init(aempty, 1);
-    mbar_init(accfull, 1);
-    mbar_init(accfull + 1, 1);
-    mbar_init(accempty, 4);
-    mbar_init(accempty + 1, 4);
+    for (int a = 0; a < kGemmAcc; ++a) {
+      mbar_init(accfull + a, 1);
+      mbar_init(accempty + a, 4);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -576,7 +580,7 @@ __global__ void __launch_bounds__(kWinThreads, 1) tc_gemm_f16_kernel(const GemmP
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kTmemCols)
+                 "r"(kGemmTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -585,13 +589,17 @@ __global__ void __launch_bounds__(kWinThreads, 1) tc_gemm_f16_kernel(const GemmP
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const size_t rblocks = (p.rows + kTile - 1) / kTile;
-  const size_t units = rblocks * static_cast<size_t>(p.splits);
+  // this CTA's tiles: an equal share of the (row block, column tile) order,
+  // in segments of one row block each (the query tile reloads per segment)
+  const size_t ctiles = (p.cols + kTile - 1) / kTile, all_tiles = rblocks * ctiles;
+  const size_t t_begin = all_tiles * blockIdx.x / gridDim.x, t_end = all_tiles * (blockIdx.x + 1) / gridDim.x;
+  const size_t rb_first = t_begin / ctiles;
+  const size_t units = t_end > t_begin ? (t_end - 1) / ctiles - rb_first + 1 : 0;  // segments
   auto unit_range = [&](size_t u, size_t &rb, size_t &c0, uint32_t &ntiles) {
-    const size_t sp = u / rblocks;
-    rb = u - sp * rblocks;
-    c0 = sp * p.split_cols;
-    const size_t c1 = min(p.cols, c0 + p.split_cols);
-    ntiles = static_cast<uint32_t>((c1 - c0 + kTile - 1) / kTile);
+    rb = rb_first + u;
+    const size_t a = max(t_begin, rb * ctiles) - rb * ctiles, b = min(t_end, (rb + 1) * ctiles) - rb * ctiles;
+    c0 = a * kTile;
+    ntiles = static_cast<uint32_t>(b - a);
   };
   auto fail = [&](int code) {
     *abort_flag = 1;
@@ -605,7 +613,7 @@ __global__ void __launch_bounds__(kWinThreads, 1) tc_gemm_f16_kernel(const GemmP
       int last_stage_it[kGemmStages];
       for (int s = 0; s < kGemmStages; ++s) last_stage_it[s] = -1;
       bool ok = true;
-      for (size_t u = blockIdx.x; ok && u < units; u += gridDim.x, ++ul) {
+      for (size_t u = 0; ok && u < units; ++u, ++ul) {
         size_t rb, c0;
         uint32_t ntiles;
         unit_range(u, rb, c0, ntiles);
@@ -638,7 +646,7 @@ __global__ void __launch_bounds__(kWinThreads, 1) tc_gemm_f16_kernel(const GemmP
     if (lane == 0) {
       uint32_t it = 0, tc = 0, ul = 0;
       bool ok = true;
-      for (size_t u = blockIdx.x; ok && u < units; u += gridDim.x, ++ul) {
+      for (size_t u = 0; ok && u < units; ++u, ++ul) {
         size_t rb, c0;
         uint32_t ntiles;
         unit_range(u, rb, c0, ntiles);
@@ -650,7 +658,7 @@ __global__ void __launch_bounds__(kWinThreads, 1) tc_gemm_f16_kernel(const GemmP
         const uint32_t a_base = smem_u32(sA);
         for (uint32_t t = 0; t < ntiles; ++t, ++it, ++tc) {
           const uint32_t stage = it % kGemmStages, ph = (it / kGemmStages) & 1;
-          const uint32_t acc = tc & 1, aph = (tc >> 1) & 1;
+          const uint32_t acc = tc % kGemmAcc, aph = (tc / kGemmAcc) & 1;
           if (!mbar_wait_sleep(full + stage, ph) || !mbar_wait_sleep(accempty + acc, aph ^ 1)) {
             ok = false;
             break;
@@ -671,92 +679,91 @@ __global__ void __launch_bounds__(kWinThreads, 1) tc_gemm_f16_kernel(const GemmP
       mbar_wait(drain, 0);
     }
   } else {
+    // epilogue warpgroup eg takes the tiles of accumulator eg; warp ew of it
+    // owns TMEM lanes (rows) 32 ew .. 32 ew + 31, lane = row
     const int eg = (warp - 2) >> 2, ew = warp & 3;
     const int rloc = ew * 32 + lane;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(eg) * kTile;
     const bool vec = (p.ld & 7) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
+    uint4 *stg = stage_out + static_cast<size_t>(warp - 2) * 32 * 4;  // [32 rows][4 chunks of 16 B]
     uint32_t tc = 0;
     bool ok = true;
-    for (size_t u = blockIdx.x; ok && u < units; u += gridDim.x) {
+    for (size_t u = 0; ok && u < units; ++u) {
       size_t rb, c0;
       uint32_t ntiles;
       unit_range(u, rb, c0, ntiles);
       const size_t row = rb * kTile + rloc;
       const bool rv = row < p.rows;
       for (uint32_t t = 0; t < ntiles; ++t, ++tc) {
-        const uint32_t acc = tc & 1;
+        const uint32_t acc = tc % kGemmAcc;
         if (acc != static_cast<uint32_t>(eg)) continue;
-        if (!__all_sync(VG_FULL_MASK, mbar_wait_sleep(accfull + acc, (tc >> 1) & 1))) {
+        if (!__all_sync(VG_FULL_MASK, mbar_wait_sleep(accfull + acc, (tc / kGemmAcc) & 1))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        uint32_t v[kTile];
-#pragma unroll
-        for (int ch = 0; ch < kTile / 32; ++ch) tmem_ld32_nowait(t_lane + ch * 32, v + ch * 32);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(accempty + acc);
         const size_t col0 = c0 + static_cast<size_t>(t) * kTile;
         const int nval = static_cast<int>(min(static_cast<size_t>(kTile), p.cols - col0));
-        if (p.cmax && rv) {
-          // the largest product of each 32-column chunk, rounded as the
-          // products are (rounding is monotone: the largest rounded product)
-          float m4[4];
-          if (nval == kTile) {
+        uint32_t mpack[2] = {0u, 0u};  // the four chunk maxima as binary16 pairs
+#pragma unroll 1
+        for (int h = 0; h < 4; ++h) {  // 32 columns (one chunk) at a time
+          uint32_t v[32];
+          tmem_ld32_nowait(t_lane + h * 32, v);
+          tmem_wait_ld();
+          if (h == 3) {  // the accumulator is read: hand it back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(accempty + acc);
+          }
+          const int nh = min(max(nval - h * 32, 0), 32);  // valid columns in this chunk
+          // the largest product of the chunk, rounded as the products are
+          // (rounding is monotone: the largest rounded product)
+          float m = -__int_as_float(0x7f800000);
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) m4[ch] = max32(v + ch * 32);
-          } else {
+          for (int j = 0; j < 32; ++j)
+            if (j < nh) m = fmaxf(m, __uint_as_float(v[j]));
+          const uint32_t mb = static_cast<uint32_t>(__half_as_ushort(__float2half_rn(m)));
+          if (h == 0) mpack[0] = mb;
+          if (h == 1) mpack[0] |= mb << 16;
+          if (h == 2) mpack[1] = mb;
+          if (h == 3) mpack[1] |= mb << 16;
+          const size_t colh = col0 + static_cast<size_t>(h) * 32;
+          if (vec && nval == kTile) {
+            // the warp's 32 rows x 64 bytes through shared memory (chunk j of
+            // row r at r * 4 + (j ^ ((r >> 1) & 3)): conflict-free both ways),
+            // then 64-byte row pieces: 4 lanes per row, 8 rows per store
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-              float m = -__int_as_float(0x7f800000);
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (ch * 32 + j < nval) m = fmaxf(m, __uint_as_float(v[ch * 32 + j]));
-              m4[ch] = m;
+            for (int j = 0; j < 4; ++j) {
+              __half2 h0 = __floats2half2_rn(__uint_as_float(v[8 * j]), __uint_as_float(v[8 * j + 1]));
+              __half2 h1 = __floats2half2_rn(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3]));
+              __half2 h2 = __floats2half2_rn(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5]));
+              __half2 h3 = __floats2half2_rn(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7]));
+              uint4 o;
+              o.x = *reinterpret_cast<uint32_t *>(&h0);
+              o.y = *reinterpret_cast<uint32_t *>(&h1);
+              o.z = *reinterpret_cast<uint32_t *>(&h2);
+              o.w = *reinterpret_cast<uint32_t *>(&h3);
+              stg[lane * 4 + (j ^ ((lane >> 1) & 3))] = o;
             }
-          }
-          __half2 mh[2] = {__floats2half2_rn(m4[0], m4[1]), __floats2half2_rn(m4[2], m4[3])};
-          uint2 o;
-          o.x = *reinterpret_cast<uint32_t *>(&mh[0]);
-          o.y = *reinterpret_cast<uint32_t *>(&mh[1]);
-          *reinterpret_cast<uint2 *>(p.cmax + row * p.cstride + (col0 / kTile) * 4) = o;
-        }
-        if (vec && nval == kTile) {
-          // the warp's 32 rows x 256 bytes through shared memory (chunk j of
-          // row r at r * 16 + (j ^ (r & 15)): conflict-free both ways), then
-          // whole 128-byte lines: lanes 0-15 one row, lanes 16-31 the next
-          uint4 *stg = stage_out + static_cast<size_t>(warp - 2) * 32 * 16;
+            __syncwarp();
+            const int rq = lane >> 2, j = lane & 3;
 #pragma unroll
-          for (int j = 0; j < kTile / 8; ++j) {
-            __half2 h0 = __floats2half2_rn(__uint_as_float(v[8 * j]), __uint_as_float(v[8 * j + 1]));
-            __half2 h1 = __floats2half2_rn(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3]));
-            __half2 h2 = __floats2half2_rn(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5]));
-            __half2 h3 = __floats2half2_rn(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7]));
-            uint4 o;
-            o.x = *reinterpret_cast<uint32_t *>(&h0);
-            o.y = *reinterpret_cast<uint32_t *>(&h1);
-            o.z = *reinterpret_cast<uint32_t *>(&h2);
-            o.w = *reinterpret_cast<uint32_t *>(&h3);
-            stg[lane * 16 + (j ^ (lane & 15))] = o;
-          }
-          __syncwarp();
-          const int half = lane >> 4, j = lane & 15;
-#pragma unroll 4
-          for (int r2 = 0; r2 < 32; r2 += 2) {
-            const int r = r2 + half;
-            const size_t grow = rb * kTile + ew * 32 + r;
-            const uint4 o = stg[r * 16 + (j ^ (r & 15))];
-            if (grow < p.rows) *reinterpret_cast<uint4 *>(p.out + grow * p.ld + col0 + 8 * j) = o;
-          }
-          __syncwarp();
-        } else if (rv) {
-          __half *dst = p.out + row * p.ld + col0;
+            for (int r8 = 0; r8 < 32; r8 += 8) {
+              const int r = r8 + rq;
+              const size_t grow = rb * kTile + ew * 32 + r;
+              const uint4 o = stg[r * 4 + (j ^ ((r >> 1) & 3))];
+              if (grow < p.rows) *reinterpret_cast<uint4 *>(p.out + grow * p.ld + colh + 8 * j) = o;
+            }
+            __syncwarp();
+          } else if (rv) {
+            __half *dst = p.out + row * p.ld + colh;
 #pragma unroll
-          for (int j = 0; j < kTile; ++j)
-            if (j < nval) dst[j] = __float2half_rn(__uint_as_float(v[j]));
+            for (int j = 0; j < 32; ++j)
+              if (j < nh) dst[j] = __float2half_rn(__uint_as_float(v[j]));
+          }
         }
+        if (p.cmax && rv) *reinterpret_cast<uint2 *>(p.cmax + row * p.cstride + (col0 / kTile) * 4) =
+            make_uint2(mpack[0], mpack[1]);
       }
     }
     if (!ok) fail(3);
@@ -765,7 +772,7 @@ __global__ void __launch_bounds__(kWinThreads, 1) tc_gemm_f16_kernel(const GemmP
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kGemmTmemCols) : "memory");
   }
 }
 
@@ -1080,10 +1087,6 @@ cudaError_t launch_tc_gemm_f16(const void *a_img, size_t rows, const void *b_img
   if (rows == 0 || cols == 0) return cudaSuccess;
   if ((kp != 64 && kp != 128) || d < 1 || d > kp) return cudaErrorInvalidValue;
   const size_t rblocks = (rows + kTile - 1) / kTile, ctiles = (cols + kTile - 1) / kTile;
-  // column ranges of at least 8 tiles, enough work units for every SM twice
-  size_t sp = std::max<size_t>(1, (2 * static_cast<size_t>(num_sms) + rblocks - 1) / rblocks);
-  sp = std::min(sp, std::max<size_t>(1, ctiles / 8));
-  const size_t per = (ctiles + sp - 1) / sp;
   GemmParams gp{};
   gp.a_img = static_cast<const uint8_t *>(a_img);
   gp.b_img = static_cast<const uint8_t *>(b_img);
@@ -1092,19 +1095,17 @@ cudaError_t launch_tc_gemm_f16(const void *a_img, size_t rows, const void *b_img
   gp.ld = ld;
   gp.kp = kp;
   gp.ksteps = (d + 15) / 16;
-  gp.splits = static_cast<int>((ctiles + per - 1) / per);
-  gp.split_cols = static_cast<uint32_t>(per * kTile);
   gp.out = static_cast<__half *>(out);
   gp.cmax = static_cast<__half *>(cmax);
   gp.cstride = cstride;
   gp.error = error;
   const size_t smem = 1024 + static_cast<size_t>(kp / kKBlock) * kBlockBytes * (1 + kGemmStages) +
-                      static_cast<size_t>(kEpiWarps) * 32 * 16 * 16 + 16 * 8 + 16;
+                      static_cast<size_t>(kGemmEpiWarps) * 32 * 4 * 16 + 32 * 8 + 16;
   cudaError_t e = cudaFuncSetAttribute(tc_gemm_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  const size_t units = rblocks * gp.splits;
-  tc_gemm_f16_kernel<<<static_cast<unsigned>(std::min<size_t>(units, num_sms)), kWinThreads, smem, s>>>(gp);
+  // one CTA per SM, each with an equal share of the tiles
+  tc_gemm_f16_kernel<<<static_cast<unsigned>(std::min<size_t>(rblocks * ctiles, num_sms)), kGemmThreads, smem, s>>>(gp);
   return cudaGetLastError();
 }
 
