@@ -220,16 +220,32 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
       if (ow) insert(__fsub_rn(1.0f, v.w));
     });
   }
-  WarpTopK<R2> cand;
-  cand.init();
+  // the k-th smallest of the lanes' 32 x 2R values: bisection on the order
+  // key, counting the values at or below the midpoint over the warp
+  // (0xffffffff marks an empty slot and is never counted)
+  uint32_t okey[R2];
+  int have = 0;
 #pragma unroll
-  for (int r = 0; r < R2; ++r)
-    cand.add(a[r] == kInf ? kEmptyKey : pack_key(a[r], static_cast<uint32_t>(lane * R2 + r)));
-  const uint64_t ub = cand.get(k - 1);
+  for (int r = 0; r < R2; ++r) {
+    okey[r] = a[r] == kInf ? 0xffffffffu : order_key(a[r]);
+    have += okey[r] != 0xffffffffu;
+  }
+  const bool full = __reduce_add_sync(VG_FULL_MASK, static_cast<unsigned>(have)) >= static_cast<unsigned>(k);
+  uint32_t klo = 0, khi = 0xfffffffeu;
+  while (full && klo < khi) {
+    const uint32_t mid = klo + ((khi - klo) >> 1);
+    int c = 0;
+#pragma unroll
+    for (int r = 0; r < R2; ++r) c += okey[r] <= mid;
+    if (__reduce_add_sync(VG_FULL_MASK, static_cast<unsigned>(c)) >= static_cast<unsigned>(k))
+      khi = mid;
+    else
+      klo = mid + 1;
+  }
   // every exact top-k list has approximate distance <= limit (rounded up)
-  const float limit =
-      ub == kEmptyKey ? __int_as_float(0x7f800000) : __double2float_ru(static_cast<double>(key_dist(ub)) + 2.0 * eps);
-  if (!(limit < __int_as_float(0x7f800000)) && ub != kEmptyKey) exact_all = true;
+  const float limit = !full ? __int_as_float(0x7f800000)
+                            : __double2float_ru(static_cast<double>(key_to_float(klo)) + 2.0 * eps);
+  if (!(limit < __int_as_float(0x7f800000)) && full) exact_all = true;
 
   int n = 0;
   auto gather = [&](size_t c, float4 v, bool ox, bool oy, bool oz, bool ow) {
