@@ -32,7 +32,7 @@ constexpr int kSelectWarps = 8;
 // inputs are not finite, is scored exactly over every centroid.
 // ---------------------------------------------------------------------------
 namespace {
-constexpr int kShortBuf = 512;  // gathered candidates per warp
+constexpr int kShortBuf = 256;  // gathered candidates per warp
 constexpr int kChunkBuf = 256;  // candidate chunks per warp (chunk-maxima path)
 
 // 1 - sum_j q_j c_j in the reference's order (the exact coarse distance).
@@ -130,7 +130,7 @@ __device__ __forceinline__ void for_each_half_quad(const __half *__restrict__ sr
 }
 
 template <int R, typename TS>
-__global__ void __launch_bounds__(kSelectWarps * 32)
+__global__ void __launch_bounds__(kSelectWarps * 32, 4)
     shortlist_kernel(const TS *__restrict__ s, size_t rows, size_t L, size_t ld, const float *__restrict__ qn,
                      int d, const float *__restrict__ cent, const float *__restrict__ cmax_p, double rel,
                      double abs_coef, int k, uint32_t *__restrict__ out_ids, float *__restrict__ out_dist,
@@ -148,6 +148,10 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
                                                                         kSelectWarps * kShortBuf) +
                                               static_cast<size_t>(kSelectWarps) * dpad) +
                  static_cast<size_t>(warp) * kChunkBuf;  // candidate chunk ids
+  // pruning bounds of the gathered candidates, by buffer position
+  float *lbv = reinterpret_cast<float *>(cl + static_cast<size_t>(kSelectWarps - warp) * kChunkBuf) +
+               static_cast<size_t>(warp) * 2 * kShortBuf;
+  float *lbqv = lbv + kShortBuf;
   const TS *srow = s + row * ld;
   const float *qrow = qn + row * d;
   for (int j = lane; j < d; j += 32) qs[j] = qrow[j];
@@ -270,19 +274,30 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
       const __half2 slo2 = __half2half2(__float2half_rd(s_lo));
       if (chunked) {
         // the ids of chunks whose maximum reaches s_lo (no product read yet),
-        // then one chunk per lane, its 64 bytes in flight at once
+        // in ascending order (lane-major: each lane holds four consecutive
+        // chunks), then one chunk per lane, its 64 bytes in flight at once;
+        // the candidates land in the buffer in ascending list order
         const __half slo = __float2half_rd(s_lo);
         int nc = 0;
         for_each_half_quad<false>(crow, nch, lane, [&](size_t c4, __half2 lo, __half2 hi, bool ok) {
           const bool mt[4] = {ok && !__hlt(__low2half(lo), slo), ok && !__hlt(__high2half(lo), slo),
                               ok && !__hlt(__low2half(hi), slo), ok && !__hlt(__high2half(hi), slo)};
+          const int cnt = static_cast<int>(mt[0]) + mt[1] + mt[2] + mt[3];
+          if (!__any_sync(VG_FULL_MASK, cnt != 0)) return;
+          int incl = cnt;
 #pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            const unsigned m = __ballot_sync(VG_FULL_MASK, mt[h]);
-            const int pos = nc + __popc(m & ((1u << lane) - 1u));
-            if (mt[h] && pos < kChunkBuf) cl[pos] = static_cast<uint32_t>(c4 + h);
-            nc += __popc(m);
+          for (int off = 1; off < 32; off <<= 1) {
+            const int y = __shfl_up_sync(VG_FULL_MASK, incl, off);
+            if (lane >= off) incl += y;
           }
+          int pos = nc + incl - cnt;
+#pragma unroll
+          for (int h = 0; h < 4; ++h)
+            if (mt[h]) {
+              if (pos < kChunkBuf) cl[pos] = static_cast<uint32_t>(c4 + h);
+              ++pos;
+            }
+          nc += __shfl_sync(VG_FULL_MASK, incl, 31);
         });
         __syncwarp();
         if (nc > kChunkBuf) {
@@ -363,7 +378,24 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
   __syncwarp();
   WarpTopK<R> tk;
   tk.init();
-  if (!exact_all) {
+  // the chunked gather leaves the buffer in ascending list order, so keys of
+  // (distance, buffer position) order as (distance, list) do; the pruning
+  // bounds then come from the same pass over each centroid row
+  const bool by_pos = !exact_all && chunked && bnd.lb != nullptr;
+  if (by_pos) {
+    for (int i0 = 0; i0 < n; i0 += 32) {
+      uint64_t key = kEmptyKey;
+      const int i = i0 + lane;
+      if (i < n) {
+        float lbf, lbq;
+        const float dot = exact_dot_and_bounds(qs, cent, d, cvec, buf[i], bnd, lbf, lbq);
+        lbv[i] = lbf;
+        lbqv[i] = lbq;
+        key = pack_key(__fsub_rn(1.0f, dot), static_cast<uint32_t>(i));
+      }
+      tk.add(key);
+    }
+  } else if (!exact_all) {
     for (int i0 = 0; i0 < n; i0 += 32) {
       uint64_t key = kEmptyKey;
       if (i0 + lane < n) {
@@ -384,9 +416,14 @@ __global__ void __launch_bounds__(kSelectWarps * 32)
     if (i < k) {
       const uint64_t key = tk.v[r];
       const bool real = key != kEmptyKey;
-      out_ids[row * out_ld + i] = real ? key_id(key) : 0xffffffffu;
+      const uint32_t pos = key_id(key);
+      const uint32_t l = !real ? 0xffffffffu : by_pos ? buf[pos] : pos;
+      out_ids[row * out_ld + i] = l;
       out_dist[row * out_ld + i] = real ? key_dist(key) : __int_as_float(0x7f800000);
-      if (bnd.lb) write_probe_bound(qs, cent, d, cvec, key_id(key), real, row * out_ld + i, bnd);
+      if (by_pos)
+        store_probe_bound(l, real, row * out_ld + i, real ? lbv[pos] : 0.0f, real ? lbqv[pos] : 0.0f, bnd);
+      else if (bnd.lb)
+        write_probe_bound(qs, cent, d, cvec, l, real, row * out_ld + i, bnd);
     }
   }
 }
@@ -396,8 +433,8 @@ cudaError_t launch_shortlist_impl(const TS *s, size_t rows, size_t L, size_t ld,
                                   const float *cent, const float *cmax, double rel, double abs_coef, int k,
                                   uint32_t *ids, float *dst, size_t out_ld, const ProbeBoundArgs &bnd,
                                   cudaStream_t st, const __half *cmx, size_t cstride) {
-  const size_t smem =
-      static_cast<size_t>(kSelectWarps) * (kShortBuf * 4 + static_cast<size_t>((d + 3) & ~3) * 4 + kChunkBuf * 4);
+  const size_t smem = static_cast<size_t>(kSelectWarps) *
+                      (kShortBuf * 4 + static_cast<size_t>((d + 3) & ~3) * 4 + kChunkBuf * 4 + 2 * kShortBuf * 4);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(shortlist_kernel<R, TS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
