@@ -74,6 +74,26 @@ def test_flat_many_column_ranges():
     _same(*flat_search_ip(db, q, 50), *_oracle(db, q, 50))
 
 
+def test_flat_sampled_threshold_edges():
+    # 300,000 rows: the chunk maxima of every 8th operand tile bound each
+    # query's k-th product before the gather pass over every column.  k up to
+    # 256; one row duplicated across sampled and unsampled tiles (ties at the
+    # top), a tight cluster, a query opposite to a row (a negative k-th product)
+    g = np.random.default_rng(21)
+    n, d = 300_000, 96
+    db = orc.normalize(g.standard_normal((n, d)).astype(np.float32))
+    db[::997] = db[3]
+    db[150_000:150_400] = orc.normalize(db[150_000] + g.standard_normal((400, d)).astype(np.float32) * 1e-4)
+    q = orc.normalize(g.standard_normal((64, d)).astype(np.float32))
+    q[0] = db[3]
+    q[1] = db[150_000]
+    q[2] = -db[3]
+    f = FlatIndex(db)
+    for k in (1, 64, 256):
+        _same(*f.search(q, k), *_oracle(db, q, k))
+    f.close()
+
+
 def test_flat_fewer_rows_than_k_and_empty():
     g = np.random.default_rng(4)
     db = orc.normalize(g.standard_normal((70, 48)).astype(np.float32))

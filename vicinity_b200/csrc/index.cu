@@ -2323,6 +2323,12 @@ int vg_ivfpq_shard(vg_index *ix, int rank, int world_size, const uint8_t nccl_id
 
 }  // extern "C"
 
+// Flat search: every kFlatSampleStride-th operand tile forms the sample of
+// the chunk-maxima pre-pass; per-call workspace of the sampled path at most
+// kFlatWorkspaceBytes (query rows in tiles beyond it).
+constexpr size_t kFlatSampleStride = 8;
+constexpr size_t kFlatWorkspaceBytes = size_t(1) << 30;
+
 // An exhaustive inner-product index over f32 rows (distance.rs:125-130; the
 // ground truth of evaluation.rs:250-268): the rows (the caller's device rows
 // in place, or a device copy of host rows), their largest norm, and the
@@ -2333,6 +2339,10 @@ struct vg_flat {
   DevBuf own_rows;
   const float *rows = nullptr;
   DevBuf img, norm_d;
+  // every 8th whole 128-row tile of img, contiguous: the sample whose chunk
+  // maxima bound each query's k-th product before the gather pass
+  DevBuf sample_img;
+  size_t sample_cols = 0;
   int kp = 0;
   float xmax = 0.0f;
   bool tc = false;  // tensor-core path usable (rows of <= 128 floats, norms below 2^14)
@@ -2414,6 +2424,14 @@ int vg_flat_create(const float *db, size_t n, size_t dim, int device, vg_flat **
     if (f->tc) {
       VG_CU(f->img.reserve(umma_image_bytes(n, f->kp)));
       VG_CU(launch_umma_image(f->rows, n, static_cast<int>(dim), f->kp, f->img.p, nullptr, 0.0, 0.0, nullptr, s));
+      const size_t full_tiles = n / 128, tile_bytes = static_cast<size_t>(f->kp) * 256;
+      if (full_tiles >= 64) {
+        const size_t st = (full_tiles + kFlatSampleStride - 1) / kFlatSampleStride;
+        VG_CU(f->sample_img.reserve(st * tile_bytes));
+        VG_CU(cudaMemcpy2DAsync(f->sample_img.p, tile_bytes, f->img.p, tile_bytes * kFlatSampleStride, tile_bytes,
+                                st, cudaMemcpyDeviceToDevice, s));
+        f->sample_cols = st * 128;
+      }
     }
   }
   VG_CU(cudaStreamSynchronize(s));
@@ -2426,7 +2444,7 @@ int vg_flat_destroy(vg_flat *f) {
   {
     DeviceGuard g(f->device);
     if (f->own_stream) cudaStreamSynchronize(f->own_stream);
-    for (DevBuf *b : {&f->own_rows, &f->img, &f->norm_d, &f->q, &f->qimg, &f->eps, &f->ws, &f->dist, &f->chunk,
+    for (DevBuf *b : {&f->own_rows, &f->img, &f->sample_img, &f->norm_d, &f->q, &f->qimg, &f->eps, &f->ws, &f->dist, &f->chunk,
                       &f->ids, &f->dst, &f->cnt})
       b->release();
     if (f->h_err) cudaFreeHost(f->h_err);
@@ -2466,6 +2484,7 @@ int vg_flat_search(vg_flat *f, const float *queries, size_t nq, size_t k, void *
     o_cnt = f->cnt.as<uint32_t>();
   }
   *reinterpret_cast<volatile int *>(f->h_err) = 0;
+  size_t launches = 3, scan_launches = 1;  // profiling counts of this call's kernels
   if (n == 0) {
     VG_CU(cudaMemsetAsync(o_ids, 0xff, nq * k * 4, s));
     std::vector<float> inf(nq * k, __builtin_inff());
@@ -2477,10 +2496,55 @@ int vg_flat_search(vg_flat *f, const float *queries, size_t nq, size_t k, void *
     tc_error_coefs(static_cast<int>(dim), &rel, &abs_coef);
     VG_CU(f->qimg.reserve(umma_image_bytes(nq, f->kp)));
     VG_CU(f->eps.reserve(nq * 4));
-    VG_CU(f->ws.reserve(tc_select_workspace_bytes(nq, n, static_cast<int>(k), f->num_sms)));
+    // the sampled path when the sample holds at least 4k chunk maxima
+    const bool sampled = f->sample_cols / 32 >= 4 * k;
+    size_t tile_rows = nq;
+    if (sampled) {
+      const size_t per_row = tc_sampled_workspace_bytes(1, n, f->sample_cols, static_cast<int>(k));
+      tile_rows = std::min(nq, std::max<size_t>(128, kFlatWorkspaceBytes / per_row / 128 * 128));
+      VG_CU(f->ws.reserve(tc_sampled_workspace_bytes(tile_rows, n, f->sample_cols, static_cast<int>(k))));
+      // per row tile: sampled GEMM, thresholds, gather GEMMs, finisher
+      const size_t range = (size_t(16) << 20) / (static_cast<size_t>(f->kp) * 256) * 128;
+      const size_t tiles = (nq + tile_rows - 1) / tile_rows;
+      scan_launches = tiles * (2 + (n + range - 1) / range);
+      launches = 1 + tiles * (3 + (n + range - 1) / range);
+    } else {
+      VG_CU(f->ws.reserve(tc_select_workspace_bytes(nq, n, static_cast<int>(k), f->num_sms)));
+    }
     if (f->profiling) VG_CU(cudaEventRecord(f->ev[0], s));
     VG_CU(launch_umma_image(dq, nq, static_cast<int>(dim), f->kp, f->qimg.p, f->norm_d.as<float>(), rel, abs_coef,
                             f->eps.as<float>(), s));
+    for (size_t r0 = 0; sampled && r0 < nq; r0 += tile_rows) {
+      const size_t rows = std::min(tile_rows, nq - r0);
+      TcSampledSelect t{};
+      if (f->profiling) {
+        if (r0 == 0) t.marks[0] = f->ev[1];
+        if (r0 + rows == nq) {
+          t.marks[1] = f->ev[2];
+          t.marks[2] = f->ev[3];
+        }
+      }
+      t.a_img = static_cast<const uint8_t *>(f->qimg.p) + r0 / 128 * static_cast<size_t>(f->kp) * 256;
+      t.q = dq + r0 * dim;
+      t.rows = rows;
+      t.b_img = f->img.p;
+      t.x = f->rows;
+      t.cols = n;
+      t.sample_img = f->sample_img.p;
+      t.sample_cols = f->sample_cols;
+      t.d = static_cast<int>(dim);
+      t.kp = f->kp;
+      t.P = static_cast<int>(k);
+      t.mode = 1;
+      t.eps = f->eps.as<float>() + r0;
+      t.workspace = f->ws.p;
+      t.out_ids = o_ids + r0 * k;
+      t.out_dist = o_dist + r0 * k;
+      t.out_ld = k;
+      t.out_count = o_cnt ? o_cnt + r0 : nullptr;
+      t.error = f->d_err;
+      VG_CU(launch_tc_sampled_select(t, f->num_sms, s));
+    }
     TcSelect t{};
     if (f->profiling) {
       t.marks[0] = f->ev[1];
@@ -2504,7 +2568,7 @@ int vg_flat_search(vg_flat *f, const float *queries, size_t nq, size_t k, void *
     t.out_ld = k;
     t.out_count = o_cnt;
     t.error = f->d_err;
-    VG_CU(launch_tc_select(t, f->num_sms, s));
+    if (!sampled) VG_CU(launch_tc_select(t, f->num_sms, s));
   } else {
     VG_TRY(flat_exact(f, dq, nq, k, o_ids, o_dist, o_cnt, s));
   }
@@ -2527,8 +2591,8 @@ int vg_flat_search(vg_flat *f, const float *queries, size_t nq, size_t k, void *
     f->prof.total_ms += a + b + c;
     f->prof.calls += 1;
     f->prof.queries += nq;
-    f->prof.kernel_launches += 3;
-    f->prof.scan_launches += 1;
+    f->prof.kernel_launches += launches;
+    f->prof.scan_launches += scan_launches;
   }
   return VG_OK;
 }

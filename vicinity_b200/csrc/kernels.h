@@ -129,6 +129,34 @@ struct TcSelect {
 };
 size_t tc_select_workspace_bytes(size_t rows, size_t cols, int P, int num_sms);
 
+// The same result as launch_tc_select (mode 1 or 0, no probe bounds) for many
+// columns: the product GEMM first writes the chunk maxima of a sample of the
+// columns' tiles (sample_img: whole 128-column tiles of b_img, sample_cols
+// columns), whose P-th largest per row bounds the row's P-th product; one
+// more pass over every column gathers the columns that can reach the top P
+// (a few P per row), and the finisher re-scores them exactly.
+struct TcSampledSelect {
+  const void *a_img;
+  const float *q;
+  size_t rows;
+  const void *b_img;
+  const float *x;
+  size_t cols;
+  const void *sample_img;
+  size_t sample_cols;     // a multiple of 128
+  int d, kp, P, mode;     // P in 1..256
+  const float *eps;
+  void *workspace;        // tc_sampled_workspace_bytes(rows, cols, sample_cols, P)
+  uint32_t *out_ids;
+  float *out_dist;
+  size_t out_ld;
+  uint32_t *out_count;    // nullable
+  int *error;
+  cudaEvent_t marks[3];   // before the sampled pass, before the finisher, after it (nullable)
+};
+size_t tc_sampled_workspace_bytes(size_t rows, size_t cols, size_t sample_cols, int P);
+cudaError_t launch_tc_sampled_select(const TcSampledSelect &t, int num_sms, cudaStream_t s);
+
 // out[r][c] (binary16, row stride ld) = q_r . x_c from the tensor cores
 // (binary16 operand images, f32 accumulation, rounded to nearest): the
 // approximate coarse products the probe shortlist ranks.  With cmax set,

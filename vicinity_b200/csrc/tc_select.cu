@@ -541,12 +541,20 @@ struct GemmParams {
   const uint8_t *a_img, *b_img;
   size_t rows, cols, ld;
   int kp, ksteps;
-  __half *out;
+  __half *out;    // [rows][ld] binary16 products (nullable: not stored)
   __half *cmax;   // [rows][cstride] largest product of every 32-column chunk (nullable)
   size_t cstride;
+  // gather mode (slo set): every column whose f32 product reaches slo[row]
+  // is appended to the row's candidates (column + col_base, bits of the
+  // product); count[row] may exceed cap, which marks an overflow
+  const float *slo;
+  uint2 *cand;
+  uint32_t *count;
+  uint32_t cap, col_base;
   int *error;
 };
 
+template <bool kGather>
 __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_f16_kernel(const GemmParams p) {
   extern __shared__ uint8_t gemm_raw[];
   const uint32_t raw = smem_u32(gemm_raw);
@@ -684,6 +692,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_f16_kernel(const Gemm
     const int eg = (warp - 2) >> 2, ew = warp & 3;
     const int rloc = ew * 32 + lane;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(eg) * kTile;
+    const bool store = p.out != nullptr;
     const bool vec = (p.ld & 7) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0;
     uint4 *stg = stage_out + static_cast<size_t>(warp - 2) * 32 * 4;  // [32 rows][4 chunks of 16 B]
     uint32_t tc = 0;
@@ -694,6 +703,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_f16_kernel(const Gemm
       unit_range(u, rb, c0, ntiles);
       const size_t row = rb * kTile + rloc;
       const bool rv = row < p.rows;
+      const float slo_row = kGather && rv ? p.slo[row] : 0.0f;
       for (uint32_t t = 0; t < ntiles; ++t, ++tc) {
         const uint32_t acc = tc % kGemmAcc;
         if (acc != static_cast<uint32_t>(eg)) continue;
@@ -728,7 +738,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_f16_kernel(const Gemm
           if (h == 2) mpack[1] = mb;
           if (h == 3) mpack[1] |= mb << 16;
           const size_t colh = col0 + static_cast<size_t>(h) * 32;
-          if (vec && nval == kTile) {
+          if (kGather && rv && m >= slo_row) {
+            // this row's columns of the chunk at or above its threshold
+            // (rare: a few hundred per row over every column)
+            uint32_t take = 0;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              take |= (j < nh && __uint_as_float(v[j]) >= slo_row ? 1u : 0u) << j;
+            uint32_t pos = atomicAdd(p.count + row, static_cast<uint32_t>(__popc(take)));
+            uint2 *dst = p.cand + row * p.cap;
+            const uint32_t cb = p.col_base + static_cast<uint32_t>(colh);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if ((take >> j) & 1u) {
+                if (pos < p.cap) dst[pos] = make_uint2(cb + static_cast<uint32_t>(j), v[j]);
+                ++pos;
+              }
+            }
+          }
+          if (!store) {
+          } else if (vec && nval == kTile) {
             // the warp's 32 rows x 64 bytes through shared memory (chunk j of
             // row r at r * 4 + (j ^ ((r >> 1) & 3)): conflict-free both ways),
             // then 64-byte row pieces: 4 lanes per row, 8 rows per store
@@ -1081,32 +1110,208 @@ cudaError_t launch_tc_select(const TcSelect &t, int num_sms, cudaStream_t s) {
   return e;
 }
 
-cudaError_t launch_tc_gemm_f16(const void *a_img, size_t rows, const void *b_img, size_t cols, int d, int kp,
-                               void *out, size_t ld, void *cmax, size_t cstride, int *error, int num_sms,
-                               cudaStream_t s) {
-  if (rows == 0 || cols == 0) return cudaSuccess;
-  if ((kp != 64 && kp != 128) || d < 1 || d > kp) return cudaErrorInvalidValue;
-  const size_t rblocks = (rows + kTile - 1) / kTile, ctiles = (cols + kTile - 1) / kTile;
+namespace {
+
+cudaError_t launch_gemm(const GemmParams &gp, int num_sms, cudaStream_t s) {
+  const size_t rblocks = (gp.rows + kTile - 1) / kTile, ctiles = (gp.cols + kTile - 1) / kTile;
+  const size_t smem = 1024 + static_cast<size_t>(gp.kp / kKBlock) * kBlockBytes * (1 + kGemmStages) +
+                      static_cast<size_t>(kGemmEpiWarps) * 32 * 4 * 16 + 32 * 8 + 16;
+  auto kern = gp.slo ? tc_gemm_f16_kernel<true> : tc_gemm_f16_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  // one CTA per SM, each with an equal share of the tiles
+  kern<<<static_cast<unsigned>(std::min<size_t>(rblocks * ctiles, num_sms)), kGemmThreads, smem, s>>>(gp);
+  return cudaGetLastError();
+}
+
+GemmParams gemm_params(const void *a_img, size_t rows, const void *b_img, size_t cols, int d, int kp, int *error) {
   GemmParams gp{};
   gp.a_img = static_cast<const uint8_t *>(a_img);
   gp.b_img = static_cast<const uint8_t *>(b_img);
   gp.rows = rows;
   gp.cols = cols;
-  gp.ld = ld;
   gp.kp = kp;
   gp.ksteps = (d + 15) / 16;
+  gp.error = error;
+  return gp;
+}
+
+// The P-th largest chunk maximum of each row turned into the row's gather
+// threshold (warp per row).  Chunk maxima are binary16 roundings of the f32
+// products; m_P, the P-th largest over the lanes' 2R largest values, is
+// reached by P distinct chunks, so P distinct columns have products
+// s >= S = m_P - 2^-11 |m_P| - 2^-25 (one binary16 rounding) and the row's
+// P-th smallest approximate distance is at most fl(1 - S).  Every column
+// whose approximate distance is within 2 eps of that -- every column the
+// finisher may need -- has s >= slo = S - 2 eps - 2^-20 (1 + |1 - S| + 2 eps)
+// (f32 rounding of the distances, with room), rounded down.  Rows with fewer
+// than P chunks, a non-finite m_P or eps >= 1 get slo = -inf (every column
+// gathered: the finisher then scores the row exactly).
+template <int R>
+__global__ void __launch_bounds__(256) chunk_threshold_kernel(const __half *__restrict__ cmax, size_t rows,
+                                                              size_t nch, size_t cstride, int P,
+                                                              const float *__restrict__ eps, float *__restrict__ slo) {
+  constexpr int R2 = 2 * R;
+  const int lane = lane_id();
+  const size_t row = static_cast<size_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float kInf = __int_as_float(0x7f800000);
+  float a[R2];  // this lane's 2R largest maxima, descending (-inf: empty)
+#pragma unroll
+  for (int r = 0; r < R2; ++r) a[r] = -kInf;
+  auto insert = [&](float x) {
+    if (!(x > a[R2 - 1])) return;  // -inf and NaN never enter
+#pragma unroll
+    for (int r = 0; r < R2; ++r) {
+      const float hi = fmaxf(x, a[r]);
+      x = fminf(x, a[r]);
+      a[r] = hi;
+    }
+  };
+  const uint2 *src = reinterpret_cast<const uint2 *>(cmax + row * cstride);
+  for (size_t i = lane; i < nch / 4; i += 32) {
+    const uint2 w = __ldcs(src + i);
+    const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&w.x));
+    const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&w.y));
+    insert(lo.x);
+    insert(lo.y);
+    insert(hi.x);
+    insert(hi.y);
+  }
+  // the P-th smallest of -a over the warp: bisection on the order key
+  uint32_t okey[R2];
+  int have = 0;
+#pragma unroll
+  for (int r = 0; r < R2; ++r) {
+    okey[r] = a[r] == -kInf ? 0xffffffffu : order_key(-a[r]);
+    have += okey[r] != 0xffffffffu;
+  }
+  const bool full = __reduce_add_sync(VG_FULL_MASK, static_cast<unsigned>(have)) >= static_cast<unsigned>(P);
+  uint32_t klo = 0, khi = 0xfffffffeu;
+  while (full && klo < khi) {
+    const uint32_t mid = klo + ((khi - klo) >> 1);
+    int c = 0;
+#pragma unroll
+    for (int r = 0; r < R2; ++r) c += okey[r] <= mid;
+    if (__reduce_add_sync(VG_FULL_MASK, static_cast<unsigned>(c)) >= static_cast<unsigned>(P))
+      khi = mid;
+    else
+      klo = mid + 1;
+  }
+  if (lane == 0) {
+    const double e = static_cast<double>(eps[row]);
+    const double mp = full ? -static_cast<double>(key_to_float(klo)) : 0.0;
+    float out = -kInf;
+    if (full && e < 1.0 && fabs(mp) < 65536.0) {
+      const double S = mp - fabs(mp) * (1.0 / 2048.0) - 2.9802322387695312e-8;
+      out = __double2float_rd(S - 2.0 * e - 9.5367431640625e-7 * (1.0 + fabs(1.0 - S) + 2.0 * e));
+    }
+    slo[row] = out;
+  }
+}
+
+// candidates per row of the gather pass: about P x (columns / sampled
+// columns) lie at or above the sampled threshold
+uint32_t sampled_cap(size_t cols, size_t sample_cols, int P) {
+  const double ratio = static_cast<double>(cols) / static_cast<double>(std::max<size_t>(sample_cols, 1));
+  const double c = 2.0 * P * std::min(ratio, 64.0) + 512.0;
+  return static_cast<uint32_t>(std::min(32768.0, std::ceil(c / 32.0) * 32.0));
+}
+
+size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
+
+}  // namespace
+
+cudaError_t launch_tc_gemm_f16(const void *a_img, size_t rows, const void *b_img, size_t cols, int d, int kp,
+                               void *out, size_t ld, void *cmax, size_t cstride, int *error, int num_sms,
+                               cudaStream_t s) {
+  if (rows == 0 || cols == 0) return cudaSuccess;
+  if ((kp != 64 && kp != 128) || d < 1 || d > kp) return cudaErrorInvalidValue;
+  GemmParams gp = gemm_params(a_img, rows, b_img, cols, d, kp, error);
+  gp.ld = ld;
   gp.out = static_cast<__half *>(out);
   gp.cmax = static_cast<__half *>(cmax);
   gp.cstride = cstride;
-  gp.error = error;
-  const size_t smem = 1024 + static_cast<size_t>(kp / kKBlock) * kBlockBytes * (1 + kGemmStages) +
-                      static_cast<size_t>(kGemmEpiWarps) * 32 * 4 * 16 + 32 * 8 + 16;
-  cudaError_t e = cudaFuncSetAttribute(tc_gemm_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+  return launch_gemm(gp, num_sms, s);
+}
+
+size_t tc_sampled_workspace_bytes(size_t rows, size_t cols, size_t sample_cols, int P) {
+  const size_t cap = sampled_cap(cols, sample_cols, P);
+  const size_t cstride = 4 * ((sample_cols + kTile - 1) / kTile);
+  return align256(rows * cap * 8) + align256(rows * 4) * 2 + align256(rows * cstride * 2) + 256;
+}
+
+cudaError_t launch_tc_sampled_select(const TcSampledSelect &t, int num_sms, cudaStream_t s) {
+  if (t.rows == 0 || t.P <= 0) return cudaSuccess;
+  if (t.P > 256 || (t.kp != 64 && t.kp != 128) || t.cols == 0 || t.cols > 0xfffffffeull || t.sample_cols == 0 ||
+      t.d < 1 || t.d > t.kp)
+    return cudaErrorInvalidValue;
+  const uint32_t cap = sampled_cap(t.cols, t.sample_cols, t.P);
+  const size_t cstride = 4 * ((t.sample_cols + kTile - 1) / kTile);
+  uint8_t *w = static_cast<uint8_t *>(t.workspace);
+  uint2 *cand = reinterpret_cast<uint2 *>(w);
+  w += align256(t.rows * cap * 8);
+  uint32_t *count = reinterpret_cast<uint32_t *>(w);
+  w += align256(t.rows * 4);
+  float *slo = reinterpret_cast<float *>(w);
+  w += align256(t.rows * 4);
+  __half *cm = reinterpret_cast<__half *>(w);
+  cudaError_t e = cudaMemsetAsync(count, 0, t.rows * 4, s);
   if (e != cudaSuccess) return e;
-  // one CTA per SM, each with an equal share of the tiles
-  tc_gemm_f16_kernel<<<static_cast<unsigned>(std::min<size_t>(rblocks * ctiles, num_sms)), kGemmThreads, smem, s>>>(gp);
-  return cudaGetLastError();
+  if (t.marks[0]) cudaEventRecord(t.marks[0], s);
+  // 1. chunk maxima over the sampled columns, then every row's threshold
+  GemmParams gp = gemm_params(t.a_img, t.rows, t.sample_img, t.sample_cols, t.d, t.kp, t.error);
+  gp.cmax = cm;
+  gp.cstride = cstride;
+  if ((e = launch_gemm(gp, num_sms, s)) != cudaSuccess) return e;
+  const unsigned tgrid = static_cast<unsigned>((t.rows + 7) / 8);
+  if (t.P <= 32)
+    chunk_threshold_kernel<1><<<tgrid, 256, 0, s>>>(cm, t.rows, cstride, cstride, t.P, t.eps, slo);
+  else if (t.P <= 64)
+    chunk_threshold_kernel<2><<<tgrid, 256, 0, s>>>(cm, t.rows, cstride, cstride, t.P, t.eps, slo);
+  else if (t.P <= 128)
+    chunk_threshold_kernel<4><<<tgrid, 256, 0, s>>>(cm, t.rows, cstride, cstride, t.P, t.eps, slo);
+  else
+    chunk_threshold_kernel<8><<<tgrid, 256, 0, s>>>(cm, t.rows, cstride, cstride, t.P, t.eps, slo);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  // 2. every column, in ranges of 16 MB of operand tiles (shared in L2 by
+  // every CTA of a launch): columns at or above the threshold are gathered
+  const size_t tile_bytes = static_cast<size_t>(t.kp) * kTile * 2;
+  const size_t range = (16u << 20) / tile_bytes * kTile;
+  for (size_t c0 = 0; c0 < t.cols; c0 += range) {
+    GemmParams g2 = gemm_params(t.a_img, t.rows, static_cast<const uint8_t *>(t.b_img) + c0 / kTile * tile_bytes,
+                                std::min(range, t.cols - c0), t.d, t.kp, t.error);
+    g2.slo = slo;
+    g2.cand = cand;
+    g2.count = count;
+    g2.cap = cap;
+    g2.col_base = static_cast<uint32_t>(c0);
+    if ((e = launch_gemm(g2, num_sms, s)) != cudaSuccess) return e;
+  }
+  if (t.marks[1]) cudaEventRecord(t.marks[1], s);
+  // 3. the P-th smallest approximate distance over the candidates, exact
+  // re-score of those within 2 eps of it, exact top-P
+  FinParams fp{};
+  fp.cand = cand;
+  fp.count = count;
+  fp.splits = 1;
+  fp.cap = static_cast<int>(cap);
+  fp.eps = t.eps;
+  fp.q = t.q;
+  fp.x = t.x;
+  fp.rows = t.rows;
+  fp.cols = t.cols;
+  fp.d = t.d;
+  fp.P = t.P;
+  fp.mode = t.mode;
+  fp.out_ids = t.out_ids;
+  fp.out_dist = t.out_dist;
+  fp.out_ld = t.out_ld;
+  fp.out_count = t.out_count;
+  e = t.P <= 32 ? launch_finish<1>(fp, s) : t.P <= 64 ? launch_finish<2>(fp, s)
+      : t.P <= 128 ? launch_finish<4>(fp, s) : launch_finish<8>(fp, s);
+  if (e == cudaSuccess && t.marks[2]) cudaEventRecord(t.marks[2], s);
+  return e;
 }
 
 }  // namespace vg
