@@ -2326,7 +2326,7 @@ int vg_ivfpq_shard(vg_index *ix, int rank, int world_size, const uint8_t nccl_id
 // Flat search: every kFlatSampleStride-th operand tile forms the sample of
 // the chunk-maxima pre-pass; per-call workspace of the sampled path at most
 // kFlatWorkspaceBytes (query rows in tiles beyond it).
-constexpr size_t kFlatSampleStride = 8;
+constexpr size_t kFlatSampleStride = 4;
 constexpr size_t kFlatWorkspaceBytes = size_t(1) << 30;
 
 // An exhaustive inner-product index over f32 rows (distance.rs:125-130; the
@@ -2339,7 +2339,7 @@ struct vg_flat {
   DevBuf own_rows;
   const float *rows = nullptr;
   DevBuf img, norm_d;
-  // every 8th whole 128-row tile of img, contiguous: the sample whose chunk
+  // every 4th whole 128-row tile of img, contiguous: the sample whose chunk
   // maxima bound each query's k-th product before the gather pass
   DevBuf sample_img;
   size_t sample_cols = 0;

@@ -729,9 +729,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_f16_kernel(const Gemm
           // the largest product of the chunk, rounded as the products are
           // (rounding is monotone: the largest rounded product)
           float m = -__int_as_float(0x7f800000);
+          if (nh == 32) {  // a whole chunk (nh is the same for the warp): a tree
+            m = max32(v);
+          } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (j < nh) m = fmaxf(m, __uint_as_float(v[j]));
+            for (int j = 0; j < 32; ++j)
+              if (j < nh) m = fmaxf(m, __uint_as_float(v[j]));
+          }
           const uint32_t mb = static_cast<uint32_t>(__half_as_ushort(__float2half_rn(m)));
           if (h == 0) mpack[0] = mb;
           if (h == 1) mpack[0] |= mb << 16;
@@ -740,7 +744,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_f16_kernel(const Gemm
           const size_t colh = col0 + static_cast<size_t>(h) * 32;
           if (kGather && rv && m >= slo_row) {
             // this row's columns of the chunk at or above its threshold
-            // (rare: a few hundred per row over every column)
+            // (a few hundred per row over every column): the lane parks its
+            // values in its own 64-byte row of the staging buffer, 16 at a
+            // time, and stores only the columns that pass
             uint32_t take = 0;
 #pragma unroll
             for (int j = 0; j < 32; ++j)
@@ -748,10 +754,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1) tc_gemm_f16_kernel(const Gemm
             uint32_t pos = atomicAdd(p.count + row, static_cast<uint32_t>(__popc(take)));
             uint2 *dst = p.cand + row * p.cap;
             const uint32_t cb = p.col_base + static_cast<uint32_t>(colh);
+            uint32_t *park = reinterpret_cast<uint32_t *>(stg + lane * 4);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if ((take >> j) & 1u) {
-                if (pos < p.cap) dst[pos] = make_uint2(cb + static_cast<uint32_t>(j), v[j]);
+            for (int half = 0; half < 2; ++half) {
+              uint32_t t16 = (take >> (16 * half)) & 0xffffu;
+              if (!t16) continue;
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                stg[lane * 4 + c] = make_uint4(v[16 * half + 4 * c], v[16 * half + 4 * c + 1],
+                                               v[16 * half + 4 * c + 2], v[16 * half + 4 * c + 3]);
+              while (t16) {
+                const int j = __ffs(t16) - 1;
+                t16 &= t16 - 1;
+                if (pos < p.cap) dst[pos] = make_uint2(cb + static_cast<uint32_t>(16 * half + j), park[j]);
                 ++pos;
               }
             }
