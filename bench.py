@@ -573,15 +573,17 @@ def run_flat(args, cfg, world, rank, local):
             "e2e": {"value": round(e2e_value, 1), "unit": "queries/s", "h2d_bytes_per_step": nq * d * 4,
                     "d2h_bytes_per_step": nq * k * 8 + nq * 4},
             "roofline": {
-                "kernel": "tc_window_kernel (tcgen05 binary16 products, TMEM accumulators, fused histogram window)",
+                "kernel": ("tc_gemm_f16_kernel (tcgen05 binary16 products, TMEM accumulators): chunk maxima of "
+                           "every 4th column tile, per-query thresholds, then a gather pass over every column"),
                 "bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4), "traffic": None, "peak_source": f"bf16_tflops ({peak_kind})",
                 "algorithmic_flops_per_launch": flops, "launch_ms": round(win_ms, 4),
-                "note": ("algorithmic FLOPs = 2 nq n d (the reference's multiply-adds); the kernel runs two passes "
-                         "over K padded to 128, i.e. 2 x 128/100 x that on the tensor pipe"),
+                "note": ("algorithmic FLOPs = 2 nq n d (the reference's multiply-adds) over the product passes' "
+                         "time (sample pass, thresholds, gather pass); the tensor pipe runs 1.25 x that over K "
+                         "padded to whole steps of 16 (112 for d = 100)"),
             },
             "phases_ms_per_step": {"query_image_ms": round(prof["normalize_ms"] / calls, 4),
-                                   "window_ms": round(win_ms, 4),
+                                   "products_ms": round(win_ms, 4),
                                    "rescore_ms": round(prof["merge_ms"] / calls, 4)},
             "gpu_launches": int(prof["kernel_launches"]),
             "clocks": clock_info,
