@@ -306,9 +306,14 @@ int vg_flat_search_ip(const float *db, size_t n, const float *queries,
 /* An exhaustive inner-product index over n rows of `dim` floats: the same
  * search as vg_flat_search_ip, with the rows' device state (the caller's
  * device rows in place -- they must outlive the index -- or a device copy of
- * host rows, plus a binary16 image for the tensor-core products) built once.
+ * host rows, plus a binary16 image for the tensor-core products and, from
+ * 8,192 rows, a copy of every 4th 128-row tile of that image: about 2.5 n kp
+ * bytes with kp = 64 or 128 the padded row length) built once.  Searches of
+ * large databases take the queries in row tiles to keep their per-call
+ * workspace near 1 GiB.
  * The reference computes this ground truth with a loop over the rows
- * (src/benchmark/evaluation.rs:250-268, src/distance.rs:125-130). */
+ * (src/benchmark/evaluation.rs:250-268, src/distance.rs:125-130).
+ */
 typedef struct vg_flat vg_flat;
 int vg_flat_create(const float *db, size_t n, size_t dim, int device, vg_flat **out);
 int vg_flat_destroy(vg_flat *f);
