@@ -18,8 +18,11 @@ constexpr size_t kSimdBatchThreshold = 16;  // search.rs:32
 constexpr size_t kFastscanMaxCodebooks = 65535 / 255;  // pq_simd.rs:517
 
 // Sequential dot product: simd.rs:90-92 (fallback `dot`), summing products in
-// index order.  The Rust fold starts at -0.0; starting at +0.0 differs only in
-// the sign of an all-zero result, which no caller can observe (1 - dot).
+// index order.  The Rust fold starts at -0.0; starting at +0.0 differs only
+// when every product is -0.0 (the sum is then +0.0 here, -0.0 there): 1 - dot
+// cannot show it, and the flat search's -dot shows it only as the sign of a
+// zero distance for such a row (a zero query against a row of negative
+// coordinates, or the reverse).  The engine sums the same way.
 inline float dot_seq(const float *a, const float *b, size_t d) {
   float s = 0.0f;
   for (size_t j = 0; j < d; ++j) s += a[j] * b[j];

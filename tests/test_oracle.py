@@ -178,6 +178,38 @@ def test_total_order_key_matches_total_cmp():
     assert keys == sorted(keys) and len(set(keys)) == len(keys)
 
 
+def _seq_dot(a, b):
+    # simd.rs:90-92 (fallback `dot`): products rounded to f32, summed in index order
+    s = np.float32(0.0)
+    for x, y in zip(a, b):
+        s = np.float32(s + np.float32(x * y))
+    return s
+
+
+@pytest.mark.parametrize("k", [1, 10, 57, 300])
+def test_flat_search_ip_is_the_sequential_exhaustive_scan(k):
+    # distance.rs:125-130 (-dot) over every row, ranked by total_cmp as the
+    # ground truth of evaluation.rs:250-268 does, ties to the lower row, rows
+    # past n padded with 0xffffffff / +inf
+    rng = np.random.default_rng(k)
+    n, d = 200, 13
+    db = rng.standard_normal((n, d)).astype(np.float32)
+    db[50:60] = db[7]          # ties
+    db[120] = 0.0              # a zero row: distance -0.0
+    q = rng.standard_normal((4, d)).astype(np.float32)
+    q[3] = db[7] * np.float32(2.0)
+    ids, dist, cnt = orc.flat_search_ip(db, q, k)
+    for i in range(q.shape[0]):
+        ds = [np.float32(-_seq_dot(q[i], db[r])) for r in range(n)]
+        order = sorted(range(n), key=lambda r: (orc.total_order_key(float(ds[r])), r))
+        want = order[:k]
+        assert cnt[i] == min(k, n)
+        assert list(ids[i, : min(k, n)]) == want
+        assert np.array_equal(dist[i, : min(k, n)].view(np.uint32),
+                              np.array([ds[r] for r in want], np.float32).view(np.uint32))
+        assert (ids[i, n:] == 0xFFFFFFFF).all() and np.isinf(dist[i, n:]).all()
+
+
 # ---- index-level properties of search.rs ----------------------------------------
 
 def _small_index(n=256, d=16, L=32, M=4, ks=16, nprobe=32, seed=7):
